@@ -1,0 +1,330 @@
+"""Benchmark of the tinyoai B200 backend on BASELINE.json's headline workload.
+
+Workload: Clio-shaped StableLM 3B (32 layers, hidden 2560, 32
+heads x 80, 25% partial rotary, SwiGLU 6912, vocab 65536) with random-init
+N(0, 0.02) weights quantised to GGUF Q8_0; a 512-token seeded uniform prompt;
+256 greedy tokens; float32 KV. One step = one complete generation: prefill
+of the prompt, then greedy decoding. value = (512 + 256) tokens per step /
+device time per step, summed over ranks (weak scaling: every GPU runs its
+own replica; there is no collective on the data path).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Under torchrun each rank drives its own GPU; the timed region is bracketed by
+a barrier and a device synchronise and the maximum over ranks is reported.
+The reference arm (--impl reference) times the CPU restatement of the
+reference's Go scalar path (oracle/) on the host cores, on bounded samples of
+the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode & prefill tok/s, 3B StableLM Q8_0, ragged branches, 1/2/4/8 B200"
+WORKLOAD = "config 2: 3B StableLM Q8_0, prompt 512 + greedy 256, f32 KV, batch 1 per GPU"
+PROMPT, GEN = 512, 256
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+# Bytes one decode forward must move: every weight once (Q8_0: 34 bytes per
+# 32 weights), one embedding row, plus the f32 KV history read and written.
+def q8_bytes(n):
+    return n * 34 // 32
+
+
+def decode_bytes(c, T):
+    d, ff, L, V = c["hidden_size"], c["intermediate_size"], c["num_hidden_layers"], c["vocab_size"]
+    kvw = d // c["num_attention_heads"] * c["num_key_value_heads"]
+    w1 = (d + 2 * kvw + 2 * ff) * d
+    w2 = d * (d + ff)
+    weights = L * q8_bytes(w1 + w2) + q8_bytes(V * d) + q8_bytes(d)
+    kv = 2 * L * kvw * 4 * (T + 1)
+    return weights + kv, q8_bytes(w1)
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons via NVML during the timed region."""
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting", 0x1: "gpu_idle"}
+
+    def __init__(self, device):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.stop = threading.Event()
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = None
+            try:
+                import torch
+                props = torch.cuda.get_device_properties(device)
+                bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+                h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                h = nv.nvmlDeviceGetHandleByIndex(device)
+            self.nv, self.h = nv, h
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def run(self):
+        while not self.stop.is_set():
+            try:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                try:
+                    r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                except AttributeError:
+                    r = self.nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                util = self.nv.nvmlDeviceGetUtilizationRates(self.h).gpu
+                if util > 50:
+                    self.samples.append(mhz)
+                    for bit, name in self.REASONS.items():
+                        if r & bit and bit != 0x1:
+                            self.reasons.add(name)
+            except Exception:
+                pass
+            self.stop.wait(0.2)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self.run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self.stop.set()
+        if self.nv:
+            self.t.join()
+
+    def summary(self):
+        if not self.nv:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "samples": len(self.samples), "reasons": sorted(self.reasons)}
+
+
+def cpu_sample(cfg, tensors, prompt, budget_s=20.0):
+    """Times the CPU oracle (a C restatement of the reference's Go scalar path,
+    OpenMP over rows and heads on every host core) on a bounded sample of the
+    workload: a short prompt prefill and a few decode forwards of the same 3B
+    model. Returns (prefill tok/s, decode tok/s, cores, sample text)."""
+    from oracle import oracle as oc
+    cores = os.cpu_count() or 1
+    oc.set_threads(cores)
+    m = oc.StableLM(cfg, tensors, capacity=64)
+    try:
+        n_pf = 8
+        t0 = time.perf_counter()
+        m.prefill(prompt[:n_pf], chunk=128)
+        t_pf = time.perf_counter() - t0
+        n_dec, t_dec = 0, 0.0
+        while n_dec < 2 or (t_dec < budget_s / 2 and n_dec < 16):
+            t0 = time.perf_counter()
+            m.forward(int(prompt[n_pf + n_dec]), n_pf + n_dec)
+            t_dec += time.perf_counter() - t0
+            n_dec += 1
+    finally:
+        m.close()
+    sample = (f"oracle (C port of the Go scalar path, {oc.threads()} OpenMP threads): prefill of {n_pf} prompt tokens "
+              f"and {n_dec} decode forwards of the full 3B Q8_0 model; step time extrapolated as "
+              f"{PROMPT}/prefill_rate + {GEN}/decode_rate")
+    return n_pf / t_pf, n_dec / t_dec, oc.threads(), sample
+
+
+def synth(device):
+    from tinyoai_b200.synth import CLIO_3B, synth_stablelm
+    return synth_stablelm(CLIO_3B, "Q8_0", seed=0, device=device)
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    try:
+        import torch
+        dev = "cuda" if torch.cuda.is_available() else "cpu"
+    except Exception:
+        dev = "cpu"
+    cfg, tensors = synth(dev)
+    from tinyoai_b200.synth import prompt_ids
+    prompt = prompt_ids(PROMPT, cfg["vocab_size"], seed=0)
+    rates = []
+    for i in range(args.warmup + args.steps):
+        pf, dc, cores, sample = cpu_sample(cfg, tensors, prompt, budget_s=4.0)
+        if i >= args.warmup:
+            rates.append((pf, dc))
+    pf = statistics.median(r[0] for r in rates)
+    dc = statistics.median(r[1] for r in rates)
+    step_s = PROMPT / pf + GEN / dc
+    value = (PROMPT + GEN) / step_s
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64-accumulate/f32", "data": "synthetic (seeded N(0,0.02) weights, uniform ids)",
+            "config": {"workload": WORKLOAD, "prompt": PROMPT, "generate": GEN, "kv": "f32"},
+            "prefill_tok_s": pf, "decode_tok_s": dc,
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    from tinyoai_b200 import Model
+    from tinyoai_b200.synth import prompt_ids
+
+    cfg, tensors = synth(f"cuda:{local}")
+    model = Model.load_stablelm(cfg, tensors, device=local)
+    if not (rank == 0 and world == 1 and args.cpu_baseline):
+        del tensors
+        tensors = None
+    prompt = prompt_ids(PROMPT, cfg["vocab_size"], seed=rank)
+    stream = torch.cuda.current_stream()
+    sess = model.session("f32")
+    sess.set_stream(stream.cuda_stream)
+
+    def step(events=None):
+        if events:
+            events[0].record(stream)
+        sess.forward(0, prompt[:-1], want_logits=False)  # prefill of 511 tokens
+        if events:
+            events[1].record(stream)
+        out = sess.generate_greedy(PROMPT - 1, prompt[-1:], GEN)  # last prompt token + 255 decode steps
+        if events:
+            events[2].record(stream)
+        return out
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i in range(args.steps):
+            toks = step(evs[i])
+        end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    total_ms = start.elapsed_time(end)
+    pf_ms = sum(e[0].elapsed_time(e[1]) for e in evs)
+    dc_ms = sum(e[1].elapsed_time(e[2]) for e in evs)
+    t = torch.tensor([total_ms, pf_ms, dc_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, pf_ms, dc_ms = t.tolist()
+
+    # End to end through the public API: host prompt in, host tokens out,
+    # one call per step (tcu_session_generate_greedy), host-timed.
+    sess.set_stream(None)
+    e2e_ms = []
+    for i in range(max(2, args.steps // 2)):
+        t0 = time.perf_counter()
+        sess.generate_greedy(0, prompt, GEN)
+        e2e_ms.append((time.perf_counter() - t0) * 1e3)
+    e2e = torch.tensor([statistics.median(e2e_ms)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+
+    # Stage profile of one more step (CUDA events around every kernel, on the
+    # stream the kernels run on): launch counts and the dominant kernel's time.
+    sess.profile(True)
+    sess.profile_read(reset=True)
+    sess.generate_greedy(0, prompt, GEN)
+    prof = sess.profile_read(reset=True)
+    sess.profile(False)
+
+    if world > 1:
+        dist.barrier()
+    line = None
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        tok_per_step = PROMPT + GEN
+        value = world * tok_per_step * args.steps / (total_ms / 1e3)
+        launches = sum(v[0] for v in prof.values())
+        w1_n, w1_ms = prof["norm_qkv_gate_up"]
+        avg_T = PROMPT + GEN / 2
+        step_bytes, w1_bytes = decode_bytes(cfg, avg_T)
+        achieved = w1_bytes / (w1_ms / w1_n / 1e3) / 1e9 if w1_n else None
+        dec_gbs = step_bytes * GEN / (dc_ms / args.steps / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q8_0 weights, f32 activations/accumulate", "data": "synthetic (seeded N(0,0.02) weights quantised to Q8_0, uniform prompt ids)",
+            "config": {"workload": WORKLOAD, "prompt": PROMPT, "generate": GEN, "kv": "f32", "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2 (2.9 GB of weights streamed per token)"},
+            "prefill_tok_s": world * (PROMPT - 1) * args.steps / (pf_ms / 1e3),
+            "decode_tok_s": world * GEN * args.steps / (dc_ms / 1e3),
+            "decode_ms_per_token": dc_ms / args.steps / GEN,
+            "roofline": {"bound": "hbm", "kernel": "k_gemv<Q8_0, LayerNorm prologue, q/k/v + SwiGLU epilogue>",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": (achieved / hbm) if achieved else None, "peak_kind": peak_kind,
+                         "traffic": None, "bytes_per_launch": w1_bytes,
+                         "avg_launch_us": (w1_ms / w1_n * 1e3) if w1_n else None,
+                         "decode_step_gbs": dec_gbs, "decode_step_frac": dec_gbs / hbm},
+            "profile": {k: {"launches": v[0], "ms": round(v[1], 3)} for k, v in prof.items()},
+            "clocks": clocks.summary(),
+            "e2e": {"value": world * tok_per_step / (e2e.item() / 1e3), "unit": "tok/s",
+                    "h2d_bytes_per_step": PROMPT * 4, "d2h_bytes_per_step": GEN * 4},
+            "gpu_launches": int(launches * args.steps),
+            "last_tokens": [int(x) for x in toks[:8]],
+        }
+        if world == 1 and args.cpu_baseline and tensors is not None:
+            pf, dc, cores, sample = cpu_sample(cfg, tensors, prompt)
+            v = (PROMPT + GEN) / (PROMPT / pf + GEN / dc)
+            line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample,
+                                    "prefill_tok_s": pf, "decode_tok_s": dc}
+    sess.close()
+    model.close()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

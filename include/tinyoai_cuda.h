@@ -1,0 +1,190 @@
+/*
+ * tinyoai_cuda.h - C ABI of the B200 (sm_100a) inference backend for tinyoai.
+ *
+ * The Go package binds these entry points through cgo (build tag `cuda`) in
+ * place of its native MLX forwarders. Each entry point names the reference
+ * interface it replaces (path:line inside the wbrown/tinyoai project).
+ *
+ * Conventions
+ *  - Every function returns an int status: TCU_OK (0) or a negative TCU_E*
+ *    code. The message of the last failure on the calling thread is returned
+ *    by tcu_last_error() (pattern of internal/mlx/bridge.c:13-33).
+ *  - Buffers are plain host pointers owned by the caller. Nothing is retained
+ *    after a call returns except where stated (weights are copied to the GPU
+ *    during load, so the caller may free its tensor bytes afterwards).
+ *  - Handles are opaque. A session (and its branches) must be used from one
+ *    thread at a time, as the Go wrapper guarantees with its request gate
+ *    (mlx.go:32, 291-296). Distinct sessions may run concurrently.
+ *  - No call allocates host memory for the caller, and no call falls back to
+ *    the CPU: without a usable sm_100a GPU, loading fails with TCU_ENODEV.
+ */
+#ifndef TINYOAI_CUDA_H
+#define TINYOAI_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TCU_ABI_VERSION 1
+
+/* Status codes. */
+#define TCU_OK 0
+#define TCU_EINVAL (-1)    /* bad argument: token, prefix, length, shape, dtype */
+#define TCU_ENODEV (-2)    /* no usable sm_100 device */
+#define TCU_ENOMEM (-3)    /* device memory or KV pool exhausted */
+#define TCU_ECUDA (-4)     /* CUDA runtime error (message has the detail) */
+#define TCU_ECLOSED (-5)   /* handle already closed */
+#define TCU_EUNSUP (-6)    /* valid request this backend does not implement */
+#define TCU_ETIMEOUT (-7)  /* a bounded device wait expired */
+
+/* Tensor dtypes: GGUF type codes (gguf.go:177-205). */
+#define TCU_F32 0
+#define TCU_F16 1
+#define TCU_Q5_1 7
+#define TCU_Q8_0 8
+#define TCU_Q5_K 13
+#define TCU_Q6_K 14
+#define TCU_BF16 30
+
+/* One checkpoint tensor as the Go loaders hold it: weightTensor{data, dtype,
+ * shape} (safetensors.go:193-197), row-major with the file's block encoding.
+ * Names use the Hugging Face convention (stablelm.go:180-191). */
+typedef struct {
+  const char* name;
+  int32_t dtype;
+  int32_t ndim;       /* 1 or 2 */
+  int64_t shape[2];   /* shape[0] = rows (or length), shape[1] = cols */
+  const void* data;
+  uint64_t nbytes;
+} tcu_tensor;
+
+/* StableLMConfig after validate() (stablelm.go:18-111). */
+typedef struct {
+  int32_t vocab_size, hidden_size, intermediate_size, num_hidden_layers;
+  int32_t num_attention_heads, num_key_value_heads, max_position_embeddings;
+  int32_t bos_token_id, eos_token_id;
+  double layer_norm_eps, rope_theta, partial_rotary_factor;
+} tcu_stablelm_config;
+
+/* Load-time options. Zero-initialise for defaults. */
+typedef struct {
+  int32_t device;         /* CUDA ordinal */
+  int32_t kv_page_tokens; /* positions per KV page; 0 -> 32 */
+  int64_t kv_pool_bytes;  /* KV pool budget per KV dtype; 0 -> 1/4 of free HBM after weights */
+} tcu_load_options;
+
+typedef struct tcu_model tcu_model;
+typedef struct tcu_session tcu_session;
+typedef struct tcu_branches tcu_branches;
+
+/* Library and device queries. */
+int tcu_abi_version(void);
+const char* tcu_last_error(void);
+int tcu_device_count(int32_t* count);
+
+/* Replaces LoadStableLM/loadStableWeights (stablelm.go:136-199) and
+ * LoadMLXNative (mlx_native.go:56-160): validates the config, checks every
+ * tensor's shape, uploads and repacks weights into the device layout. */
+int tcu_stablelm_load(const tcu_stablelm_config* config, const tcu_tensor* tensors, int32_t n_tensors,
+                      const tcu_load_options* options, tcu_model** out);
+
+/* Replaces LoadModel/readWeights (model.go:90-166) for the legacy llama2.c
+ * checkpoint (7 x int32 header then float32 tensors), and DefaultMLX /
+ * LoadLlamaMLX (mlx_llama.go:37-53). */
+int tcu_llama_load(const void* checkpoint, uint64_t nbytes, const tcu_load_options* options, tcu_model** out);
+
+/* Model dimensions: vocab, hidden, layers, heads, kv heads, max positions. */
+int tcu_model_info(const tcu_model* model, int32_t* vocab, int32_t* hidden, int32_t* layers, int32_t* heads,
+                   int32_t* kv_heads, int32_t* max_positions);
+/* Device bytes held by weights, and by the KV pool (allocated / in use). */
+int tcu_model_memory(const tcu_model* model, uint64_t* weight_bytes, uint64_t* kv_pool_bytes, uint64_t* kv_used_bytes);
+/* Releases weights and the KV pool. Every session must be closed first. */
+int tcu_model_free(tcu_model* model);
+
+/* A generation session: the resident token prefix of one request stream and
+ * its paged KV (the state nativeMLX keeps per model, mlx_native.go:24-45).
+ * kv_dtype is TCU_F32 or TCU_F16 (StableLMOptions.KVCache, kv_cache.go:8-24). */
+int tcu_session_new(tcu_model* model, int32_t kv_dtype, tcu_session** out);
+int tcu_session_free(tcu_session* session);
+/* Number of resident positions (nativeMLX.offset). */
+int tcu_session_length(const tcu_session* session, int32_t* length);
+
+/* mlxForwarder.Forward (mlx.go:45-51, mlx_native.go:294-297): evaluates tokens
+ * at positions prefix.. after keeping the first `prefix` resident positions.
+ * When want_logits != 0 the final vocabulary row is written to logits_out
+ * (vocab floats). Requires 0 <= prefix <= length and prefix + n <= max
+ * positions. On failure the resident prefix is discarded (mlx_native.go:487-489). */
+int tcu_session_forward(tcu_session* session, int32_t prefix, const int32_t* tokens, int32_t n, int32_t want_logits,
+                        float* logits_out);
+
+/* llamaMLXForwarder.Forward with allLogits (mlx_llama.go:27-35): one logits
+ * row per input token (n x vocab floats). */
+int tcu_session_forward_all(tcu_session* session, int32_t prefix, const int32_t* tokens, int32_t n, float* logits_out);
+
+/* Greedy decoding on the device (sampleWithOptions with Temperature == 0,
+ * sampling.go:150-163 / model.go:622-630, inside the loops of
+ * stablelm.go:519-540 and mlx.go:414-468): evaluates tokens after `prefix`,
+ * then emits `steps` argmax tokens, feeding each back without a host round
+ * trip. The resident prefix afterwards holds prompt + steps-1 tokens, as in
+ * the reference loop (the final sampled token is not evaluated). */
+int tcu_session_generate_greedy(tcu_session* session, int32_t prefix, const int32_t* tokens, int32_t n, int32_t steps,
+                                int32_t* out_tokens);
+
+/* Device-side sampling shortlist over the logits of the last forward:
+ * samplingCandidates (sampling.go:112-143) over float32 logits, returning up to
+ * k (id, logit) pairs in descending order with ties broken by lower id, plus
+ * the full-vocabulary log-sum-exp (logprobs.go:64-95). */
+int tcu_session_shortlist(tcu_session* session, int32_t k, int32_t* ids, float* logits, double* logsumexp,
+                          int32_t* n_out);
+
+/* mlxForker.Fork (sessions.go:26-30, mlx_sessions.go:10-71): the child shares
+ * every full KV page copy-free (reference counted) and copies only the
+ * partially filled tail page. Parent and child then diverge independently. */
+int tcu_session_fork(tcu_session* session, tcu_session** child);
+
+/* LimitCache / SetKVBits (mlx_native.go:231-244, mlx_kv.go:78-91). cleared
+ * reports whether resident KV was discarded. */
+int tcu_session_limit(tcu_session* session, int32_t window, int32_t* cleared);
+int tcu_session_set_kv_dtype(tcu_session* session, int32_t kv_dtype, int32_t* cleared);
+/* llamaMLXForwarder.Reset: drop all resident positions. */
+int tcu_session_reset(tcu_session* session);
+
+/* Runs the session's work on a caller-owned CUDA stream (a cudaStream_t;
+ * NULL restores the session's own stream). Lets a host that already owns a
+ * stream order its copies and events with the session's kernels. */
+int tcu_session_set_stream(tcu_session* session, void* stream);
+
+/* Opt-in stage timing, the device counterpart of stableProfile
+ * (stablelm.go:229-250): when enabled, CUDA events bracket every kernel and
+ * the per-stage launch counts and milliseconds accumulate. Stages, in order:
+ * embedding, norm+q/k/v/gate/up projection, decode attention, out/down
+ * projection + residual, final norm+head, prefill projection, prefill
+ * attention, other. tcu_session_profile_read returns the number of stages
+ * (8) and fills up to n_stages entries; reset != 0 clears the totals.
+ * Profiling synchronises after every decode step, so it is for diagnosis,
+ * not for throughput runs. */
+int tcu_session_profile(tcu_session* session, int32_t enable);
+int tcu_session_profile_read(tcu_session* session, int32_t n_stages, int64_t* launches, double* ms, int32_t reset);
+
+/* mlxBrancher.NewBranches (branches.go:55-59, mlx_branches.go:25-32): count
+ * suffixes that share the first `prefix` resident positions read-only.
+ * Unlike the MLX backend, grouped-query attention is supported. */
+int tcu_branches_open(tcu_session* session, int32_t prefix, int32_t count, tcu_branches** out);
+/* mlxBranches.Forward (mlx_branches.go:120-184): one token per branch at the
+ * same absolute position; writes count x vocab logits (rows_out may be NULL
+ * to skip the copy). */
+int tcu_branches_forward(tcu_branches* branches, const int32_t* tokens, float* rows_out);
+/* Greedy argmax of each branch's last row (count ints). */
+int tcu_branches_argmax(tcu_branches* branches, int32_t* ids);
+/* mlxBranches.Close: releases suffix pages (the shared prefix stays resident)
+ * and frees the handle, which must not be used afterwards. A failed
+ * tcu_branches_forward already released the pages; close it all the same. */
+int tcu_branches_close(tcu_branches* branches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,241 @@
+"""tinyoai_b200: a B200 (sm_100a) backend for tinyoai's StableLM and llama2.c
+forward path, reached through the C ABI of include/tinyoai_cuda.h.
+
+This module is the host-side mirror of the reference's native forwarder
+interfaces, as a cgo wrapper would expose them to Go:
+
+  Session.forward          mlxForwarder.Forward            (mlx.go:45-51)
+  Session.forward_all      llamaMLXForwarder.Forward(all)  (mlx_llama.go:27-35)
+  Session.fork             mlxForker.Fork                  (sessions.go:26-30)
+  Session.new_branches     mlxBrancher.NewBranches         (branches.go:55-59)
+  Branches.forward / close mlxBranches                     (branches.go:49-54)
+  Session.limit_cache      LimitCache                      (mlx_native.go:231-244)
+  Session.set_kv_bits      SetKVBits                       (mlx_kv.go:78-91)
+  Session.reset            llamaMLXForwarder.Reset
+
+All computation runs in libtinyoai_cuda.so on the GPU; there is no CPU path.
+Errors raise BackendError carrying the library's status and message.
+"""
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+from ._lib import BackendError, check, lib
+from .checkpoint import as_bytes, dtype_code
+
+__all__ = ["Model", "Session", "Branches", "BackendError", "device_count"]
+
+
+def _i32(a):
+    a = np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+    return a, a.ctypes.data_as(C.POINTER(C.c_int32))
+
+
+def device_count():
+    n = C.c_int32()
+    check(lib().tcu_device_count(C.byref(n)))
+    return n.value
+
+
+def _options(device, kv_page_tokens, kv_pool_bytes):
+    return _lib.LoadOptions(device, kv_page_tokens, kv_pool_bytes)
+
+
+class Model:
+    """Weights resident on one GPU plus the model's paged KV pool."""
+
+    def __init__(self, handle, arch):
+        self._h = C.c_void_p(handle)
+        self.arch = arch
+        v, d, L, H, KVH, P = (C.c_int32() for _ in range(6))
+        check(lib().tcu_model_info(self._h, C.byref(v), C.byref(d), C.byref(L), C.byref(H), C.byref(KVH), C.byref(P)))
+        self.vocab_size, self.hidden_size, self.num_layers = v.value, d.value, L.value
+        self.num_heads, self.num_kv_heads, self.max_positions = H.value, KVH.value, P.value
+
+    @classmethod
+    def load_stablelm(cls, config, tensors, device=0, kv_page_tokens=0, kv_pool_bytes=0):
+        """config: validated dict (checkpoint.stablelm_config); tensors: {name:
+        (dtype name, shape, payload)} in file encoding (LoadStableLM)."""
+        cfg = _lib.StableLMConfig(
+            config["vocab_size"], config["hidden_size"], config["intermediate_size"], config["num_hidden_layers"],
+            config["num_attention_heads"], config["num_key_value_heads"], config["max_position_embeddings"],
+            int(config.get("bos_token_id", 0)), int(config.get("eos_token_id", 0)), float(config["layer_norm_eps"]),
+            float(config["rope_theta"]), float(config["partial_rotary_factor"]))
+        arr = (_lib.Tensor * len(tensors))()
+        keep = []
+        for i, (name, (dt, shape, payload)) in enumerate(tensors.items()):
+            buf = as_bytes(payload)
+            if isinstance(buf, np.ndarray):
+                ptr, n = buf.ctypes.data, buf.nbytes
+            else:
+                cb = C.create_string_buffer(bytes(buf), len(buf))
+                ptr, n = C.addressof(cb), len(buf)
+                buf = cb
+            keep.append(buf)
+            nm = name.encode()
+            keep.append(nm)
+            sh = (C.c_int64 * 2)(*(list(shape) + [0] * (2 - len(shape))))
+            arr[i] = _lib.Tensor(nm, dtype_code(dt), len(shape), sh, ptr, n)
+        out = C.c_void_p()
+        opts = _options(device, kv_page_tokens, kv_pool_bytes)
+        check(lib().tcu_stablelm_load(C.byref(cfg), arr, len(tensors), C.byref(opts), C.byref(out)))
+        m = cls(out.value, "stablelm")
+        m.config = dict(config)
+        return m
+
+    @classmethod
+    def load_llama(cls, checkpoint, device=0, kv_page_tokens=0, kv_pool_bytes=0):
+        """llama2.c checkpoint bytes (LoadModel, model.go:90-122)."""
+        buf = C.create_string_buffer(bytes(checkpoint), len(checkpoint))
+        out = C.c_void_p()
+        opts = _options(device, kv_page_tokens, kv_pool_bytes)
+        check(lib().tcu_llama_load(buf, len(checkpoint), C.byref(opts), C.byref(out)))
+        return cls(out.value, "llama")
+
+    def memory(self):
+        w, p, u = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        check(lib().tcu_model_memory(self._h, C.byref(w), C.byref(p), C.byref(u)))
+        return {"weights": w.value, "kv_pool": p.value, "kv_used": u.value}
+
+    def session(self, kv="f32"):
+        return Session(self, kv)
+
+    def close(self):
+        if self._h:
+            check(lib().tcu_model_free(self._h))
+            self._h = None
+
+
+class Session:
+    """One resident token stream with paged KV (the native forwarder)."""
+
+    def __init__(self, model, kv="f32", handle=None):
+        self.model = model
+        if kv not in ("f32", "f16"):
+            raise ValueError(f"unsupported KV cache precision {kv!r}: use f32 or f16")
+        self.kv = kv
+        if handle is None:
+            h = C.c_void_p()
+            check(lib().tcu_session_new(model._h, _lib.F32 if kv == "f32" else _lib.F16, C.byref(h)))
+            handle = h.value
+        self._h = C.c_void_p(handle)
+
+    @property
+    def length(self):
+        n = C.c_int32()
+        check(lib().tcu_session_length(self._h, C.byref(n)))
+        return n.value
+
+    def forward(self, prefix, tokens, want_logits=True):
+        t, tp = _i32(tokens)
+        if want_logits:
+            out = np.empty(self.model.vocab_size, np.float32)
+            check(lib().tcu_session_forward(self._h, prefix, tp, len(t), 1, out.ctypes.data_as(C.POINTER(C.c_float))))
+            return out
+        check(lib().tcu_session_forward(self._h, prefix, tp, len(t), 0, None))
+        return None
+
+    def forward_all(self, prefix, tokens):
+        t, tp = _i32(tokens)
+        out = np.empty((len(t), self.model.vocab_size), np.float32)
+        check(lib().tcu_session_forward_all(self._h, prefix, tp, len(t), out.ctypes.data_as(C.POINTER(C.c_float))))
+        return out
+
+    def generate_greedy(self, prefix, tokens, steps):
+        t, tp = _i32(tokens)
+        out = np.empty(steps, np.int32)
+        check(lib().tcu_session_generate_greedy(self._h, prefix, tp, len(t), steps, out.ctypes.data_as(C.POINTER(C.c_int32))))
+        return out
+
+    def shortlist(self, k):
+        ids = np.empty(k, np.int32)
+        vals = np.empty(k, np.float32)
+        lse = C.c_double()
+        n = C.c_int32()
+        check(lib().tcu_session_shortlist(self._h, k, ids.ctypes.data_as(C.POINTER(C.c_int32)),
+                                          vals.ctypes.data_as(C.POINTER(C.c_float)), C.byref(lse), C.byref(n)))
+        return ids[:n.value], vals[:n.value], lse.value
+
+    def fork(self):
+        h = C.c_void_p()
+        check(lib().tcu_session_fork(self._h, C.byref(h)))
+        return Session(self.model, self.kv, handle=h.value)
+
+    def limit_cache(self, window):
+        c = C.c_int32()
+        check(lib().tcu_session_limit(self._h, window, C.byref(c)))
+        return bool(c.value)
+
+    def set_kv_bits(self, bits):
+        """16 -> binary16 KV, 32 -> float32 KV; reports whether KV was cleared."""
+        if bits not in (16, 32):
+            raise ValueError("kv bits must be 16 or 32")
+        c = C.c_int32()
+        check(lib().tcu_session_set_kv_dtype(self._h, _lib.F16 if bits == 16 else _lib.F32, C.byref(c)))
+        self.kv = "f16" if bits == 16 else "f32"
+        return bool(c.value)
+
+    def reset(self):
+        check(lib().tcu_session_reset(self._h))
+
+    def set_stream(self, stream):
+        """Run on a caller-owned CUDA stream handle (int), or None for the
+        session's own stream."""
+        check(lib().tcu_session_set_stream(self._h, C.c_void_p(stream) if stream else None))
+
+    STAGES = ("embed", "norm_qkv_gate_up", "attention", "out_down_residual", "head", "prefill_projection",
+              "prefill_attention", "other")
+
+    def profile(self, enable=True):
+        check(lib().tcu_session_profile(self._h, int(bool(enable))))
+
+    def profile_read(self, reset=False):
+        """{stage: (launches, milliseconds)} accumulated while profiling."""
+        n = len(self.STAGES)
+        launches = (C.c_int64 * n)()
+        ms = (C.c_double * n)()
+        rc = lib().tcu_session_profile_read(self._h, n, launches, ms, int(bool(reset)))
+        if rc < 0:
+            check(rc)
+        return {name: (launches[i], ms[i]) for i, name in enumerate(self.STAGES)}
+
+    def new_branches(self, prefix, count):
+        h = C.c_void_p()
+        check(lib().tcu_branches_open(self._h, prefix, count, C.byref(h)))
+        return Branches(self, h.value, count)
+
+    def close(self):
+        if self._h:
+            check(lib().tcu_session_free(self._h))
+            self._h = None
+
+
+class Branches:
+    """count suffixes sharing a session's resident prefix read-only."""
+
+    def __init__(self, session, handle, count):
+        self.session = session
+        self.count = count
+        self._h = C.c_void_p(handle)
+
+    def forward(self, tokens, want_rows=True):
+        t, tp = _i32(tokens)
+        if len(t) != self.count:
+            raise ValueError("invalid branch batch")
+        if want_rows:
+            out = np.empty((self.count, self.session.model.vocab_size), np.float32)
+            check(lib().tcu_branches_forward(self._h, tp, out.ctypes.data_as(C.POINTER(C.c_float))))
+            return out
+        check(lib().tcu_branches_forward(self._h, tp, None))
+        return None
+
+    def argmax(self):
+        ids = np.empty(self.count, np.int32)
+        check(lib().tcu_branches_argmax(self._h, ids.ctypes.data_as(C.POINTER(C.c_int32))))
+        return ids
+
+    def close(self):
+        if self._h:
+            check(lib().tcu_branches_close(self._h))
+            self._h = None

@@ -1,0 +1,475 @@
+// Attention over the paged KV pool, RoPE, KV append and embedding gather.
+//
+// KV pool layout (one pool per KV dtype, shared by every session of a model):
+//   K, V: [layer][page][kv_head][P][head_dim]   (float32 or binary16)
+// A sequence's page table maps logical page i (positions i*P .. i*P+P-1) to a
+// physical page. Full pages may be shared by several sequences (fork,
+// branches); a sequence only ever writes pages it owns alone.
+#pragma once
+#include "common.cuh"
+
+namespace tcu {
+
+struct KVView {
+  void* k;
+  void* v;
+  int half;       // 1: binary16 storage (kv_cache.go:27-65), 0: float32
+  int P;          // positions per page
+  int num_pages;  // pages in the pool
+  int kvh, hd;
+  __device__ __forceinline__ size_t off(int layer, int page, int g, int row) const {
+    return ((((size_t)layer * num_pages + page) * kvh + g) * P + row) * hd;
+  }
+};
+
+// RoPE tables. StableLM (stablelm.go:309-326): cos/sin of the float32 angle
+// float32(pos) * (1 / float32(theta^(2i/rotary))) evaluated in float64 and
+// rounded, tabulated on the host per (pos, i < rotary/2). llama2.c
+// (model.go:611-618): the checkpoint's freq_cis_real/imag rows per (pos, i < hd/2).
+struct Rope {
+  const float2* table;  // [max_pos][pairs] (cos, sin)
+  int pairs;
+  int mode;  // 0: StableLM split-half over the first 2*pairs dims; 1: llama adjacent pairs
+};
+
+// Rotates one head vector x[hd] in place for position pos (split-half) or
+// (adjacent pairs); operations are separately rounded as in the reference.
+__device__ __forceinline__ void rope_pair(float* x, int i, const Rope& r, int pos) {
+  float2 cs = r.table[(size_t)pos * r.pairs + i];
+  if (r.mode == 0) {
+    int j = i + r.pairs;
+    float a = x[i], b = x[j];
+    x[i] = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+    x[j] = __fadd_rn(__fmul_rn(b, cs.x), __fmul_rn(a, cs.y));
+  } else {
+    int j = 2 * i;
+    float v0 = x[j], v1 = x[j + 1];
+    x[j] = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+    x[j + 1] = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+  }
+}
+
+__device__ __forceinline__ float kv_round(float v, int half) { return half ? __half2float(__float2half_rn(v)) : v; }
+
+__device__ __forceinline__ void kv_store(const KVView& kv, void* base, size_t off, float v) {
+  if (kv.half)
+    reinterpret_cast<__half*>(base)[off] = __float2half_rn(v);
+  else
+    reinterpret_cast<float*>(base)[off] = v;
+}
+
+// Loads rows [0, n) of one page (kv head g) into smem with row stride hd+1.
+__device__ __forceinline__ void load_page_rows(const KVView& kv, const void* base, int layer, int page, int g, int n,
+                                               float* dst, int dst_row0) {
+  const int hd = kv.hd;
+  const size_t o = kv.off(layer, page, g, 0);
+  if (kv.half) {
+    const __half* src = reinterpret_cast<const __half*>(base) + o;
+    for (int e = threadIdx.x; e < n * hd; e += blockDim.x) {
+      int r = e / hd, c = e % hd;
+      dst[(dst_row0 + r) * (hd + 1) + c] = __half2float(src[e]);
+    }
+  } else {
+    const float* src = reinterpret_cast<const float*>(base) + o;
+    if ((hd & 3) == 0) {
+      const float4* s4 = reinterpret_cast<const float4*>(src);
+      for (int e = threadIdx.x; e < n * hd / 4; e += blockDim.x) {
+        float4 f = s4[e];
+        int r = (e * 4) / hd, c = (e * 4) % hd;
+        float* d = dst + (dst_row0 + r) * (hd + 1) + c;
+        d[0] = f.x;
+        d[1] = f.y;
+        d[2] = f.z;
+        d[3] = f.w;
+      }
+    } else {
+      for (int e = threadIdx.x; e < n * hd; e += blockDim.x) {
+        int r = e / hd, c = e % hd;
+        dst[(dst_row0 + r) * (hd + 1) + c] = src[e];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention: one token per sequence, split over the history.
+//
+// Restates attendHeads (stablelm.go:401-427) / model.go:443-462: scores are
+// float32 q.k / float32(sqrt(hd)), softmax subtracts the maximum, and the
+// output is the probability-weighted sum of values. The history is split into
+// chunks of `split` positions handled by separate CTAs; the last CTA of each
+// (sequence, kv head) merges the partial softmax states. This CTA also
+// rotates q/k at the sequence's position and appends k/v to the KV page.
+
+struct DecodeAttnArgs {
+  int M, H, KVH, hd;
+  Rope rope;
+  const float* qkv;  // q at [m*qkv_stride + h*hd], k after H*hd, v after (H+KVH)*hd
+  int qkv_stride;
+  KVView kv;
+  int layer;
+  const int* page_table;  // [M][pt_stride]
+  int pt_stride;
+  const int* pos;  // [M]: position of the new token
+  int split;       // positions per CTA (multiple of P)
+  int max_splits;
+  float* part;    // [M][H][max_splits][hd + 2]
+  int* counters;  // [M][KVH], zero between launches
+  float* out;     // out[m*out_stride + h*hd + i]
+  int out_stride;
+  float scale;  // float32(sqrt(hd))
+};
+
+__global__ void __launch_bounds__(128) k_attn_decode(DecodeAttnArgs a) {
+  extern __shared__ __align__(16) float att_smem[];
+  const int s = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
+  const int hd = a.hd, G = a.H / a.KVH, split = a.split;
+  const int pos = a.pos[m];
+  const int T = pos + 1;
+  const int nsplit = (T + split - 1) / split;
+  if (s >= nsplit) return;
+  const int t0 = s * split;
+  const int nt = min(T, t0 + split) - t0;
+  const bool has_cur = (s == nsplit - 1);  // this chunk holds position pos
+
+  float* qs = att_smem;                   // [G][hd]
+  float* ks = qs + G * hd;                // [split][hd+1]
+  float* vs = ks + split * (hd + 1);      // [split][hd+1]
+  float* sc = vs + split * (hd + 1);      // [G][split]
+  float* cur = sc + G * split;            // [2][hd]
+  __shared__ int is_last;
+
+  const float* q_in = a.qkv + (size_t)m * a.qkv_stride;
+  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) qs[e] = q_in[(g * G) * hd + e];
+  if (has_cur) {
+    for (int e = threadIdx.x; e < hd; e += blockDim.x) {
+      cur[e] = q_in[a.H * hd + g * hd + e];
+      cur[hd + e] = q_in[(a.H + a.KVH) * hd + g * hd + e];
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * a.rope.pairs; e += blockDim.x) rope_pair(qs + (e / a.rope.pairs) * hd, e % a.rope.pairs, a.rope, pos);
+  if (has_cur)
+    for (int e = threadIdx.x; e < a.rope.pairs; e += blockDim.x) rope_pair(cur, e, a.rope, pos);
+  __syncthreads();
+  const int* pt = a.page_table + (size_t)m * a.pt_stride;
+  if (has_cur) {
+    // Round to the KV storage precision: attention reads stored values
+    // (kv_cache.go:71-86), and the new position is appended here.
+    for (int e = threadIdx.x; e < 2 * hd; e += blockDim.x) cur[e] = kv_round(cur[e], a.kv.half);
+    __syncthreads();
+    const int page = pt[pos / a.kv.P], row = pos % a.kv.P;
+    const size_t o = a.kv.off(a.layer, page, g, row);
+    for (int e = threadIdx.x; e < hd; e += blockDim.x) {
+      kv_store(a.kv, a.kv.k, o + e, cur[e]);
+      kv_store(a.kv, a.kv.v, o + e, cur[hd + e]);
+    }
+  }
+  // Stage the chunk's history (positions < pos) page by page.
+  const int n_hist = has_cur ? nt - 1 : nt;
+  for (int t = 0; t < n_hist;) {
+    const int ta = t0 + t;
+    const int page = pt[ta / a.kv.P], row = ta % a.kv.P;
+    const int n = min(n_hist - t, a.kv.P - row);
+    // rows [row, row+n) of this page
+    {
+      const size_t o = a.kv.off(a.layer, page, g, row);
+      for (int e = threadIdx.x; e < n * hd; e += blockDim.x) {
+        int r = e / hd, c = e % hd;
+        float kvk, kvv;
+        if (a.kv.half) {
+          kvk = __half2float(reinterpret_cast<const __half*>(a.kv.k)[o + e]);
+          kvv = __half2float(reinterpret_cast<const __half*>(a.kv.v)[o + e]);
+        } else {
+          kvk = reinterpret_cast<const float*>(a.kv.k)[o + e];
+          kvv = reinterpret_cast<const float*>(a.kv.v)[o + e];
+        }
+        ks[(t + r) * (hd + 1) + c] = kvk;
+        vs[(t + r) * (hd + 1) + c] = kvv;
+      }
+    }
+    t += n;
+  }
+  if (has_cur) {
+    for (int e = threadIdx.x; e < hd; e += blockDim.x) {
+      ks[(nt - 1) * (hd + 1) + e] = cur[e];
+      vs[(nt - 1) * (hd + 1) + e] = cur[hd + e];
+    }
+  }
+  __syncthreads();
+  // Scores.
+  for (int e = threadIdx.x; e < G * split; e += blockDim.x) {
+    const int hh = e / split, t = e % split;
+    if (t < nt) {
+      const float* q = qs + hh * hd;
+      const float* k = ks + t * (hd + 1);
+      float d = 0.f;
+      for (int i = 0; i < hd; i++) d = fmaf(q[i], k[i], d);
+      sc[hh * split + t] = __fdiv_rn(d, a.scale);
+    }
+  }
+  __syncthreads();
+  // Per-head local softmax state.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  __shared__ float mloc[32], lloc[32];
+  for (int hh = warp; hh < G; hh += nwarps) {
+    float mx = -INFINITY;
+    for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, sc[hh * split + t]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float l = 0.f;
+    for (int t = lane; t < nt; t += 32) {
+      float p = expf(sc[hh * split + t] - mx);
+      sc[hh * split + t] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      mloc[hh] = mx;
+      lloc[hh] = l;
+    }
+  }
+  __syncthreads();
+  float* part = a.part + ((size_t)m * a.H + g * G) * a.max_splits * (hd + 2);
+  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
+    const int hh = e / hd, i = e % hd;
+    float o = 0.f;
+    for (int t = 0; t < nt; t++) o = fmaf(sc[hh * split + t], vs[t * (hd + 1) + i], o);
+    part[((size_t)hh * a.max_splits + s) * (hd + 2) + i] = o;
+  }
+  if (threadIdx.x < G) {
+    part[((size_t)threadIdx.x * a.max_splits + s) * (hd + 2) + hd] = mloc[threadIdx.x];
+    part[((size_t)threadIdx.x * a.max_splits + s) * (hd + 2) + hd + 1] = lloc[threadIdx.x];
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int prev = atomicAdd(a.counters + m * a.KVH + g, 1);
+    is_last = (prev == nsplit - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // Merge the nsplit partial states of each head in the group.
+  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
+    const int hh = e / hd, i = e % hd;
+    const float* ph = part + (size_t)hh * a.max_splits * (hd + 2);
+    float mx = -INFINITY;
+    for (int j = 0; j < nsplit; j++) mx = fmaxf(mx, __ldcg(ph + (size_t)j * (hd + 2) + hd));
+    float l = 0.f, o = 0.f;
+    for (int j = 0; j < nsplit; j++) {
+      const float* pj = ph + (size_t)j * (hd + 2);
+      float w = expf(__ldcg(pj + hd) - mx);
+      l = fmaf(__ldcg(pj + hd + 1), w, l);
+      o = fmaf(__ldcg(pj + i), w, o);
+    }
+    a.out[(size_t)m * a.out_stride + (g * G + hh) * hd + i] = __fdiv_rn(o, l);
+  }
+  if (threadIdx.x == 0) a.counters[m * a.KVH + g] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Prefill: rotate q/k of n new tokens (positions start..start+n-1) in place
+// and append k/v to the pages (prefill.go:74-84).
+struct RopeStoreArgs {
+  int n, H, KVH, hd, start;
+  Rope rope;
+  float* qkv;
+  int qkv_stride;
+  KVView kv;
+  int layer;
+  const int* page_table;
+};
+
+__global__ void k_rope_store(RopeStoreArgs a) {
+  const int j = blockIdx.x;
+  const int pos = a.start + j;
+  float* row = a.qkv + (size_t)j * a.qkv_stride;
+  const int hd = a.hd, pairs = a.rope.pairs;
+  // q and k heads: rotate (each pair touched by exactly one thread).
+  for (int e = threadIdx.x; e < (a.H + a.KVH) * pairs; e += blockDim.x) rope_pair(row + (e / pairs) * hd, e % pairs, a.rope, pos);
+  __syncthreads();
+  const int page = a.page_table[pos / a.kv.P], r = pos % a.kv.P;
+  for (int e = threadIdx.x; e < a.KVH * hd; e += blockDim.x) {
+    const int g = e / hd, i = e % hd;
+    const size_t o = a.kv.off(a.layer, page, g, r) + i;
+    kv_store(a.kv, a.kv.k, o, row[a.H * hd + e]);
+    kv_store(a.kv, a.kv.v, o, row[(a.H + a.KVH) * hd + e]);
+  }
+}
+
+// Causal attention of n queries (positions start..start+n-1, already rotated)
+// over positions [0, start+n) of one sequence (attention.go:6-45, scalar build:
+// every query attends to its exact causal prefix).
+struct PrefillAttnArgs {
+  int n, H, KVH, hd, start;
+  const float* qkv;
+  int qkv_stride;
+  KVView kv;
+  int layer;
+  const int* page_table;
+  float* out;
+  int out_stride;
+  float scale;
+};
+
+constexpr int PA_QT = 16;  // queries per CTA
+constexpr int PA_KT = 64;  // keys per tile
+
+__global__ void __launch_bounds__(128) k_attn_prefill(PrefillAttnArgs a) {
+  extern __shared__ __align__(16) float pa_smem[];
+  const int hd = a.hd, h = blockIdx.y, g = h / (a.H / a.KVH);
+  const int q0 = blockIdx.x * PA_QT;
+  const int nq = min(PA_QT, a.n - q0);
+  float* qs = pa_smem;                    // [QT][hd+1]
+  float* ks = qs + PA_QT * (hd + 1);      // [KT][hd+1]
+  float* vs = ks + PA_KT * (hd + 1);      // [KT][hd+1]
+  float* ps = vs + PA_KT * (hd + 1);      // [QT][KT]
+  __shared__ float mrow[PA_QT], lrow[PA_QT], alpha[PA_QT];
+  for (int e = threadIdx.x; e < PA_QT * hd; e += blockDim.x) {
+    const int qi = e / hd, i = e % hd;
+    qs[qi * (hd + 1) + i] = qi < nq ? a.qkv[(size_t)(q0 + qi) * a.qkv_stride + h * hd + i] : 0.f;
+  }
+  if (threadIdx.x < PA_QT) {
+    mrow[threadIdx.x] = -INFINITY;
+    lrow[threadIdx.x] = 0.f;
+  }
+  // Output accumulators: thread owns (qi, i) pairs e = tid + 128*j.
+  constexpr int MAXO = (PA_QT * 128 + 127) / 128;  // supports hd <= 128
+  float acc[MAXO];
+#pragma unroll
+  for (int j = 0; j < MAXO; j++) acc[j] = 0.f;
+  const int last_pos = a.start + q0 + nq - 1;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int t0 = 0; t0 <= last_pos; t0 += PA_KT) {
+    const int nt = min(PA_KT, last_pos + 1 - t0);
+    __syncthreads();
+    for (int t = 0; t < nt;) {
+      const int ta = t0 + t;
+      const int page = a.page_table[ta / a.kv.P], row = ta % a.kv.P;
+      const int n = min(nt - t, a.kv.P - row);
+      const size_t o = a.kv.off(a.layer, page, g, row);
+      for (int e = threadIdx.x; e < n * hd; e += blockDim.x) {
+        const int r = e / hd, c = e % hd;
+        float kk, vv;
+        if (a.kv.half) {
+          kk = __half2float(reinterpret_cast<const __half*>(a.kv.k)[o + e]);
+          vv = __half2float(reinterpret_cast<const __half*>(a.kv.v)[o + e]);
+        } else {
+          kk = reinterpret_cast<const float*>(a.kv.k)[o + e];
+          vv = reinterpret_cast<const float*>(a.kv.v)[o + e];
+        }
+        ks[(t + r) * (hd + 1) + c] = kk;
+        vs[(t + r) * (hd + 1) + c] = vv;
+      }
+      t += n;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < PA_QT * PA_KT; e += blockDim.x) {
+      const int qi = e / PA_KT, t = e % PA_KT;
+      float sv = -INFINITY;
+      if (qi < nq && t < nt && t0 + t <= a.start + q0 + qi) {
+        const float* q = qs + qi * (hd + 1);
+        const float* k = ks + t * (hd + 1);
+        float d = 0.f;
+        for (int i = 0; i < hd; i++) d = fmaf(q[i], k[i], d);
+        sv = __fdiv_rn(d, a.scale);
+      }
+      ps[qi * PA_KT + t] = sv;
+    }
+    __syncthreads();
+    for (int qi = warp; qi < PA_QT; qi += 4) {
+      float mx = -INFINITY;
+      for (int t = lane; t < PA_KT; t += 32) mx = fmaxf(mx, ps[qi * PA_KT + t]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mnew = fmaxf(mrow[qi], mx);
+      float l = 0.f;
+      for (int t = lane; t < PA_KT; t += 32) {
+        float sv = ps[qi * PA_KT + t];
+        float p = (sv == -INFINITY) ? 0.f : expf(sv - mnew);
+        ps[qi * PA_KT + t] = p;
+        l += p;
+      }
+      l = warp_sum(l);
+      if (lane == 0) {
+        float al = (mrow[qi] == -INFINITY) ? 0.f : expf(mrow[qi] - mnew);
+        alpha[qi] = al;
+        lrow[qi] = lrow[qi] * al + l;
+        mrow[qi] = mnew;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < MAXO; j++) {
+      const int e = threadIdx.x + 128 * j;
+      if (e < PA_QT * hd) {
+        const int qi = e / hd, i = e % hd;
+        float o = acc[j] * alpha[qi];
+        for (int t = 0; t < nt; t++) o = fmaf(ps[qi * PA_KT + t], vs[t * (hd + 1) + i], o);
+        acc[j] = o;
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < MAXO; j++) {
+    const int e = threadIdx.x + 128 * j;
+    if (e < PA_QT * hd) {
+      const int qi = e / hd, i = e % hd;
+      if (qi < nq) a.out[(size_t)(q0 + qi) * a.out_stride + h * hd + i] = __fdiv_rn(acc[j], lrow[qi]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Embedding rows (stablelm.go:338, prefill.go:58-60, model.go:419). In step
+// mode the token of sequence m is the argmax of the previous step
+// (greedy decoding kept on the device), and the step bookkeeping advances.
+struct EmbedArgs {
+  DMat E;
+  int n;
+  const int* tokens;  // [n] (token mode)
+  // step mode (tokens == nullptr)
+  unsigned long long* argmax;  // [n], consumed and cleared
+  int* pos;                    // [n], advanced by one
+  int* out_tokens;             // [n][out_stride] token log
+  int out_stride;
+  int* out_count;              // [n]
+  float* x;
+  int x_stride;
+};
+
+__global__ void k_embed(EmbedArgs a) {
+  const int m = blockIdx.x;
+  __shared__ int tok;
+  if (threadIdx.x == 0) {
+    int t;
+    if (a.tokens) {
+      t = a.tokens[m];
+    } else {
+      t = argmax_index(a.argmax[m]);
+      a.argmax[m] = 0ull;
+      a.pos[m] += 1;
+      int c = a.out_count[m];
+      a.out_tokens[(size_t)m * a.out_stride + c] = t;
+      a.out_count[m] = c + 1;
+    }
+    tok = (t >= 0 && t < a.E.rows) ? t : 0;
+  }
+  __syncthreads();
+  const int d = a.E.cols;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) a.x[(size_t)m * a.x_stride + i] = dmat_at(a.E, tok, i);
+}
+
+// Writes the final greedy token (the argmax of the last evaluated step).
+__global__ void k_finish_greedy(const unsigned long long* argmax, int* out_tokens, int out_stride, int* out_count, int n) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m < n) {
+    int c = out_count[m];
+    out_tokens[(size_t)m * out_stride + c] = argmax_index(argmax[m]);
+    out_count[m] = c + 1;
+  }
+}
+
+}  // namespace tcu

@@ -1,0 +1,155 @@
+// Load-time repacking, KV page copy-on-write and the sampling shortlist.
+#pragma once
+#include "common.cuh"
+
+namespace tcu {
+
+// Copies a checkpoint tensor (file encoding) into a device matrix at
+// (row0 + i*row_step, col0), splitting Q8_0 blocks (gguf.go:186-189: 2-byte
+// binary16 scale + 32 int8) into the quant and scale planes.
+struct RepackArgs {
+  const uint8_t* raw;
+  int fmt;
+  int rows, cols;  // source shape
+  DMat dst;        // destination (dst.w / dst.s writable)
+  int row0, row_step, col0;
+};
+
+__global__ void k_repack(RepackArgs a) {
+  const int K2 = a.dst.cols;
+  uint8_t* dw = const_cast<uint8_t*>(a.dst.w);
+  if (a.fmt == FMT_Q8_0) {
+    const int nb = a.cols / 32;
+    const size_t total = (size_t)a.rows * nb;
+    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
+      const int r = (int)(idx / nb), b = (int)(idx % nb);
+      const uint8_t* blk = a.raw + idx * 34;
+      const int dr = a.row0 + r * a.row_step;
+      __half* ds = const_cast<__half*>(a.dst.s);
+      ds[(size_t)dr * (K2 / 32) + a.col0 / 32 + b] = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
+      uint8_t* q = dw + (size_t)dr * K2 + a.col0 + b * 32;
+#pragma unroll
+      for (int i = 0; i < 32; i++) q[i] = blk[2 + i];
+    }
+  } else if (a.fmt == FMT_F32 || a.fmt == FMT_F16 || a.fmt == FMT_BF16) {
+    const int es = a.fmt == FMT_F32 ? 4 : 2;
+    const size_t total = (size_t)a.rows * a.cols;
+    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
+      const int r = (int)(idx / a.cols), c = (int)(idx % a.cols);
+      const int dr = a.row0 + r * a.row_step;
+      uint8_t* d = dw + ((size_t)dr * K2 + a.col0 + c) * es;
+      const uint8_t* s = a.raw + idx * es;
+      for (int i = 0; i < es; i++) d[i] = s[i];
+    }
+  } else {
+    const int width = kquant_block_width(a.fmt), bytes = kquant_block_bytes(a.fmt);
+    const int nb = a.cols / width;
+    const size_t total = (size_t)a.rows * nb;
+    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
+      const int r = (int)(idx / nb), b = (int)(idx % nb);
+      const int dr = a.row0 + r * a.row_step;
+      uint8_t* d = dw + ((size_t)dr * (K2 / width) + a.col0 / width + b) * bytes;
+      const uint8_t* s = a.raw + idx * bytes;
+      for (int i = 0; i < bytes; i++) d[i] = s[i];
+    }
+  }
+}
+
+// Copy-on-write of one KV page (all layers, all kv heads): the
+// partially-filled tail page a fork or a branch writes into.
+__global__ void k_copy_page(uint4* k, uint4* v, size_t page_vec, int num_pages, int src, int dst, int layers) {
+  // page_vec: 16-byte vectors per page per layer (kvh * P * hd * elem / 16)
+  const size_t total = page_vec * layers;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t l = i / page_vec, e = i % page_vec;
+    const size_t so = (l * num_pages + src) * page_vec + e, dO = (l * num_pages + dst) * page_vec + e;
+    k[dO] = k[so];
+    v[dO] = v[so];
+  }
+}
+
+// Sampling shortlist over one logits row (sampling.go:112-143 ordering:
+// descending value, ties by ascending id) and the full-vocabulary
+// log-sum-exp in float64 (logprobs.go:67-90). One CTA; k <= 256.
+__global__ void __launch_bounds__(1024) k_shortlist(const float* logits, int V, int k, int* ids, float* vals, double* lse) {
+  extern __shared__ uint32_t taken[];  // V bits
+  __shared__ double red_d[32];
+  __shared__ unsigned long long red_k[32];
+  __shared__ float mx_s;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int i = threadIdx.x; i < (V + 31) / 32; i += blockDim.x) taken[i] = 0;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) mx = fmaxf(mx, logits[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red_d[warp] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = -INFINITY;
+    for (int w = 0; w < nw; w++) m = fmaxf(m, (float)red_d[w]);
+    mx_s = m;
+  }
+  __syncthreads();
+  const double best = (double)mx_s;
+  double s = 0;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) s += exp((double)logits[i] - best);
+  s = warp_sum_d(s);
+  __syncthreads();
+  if (lane == 0) red_d[warp] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0;
+    for (int w = 0; w < nw; w++) t += red_d[w];
+    *lse = best + log(t);
+  }
+  for (int j = 0; j < k; j++) {
+    unsigned long long b = 0;
+    for (int i = threadIdx.x; i < V; i += blockDim.x)
+      if (!((taken[i >> 5] >> (i & 31)) & 1u)) {
+        unsigned long long key = argmax_pack(logits[i], i);
+        b = key > b ? key : b;
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
+      b = t > b ? t : b;
+    }
+    __syncthreads();
+    if (lane == 0) red_k[warp] = b;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long t = 0;
+      for (int w = 0; w < nw; w++) t = red_k[w] > t ? red_k[w] : t;
+      const int id = argmax_index(t);
+      ids[j] = id;
+      vals[j] = logits[id];
+      taken[id >> 5] |= 1u << (id & 31);
+    }
+    __syncthreads();
+  }
+}
+
+// Per-row argmax of a logits matrix (batched branch steps).
+__global__ void k_argmax_rows(const float* logits, int V, int stride, unsigned long long* out) {
+  const int r = blockIdx.x;
+  unsigned long long b = 0;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    unsigned long long key = argmax_pack(logits[(size_t)r * stride + i], i);
+    b = key > b ? key : b;
+  }
+  __shared__ unsigned long long red[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long t = __shfl_xor_sync(0xffffffffu, b, o);
+    b = t > b ? t : b;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = b;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long t = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) t = red[w] > t ? red[w] : t;
+    out[r] = t;
+  }
+}
+
+}  // namespace tcu

@@ -1,0 +1,1726 @@
+// tinyoai B200 backend: model upload, paged KV pool, sessions, branches and
+// the C ABI declared in include/tinyoai_cuda.h.
+//
+// The host side mirrors the reference's native-forwarder contract
+// (mlx.go:45-57, branches.go:49-59, sessions.go:26-30, mlx_llama.go:27-35):
+// a session holds a resident token prefix whose KV lives in pages of a
+// per-model pool; Forward replaces the suffix after `prefix`; Fork and
+// branches share full pages by reference count and copy only a page they
+// write while it is shared.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/tinyoai_cuda.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm_simt.cuh"
+#include "gemv.cuh"
+#include "misc.cuh"
+
+using namespace tcu;
+
+// ---------------------------------------------------------------------------
+// Errors: integer status + thread-local message (internal/mlx/bridge.c:13-33).
+static thread_local std::string g_err;
+
+static int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+#define CK(x)                                                                                   \
+  do {                                                                                          \
+    cudaError_t e_ = (x);                                                                       \
+    if (e_ != cudaSuccess) return fail(TCU_ECUDA, "%s (%s:%d): %s", #x, __FILE__, __LINE__, cudaGetErrorString(e_)); \
+  } while (0)
+#define TRY(x)               \
+  do {                       \
+    int r_ = (x);            \
+    if (r_ != TCU_OK) return r_; \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// Model
+
+enum Arch { ARCH_STABLELM = 0, ARCH_LLAMA = 1 };
+
+struct Layer {
+  DMat w1{}, w2{}, w3{}, w4{};
+  float *n1w = nullptr, *n1b = nullptr, *n2w = nullptr;
+};
+
+struct KVPool {
+  int half = 0, P = 32, L = 0, kvh = 0, hd = 0, num_pages = 0;
+  void *k = nullptr, *v = nullptr;
+  std::vector<int> ref;
+  std::vector<int> free_list;
+  size_t used() const { return (size_t)(num_pages - (int)free_list.size()); }
+  size_t page_elems() const { return (size_t)kvh * P * hd; }
+  size_t elem() const { return half ? 2 : 4; }
+  KVView view() const {
+    KVView w;
+    w.k = k;
+    w.v = v;
+    w.half = half;
+    w.P = P;
+    w.num_pages = num_pages;
+    w.kvh = kvh;
+    w.hd = hd;
+    return w;
+  }
+};
+
+struct tcu_model {
+  Arch arch = ARCH_STABLELM;
+  int device = 0;
+  int V = 0, d = 0, ff = 0, L = 0, H = 0, KVH = 0, hd = 0, max_pos = 0;
+  int kvw = 0;  // KVH * hd
+  double eps = 1e-5;
+  Rope rope{};
+  std::vector<Layer> layers;
+  DMat embed{}, head{};
+  float *fnw = nullptr, *fnb = nullptr;
+  std::vector<void*> allocs;
+  uint64_t weight_bytes = 0;
+  int P = 32;
+  int64_t pool_budget = 0;
+  KVPool* pools[2] = {nullptr, nullptr};
+  std::mutex mu;
+  int sessions = 0;
+  int sm_count = 148;
+  int gemv_smem_optin = 0;
+};
+
+static int dalloc(tcu_model* m, void** p, size_t n) {
+  if (n == 0) n = 16;
+  cudaError_t e = cudaMalloc(p, n);
+  if (e != cudaSuccess) return fail(e == cudaErrorMemoryAllocation ? TCU_ENOMEM : TCU_ECUDA, "cudaMalloc(%zu): %s", n, cudaGetErrorString(e));
+  m->allocs.push_back(*p);
+  m->weight_bytes += n;
+  return TCU_OK;
+}
+
+static void model_release(tcu_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  for (void* p : m->allocs) cudaFree(p);
+  for (KVPool* p : m->pools)
+    if (p) {
+      cudaFree(p->k);
+      cudaFree(p->v);
+      delete p;
+    }
+  delete m;
+}
+
+static size_t fmt_row_bytes(int fmt, int cols) {
+  switch (fmt) {
+    case FMT_Q8_0:
+      return (size_t)cols;  // quant plane; scales separate
+    case FMT_F32:
+      return (size_t)cols * 4;
+    case FMT_F16:
+    case FMT_BF16:
+      return (size_t)cols * 2;
+    default:
+      return (size_t)cols / kquant_block_width(fmt) * kquant_block_bytes(fmt);
+  }
+}
+
+static size_t file_bytes(int fmt, int64_t rows, int64_t cols) {
+  switch (fmt) {
+    case FMT_Q8_0:
+      return (size_t)(rows * cols / 32 * 34);
+    case FMT_F32:
+      return (size_t)(rows * cols * 4);
+    case FMT_F16:
+    case FMT_BF16:
+      return (size_t)(rows * cols * 2);
+    case FMT_Q5_1:
+    case FMT_Q5_K:
+    case FMT_Q6_K:
+      return (size_t)(rows * cols / kquant_block_width(fmt) * kquant_block_bytes(fmt));
+    default:
+      return 0;
+  }
+}
+
+static bool fmt_known(int f) {
+  return f == FMT_F32 || f == FMT_F16 || f == FMT_BF16 || f == FMT_Q8_0 || f == FMT_Q5_1 || f == FMT_Q5_K || f == FMT_Q6_K;
+}
+
+static int alloc_dmat(tcu_model* m, DMat* out, int fmt, int rows, int cols) {
+  DMat w{};
+  w.fmt = fmt;
+  w.rows = rows;
+  w.cols = cols;
+  void* p = nullptr;
+  TRY(dalloc(m, &p, fmt_row_bytes(fmt, cols) * rows));
+  w.w = (const uint8_t*)p;
+  if (fmt == FMT_Q8_0) {
+    void* s = nullptr;
+    TRY(dalloc(m, &s, (size_t)rows * (cols / 32) * 2));
+    w.s = (const __half*)s;
+  }
+  *out = w;
+  return TCU_OK;
+}
+
+// Staging: raw tensor bytes go to a device scratch buffer, then k_repack
+// writes them into their place in the fused device matrix.
+struct Stager {
+  uint8_t* buf = nullptr;
+  size_t cap = 0;
+  ~Stager() {
+    if (buf) cudaFree(buf);
+  }
+};
+
+static int place(Stager& st, const void* data, size_t nbytes, int fmt, int rows, int cols, const DMat& dst, int row0, int row_step,
+                 int col0) {
+  if (nbytes > st.cap) {
+    if (st.buf) cudaFree(st.buf);
+    st.buf = nullptr;
+    st.cap = 0;
+    CK(cudaMalloc(&st.buf, nbytes));
+    st.cap = nbytes;
+  }
+  CK(cudaMemcpy(st.buf, data, nbytes, cudaMemcpyHostToDevice));
+  RepackArgs a{st.buf, fmt, rows, cols, dst, row0, row_step, col0};
+  k_repack<<<1184, 256>>>(a);
+  CK(cudaGetLastError());
+  CK(cudaDeviceSynchronize());
+  return TCU_OK;
+}
+
+static float host_half(uint16_t h) {
+  uint32_t sign = (uint32_t)(h & 0x8000) << 16, ex = (h >> 10) & 31, frac = h & 1023, u;
+  if (ex == 0) {
+    float v = (float)ldexp((double)frac, -24);
+    return sign ? -v : v;
+  }
+  if (ex == 31)
+    u = sign | 0x7f800000u | frac << 13;
+  else
+    u = sign | (ex + 112) << 23 | frac << 13;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+// Decodes a 1-D norm tensor to float32 (weightTensor.at, safetensors.go:230-246).
+static int decode_vec(const tcu_tensor* t, int n, std::vector<float>& out) {
+  out.resize(n);
+  const uint8_t* p = (const uint8_t*)t->data;
+  for (int i = 0; i < n; i++) {
+    switch (t->dtype) {
+      case TCU_F32:
+        memcpy(&out[i], p + 4 * i, 4);
+        break;
+      case TCU_F16:
+        out[i] = host_half((uint16_t)(p[2 * i] | (p[2 * i + 1] << 8)));
+        break;
+      case TCU_BF16: {
+        uint32_t u = (uint32_t)(p[2 * i] | (p[2 * i + 1] << 8)) << 16;
+        memcpy(&out[i], &u, 4);
+        break;
+      }
+      default:
+        return fail(TCU_EUNSUP, "tensor %s: unsupported dtype %d for a norm vector", t->name, t->dtype);
+    }
+  }
+  return TCU_OK;
+}
+
+static int upload_floats(tcu_model* m, const std::vector<float>& v, float** out) {
+  void* p = nullptr;
+  TRY(dalloc(m, &p, v.size() * 4));
+  CK(cudaMemcpy(p, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+  *out = (float*)p;
+  return TCU_OK;
+}
+
+static int check_device(int device) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return fail(TCU_ENODEV, "no CUDA device available");
+  if (device < 0 || device >= n) return fail(TCU_ENODEV, "device %d out of range (%d devices)", device, n);
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10) return fail(TCU_ENODEV, "device %d is sm_%d%d; this library is built for sm_100a", device, prop.major, prop.minor);
+  CK(cudaSetDevice(device));
+  return TCU_OK;
+}
+
+static void init_common(tcu_model* m, const tcu_load_options* o) {
+  m->device = o ? o->device : 0;
+  m->P = (o && o->kv_page_tokens > 0) ? o->kv_page_tokens : 32;
+  m->pool_budget = o ? o->kv_pool_bytes : 0;
+  cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, m->device);
+  cudaDeviceGetAttribute(&m->gemv_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
+}
+
+// StableLM rotary table (stablelm.go:309-326): per position and rotary pair,
+// the float32 angle and its float64 sine/cosine rounded to float32.
+static int build_stablelm_rope(tcu_model* m, double theta, int rotary) {
+  const int pairs = rotary / 2;
+  std::vector<float2> tab((size_t)m->max_pos * pairs);
+  for (int i = 0; i < pairs; i++) {
+    volatile float ftheta = (float)theta;
+    volatile float expo = (float)(2 * i) / (float)rotary;
+    volatile float power = (float)pow((double)ftheta, (double)expo);
+    volatile float inv = 1.0f / power;
+    for (int pos = 0; pos < m->max_pos; pos++) {
+      volatile float angle = (float)pos * inv;
+      tab[(size_t)pos * pairs + i] = make_float2((float)cos((double)angle), (float)sin((double)angle));
+    }
+  }
+  void* p = nullptr;
+  TRY(dalloc(m, &p, tab.size() * sizeof(float2)));
+  CK(cudaMemcpy(p, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  m->rope.table = (const float2*)p;
+  m->rope.pairs = pairs;
+  m->rope.mode = 0;
+  return TCU_OK;
+}
+
+static const tcu_tensor* find_tensor(const tcu_tensor* t, int n, const std::string& name) {
+  for (int i = 0; i < n; i++)
+    if (t[i].name && name == t[i].name) return &t[i];
+  return nullptr;
+}
+
+static int check_tensor(const tcu_tensor* t, const std::string& name, int64_t rows, int64_t cols) {
+  if (!t) return fail(TCU_EINVAL, "missing tensor %s", name.c_str());
+  if (!fmt_known(t->dtype)) return fail(TCU_EUNSUP, "tensor %s: unsupported dtype %d", name.c_str(), t->dtype);
+  const int64_t want_rows = cols ? rows : 1, want_cols = cols ? cols : rows;
+  const int64_t r = t->ndim == 2 ? t->shape[0] : 1, c = t->ndim == 2 ? t->shape[1] : t->shape[0];
+  if ((cols && t->ndim != 2) || (!cols && t->ndim != 1) || r != want_rows || c != want_cols)
+    return fail(TCU_EINVAL, "tensor %s: shape mismatch (want %lld x %lld)", name.c_str(), (long long)want_rows, (long long)want_cols);
+  if ((t->dtype == FMT_Q8_0 || t->dtype == FMT_Q5_1) && c % 32)
+    return fail(TCU_EINVAL, "tensor %s: %s rows must be divisible by 32", name.c_str(), t->dtype == FMT_Q8_0 ? "Q8_0" : "Q5_1");
+  if ((t->dtype == FMT_Q5_K || t->dtype == FMT_Q6_K) && c % 256)
+    return fail(TCU_EINVAL, "tensor %s: K-quant rows must be divisible by 256", name.c_str());
+  if (t->nbytes != file_bytes(t->dtype, r, c)) return fail(TCU_EINVAL, "tensor %s: %llu bytes, want %zu", name.c_str(), (unsigned long long)t->nbytes, file_bytes(t->dtype, r, c));
+  if (!t->data) return fail(TCU_EINVAL, "tensor %s: null data", name.c_str());
+  return TCU_OK;
+}
+
+static int stablelm_load(const tcu_stablelm_config* c, const tcu_tensor* t, int n, const tcu_load_options* o, tcu_model** out) {
+  // stablelm.go:85-111 validate() (the structural flags are checked by the caller's config parser).
+  if (!c || !out || (n > 0 && !t)) return fail(TCU_EINVAL, "null argument");
+  if (c->hidden_size <= 0 || c->intermediate_size <= 0 || c->num_hidden_layers <= 0 || c->num_attention_heads <= 0 ||
+      c->num_key_value_heads <= 0 || c->vocab_size <= 0 || c->max_position_embeddings <= 0 ||
+      c->hidden_size % c->num_attention_heads != 0 || c->num_attention_heads % c->num_key_value_heads != 0)
+    return fail(TCU_EINVAL, "invalid StableLM dimensions");
+  const double rotary_f = (double)(c->hidden_size / c->num_attention_heads) * c->partial_rotary_factor;
+  if (!(c->layer_norm_eps > 0) || std::isinf(c->layer_norm_eps) || !(c->rope_theta > 0) || std::isinf(c->rope_theta) ||
+      !(c->partial_rotary_factor > 0) || c->partial_rotary_factor > 1 || rotary_f != std::trunc(rotary_f) || (int)rotary_f % 2 != 0 ||
+      rotary_f < 2)
+    return fail(TCU_EINVAL, "invalid LayerNorm or partial RoPE settings");
+  if (c->bos_token_id < 0 || c->bos_token_id >= c->vocab_size || c->eos_token_id < 0 || c->eos_token_id >= c->vocab_size)
+    return fail(TCU_EINVAL, "invalid BOS/EOS token IDs");
+  const int device = o ? o->device : 0;
+  TRY(check_device(device));
+  tcu_model* m = new tcu_model();
+  init_common(m, o);
+  m->arch = ARCH_STABLELM;
+  m->V = c->vocab_size;
+  m->d = c->hidden_size;
+  m->ff = c->intermediate_size;
+  m->L = c->num_hidden_layers;
+  m->H = c->num_attention_heads;
+  m->KVH = c->num_key_value_heads;
+  m->hd = m->d / m->H;
+  m->kvw = m->hd * m->KVH;
+  m->max_pos = c->max_position_embeddings;
+  m->eps = c->layer_norm_eps;
+  const int d = m->d, ff = m->ff, kvw = m->kvw;
+  auto bail = [&](int code) {
+    model_release(m);
+    return code;
+  };
+  // Validate every tensor before allocating (loadStableWeights, stablelm.go:167-199).
+  std::vector<std::string> names;
+  auto chk = [&](const std::string& name, int64_t r, int64_t cc) { return check_tensor(find_tensor(t, n, name), name, r, cc); };
+  int rc;
+  if ((rc = chk("model.embed_tokens.weight", m->V, d)) || (rc = chk("lm_head.weight", m->V, d)) || (rc = chk("model.norm.weight", d, 0)) ||
+      (rc = chk("model.norm.bias", d, 0)))
+    return bail(rc);
+  for (int l = 0; l < m->L; l++) {
+    std::string p = "model.layers." + std::to_string(l) + ".";
+    if ((rc = chk(p + "input_layernorm.weight", d, 0)) || (rc = chk(p + "input_layernorm.bias", d, 0)) ||
+        (rc = chk(p + "self_attn.q_proj.weight", d, d)) || (rc = chk(p + "self_attn.k_proj.weight", kvw, d)) ||
+        (rc = chk(p + "self_attn.v_proj.weight", kvw, d)) || (rc = chk(p + "self_attn.o_proj.weight", d, d)) ||
+        (rc = chk(p + "mlp.gate_proj.weight", ff, d)) || (rc = chk(p + "mlp.up_proj.weight", ff, d)) ||
+        (rc = chk(p + "mlp.down_proj.weight", d, ff)))
+      return bail(rc);
+    const int f1 = find_tensor(t, n, p + "self_attn.q_proj.weight")->dtype;
+    for (const char* nm : {"self_attn.k_proj.weight", "self_attn.v_proj.weight", "mlp.gate_proj.weight", "mlp.up_proj.weight"})
+      if (find_tensor(t, n, p + nm)->dtype != f1)
+        return bail(fail(TCU_EUNSUP, "layer %d: q/k/v/gate/up must share one dtype (fused projection)", l));
+    const int f2 = find_tensor(t, n, p + "self_attn.o_proj.weight")->dtype;
+    if (find_tensor(t, n, p + "mlp.down_proj.weight")->dtype != f2)
+      return bail(fail(TCU_EUNSUP, "layer %d: o_proj and down_proj must share one dtype (fused projection)", l));
+    if ((f2 == FMT_Q5_K || f2 == FMT_Q6_K) && d % 256) return bail(fail(TCU_EUNSUP, "layer %d: K-quant o|down fusion needs hidden %% 256 == 0", l));
+  }
+  if ((rc = build_stablelm_rope(m, c->rope_theta, (int)rotary_f))) return bail(rc);
+  Stager st;
+  m->layers.resize(m->L);
+  const int n_plain = d + 2 * kvw;
+  for (int l = 0; l < m->L; l++) {
+    std::string p = "model.layers." + std::to_string(l) + ".";
+    Layer& ly = m->layers[l];
+    auto T = [&](const char* nm) { return find_tensor(t, n, p + nm); };
+    const tcu_tensor *q = T("self_attn.q_proj.weight"), *k = T("self_attn.k_proj.weight"), *v = T("self_attn.v_proj.weight");
+    const tcu_tensor *o_ = T("self_attn.o_proj.weight"), *g = T("mlp.gate_proj.weight"), *u = T("mlp.up_proj.weight"),
+                     *dn = T("mlp.down_proj.weight");
+    // W1 rows: [q | k | v | (gate_i, up_i) interleaved]; W2 columns: [o | down].
+    if ((rc = alloc_dmat(m, &ly.w1, q->dtype, n_plain + 2 * ff, d)) || (rc = alloc_dmat(m, &ly.w2, o_->dtype, d, d + ff)) ||
+        (rc = place(st, q->data, q->nbytes, q->dtype, d, d, ly.w1, 0, 1, 0)) ||
+        (rc = place(st, k->data, k->nbytes, k->dtype, kvw, d, ly.w1, d, 1, 0)) ||
+        (rc = place(st, v->data, v->nbytes, v->dtype, kvw, d, ly.w1, d + kvw, 1, 0)) ||
+        (rc = place(st, g->data, g->nbytes, g->dtype, ff, d, ly.w1, n_plain, 2, 0)) ||
+        (rc = place(st, u->data, u->nbytes, u->dtype, ff, d, ly.w1, n_plain + 1, 2, 0)) ||
+        (rc = place(st, o_->data, o_->nbytes, o_->dtype, d, d, ly.w2, 0, 1, 0)) ||
+        (rc = place(st, dn->data, dn->nbytes, dn->dtype, d, ff, ly.w2, 0, 1, d)))
+      return bail(rc);
+    std::vector<float> nw, nb;
+    if ((rc = decode_vec(T("input_layernorm.weight"), d, nw)) || (rc = decode_vec(T("input_layernorm.bias"), d, nb)) ||
+        (rc = upload_floats(m, nw, &ly.n1w)) || (rc = upload_floats(m, nb, &ly.n1b)))
+      return bail(rc);
+  }
+  const tcu_tensor *e = find_tensor(t, n, "model.embed_tokens.weight"), *h = find_tensor(t, n, "lm_head.weight");
+  if ((rc = alloc_dmat(m, &m->embed, e->dtype, m->V, d)) || (rc = place(st, e->data, e->nbytes, e->dtype, m->V, d, m->embed, 0, 1, 0)) ||
+      (rc = alloc_dmat(m, &m->head, h->dtype, m->V, d)) || (rc = place(st, h->data, h->nbytes, h->dtype, m->V, d, m->head, 0, 1, 0)))
+    return bail(rc);
+  std::vector<float> fw, fb;
+  if ((rc = decode_vec(find_tensor(t, n, "model.norm.weight"), d, fw)) || (rc = decode_vec(find_tensor(t, n, "model.norm.bias"), d, fb)) ||
+      (rc = upload_floats(m, fw, &m->fnw)) || (rc = upload_floats(m, fb, &m->fnb)))
+    return bail(rc);
+  *out = m;
+  return TCU_OK;
+}
+
+// llama2.c checkpoint (model.go:90-166): 7 int32 header fields, then float32
+// tensors in the legacy order; the classifier is the embedding table.
+static int llama_load(const void* ck, uint64_t nbytes, const tcu_load_options* o, tcu_model** out) {
+  if (!ck || !out) return fail(TCU_EINVAL, "null argument");
+  if (nbytes < 28) return fail(TCU_EINVAL, "read config header: truncated checkpoint");
+  int32_t h[7];
+  memcpy(h, ck, 28);
+  if (h[0] <= 0 || h[1] <= 0 || h[2] <= 0 || h[3] <= 0 || h[4] <= 0 || h[3] % h[4] != 0 || h[5] < 2 || h[6] <= 0 || h[0] % h[3] != 0 ||
+      (h[0] / h[3]) % 2 != 0)
+    return fail(TCU_EINVAL, "invalid config header");
+  const int64_t dim = h[0], hid = h[1], L = h[2], V = h[5], seq = h[6], hs = dim / h[3], kvd = hs * h[4];
+  const int64_t sizes[13] = {V * dim, L * dim, L * dim * dim, L * dim * kvd, L * dim * kvd, L * dim * dim, L * dim,
+                             L * hid * dim, L * dim * hid, L * hid * dim, dim, seq * hs / 2, seq * hs / 2};
+  int64_t total = 0;
+  for (int64_t s : sizes) total += s;
+  if ((uint64_t)(28 + total * 4) != nbytes)
+    return fail(TCU_EINVAL, "checkpoint has %lld bytes, weight layout needs %lld", (long long)nbytes, (long long)(28 + total * 4));
+  const int device = o ? o->device : 0;
+  TRY(check_device(device));
+  tcu_model* m = new tcu_model();
+  init_common(m, o);
+  m->arch = ARCH_LLAMA;
+  m->V = (int)V;
+  m->d = (int)dim;
+  m->ff = (int)hid;
+  m->L = (int)L;
+  m->H = h[3];
+  m->KVH = h[4];
+  m->hd = (int)hs;
+  m->kvw = (int)kvd;
+  m->max_pos = (int)seq;
+  auto bail = [&](int code) {
+    model_release(m);
+    return code;
+  };
+  const float* f = (const float*)((const uint8_t*)ck + 28);
+  const float* ptr[13];
+  {
+    const float* p = f;
+    for (int i = 0; i < 13; i++) {
+      ptr[i] = p;
+      p += sizes[i];
+    }
+  }
+  Stager st;
+  int rc;
+  m->layers.resize(m->L);
+  for (int l = 0; l < m->L; l++) {
+    Layer& ly = m->layers[l];
+    const int64_t dd = dim * dim, dk = dim * kvd, dh = dim * hid;
+    if ((rc = alloc_dmat(m, &ly.w1, FMT_F32, (int)(dim + 2 * kvd), (int)dim)) ||
+        (rc = place(st, ptr[2] + l * dd, dd * 4, FMT_F32, (int)dim, (int)dim, ly.w1, 0, 1, 0)) ||
+        (rc = place(st, ptr[3] + l * dk, dk * 4, FMT_F32, (int)kvd, (int)dim, ly.w1, (int)dim, 1, 0)) ||
+        (rc = place(st, ptr[4] + l * dk, dk * 4, FMT_F32, (int)kvd, (int)dim, ly.w1, (int)(dim + kvd), 1, 0)) ||
+        (rc = alloc_dmat(m, &ly.w2, FMT_F32, (int)dim, (int)dim)) ||
+        (rc = place(st, ptr[5] + l * dd, dd * 4, FMT_F32, (int)dim, (int)dim, ly.w2, 0, 1, 0)) ||
+        (rc = alloc_dmat(m, &ly.w3, FMT_F32, (int)(2 * hid), (int)dim)) ||
+        (rc = place(st, ptr[7] + l * dh, dh * 4, FMT_F32, (int)hid, (int)dim, ly.w3, 0, 2, 0)) ||
+        (rc = place(st, ptr[9] + l * dh, dh * 4, FMT_F32, (int)hid, (int)dim, ly.w3, 1, 2, 0)) ||
+        (rc = alloc_dmat(m, &ly.w4, FMT_F32, (int)dim, (int)hid)) ||
+        (rc = place(st, ptr[8] + l * dh, dh * 4, FMT_F32, (int)dim, (int)hid, ly.w4, 0, 1, 0)))
+      return bail(rc);
+    std::vector<float> a(ptr[1] + l * dim, ptr[1] + (l + 1) * dim), b(ptr[6] + l * dim, ptr[6] + (l + 1) * dim);
+    if ((rc = upload_floats(m, a, &ly.n1w)) || (rc = upload_floats(m, b, &ly.n2w))) return bail(rc);
+  }
+  if ((rc = alloc_dmat(m, &m->embed, FMT_F32, (int)V, (int)dim)) ||
+      (rc = place(st, ptr[0], V * dim * 4, FMT_F32, (int)V, (int)dim, m->embed, 0, 1, 0)))
+    return bail(rc);
+  m->head = m->embed;
+  std::vector<float> fw(ptr[10], ptr[10] + dim);
+  if ((rc = upload_floats(m, fw, &m->fnw))) return bail(rc);
+  // Rotary tables from the checkpoint (freq_cis_real/imag [seq][hs/2]).
+  std::vector<float2> tab((size_t)seq * (hs / 2));
+  for (size_t i = 0; i < tab.size(); i++) tab[i] = make_float2(ptr[11][i], ptr[12][i]);
+  void* p = nullptr;
+  if ((rc = dalloc(m, &p, tab.size() * sizeof(float2)))) return bail(rc);
+  if (cudaMemcpy(p, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess)
+    return bail(fail(TCU_ECUDA, "rope table upload failed"));
+  m->rope.table = (const float2*)p;
+  m->rope.pairs = (int)(hs / 2);
+  m->rope.mode = 1;
+  *out = m;
+  return TCU_OK;
+}
+
+// ---------------------------------------------------------------------------
+// KV pool
+
+static int pool_get(tcu_model* m, int half, KVPool** out) {
+  std::lock_guard<std::mutex> g(m->mu);
+  if (m->pools[half]) {
+    *out = m->pools[half];
+    return TCU_OK;
+  }
+  KVPool* p = new KVPool();
+  p->half = half;
+  p->P = m->P;
+  p->L = m->L;
+  p->kvh = m->KVH;
+  p->hd = m->hd;
+  const size_t page_bytes = (size_t)m->L * p->page_elems() * p->elem() * 2;  // K + V, all layers
+  int64_t budget = m->pool_budget;
+  if (budget <= 0) {
+    size_t fr = 0, tot = 0;
+    cudaMemGetInfo(&fr, &tot);
+    budget = (int64_t)(fr / 4);
+  }
+  int64_t pages = budget / (int64_t)page_bytes;
+  // Never fewer pages than one full-context sequence.
+  const int64_t min_pages = (m->max_pos + m->P - 1) / m->P + 1;
+  pages = std::max<int64_t>(pages, min_pages);
+  p->num_pages = (int)std::min<int64_t>(pages, 1 << 24);
+  const size_t half_bytes = page_bytes / 2 * (size_t)p->num_pages;
+  if (cudaMalloc(&p->k, half_bytes) != cudaSuccess || cudaMalloc(&p->v, half_bytes) != cudaSuccess) {
+    if (p->k) cudaFree(p->k);
+    delete p;
+    cudaGetLastError();
+    return fail(TCU_ENOMEM, "KV pool: cannot allocate %d pages (%zu bytes)", (int)pages, 2 * half_bytes);
+  }
+  cudaMemset(p->k, 0, half_bytes);
+  cudaMemset(p->v, 0, half_bytes);
+  p->ref.assign(p->num_pages, 0);
+  p->free_list.reserve(p->num_pages);
+  for (int i = p->num_pages - 1; i >= 0; i--) p->free_list.push_back(i);
+  m->pools[half] = p;
+  *out = p;
+  return TCU_OK;
+}
+
+static int page_alloc(tcu_model* m, KVPool* p, int* page) {
+  std::lock_guard<std::mutex> g(m->mu);
+  if (p->free_list.empty()) return fail(TCU_ENOMEM, "KV pool exhausted (%d pages)", p->num_pages);
+  *page = p->free_list.back();
+  p->free_list.pop_back();
+  p->ref[*page] = 1;
+  return TCU_OK;
+}
+static void page_ref(tcu_model* m, KVPool* p, int page) {
+  std::lock_guard<std::mutex> g(m->mu);
+  p->ref[page]++;
+}
+static void page_unref(tcu_model* m, KVPool* p, int page) {
+  std::lock_guard<std::mutex> g(m->mu);
+  if (--p->ref[page] == 0) p->free_list.push_back(page);
+}
+static int page_refcount(tcu_model* m, KVPool* p, int page) {
+  std::lock_guard<std::mutex> g(m->mu);
+  return p->ref[page];
+}
+
+// ---------------------------------------------------------------------------
+// Workspace for M concurrent sequences (a session: M = 1 decode or a prompt
+// chunk of up to CHUNK tokens; branches: M = count).
+
+static const int CHUNK = 512;  // prompt tokens per internal chunk (mlx.go:352-355)
+static const int SPLIT_PAGES = 2;
+
+struct Work {
+  int rows = 0, seqs = 0, logits_rows = 0;
+  float *x = nullptr, *xn = nullptr, *qkv = nullptr, *ah = nullptr, *logits = nullptr;
+  int *tokens = nullptr, *pos = nullptr, *out_tokens = nullptr, *out_count = nullptr;
+  unsigned long long* argmax = nullptr;
+  float* part = nullptr;
+  int* counters = nullptr;
+  int* pt = nullptr;
+  int pt_stride = 0, max_splits = 0, out_cap = 0;
+  int* sl_ids = nullptr;
+  float* sl_vals = nullptr;
+  double* sl_lse = nullptr;
+  std::vector<void*> allocs;
+  ~Work() {
+    for (void* p : allocs) cudaFree(p);
+  }
+  template <class T>
+  int get(T** p, size_t n) {
+    void* q = nullptr;
+    cudaError_t e = cudaMalloc(&q, std::max<size_t>(n * sizeof(T), 16));
+    if (e != cudaSuccess) return fail(TCU_ENOMEM, "workspace: %s", cudaGetErrorString(e));
+    cudaMemset(q, 0, std::max<size_t>(n * sizeof(T), 16));
+    allocs.push_back(q);
+    *p = (T*)q;
+    return TCU_OK;
+  }
+};
+
+static int work_init(tcu_model* m, Work* w, int rows, int seqs, int logits_rows, int out_cap) {
+  w->rows = rows;
+  w->seqs = seqs;
+  w->logits_rows = logits_rows;
+  w->pt_stride = (m->max_pos + m->P - 1) / m->P;
+  const int split = SPLIT_PAGES * m->P;
+  w->max_splits = (m->max_pos + split - 1) / split;
+  w->out_cap = out_cap;
+  const int qkvw = m->d + 2 * m->kvw;
+  TRY(w->get(&w->x, (size_t)rows * m->d));
+  TRY(w->get(&w->xn, (size_t)rows * m->d));
+  TRY(w->get(&w->qkv, (size_t)rows * qkvw));
+  TRY(w->get(&w->ah, (size_t)rows * (m->d + m->ff)));
+  TRY(w->get(&w->logits, (size_t)logits_rows * m->V));
+  TRY(w->get(&w->tokens, (size_t)std::max(rows, seqs)));
+  TRY(w->get(&w->pos, (size_t)seqs));
+  TRY(w->get(&w->out_tokens, (size_t)seqs * out_cap));
+  TRY(w->get(&w->out_count, (size_t)seqs));
+  TRY(w->get(&w->argmax, (size_t)seqs));
+  TRY(w->get(&w->part, (size_t)seqs * m->H * w->max_splits * (m->hd + 2)));
+  TRY(w->get(&w->counters, (size_t)seqs * m->KVH));
+  TRY(w->get(&w->pt, (size_t)seqs * w->pt_stride));
+  TRY(w->get(&w->sl_ids, 256));
+  TRY(w->get(&w->sl_vals, 256));
+  TRY(w->get(&w->sl_lse, 1));
+  return TCU_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Opt-in stage timing (the device counterpart of stableProfile,
+// stablelm.go:229-250): CUDA events bracket every kernel of a stage; totals
+// are accumulated after the stream is synchronised. With profiling off no
+// event is recorded.
+
+enum Stage { ST_EMBED = 0, ST_W1, ST_ATTN, ST_W2, ST_HEAD, ST_PF_GEMM, ST_PF_ATTN, ST_OTHER, ST_COUNT };
+
+struct Prof {
+  bool on = false;
+  std::vector<cudaEvent_t> ev;  // pairs
+  std::vector<int> stage;
+  size_t used = 0;
+  int64_t launches[ST_COUNT] = {};
+  double ms[ST_COUNT] = {};
+  ~Prof() {
+    for (cudaEvent_t e : ev) cudaEventDestroy(e);
+  }
+  void begin(int st, cudaStream_t s) {
+    if (!on) return;
+    if (2 * used + 2 > ev.size()) {
+      cudaEvent_t a, b;
+      cudaEventCreate(&a);
+      cudaEventCreate(&b);
+      ev.push_back(a);
+      ev.push_back(b);
+      stage.push_back(0);
+    }
+    stage[used] = st;
+    cudaEventRecord(ev[2 * used], s);
+  }
+  void end(cudaStream_t s) {
+    if (!on) return;
+    cudaEventRecord(ev[2 * used + 1], s);
+    used++;
+  }
+  // Call after the stream is synchronised.
+  void collect(size_t n) {
+    for (size_t i = 0; i < n; i++) {
+      float t = 0;
+      if (cudaEventElapsedTime(&t, ev[2 * i], ev[2 * i + 1]) == cudaSuccess) {
+        ms[stage[i]] += t;
+        launches[stage[i]]++;
+      }
+    }
+  }
+};
+
+static thread_local Prof* g_prof = nullptr;  // set while enqueueing for a profiled session
+#define PROF_BEGIN(st, s) \
+  if (g_prof) g_prof->begin(st, s)
+#define PROF_END(s) \
+  if (g_prof) g_prof->end(s)
+
+// ---------------------------------------------------------------------------
+// Kernel launch helpers
+
+template <int FMT, int PRO, int EPI>
+static void launch_gemv_fmt(const tcu_model* m, const GemvArgs& a, cudaStream_t s) {
+  const int K = a.W.cols;
+  const size_t smem = (size_t)a.M * K * sizeof(float);
+  const int pairs = (a.W.rows + 1) / 2;
+  int blocks = (pairs + GEMV_WARPS - 1) / GEMV_WARPS;
+  blocks = std::min(blocks, m->sm_count * 2);
+  switch (a.M) {
+#define TCU_GEMV_CASE(MM)                                                                   \
+  case MM: {                                                                                \
+    auto kern = k_gemv<FMT, MM, PRO, EPI>;                                                  \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);     \
+    kern<<<blocks, GEMV_THREADS, smem, s>>>(a);                                             \
+    break;                                                                                  \
+  }
+    TCU_GEMV_CASE(1)
+    TCU_GEMV_CASE(2)
+    TCU_GEMV_CASE(3)
+    TCU_GEMV_CASE(4)
+#undef TCU_GEMV_CASE
+  }
+}
+
+template <int PRO, int EPI>
+static void launch_gemv_generic(const tcu_model* m, const GemvArgs& a, cudaStream_t s) {
+  const int K = a.W.cols;
+  const size_t smem = (size_t)a.M * K * sizeof(float);
+  const int pairs = (a.W.rows + 1) / 2;
+  int blocks = std::min((pairs + GEMV_WARPS - 1) / GEMV_WARPS, m->sm_count * 2);
+  switch (a.M) {
+#define TCU_GEMV_CASE(MM)                                                               \
+  case MM: {                                                                            \
+    auto kern = k_gemv_generic<MM, PRO, EPI>;                                           \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    kern<<<blocks, GEMV_THREADS, smem, s>>>(a);                                         \
+    break;                                                                              \
+  }
+    TCU_GEMV_CASE(1)
+    TCU_GEMV_CASE(2)
+    TCU_GEMV_CASE(3)
+    TCU_GEMV_CASE(4)
+#undef TCU_GEMV_CASE
+  }
+}
+
+static bool gemv_vector_ok(const DMat& W) {
+  switch (W.fmt) {
+    case FMT_Q8_0:
+      return W.cols % 32 == 0;
+    case FMT_BF16:
+    case FMT_F16:
+      return W.cols % 8 == 0;
+    case FMT_F32:
+      return W.cols % 4 == 0;
+    default:
+      return false;
+  }
+}
+
+static thread_local int g_stage = ST_OTHER;  // stage charged by the next launch helper
+
+template <int PRO, int EPI>
+static void launch_gemv_impl(const tcu_model* m, const GemvArgs& a, cudaStream_t s);
+
+template <int PRO, int EPI>
+static void launch_gemv(const tcu_model* m, const GemvArgs& a, cudaStream_t s) {
+  PROF_BEGIN(g_stage, s);
+  launch_gemv_impl<PRO, EPI>(m, a, s);
+  PROF_END(s);
+}
+
+template <int PRO, int EPI>
+static void launch_gemv_impl(const tcu_model* m, const GemvArgs& a, cudaStream_t s) {
+  if (gemv_vector_ok(a.W)) {
+    switch (a.W.fmt) {
+      case FMT_Q8_0:
+        return launch_gemv_fmt<FMT_Q8_0, PRO, EPI>(m, a, s);
+      case FMT_BF16:
+        return launch_gemv_fmt<FMT_BF16, PRO, EPI>(m, a, s);
+      case FMT_F16:
+        return launch_gemv_fmt<FMT_F16, PRO, EPI>(m, a, s);
+      case FMT_F32:
+        return launch_gemv_fmt<FMT_F32, PRO, EPI>(m, a, s);
+    }
+  }
+  launch_gemv_generic<PRO, EPI>(m, a, s);
+}
+
+template <int EPI>
+static void launch_gemm(const GemmArgs& a, cudaStream_t s) {
+  PROF_BEGIN(g_stage, s);
+  dim3 grid((a.W.rows + SG_BN - 1) / SG_BN, (a.n + SG_BM - 1) / SG_BM);
+  k_gemm_simt<EPI><<<grid, SG_THREADS, 0, s>>>(a);
+  PROF_END(s);
+}
+
+static void launch_norm_rows(const tcu_model* m, const float* in, float* out, int n, const float* w, const float* b, cudaStream_t s) {
+  PROF_BEGIN(ST_OTHER, s);
+  NormRowsArgs a{n, m->d, in, m->d, out, m->d, w, b, m->eps, m->arch == ARCH_LLAMA};
+  k_norm_rows<<<n, 256, 0, s>>>(a);
+  PROF_END(s);
+}
+
+static size_t attn_decode_smem(const tcu_model* m) {
+  const int G = m->H / m->KVH, split = SPLIT_PAGES * m->P, hd = m->hd;
+  return sizeof(float) * ((size_t)G * hd + 2 * (size_t)split * (hd + 1) + (size_t)G * split + 2 * hd);
+}
+
+static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M, int layer, int grid_splits, cudaStream_t s) {
+  PROF_BEGIN(ST_ATTN, s);
+  DecodeAttnArgs a;
+  a.M = M;
+  a.H = m->H;
+  a.KVH = m->KVH;
+  a.hd = m->hd;
+  a.rope = m->rope;
+  a.qkv = w->qkv;
+  a.qkv_stride = m->d + 2 * m->kvw;
+  a.kv = pool->view();
+  a.layer = layer;
+  a.page_table = w->pt;
+  a.pt_stride = w->pt_stride;
+  a.pos = w->pos;
+  a.split = SPLIT_PAGES * m->P;
+  a.max_splits = w->max_splits;
+  a.part = w->part;
+  a.counters = w->counters;
+  a.out = w->ah;
+  a.out_stride = m->d + m->ff;
+  a.scale = (float)sqrt((double)m->hd);
+  const size_t smem = attn_decode_smem(m);
+  cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_attn_decode<<<dim3(grid_splits, m->KVH, M), 128, smem, s>>>(a);
+  PROF_END(s);
+}
+
+// One decode step for M sequences whose tokens are in w->tokens (token mode)
+// or in w->argmax (step mode) and whose new positions are w->pos (token
+// mode) / w->pos + 1 (step mode). Ends with the head: logits rows and argmax.
+static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, bool step_mode, int grid_splits, bool write_logits,
+                           cudaStream_t s) {
+  const int d = m->d, ff = m->ff, qkvw = d + 2 * m->kvw;
+  EmbedArgs ea{};
+  ea.E = m->embed;
+  ea.n = M;
+  ea.tokens = step_mode ? nullptr : w->tokens;
+  ea.argmax = w->argmax;
+  ea.pos = w->pos;
+  ea.out_tokens = w->out_tokens;
+  ea.out_stride = w->out_cap;
+  ea.out_count = w->out_count;
+  ea.x = w->x;
+  ea.x_stride = d;
+  PROF_BEGIN(ST_EMBED, s);
+  k_embed<<<M, 256, 0, s>>>(ea);
+  PROF_END(s);
+  const bool gemv = M <= GEMV_MAX_M;
+  for (int l = 0; l < m->L; l++) {
+    const Layer& ly = m->layers[l];
+    if (m->arch == ARCH_STABLELM) {
+      g_stage = ST_W1;
+      if (gemv) {
+        GemvArgs a{};
+        a.W = ly.w1;
+        a.M = M;
+        a.in = w->x;
+        a.in_stride = d;
+        a.nw = ly.n1w;
+        a.nb = ly.n1b;
+        a.eps = m->eps;
+        a.out = w->qkv;
+        a.out_stride = qkvw;
+        a.n_plain = qkvw;
+        a.glu_out = w->ah + d;
+        a.glu_stride = d + ff;
+        a.glu_act = 0;
+        launch_gemv<PRO_LN, EPI_GLU>(m, a, s);
+      } else {
+        launch_norm_rows(m, w->x, w->xn, M, ly.n1w, ly.n1b, s);
+        GemmArgs g{};
+        g.W = ly.w1;
+        g.n = M;
+        g.A = w->xn;
+        g.lda = d;
+        g.out = w->qkv;
+        g.out_stride = qkvw;
+        g.n_plain = qkvw;
+        g.glu_out = w->ah + d;
+        g.glu_stride = d + ff;
+        g.glu_act = 0;
+        launch_gemm<EPI_GLU>(g, s);
+      }
+      launch_attn_decode(m, pool, w, M, l, grid_splits, s);
+      g_stage = ST_W2;
+      if (gemv) {
+        GemvArgs a{};
+        a.W = ly.w2;
+        a.M = M;
+        a.in = w->ah;
+        a.in_stride = d + ff;
+        a.resid = w->x;
+        a.resid_stride = d;
+        a.k_split = d;
+        launch_gemv<PRO_COPY, EPI_RESID2>(m, a, s);
+      } else {
+        GemmArgs g{};
+        g.W = ly.w2;
+        g.n = M;
+        g.A = w->ah;
+        g.lda = d + ff;
+        g.resid = w->x;
+        g.resid_stride = d;
+        g.k_split = d;
+        launch_gemm<EPI_RESID2>(g, s);
+      }
+    } else {
+      g_stage = ST_W1;
+      if (gemv) {
+        GemvArgs a{};
+        a.W = ly.w1;
+        a.M = M;
+        a.in = w->x;
+        a.in_stride = d;
+        a.nw = ly.n1w;
+        a.out = w->qkv;
+        a.out_stride = qkvw;
+        launch_gemv<PRO_RMS, EPI_STORE>(m, a, s);
+      } else {
+        launch_norm_rows(m, w->x, w->xn, M, ly.n1w, nullptr, s);
+        GemmArgs g{};
+        g.W = ly.w1;
+        g.n = M;
+        g.A = w->xn;
+        g.lda = d;
+        g.out = w->qkv;
+        g.out_stride = qkvw;
+        launch_gemm<EPI_STORE>(g, s);
+      }
+      launch_attn_decode(m, pool, w, M, l, grid_splits, s);
+      g_stage = ST_W2;
+      if (gemv) {
+        GemvArgs a{};
+        a.W = ly.w2;
+        a.M = M;
+        a.in = w->ah;
+        a.in_stride = d + ff;
+        a.resid = w->x;
+        a.resid_stride = d;
+        launch_gemv<PRO_COPY, EPI_RESID1>(m, a, s);
+        GemvArgs b{};
+        b.W = ly.w3;
+        b.M = M;
+        b.in = w->x;
+        b.in_stride = d;
+        b.nw = ly.n2w;
+        b.n_plain = 0;
+        b.glu_out = w->ah + d;
+        b.glu_stride = d + ff;
+        b.glu_act = 1;
+        launch_gemv<PRO_RMS, EPI_GLU>(m, b, s);
+        GemvArgs c{};
+        c.W = ly.w4;
+        c.M = M;
+        c.in = w->ah + d;
+        c.in_stride = d + ff;
+        c.resid = w->x;
+        c.resid_stride = d;
+        launch_gemv<PRO_COPY, EPI_RESID1>(m, c, s);
+      } else {
+        GemmArgs g{};
+        g.W = ly.w2;
+        g.n = M;
+        g.A = w->ah;
+        g.lda = d + ff;
+        g.resid = w->x;
+        g.resid_stride = d;
+        launch_gemm<EPI_RESID1>(g, s);
+        launch_norm_rows(m, w->x, w->xn, M, ly.n2w, nullptr, s);
+        GemmArgs g3{};
+        g3.W = ly.w3;
+        g3.n = M;
+        g3.A = w->xn;
+        g3.lda = d;
+        g3.n_plain = 0;
+        g3.glu_out = w->ah + d;
+        g3.glu_stride = d + ff;
+        g3.glu_act = 1;
+        launch_gemm<EPI_GLU>(g3, s);
+        GemmArgs g4{};
+        g4.W = ly.w4;
+        g4.n = M;
+        g4.A = w->ah + d;
+        g4.lda = d + ff;
+        g4.resid = w->x;
+        g4.resid_stride = d;
+        launch_gemm<EPI_RESID1>(g4, s);
+      }
+    }
+  }
+  // Final norm + head (stablelm.go:380-385, model.go:479-480).
+  g_stage = ST_HEAD;
+  if (gemv) {
+    GemvArgs a{};
+    a.W = m->head;
+    a.M = M;
+    a.in = w->x;
+    a.in_stride = d;
+    a.nw = m->fnw;
+    a.nb = m->fnb;
+    a.eps = m->eps;
+    a.argmax = w->argmax;
+    a.logits = write_logits ? w->logits : nullptr;
+    a.logits_stride = m->V;
+    if (m->arch == ARCH_STABLELM)
+      launch_gemv<PRO_LN, EPI_HEAD>(m, a, s);
+    else
+      launch_gemv<PRO_RMS, EPI_HEAD>(m, a, s);
+  } else {
+    launch_norm_rows(m, w->x, w->xn, M, m->fnw, m->fnb, s);
+    GemmArgs g{};
+    g.W = m->head;
+    g.n = M;
+    g.A = w->xn;
+    g.lda = d;
+    g.out = w->logits;
+    g.out_stride = m->V;
+    launch_gemm<EPI_STORE>(g, s);
+    PROF_BEGIN(ST_HEAD, s);
+    k_argmax_rows<<<M, 256, 0, s>>>(w->logits, m->V, m->V, w->argmax);
+    PROF_END(s);
+  }
+}
+
+// Prompt chunk of n tokens for one sequence at positions start..start+n-1
+// (prefill.go:33-115 / mlx_native.go:324-495). Tokens are in w->tokens.
+static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, int start, cudaStream_t s) {
+  const int d = m->d, ff = m->ff, qkvw = d + 2 * m->kvw;
+  EmbedArgs ea{};
+  ea.E = m->embed;
+  ea.n = n;
+  ea.tokens = w->tokens;
+  ea.x = w->x;
+  ea.x_stride = d;
+  PROF_BEGIN(ST_EMBED, s);
+  k_embed<<<n, 256, 0, s>>>(ea);
+  PROF_END(s);
+  g_stage = ST_PF_GEMM;
+  for (int l = 0; l < m->L; l++) {
+    const Layer& ly = m->layers[l];
+    launch_norm_rows(m, w->x, w->xn, n, ly.n1w, ly.n1b, s);
+    GemmArgs g{};
+    g.W = ly.w1;
+    g.n = n;
+    g.A = w->xn;
+    g.lda = d;
+    g.out = w->qkv;
+    g.out_stride = qkvw;
+    if (m->arch == ARCH_STABLELM) {
+      g.n_plain = qkvw;
+      g.glu_out = w->ah + d;
+      g.glu_stride = d + ff;
+      g.glu_act = 0;
+      launch_gemm<EPI_GLU>(g, s);
+    } else {
+      launch_gemm<EPI_STORE>(g, s);
+    }
+    RopeStoreArgs r{};
+    r.n = n;
+    r.H = m->H;
+    r.KVH = m->KVH;
+    r.hd = m->hd;
+    r.start = start;
+    r.rope = m->rope;
+    r.qkv = w->qkv;
+    r.qkv_stride = qkvw;
+    r.kv = pool->view();
+    r.layer = l;
+    r.page_table = w->pt;
+    PROF_BEGIN(ST_OTHER, s);
+    k_rope_store<<<n, 128, 0, s>>>(r);
+    PROF_END(s);
+    PrefillAttnArgs pa{};
+    pa.n = n;
+    pa.H = m->H;
+    pa.KVH = m->KVH;
+    pa.hd = m->hd;
+    pa.start = start;
+    pa.qkv = w->qkv;
+    pa.qkv_stride = qkvw;
+    pa.kv = pool->view();
+    pa.layer = l;
+    pa.page_table = w->pt;
+    pa.out = w->ah;
+    pa.out_stride = d + ff;
+    pa.scale = (float)sqrt((double)m->hd);
+    const size_t smem = sizeof(float) * ((size_t)PA_QT * (m->hd + 1) + 2 * (size_t)PA_KT * (m->hd + 1) + (size_t)PA_QT * PA_KT);
+    cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    PROF_BEGIN(ST_PF_ATTN, s);
+    k_attn_prefill<<<dim3((n + PA_QT - 1) / PA_QT, m->H), 128, smem, s>>>(pa);
+    PROF_END(s);
+    if (m->arch == ARCH_STABLELM) {
+      GemmArgs g2{};
+      g2.W = ly.w2;
+      g2.n = n;
+      g2.A = w->ah;
+      g2.lda = d + ff;
+      g2.resid = w->x;
+      g2.resid_stride = d;
+      g2.k_split = d;
+      launch_gemm<EPI_RESID2>(g2, s);
+    } else {
+      GemmArgs g2{};
+      g2.W = ly.w2;
+      g2.n = n;
+      g2.A = w->ah;
+      g2.lda = d + ff;
+      g2.resid = w->x;
+      g2.resid_stride = d;
+      launch_gemm<EPI_RESID1>(g2, s);
+      launch_norm_rows(m, w->x, w->xn, n, ly.n2w, nullptr, s);
+      GemmArgs g3{};
+      g3.W = ly.w3;
+      g3.n = n;
+      g3.A = w->xn;
+      g3.lda = d;
+      g3.n_plain = 0;
+      g3.glu_out = w->ah + d;
+      g3.glu_stride = d + ff;
+      g3.glu_act = 1;
+      launch_gemm<EPI_GLU>(g3, s);
+      GemmArgs g4{};
+      g4.W = ly.w4;
+      g4.n = n;
+      g4.A = w->ah + d;
+      g4.lda = d + ff;
+      g4.resid = w->x;
+      g4.resid_stride = d;
+      launch_gemm<EPI_RESID1>(g4, s);
+    }
+  }
+}
+
+// Head over the last row of a prefill chunk (prefill.go:103-109).
+static void enqueue_head_row(const tcu_model* m, Work* w, int row, float* logits, cudaStream_t s) {
+  cudaMemsetAsync(w->argmax, 0, sizeof(unsigned long long), s);
+  g_stage = ST_HEAD;
+  GemvArgs a{};
+  a.W = m->head;
+  a.M = 1;
+  a.in = w->x + (size_t)row * m->d;
+  a.in_stride = m->d;
+  a.nw = m->fnw;
+  a.nb = m->fnb;
+  a.eps = m->eps;
+  a.argmax = w->argmax;
+  a.logits = logits;
+  a.logits_stride = m->V;
+  if (m->arch == ARCH_STABLELM)
+    launch_gemv<PRO_LN, EPI_HEAD>(m, a, s);
+  else
+    launch_gemv<PRO_RMS, EPI_HEAD>(m, a, s);
+}
+
+// ---------------------------------------------------------------------------
+// Sessions
+
+struct tcu_session {
+  tcu_model* m = nullptr;
+  KVPool* pool = nullptr;
+  int half = 0;
+  std::vector<int> pages;
+  int length = 0;
+  cudaStream_t stream = nullptr;
+  Work w;
+  bool closed = false;
+  cudaStream_t own_stream = nullptr;  // created by the session; stream may be the caller's
+  // cached decode-step graph (step mode, M = 1)
+  cudaGraphExec_t graph = nullptr;
+  int graph_splits = 0;
+  bool graph_prof = false;
+  size_t graph_events = 0;
+  int branches_open = 0;
+  Prof prof;
+};
+
+// Routes the launch helpers' stage events to a profiled session while a call runs.
+struct ProfScope {
+  explicit ProfScope(tcu_session* s) { g_prof = (s && s->prof.on) ? &s->prof : nullptr; }
+  ~ProfScope() { g_prof = nullptr; }
+};
+
+// Accumulates recorded stage events (the stream must be synchronised).
+static void prof_collect(tcu_session* s) {
+  if (!s->prof.on) return;
+  s->prof.collect(s->prof.used);
+  s->prof.used = 0;
+}
+
+struct tcu_branches {
+  tcu_session* s = nullptr;
+  int prefix = 0, count = 0, step = 0;
+  std::vector<std::vector<int>> pages;
+  Work w;
+  bool closed = false;
+};
+
+static void release_pages(tcu_model* m, KVPool* pool, std::vector<int>& pages, size_t keep) {
+  while (pages.size() > keep) {
+    page_unref(m, pool, pages.back());
+    pages.pop_back();
+  }
+}
+
+// Makes positions [lo, hi) of a page list writable and allocated: pages past
+// the end are allocated; shared pages in range are copied (copy-on-write).
+static int prepare_pages(tcu_model* m, KVPool* pool, std::vector<int>& pages, int lo, int hi, cudaStream_t s) {
+  const int P = pool->P;
+  const size_t need = (size_t)(hi + P - 1) / P;
+  while (pages.size() < need) {
+    int pg;
+    TRY(page_alloc(m, pool, &pg));
+    pages.push_back(pg);
+  }
+  for (int i = lo / P; i < (int)need; i++) {
+    if (page_refcount(m, pool, pages[i]) > 1) {
+      int pg;
+      TRY(page_alloc(m, pool, &pg));
+      const size_t page_vec = pool->page_elems() * pool->elem() / 16;
+      k_copy_page<<<592, 256, 0, s>>>((uint4*)pool->k, (uint4*)pool->v, page_vec, pool->num_pages, pages[i], pg, pool->L);
+      CK(cudaGetLastError());
+      page_unref(m, pool, pages[i]);
+      pages[i] = pg;
+    }
+  }
+  return TCU_OK;
+}
+
+static int session_sync(tcu_session* s) {
+  cudaError_t e = cudaStreamSynchronize(s->stream);
+  if (e != cudaSuccess) return fail(TCU_ECUDA, "device execution failed: %s", cudaGetErrorString(e));
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(TCU_ECUDA, "launch failed: %s", cudaGetErrorString(e));
+  return TCU_OK;
+}
+
+static int upload_pt(tcu_session* s) {
+  CK(cudaMemcpyAsync(s->w.pt, s->pages.data(), s->pages.size() * sizeof(int), cudaMemcpyHostToDevice, s->stream));
+  return TCU_OK;
+}
+
+static int check_tokens(const tcu_model* m, const int32_t* tokens, int n) {
+  if (n > 0 && !tokens) return fail(TCU_EINVAL, "null tokens");
+  for (int i = 0; i < n; i++)
+    if (tokens[i] < 0 || tokens[i] >= m->V) return fail(TCU_EINVAL, "invalid token %d", tokens[i]);
+  return TCU_OK;
+}
+
+// Runs tokens[0..n) at positions prefix.. and leaves the last row's argmax in
+// w.argmax[0] and (if logits) its logits in w.logits.
+static int session_run(tcu_session* s, int prefix, const int32_t* tokens, int n, float* all_logits) {
+  tcu_model* m = s->m;
+  TRY(prepare_pages(m, s->pool, s->pages, prefix, prefix + n, s->stream));
+  TRY(upload_pt(s));
+  if (n == 1 && !all_logits) {
+    CK(cudaMemcpyAsync(s->w.tokens, tokens, sizeof(int), cudaMemcpyHostToDevice, s->stream));
+    CK(cudaMemcpyAsync(s->w.pos, &prefix, sizeof(int), cudaMemcpyHostToDevice, s->stream));
+    CK(cudaMemsetAsync(s->w.argmax, 0, sizeof(unsigned long long), s->stream));
+    const int split = SPLIT_PAGES * m->P;
+    enqueue_decode(m, s->pool, &s->w, 1, false, (prefix + 1 + split - 1) / split, true, s->stream);
+    CK(cudaGetLastError());
+    return TCU_OK;
+  }
+  for (int off = 0; off < n; off += CHUNK) {
+    const int c = std::min(CHUNK, n - off);
+    CK(cudaMemcpyAsync(s->w.tokens, tokens + off, c * sizeof(int), cudaMemcpyHostToDevice, s->stream));
+    enqueue_prefill(m, s->pool, &s->w, c, prefix + off, s->stream);
+    CK(cudaGetLastError());
+    if (all_logits) {
+      for (int j = 0; j < c; j++) {
+        enqueue_head_row(m, &s->w, j, s->w.logits, s->stream);
+        CK(cudaMemcpyAsync(all_logits + (size_t)(off + j) * m->V, s->w.logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, s->stream));
+      }
+    } else if (off + c == n) {
+      enqueue_head_row(m, &s->w, c - 1, s->w.logits, s->stream);
+    }
+    CK(cudaGetLastError());
+  }
+  return TCU_OK;
+}
+
+static int validate_forward(tcu_session* s, int prefix, const int32_t* tokens, int n) {
+  if (!s) return fail(TCU_EINVAL, "null session");
+  if (s->closed) return fail(TCU_ECLOSED, "session is closed");
+  if (s->branches_open) return fail(TCU_EINVAL, "close the open branches first");
+  // mlx_native.go:328-335
+  if (prefix < 0 || prefix > s->length || n <= 0 || prefix + n > s->m->max_pos)
+    return fail(TCU_EINVAL, "invalid cached prefix or context length (prefix %d, resident %d, tokens %d, limit %d)", prefix, s->length, n,
+                s->m->max_pos);
+  return check_tokens(s->m, tokens, n);
+}
+
+static void session_invalidate(tcu_session* s) {
+  release_pages(s->m, s->pool, s->pages, 0);
+  s->length = 0;
+}
+
+static int session_finish(tcu_session* s, int rc, int new_length) {
+  if (rc == TCU_OK) rc = session_sync(s);
+  if (rc == TCU_OK) prof_collect(s);
+  s->prof.used = 0;
+  if (rc != TCU_OK) {
+    std::string msg = g_err;
+    cudaStreamSynchronize(s->stream);
+    session_invalidate(s);
+    g_err = msg;
+    return rc;
+  }
+  s->length = new_length;
+  release_pages(s->m, s->pool, s->pages, (size_t)(new_length + s->pool->P - 1) / s->pool->P);
+  return TCU_OK;
+}
+
+// Captures one greedy decode step (embed from argmax .. head) as a graph.
+static int session_graph(tcu_session* s, int splits) {
+  if (s->graph && s->graph_splits >= splits && s->graph_prof == s->prof.on) return TCU_OK;
+  if (s->graph) {
+    cudaGraphExecDestroy(s->graph);
+    s->graph = nullptr;
+  }
+  cudaGraph_t g;
+  s->prof.used = 0;
+  CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeRelaxed));
+  enqueue_decode(s->m, s->pool, &s->w, 1, true, splits, true, s->stream);
+  cudaError_t e = cudaStreamEndCapture(s->stream, &g);
+  s->graph_events = s->prof.used;
+  s->graph_prof = s->prof.on;
+  s->prof.used = 0;
+  if (e != cudaSuccess) return fail(TCU_ECUDA, "graph capture: %s", cudaGetErrorString(e));
+  e = cudaGraphInstantiate(&s->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return fail(TCU_ECUDA, "graph instantiate: %s", cudaGetErrorString(e));
+  s->graph_splits = splits;
+  return TCU_OK;
+}
+
+// Releases the suffix pages of a branch batch (the shared prefix stays with
+// its session); idempotent.
+static void branches_release(tcu_branches* b) {
+  if (b->closed) return;
+  b->closed = true;
+  tcu_session* s = b->s;
+  cudaStreamSynchronize(s->stream);
+  for (auto& pl : b->pages) release_pages(s->m, s->pool, pl, 0);
+  s->branches_open--;
+}
+
+// ---------------------------------------------------------------------------
+// C ABI
+
+extern "C" {
+
+int tcu_abi_version(void) { return TCU_ABI_VERSION; }
+
+const char* tcu_last_error(void) { return g_err.c_str(); }
+
+int tcu_device_count(int32_t* count) {
+  if (!count) return fail(TCU_EINVAL, "null count");
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    *count = 0;
+    return TCU_OK;
+  }
+  *count = n;
+  return TCU_OK;
+}
+
+int tcu_stablelm_load(const tcu_stablelm_config* config, const tcu_tensor* tensors, int32_t n_tensors, const tcu_load_options* options,
+                      tcu_model** out) {
+  return stablelm_load(config, tensors, n_tensors, options, out);
+}
+
+int tcu_llama_load(const void* checkpoint, uint64_t nbytes, const tcu_load_options* options, tcu_model** out) {
+  return llama_load(checkpoint, nbytes, options, out);
+}
+
+int tcu_model_info(const tcu_model* m, int32_t* vocab, int32_t* hidden, int32_t* layers, int32_t* heads, int32_t* kv_heads,
+                   int32_t* max_positions) {
+  if (!m) return fail(TCU_EINVAL, "null model");
+  if (vocab) *vocab = m->V;
+  if (hidden) *hidden = m->d;
+  if (layers) *layers = m->L;
+  if (heads) *heads = m->H;
+  if (kv_heads) *kv_heads = m->KVH;
+  if (max_positions) *max_positions = m->max_pos;
+  return TCU_OK;
+}
+
+int tcu_model_memory(const tcu_model* m, uint64_t* weight_bytes, uint64_t* kv_pool_bytes, uint64_t* kv_used_bytes) {
+  if (!m) return fail(TCU_EINVAL, "null model");
+  uint64_t pool = 0, used = 0;
+  for (KVPool* p : m->pools)
+    if (p) {
+      const uint64_t pb = (uint64_t)p->L * p->page_elems() * p->elem() * 2;
+      pool += pb * p->num_pages;
+      used += pb * p->used();
+    }
+  if (weight_bytes) *weight_bytes = m->weight_bytes;
+  if (kv_pool_bytes) *kv_pool_bytes = pool;
+  if (kv_used_bytes) *kv_used_bytes = used;
+  return TCU_OK;
+}
+
+int tcu_model_free(tcu_model* m) {
+  if (!m) return TCU_OK;
+  if (m->sessions > 0) return fail(TCU_EINVAL, "%d sessions still open", m->sessions);
+  model_release(m);
+  return TCU_OK;
+}
+
+int tcu_session_new(tcu_model* m, int32_t kv_dtype, tcu_session** out) {
+  if (!m || !out) return fail(TCU_EINVAL, "null argument");
+  if (kv_dtype != TCU_F32 && kv_dtype != TCU_F16) return fail(TCU_EINVAL, "unsupported KV cache precision %d: use f32 or f16", kv_dtype);
+  CK(cudaSetDevice(m->device));
+  tcu_session* s = new tcu_session();
+  s->m = m;
+  s->half = kv_dtype == TCU_F16;
+  int rc = pool_get(m, s->half, &s->pool);
+  if (rc == TCU_OK) rc = work_init(m, &s->w, CHUNK, 1, 1, m->max_pos + 1);
+  if (rc == TCU_OK && cudaStreamCreateWithFlags(&s->own_stream, cudaStreamNonBlocking) != cudaSuccess) rc = fail(TCU_ECUDA, "stream create");
+  s->stream = s->own_stream;
+  if (rc != TCU_OK) {
+    delete s;
+    return rc;
+  }
+  {
+    std::lock_guard<std::mutex> g(m->mu);
+    m->sessions++;
+  }
+  *out = s;
+  return TCU_OK;
+}
+
+int tcu_session_free(tcu_session* s) {
+  if (!s) return TCU_OK;
+  cudaSetDevice(s->m->device);
+  if (s->branches_open) return fail(TCU_EINVAL, "close the open branches first");
+  cudaStreamSynchronize(s->stream);
+  release_pages(s->m, s->pool, s->pages, 0);
+  if (s->graph) cudaGraphExecDestroy(s->graph);
+  if (s->own_stream) cudaStreamDestroy(s->own_stream);
+  {
+    std::lock_guard<std::mutex> g(s->m->mu);
+    s->m->sessions--;
+  }
+  delete s;
+  return TCU_OK;
+}
+
+int tcu_session_length(const tcu_session* s, int32_t* length) {
+  if (!s || !length) return fail(TCU_EINVAL, "null argument");
+  *length = s->length;
+  return TCU_OK;
+}
+
+int tcu_session_forward(tcu_session* s, int32_t prefix, const int32_t* tokens, int32_t n, int32_t want_logits, float* logits_out) {
+  TRY(validate_forward(s, prefix, tokens, n));
+  if (want_logits && !logits_out) return fail(TCU_EINVAL, "null logits buffer");
+  CK(cudaSetDevice(s->m->device));
+  ProfScope ps(s);
+  int rc = session_run(s, prefix, tokens, n, nullptr);
+  if (rc == TCU_OK && want_logits) {
+    cudaError_t e = cudaMemcpyAsync(logits_out, s->w.logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToHost, s->stream);
+    if (e != cudaSuccess) rc = fail(TCU_ECUDA, "logits copy: %s", cudaGetErrorString(e));
+  }
+  return session_finish(s, rc, prefix + n);
+}
+
+int tcu_session_forward_all(tcu_session* s, int32_t prefix, const int32_t* tokens, int32_t n, float* logits_out) {
+  TRY(validate_forward(s, prefix, tokens, n));
+  if (!logits_out) return fail(TCU_EINVAL, "null logits buffer");
+  CK(cudaSetDevice(s->m->device));
+  ProfScope ps(s);
+  int rc = session_run(s, prefix, tokens, n, logits_out);
+  return session_finish(s, rc, prefix + n);
+}
+
+int tcu_session_generate_greedy(tcu_session* s, int32_t prefix, const int32_t* tokens, int32_t n, int32_t steps, int32_t* out_tokens) {
+  TRY(validate_forward(s, prefix, tokens, n));
+  if (steps < 1 || !out_tokens) return fail(TCU_EINVAL, "invalid steps or output buffer");
+  tcu_model* m = s->m;
+  if (prefix + n + steps - 1 > m->max_pos) return fail(TCU_EINVAL, "generation exceeds the context length %d", m->max_pos);
+  CK(cudaSetDevice(m->device));
+  ProfScope ps(s);
+  int rc = session_run(s, prefix, tokens, n, nullptr);
+  if (rc == TCU_OK && s->prof.on) {
+    rc = session_sync(s);
+    prof_collect(s);
+  }
+  const int end = prefix + n + steps - 1;  // resident positions afterwards
+  if (rc == TCU_OK) rc = prepare_pages(m, s->pool, s->pages, prefix + n, end, s->stream);
+  if (rc == TCU_OK) rc = upload_pt(s);
+  if (rc == TCU_OK) {
+    const int last = prefix + n - 1;
+    cudaMemcpyAsync(s->w.pos, &last, sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    cudaMemsetAsync(s->w.out_count, 0, sizeof(int), s->stream);
+    const int split = SPLIT_PAGES * m->P;
+    int splits = (end + split - 1) / split;
+    int bucket = 1;
+    while (bucket < splits) bucket *= 2;
+    bucket = std::min(bucket, s->w.max_splits);
+    if (steps > 1) rc = session_graph(s, bucket);
+    for (int i = 1; rc == TCU_OK && i < steps; i++) {
+      cudaError_t e = cudaGraphLaunch(s->graph, s->stream);
+      if (e != cudaSuccess) rc = fail(TCU_ECUDA, "graph launch: %s", cudaGetErrorString(e));
+      if (rc == TCU_OK && s->prof.on) {
+        // Events inside the graph are re-recorded by every replay.
+        rc = session_sync(s);
+        s->prof.collect(s->graph_events);
+      }
+    }
+    if (rc == TCU_OK) {
+      k_finish_greedy<<<1, 32, 0, s->stream>>>(s->w.argmax, s->w.out_tokens, s->w.out_cap, s->w.out_count, 1);
+      cudaError_t e = cudaMemcpyAsync(out_tokens, s->w.out_tokens, (size_t)steps * sizeof(int), cudaMemcpyDeviceToHost, s->stream);
+      if (e != cudaSuccess) rc = fail(TCU_ECUDA, "token copy: %s", cudaGetErrorString(e));
+    }
+  }
+  return session_finish(s, rc, end);
+}
+
+int tcu_session_shortlist(tcu_session* s, int32_t k, int32_t* ids, float* logits, double* logsumexp, int32_t* n_out) {
+  if (!s || !ids || !logits || !logsumexp || !n_out) return fail(TCU_EINVAL, "null argument");
+  if (s->closed) return fail(TCU_ECLOSED, "session is closed");
+  if (k < 1 || k > 256) return fail(TCU_EINVAL, "shortlist size must be in [1, 256]");
+  if (s->length == 0) return fail(TCU_EINVAL, "no logits: forward first");
+  CK(cudaSetDevice(s->m->device));
+  const int kk = std::min<int>(k, s->m->V);
+  const size_t smem = ((size_t)s->m->V + 31) / 32 * 4;
+  cudaFuncSetAttribute(k_shortlist, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_shortlist<<<1, 1024, smem, s->stream>>>(s->w.logits, s->m->V, kk, s->w.sl_ids, s->w.sl_vals, s->w.sl_lse);
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(ids, s->w.sl_ids, kk * sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaMemcpyAsync(logits, s->w.sl_vals, kk * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaMemcpyAsync(logsumexp, s->w.sl_lse, sizeof(double), cudaMemcpyDeviceToHost, s->stream));
+  TRY(session_sync(s));
+  *n_out = kk;
+  return TCU_OK;
+}
+
+int tcu_session_fork(tcu_session* s, tcu_session** child) {
+  if (!s || !child) return fail(TCU_EINVAL, "null argument");
+  if (s->closed) return fail(TCU_ECLOSED, "session is closed");
+  tcu_session* c = nullptr;
+  TRY(tcu_session_new(s->m, s->half ? TCU_F16 : TCU_F32, &c));
+  CK(cudaStreamSynchronize(s->stream));
+  for (int pg : s->pages) page_ref(s->m, s->pool, pg);
+  c->pages = s->pages;
+  c->length = s->length;
+  // The child starts with the parent's last logits row (sessions.go:36-72
+  // keeps probability rows; the next Forward recomputes them anyway).
+  CK(cudaMemcpyAsync(c->w.logits, s->w.logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToDevice, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  *child = c;
+  return TCU_OK;
+}
+
+int tcu_session_limit(tcu_session* s, int32_t window, int32_t* cleared) {
+  if (!s) return fail(TCU_EINVAL, "null session");
+  if (window <= 0 || window > s->m->max_pos) return fail(TCU_EINVAL, "invalid window %d", window);
+  int c = 0;
+  if (s->length > window) {
+    cudaStreamSynchronize(s->stream);
+    session_invalidate(s);
+    c = 1;
+  }
+  if (cleared) *cleared = c;
+  return TCU_OK;
+}
+
+int tcu_session_set_kv_dtype(tcu_session* s, int32_t kv_dtype, int32_t* cleared) {
+  if (!s) return fail(TCU_EINVAL, "null session");
+  if (kv_dtype != TCU_F32 && kv_dtype != TCU_F16) return fail(TCU_EINVAL, "unsupported KV cache precision %d", kv_dtype);
+  const int half = kv_dtype == TCU_F16;
+  int c = 0;
+  if (half != s->half) {
+    if (s->branches_open) return fail(TCU_EINVAL, "close the open branches first");
+    KVPool* p = nullptr;
+    TRY(pool_get(s->m, half, &p));
+    cudaStreamSynchronize(s->stream);
+    c = s->length > 0;
+    session_invalidate(s);
+    if (s->graph) {
+      cudaGraphExecDestroy(s->graph);
+      s->graph = nullptr;
+      s->graph_splits = 0;
+    }
+    s->pool = p;
+    s->half = half;
+  }
+  if (cleared) *cleared = c;
+  return TCU_OK;
+}
+
+int tcu_session_reset(tcu_session* s) {
+  if (!s) return fail(TCU_EINVAL, "null session");
+  cudaStreamSynchronize(s->stream);
+  session_invalidate(s);
+  return TCU_OK;
+}
+
+int tcu_session_set_stream(tcu_session* s, void* stream) {
+  if (!s) return fail(TCU_EINVAL, "null session");
+  if (s->closed) return fail(TCU_ECLOSED, "session is closed");
+  CK(cudaSetDevice(s->m->device));
+  CK(cudaStreamSynchronize(s->stream));
+  cudaStream_t next = stream ? (cudaStream_t)stream : s->own_stream;
+  if (next != s->stream && s->graph) {
+    cudaGraphExecDestroy(s->graph);
+    s->graph = nullptr;
+    s->graph_splits = 0;
+  }
+  s->stream = next;
+  return TCU_OK;
+}
+
+int tcu_session_profile(tcu_session* s, int32_t enable) {
+  if (!s) return fail(TCU_EINVAL, "null session");
+  s->prof.on = enable != 0;
+  s->prof.used = 0;
+  return TCU_OK;
+}
+
+int tcu_session_profile_read(tcu_session* s, int32_t n_stages, int64_t* launches, double* ms, int32_t reset) {
+  if (!s || !launches || !ms) return fail(TCU_EINVAL, "null argument");
+  for (int i = 0; i < n_stages && i < ST_COUNT; i++) {
+    launches[i] = s->prof.launches[i];
+    ms[i] = s->prof.ms[i];
+  }
+  if (reset)
+    for (int i = 0; i < ST_COUNT; i++) {
+      s->prof.launches[i] = 0;
+      s->prof.ms[i] = 0;
+    }
+  return ST_COUNT;
+}
+
+int tcu_branches_open(tcu_session* s, int32_t prefix, int32_t count, tcu_branches** out) {
+  if (!s || !out) return fail(TCU_EINVAL, "null argument");
+  if (s->closed) return fail(TCU_ECLOSED, "session is closed");
+  // mlx_branches.go:25-32 (GQA is supported here).
+  if (prefix < 0 || prefix > s->length || count < 1 || count > s->m->V || prefix >= s->m->max_pos)
+    return fail(TCU_EINVAL, "invalid branch prefix or batch size");
+  CK(cudaSetDevice(s->m->device));
+  tcu_branches* b = new tcu_branches();
+  b->s = s;
+  b->prefix = prefix;
+  b->count = count;
+  int rc = work_init(s->m, &b->w, count, count, count, 2);
+  if (rc != TCU_OK) {
+    delete b;
+    return rc;
+  }
+  CK(cudaStreamSynchronize(s->stream));
+  const size_t shared = (size_t)(prefix + s->m->P - 1) / s->m->P;
+  b->pages.resize(count);
+  for (int i = 0; i < count; i++) {
+    b->pages[i].assign(s->pages.begin(), s->pages.begin() + shared);
+    for (int pg : b->pages[i]) page_ref(s->m, s->pool, pg);
+  }
+  s->branches_open++;
+  *out = b;
+  return TCU_OK;
+}
+
+int tcu_branches_forward(tcu_branches* b, const int32_t* tokens, float* rows_out) {
+  if (!b) return fail(TCU_EINVAL, "null branches");
+  if (b->closed) return fail(TCU_ECLOSED, "token branches are closed");
+  tcu_session* s = b->s;
+  tcu_model* m = s->m;
+  if (b->prefix + b->step >= m->max_pos) return fail(TCU_EINVAL, "invalid branch batch or context length");
+  TRY(check_tokens(m, tokens, b->count));
+  CK(cudaSetDevice(m->device));
+  ProfScope ps(s);
+  const int pos = b->prefix + b->step;
+  int rc = TCU_OK;
+  std::vector<int> pt((size_t)b->count * b->w.pt_stride, 0);
+  for (int i = 0; rc == TCU_OK && i < b->count; i++) {
+    rc = prepare_pages(m, s->pool, b->pages[i], pos, pos + 1, s->stream);
+    std::copy(b->pages[i].begin(), b->pages[i].end(), pt.begin() + (size_t)i * b->w.pt_stride);
+  }
+  if (rc == TCU_OK) {
+    std::vector<int> posv(b->count, pos);
+    cudaMemcpyAsync(b->w.pt, pt.data(), pt.size() * sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    cudaMemcpyAsync(b->w.pos, posv.data(), b->count * sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    cudaMemcpyAsync(b->w.tokens, tokens, b->count * sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    cudaMemsetAsync(b->w.argmax, 0, b->count * sizeof(unsigned long long), s->stream);
+    const int split = SPLIT_PAGES * m->P;
+    enqueue_decode(m, s->pool, &b->w, b->count, false, (pos + 1 + split - 1) / split, true, s->stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) rc = fail(TCU_ECUDA, "launch: %s", cudaGetErrorString(e));
+    if (rc == TCU_OK && rows_out) {
+      e = cudaMemcpyAsync(rows_out, b->w.logits, (size_t)b->count * m->V * 4, cudaMemcpyDeviceToHost, s->stream);
+      if (e != cudaSuccess) rc = fail(TCU_ECUDA, "rows copy: %s", cudaGetErrorString(e));
+    }
+  }
+  if (rc == TCU_OK) rc = session_sync(s);
+  if (rc == TCU_OK) prof_collect(s);
+  s->prof.used = 0;
+  if (rc != TCU_OK) {
+    // mlx_branches.go:176-178: evaluation errors close the suffix caches; the
+    // handle stays valid until tcu_branches_close.
+    std::string msg = g_err;
+    branches_release(b);
+    g_err = msg;
+    return rc;
+  }
+  b->step++;
+  return TCU_OK;
+}
+
+int tcu_branches_argmax(tcu_branches* b, int32_t* ids) {
+  if (!b || !ids) return fail(TCU_EINVAL, "null argument");
+  if (b->closed) return fail(TCU_ECLOSED, "token branches are closed");
+  if (b->step == 0) return fail(TCU_EINVAL, "no rows: forward first");
+  std::vector<unsigned long long> keys(b->count);
+  CK(cudaMemcpy(keys.data(), b->w.argmax, b->count * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+  for (int i = 0; i < b->count; i++) ids[i] = (int)(0xffffffffu - (uint32_t)(keys[i] & 0xffffffffu));
+  return TCU_OK;
+}
+
+int tcu_branches_close(tcu_branches* b) {
+  if (!b) return TCU_OK;
+  branches_release(b);
+  delete b;
+  return TCU_OK;
+}
+
+}  // extern "C"
