@@ -147,9 +147,12 @@ def cpu_sample(cfg, tensors, prompt, budget_s=20.0):
     return n_pf / t_pf, n_dec / t_dec, oc.threads(), sample
 
 
-def synth(device):
+def synth(device, layers=None):
     from tinyoai_b200.synth import CLIO_3B, synth_stablelm
-    return synth_stablelm(CLIO_3B, "Q8_0", seed=0, device=device)
+    cfg = dict(CLIO_3B)
+    if layers:
+        cfg["num_hidden_layers"] = layers
+    return synth_stablelm(cfg, "Q8_0", seed=0, device=device)
 
 
 def run_reference(args):
@@ -198,13 +201,18 @@ def run_b200(args):
     from tinyoai_b200 import Model
     from tinyoai_b200.synth import prompt_ids
 
-    cfg, tensors = synth(f"cuda:{local}")
-    model = Model.load_stablelm(cfg, tensors, device=local)
+    cfg, tensors = synth(f"cuda:{local}", args.layers)
+    model = Model.load_stablelm(cfg, tensors, device=local, kv_pool_bytes=args.kv_pool_mb << 20)
+    torch.cuda.empty_cache()
     if not (rank == 0 and world == 1 and args.cpu_baseline):
         del tensors
         tensors = None
     prompt = prompt_ids(PROMPT, cfg["vocab_size"], seed=rank)
-    stream = torch.cuda.current_stream()
+    # A dedicated stream (the default stream's handle is 0, which the library
+    # reads as "use your own stream"); events are recorded on the same stream
+    # the library launches on.
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     sess = model.session("f32")
     sess.set_stream(stream.cuda_stream)
 
@@ -272,25 +280,33 @@ def run_b200(args):
         tok_per_step = PROMPT + GEN
         value = world * tok_per_step * args.steps / (total_ms / 1e3)
         launches = sum(v[0] for v in prof.values())
-        w1_n, w1_ms = prof["norm_qkv_gate_up"]
         avg_T = PROMPT + GEN / 2
         step_bytes, w1_bytes = decode_bytes(cfg, avg_T)
-        achieved = w1_bytes / (w1_ms / w1_n / 1e3) / 1e9 if w1_n else None
         dec_gbs = step_bytes * GEN / (dc_ms / args.steps / 1e3) / 1e9
+        # Dominant kernel: the persistent decode step when it runs (one launch
+        # per token, moving step_bytes), else the fused W1 GEMV (w1_bytes).
+        if prof["decode_step"][0]:
+            dom_n, dom_ms = prof["decode_step"]
+            dom_bytes, dom_kernel = step_bytes, "k_decode_mega (persistent decode step: all layers, lm_head, argmax)"
+        else:
+            dom_n, dom_ms = prof["norm_qkv_gate_up"]
+            dom_bytes, dom_kernel = w1_bytes, "k_gemv<Q8_0, LayerNorm prologue, q/k/v + SwiGLU epilogue>"
+        achieved = dom_bytes / (dom_ms / dom_n / 1e3) / 1e9 if dom_n else None
+        workload = WORKLOAD if not args.layers else WORKLOAD + f" [PROFILING CASE: {args.layers} layers, not a bench line]"
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "q8_0 weights, f32 activations/accumulate", "data": "synthetic (seeded N(0,0.02) weights quantised to Q8_0, uniform prompt ids)",
-            "config": {"workload": WORKLOAD, "prompt": PROMPT, "generate": GEN, "kv": "f32", "parallelism": f"replicas x{world}",
+            "config": {"workload": workload, "prompt": PROMPT, "generate": GEN, "kv": "f32", "parallelism": f"replicas x{world}",
                        "l2": "inputs larger than L2 (2.9 GB of weights streamed per token)"},
             "prefill_tok_s": world * (PROMPT - 1) * args.steps / (pf_ms / 1e3),
             "decode_tok_s": world * GEN * args.steps / (dc_ms / 1e3),
             "decode_ms_per_token": dc_ms / args.steps / GEN,
-            "roofline": {"bound": "hbm", "kernel": "k_gemv<Q8_0, LayerNorm prologue, q/k/v + SwiGLU epilogue>",
+            "roofline": {"bound": "hbm", "kernel": dom_kernel,
                          "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": (achieved / hbm) if achieved else None, "peak_kind": peak_kind,
-                         "traffic": None, "bytes_per_launch": w1_bytes,
-                         "avg_launch_us": (w1_ms / w1_n * 1e3) if w1_n else None,
+                         "traffic": None, "bytes_per_launch": dom_bytes,
+                         "avg_launch_us": (dom_ms / dom_n * 1e3) if dom_n else None,
                          "decode_step_gbs": dec_gbs, "decode_step_frac": dec_gbs / hbm},
             "profile": {k: {"launches": v[0], "ms": round(v[1], 3)} for k, v in prof.items()},
             "clocks": clocks.summary(),
@@ -319,6 +335,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--kv-pool-mb", type=int, default=2048, help="KV page pool per GPU (config 2 needs ~0.5 GB)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="profiling only: fewer layers of the 3B shape (a bench line always uses all 32)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

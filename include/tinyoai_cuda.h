@@ -162,8 +162,9 @@ int tcu_session_set_stream(tcu_session* session, void* stream);
  * the per-stage launch counts and milliseconds accumulate. Stages, in order:
  * embedding, norm+q/k/v/gate/up projection, decode attention, out/down
  * projection + residual, final norm+head, prefill projection, prefill
- * attention, other. tcu_session_profile_read returns the number of stages
- * (8) and fills up to n_stages entries; reset != 0 clears the totals.
+ * attention, other, whole persistent decode step. tcu_session_profile_read
+ * returns the number of stages (9) and fills up to n_stages entries;
+ * reset != 0 clears the totals.
  * Profiling synchronises after every decode step, so it is for diagnosis,
  * not for throughput runs. */
 int tcu_session_profile(tcu_session* session, int32_t enable);

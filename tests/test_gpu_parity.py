@@ -328,3 +328,27 @@ def test_llama_greedy_128(stories):
         s.close()
         ora.close()
     assert list(got) == list(want)
+
+
+def test_stage_profile(small):
+    """Stage timing (stableProfile, stablelm.go:229-250): every stage of a
+    prefill + greedy decode is counted once per launch; results are unchanged."""
+    cfg, tensors, m = small
+    ids = prompt_ids(40, cfg["vocab_size"], seed=61)
+    s = m.session()
+    try:
+        want = s.generate_greedy(0, ids, 6)
+        s.profile(True)
+        got = s.generate_greedy(0, ids, 6)
+        prof = s.profile_read(reset=True)
+        s.profile(False)
+        assert list(got) == list(want)
+        L = cfg["num_hidden_layers"]
+        assert prof["prefill_projection"][0] == 2 * L
+        assert prof["prefill_attention"][0] == L
+        assert prof["norm_qkv_gate_up"][0] == 5 * L  # five decode forwards (steps - 1)
+        assert prof["attention"][0] == 5 * L and prof["out_down_residual"][0] == 5 * L
+        assert prof["head"][0] == 6  # prefill head + five decode heads
+        assert all(ms >= 0 for _, ms in prof.values()) and prof["norm_qkv_gate_up"][1] > 0
+    finally:
+        s.close()

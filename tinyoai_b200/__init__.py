@@ -185,7 +185,7 @@ class Session:
         check(lib().tcu_session_set_stream(self._h, C.c_void_p(stream) if stream else None))
 
     STAGES = ("embed", "norm_qkv_gate_up", "attention", "out_down_residual", "head", "prefill_projection",
-              "prefill_attention", "other")
+              "prefill_attention", "other", "decode_step")
 
     def profile(self, enable=True):
         check(lib().tcu_session_profile(self._h, int(bool(enable))))

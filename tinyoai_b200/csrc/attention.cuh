@@ -7,6 +7,7 @@
 // branches); a sequence only ever writes pages it owns alone.
 #pragma once
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace tcu {
 
@@ -470,6 +471,173 @@ __global__ void k_finish_greedy(const unsigned long long* argmax, int* out_token
     out_tokens[(size_t)m * out_stride + c] = argmax_index(argmax[m]);
     out_count[m] = c + 1;
   }
+}
+
+
+
+// ---------------------------------------------------------------------------
+// Decode attention with the history staged by bulk copies: each CTA copies its
+// chunk's K and V page tiles ([P][hd], contiguous per page and kv head) into
+// shared memory with cp.async.bulk while it rotates q and the new k. Same
+// arithmetic and merge as k_attn_decode.
+
+__device__ __forceinline__ float kv_ld(const void* base, int half, size_t i) {
+  return half ? __half2float(reinterpret_cast<const __half*>(base)[i]) : reinterpret_cast<const float*>(base)[i];
+}
+
+struct DecodeAttn2Extra {
+  int* err;
+};
+
+__global__ void __launch_bounds__(128) k_attn_decode_bulk(DecodeAttnArgs a, DecodeAttn2Extra x) {
+  extern __shared__ __align__(128) uint8_t ab_smem[];
+  const int s = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
+  const int hd = a.hd, G = a.H / a.KVH, split = a.split, P = a.kv.P;
+  const int es = a.kv.half ? 2 : 4;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int pos = a.pos[m];
+  const int T = pos + 1;
+  const int nsplit = (T + split - 1) / split;
+  if (s >= nsplit) return;
+  const int t0 = s * split;
+  const int nt = min(T, t0 + split) - t0;
+  const bool has_cur = (s == nsplit - 1);
+  const int n_hist = has_cur ? nt - 1 : nt;
+
+  uint64_t* bar = reinterpret_cast<uint64_t*>(ab_smem);
+  uint8_t* ktile = ab_smem + 128;
+  uint8_t* vtile = ktile + (size_t)split * hd * es;
+  float* qs = reinterpret_cast<float*>(vtile + (size_t)split * hd * es);
+  float* sc = qs + G * hd;
+  float* cur = sc + G * split;
+  __shared__ int is_last;
+  __shared__ float mloc[32], lloc[32];
+
+  const int* pt = a.page_table + (size_t)m * a.pt_stride;
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int npages = (n_hist + P - 1) / P;
+  if (threadIdx.x == 0 && npages > 0) {
+    const uint32_t pbytes = (uint32_t)(P * hd * es);
+    mbar_expect_tx(bar, 2u * npages * pbytes);
+    for (int j = 0; j < npages; j++) {
+      const int page = pt[t0 / P + j];
+      const size_t o = a.kv.off(a.layer, page, g, 0) * es;
+      bulk_g2s(ktile + (size_t)j * pbytes, reinterpret_cast<const uint8_t*>(a.kv.k) + o, pbytes, bar);
+      bulk_g2s(vtile + (size_t)j * pbytes, reinterpret_cast<const uint8_t*>(a.kv.v) + o, pbytes, bar);
+    }
+  }
+  // While the copies fly: q of the group and, in the last chunk, the new k/v.
+  const float* q_in = a.qkv + (size_t)m * a.qkv_stride;
+  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) qs[e] = q_in[(g * G) * hd + e];
+  if (has_cur) {
+    for (int e = threadIdx.x; e < hd; e += blockDim.x) {
+      cur[e] = q_in[a.H * hd + g * hd + e];
+      cur[hd + e] = q_in[(a.H + a.KVH) * hd + g * hd + e];
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * a.rope.pairs; e += blockDim.x) rope_pair(qs + (e / a.rope.pairs) * hd, e % a.rope.pairs, a.rope, pos);
+  if (has_cur)
+    for (int e = threadIdx.x; e < a.rope.pairs; e += blockDim.x) rope_pair(cur, e, a.rope, pos);
+  __syncthreads();
+  if (has_cur) {
+    for (int e = threadIdx.x; e < 2 * hd; e += blockDim.x) cur[e] = kv_round(cur[e], a.kv.half);
+    __syncthreads();
+    const int page = pt[pos / P], row = pos % P;
+    const size_t o = a.kv.off(a.layer, page, g, row);
+    for (int e = threadIdx.x; e < hd; e += blockDim.x) {
+      kv_store(a.kv, a.kv.k, o + e, cur[e]);
+      kv_store(a.kv, a.kv.v, o + e, cur[hd + e]);
+    }
+  }
+  if (npages > 0) mbar_wait(bar, 0, x.err);
+  __syncthreads();
+  // Scores. Each thread walks the head dimension starting at its own offset,
+  // so the threads of a warp read distinct banks of their key rows.
+  for (int e = threadIdx.x; e < G * split; e += blockDim.x) {
+    const int hh = e / split, t = e % split;
+    if (t < nt) {
+      const float* q = qs + hh * hd;
+      float d = 0.f;
+      int i0 = t % hd;
+      if (has_cur && t == nt - 1) {
+        for (int i = 0; i < hd; i++) {
+          int ii = i0 + i;
+          ii -= ii >= hd ? hd : 0;
+          d = fmaf(q[ii], cur[ii], d);
+        }
+      } else {
+        const size_t rowo = (size_t)t * hd;
+        for (int i = 0; i < hd; i++) {
+          int ii = i0 + i;
+          ii -= ii >= hd ? hd : 0;
+          d = fmaf(q[ii], kv_ld(ktile, a.kv.half, rowo + ii), d);
+        }
+      }
+      sc[hh * split + t] = __fdiv_rn(d, a.scale);
+    }
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  for (int hh = warp; hh < G; hh += nwarps) {
+    float mx = -INFINITY;
+    for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, sc[hh * split + t]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float l = 0.f;
+    for (int t = lane; t < nt; t += 32) {
+      float p = expf(sc[hh * split + t] - mx);
+      sc[hh * split + t] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      mloc[hh] = mx;
+      lloc[hh] = l;
+    }
+  }
+  __syncthreads();
+  float* part = a.part + ((size_t)m * a.H + g * G) * a.max_splits * (hd + 2);
+  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
+    const int hh = e / hd, i = e % hd;
+    float o = 0.f;
+    for (int t = 0; t < n_hist; t++) o = fmaf(sc[hh * split + t], kv_ld(vtile, a.kv.half, (size_t)t * hd + i), o);
+    if (has_cur) o = fmaf(sc[hh * split + nt - 1], cur[hd + i], o);
+    part[((size_t)hh * a.max_splits + s) * (hd + 2) + i] = o;
+  }
+  if (threadIdx.x < G) {
+    part[((size_t)threadIdx.x * a.max_splits + s) * (hd + 2) + hd] = mloc[threadIdx.x];
+    part[((size_t)threadIdx.x * a.max_splits + s) * (hd + 2) + hd + 1] = lloc[threadIdx.x];
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int prev = atomicAdd(a.counters + m * a.KVH + g, 1);
+    is_last = (prev == nsplit - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
+    const int hh = e / hd, i = e % hd;
+    const float* ph = part + (size_t)hh * a.max_splits * (hd + 2);
+    float mx = -INFINITY;
+    for (int j = 0; j < nsplit; j++) mx = fmaxf(mx, __ldcg(ph + (size_t)j * (hd + 2) + hd));
+    float l = 0.f, o = 0.f;
+    for (int j = 0; j < nsplit; j++) {
+      const float* pj = ph + (size_t)j * (hd + 2);
+      float w = expf(__ldcg(pj + hd) - mx);
+      l = fmaf(__ldcg(pj + hd + 1), w, l);
+      o = fmaf(__ldcg(pj + i), w, o);
+    }
+    a.out[(size_t)m * a.out_stride + (g * G + hh) * hd + i] = __fdiv_rn(o, l);
+  }
+  if (threadIdx.x == 0) a.counters[m * a.KVH + g] = 0;
 }
 
 }  // namespace tcu

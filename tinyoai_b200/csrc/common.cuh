@@ -11,8 +11,9 @@ namespace tcu {
 enum Fmt : int { FMT_F32 = 0, FMT_F16 = 1, FMT_Q5_1 = 7, FMT_Q8_0 = 8, FMT_Q5_K = 13, FMT_Q6_K = 14, FMT_BF16 = 30 };
 
 // A weight matrix in device layout, row-major [rows][cols].
-//  Q8_0: w = int8 quants [rows][cols], s = binary16 block scales [rows][cols/32]
-//        (the 34-byte GGUF block split into two 16-byte-aligned planes).
+//  Q8_0: w = int8 quants [rows][cols], s = binary16 block scales
+//        [rows][sstride] with sstride = cols/32 rounded up to 8 (the 34-byte
+//        GGUF block split into two planes whose rows start on 16 bytes).
 //  F32 / F16 / BF16: w = the raw elements.
 //  Q6_K / Q5_K / Q5_1: w = the GGUF blocks as stored (row-major blocks).
 struct DMat {
@@ -20,6 +21,7 @@ struct DMat {
   int rows, cols;
   const uint8_t* w;
   const __half* s;
+  int sstride;  // Q8_0 scale row stride in halves
 };
 
 __device__ __forceinline__ float bf16_bits_to_float(uint32_t b) { return __uint_as_float(b << 16); }
@@ -121,7 +123,7 @@ __host__ __device__ inline int kquant_block_width(int fmt) { return fmt == FMT_Q
 __device__ __forceinline__ float dmat_at(const DMat& m, int r, int c) {
   switch (m.fmt) {
     case FMT_Q8_0:
-      return __fmul_rn(__half2float(m.s[(size_t)r * (m.cols / 32) + c / 32]), (float)((const int8_t*)m.w)[(size_t)r * m.cols + c]);
+      return __fmul_rn(__half2float(m.s[(size_t)r * m.sstride + c / 32]), (float)((const int8_t*)m.w)[(size_t)r * m.cols + c]);
     case FMT_F32:
       return ((const float*)m.w)[(size_t)r * m.cols + c];
     case FMT_F16:

@@ -38,7 +38,7 @@ __device__ __forceinline__ void decode8(const DMat& W, int r, int k0, float* dst
   }
   const int K = W.cols;
   if (W.fmt == FMT_Q8_0 && k0 + 8 <= K) {
-    const float s = __half2float(W.s[(size_t)r * (K / 32) + k0 / 32]);
+    const float s = __half2float(W.s[(size_t)r * W.sstride + k0 / 32]);
     const uint2 q = *reinterpret_cast<const uint2*>(W.w + (size_t)r * K + k0);
     const uint32_t a = q.x ^ 0x80808080u, b = q.y ^ 0x80808080u;
 #pragma unroll

@@ -262,8 +262,8 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv(GemvArgs a) {
     const bool has1 = r0 + 1 < R;
     const uint8_t* w0 = a.W.w + (size_t)r0 * row_bytes;
     const uint8_t* w1 = has1 ? w0 + row_bytes : w0;
-    const __half* s0 = (FMT == FMT_Q8_0) ? a.W.s + (size_t)r0 * (K / 32) : nullptr;
-    const __half* s1 = (FMT == FMT_Q8_0) ? (has1 ? s0 + K / 32 : s0) : nullptr;
+    const __half* s0 = (FMT == FMT_Q8_0) ? a.W.s + (size_t)r0 * a.W.sstride : nullptr;
+    const __half* s1 = (FMT == FMT_Q8_0) ? (has1 ? s0 + a.W.sstride : s0) : nullptr;
     float lo[M][2], hi[M][2];
 #pragma unroll
     for (int m = 0; m < M; m++) lo[m][0] = lo[m][1] = hi[m][0] = hi[m][1] = 0.f;

@@ -26,7 +26,7 @@ __global__ void k_repack(RepackArgs a) {
       const uint8_t* blk = a.raw + idx * 34;
       const int dr = a.row0 + r * a.row_step;
       __half* ds = const_cast<__half*>(a.dst.s);
-      ds[(size_t)dr * (K2 / 32) + a.col0 / 32 + b] = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
+      ds[(size_t)dr * a.dst.sstride + a.col0 / 32 + b] = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
       uint8_t* q = dw + (size_t)dr * K2 + a.col0 + b * 32;
 #pragma unroll
       for (int i = 0; i < 32; i++) q[i] = blk[2 + i];

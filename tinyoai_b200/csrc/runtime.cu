@@ -24,9 +24,14 @@
 #include "common.cuh"
 #include "gemm_simt.cuh"
 #include "gemv.cuh"
+#include "gemv_stream.cuh"
+#include "decode_mega.cuh"
 #include "misc.cuh"
 
 using namespace tcu;
+
+static const int CHUNK = 512;      // prompt tokens per internal chunk (mlx.go:352-355)
+static const int SPLIT_PAGES = 2;  // KV pages per decode attention unit
 
 // ---------------------------------------------------------------------------
 // Errors: integer status + thread-local message (internal/mlx/bridge.c:13-33).
@@ -47,6 +52,14 @@ static int fail(int code, const char* fmt, ...) {
     cudaError_t e_ = (x);                                                                       \
     if (e_ != cudaSuccess) return fail(TCU_ECUDA, "%s (%s:%d): %s", #x, __FILE__, __LINE__, cudaGetErrorString(e_)); \
   } while (0)
+// First kernel launch or async call on this thread whose launch reported an
+// error, named in the message of the call that fails.
+static thread_local const char* g_err_site = nullptr;
+static inline void note_launch(const char* site) {
+  if (!g_err_site && cudaPeekAtLastError() != cudaSuccess) g_err_site = site;
+}
+#define NOTE(site) note_launch(site)
+
 #define TRY(x)               \
   do {                       \
     int r_ = (x);            \
@@ -103,6 +116,13 @@ struct tcu_model {
   int sessions = 0;
   int sm_count = 148;
   int gemv_smem_optin = 0;
+  bool disable_stream = false;  // TCU_DECODE_KERNELS=portable selects the non-TMA kernels
+  // Persistent decode step (decode_mega.cuh): Q8_0 StableLM shapes that fit.
+  bool mega = false;
+  MegaLayer* mega_layers = nullptr;  // device array
+  uint32_t mega_slot_bytes = 0, mega_off[5] = {0, 0, 0, 0, 0};
+  int mega_slots = 0, mega_split = 0;
+  size_t mega_smem = 0;
 };
 
 static int dalloc(tcu_model* m, void** p, size_t n) {
@@ -172,8 +192,9 @@ static int alloc_dmat(tcu_model* m, DMat* out, int fmt, int rows, int cols) {
   TRY(dalloc(m, &p, fmt_row_bytes(fmt, cols) * rows));
   w.w = (const uint8_t*)p;
   if (fmt == FMT_Q8_0) {
+    w.sstride = (cols / 32 + 7) / 8 * 8;
     void* s = nullptr;
-    TRY(dalloc(m, &s, (size_t)rows * (cols / 32) * 2));
+    TRY(dalloc(m, &s, (size_t)rows * w.sstride * 2));
     w.s = (const __half*)s;
   }
   *out = w;
@@ -202,6 +223,7 @@ static int place(Stager& st, const void* data, size_t nbytes, int fmt, int rows,
   CK(cudaMemcpy(st.buf, data, nbytes, cudaMemcpyHostToDevice));
   RepackArgs a{st.buf, fmt, rows, cols, dst, row0, row_step, col0};
   k_repack<<<1184, 256>>>(a);
+  NOTE("k_repack");
   CK(cudaGetLastError());
   CK(cudaDeviceSynchronize());
   return TCU_OK;
@@ -271,6 +293,8 @@ static void init_common(tcu_model* m, const tcu_load_options* o) {
   m->pool_budget = o ? o->kv_pool_bytes : 0;
   cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, m->device);
   cudaDeviceGetAttribute(&m->gemv_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
+  const char* k = getenv("TCU_DECODE_KERNELS");
+  m->disable_stream = k && strcmp(k, "portable") == 0;
 }
 
 // StableLM rotary table (stablelm.go:309-326): per position and rotary pair,
@@ -316,6 +340,63 @@ static int check_tensor(const tcu_tensor* t, const std::string& name, int64_t ro
     return fail(TCU_EINVAL, "tensor %s: K-quant rows must be divisible by 256", name.c_str());
   if (t->nbytes != file_bytes(t->dtype, r, c)) return fail(TCU_EINVAL, "tensor %s: %llu bytes, want %zu", name.c_str(), (unsigned long long)t->nbytes, file_bytes(t->dtype, r, c));
   if (!t->data) return fail(TCU_EINVAL, "tensor %s: null data", name.c_str());
+  return TCU_OK;
+}
+
+// Decides whether the persistent decode kernel serves this model and lays out
+// its shared memory: Q8_0 weights everywhere, hidden <= 2560 (one register
+// chunk per warp), intermediate <= 3 * 2560, head_dim such that an attention
+// unit's K and V tiles fit one ring slot.
+static int build_mega(tcu_model* m) {
+  m->mega = false;
+  if (m->disable_stream || m->arch != ARCH_STABLELM) return TCU_OK;
+  if (m->embed.fmt != FMT_Q8_0 || m->head.fmt != FMT_Q8_0) return TCU_OK;
+  for (const Layer& ly : m->layers)
+    if (ly.w1.fmt != FMT_Q8_0 || ly.w2.fmt != FMT_Q8_0) return TCU_OK;
+  const int d = m->d, ff = m->ff, K2 = d + ff;
+  if (d % 32 || ff % 32 || d / 16 > 32 * MG_NJ || ff / 16 / 3 + 1 > 32 * MG_NJ || K2 > MG_MAXK) return TCU_OK;
+  if (m->H / m->KVH > 32 || m->hd % 2) return TCU_OK;
+  if (2 * ((d / 2 + m->sm_count - 1) / m->sm_count) > MG_CPART_ROWS) return TCU_OK;
+  const size_t w1 = (size_t)MG_W1_RS * (d + m->layers[0].w1.sstride * 2);
+  const size_t w2 = (size_t)MG_W2_RS * (K2 + m->layers[0].w2.sstride * 2);
+  const size_t hb = (size_t)MG_W1_RS * (d + m->head.sstride * 2);
+  size_t slot = std::max(w1, std::max(w2, hb));
+  int split = 2 * m->P;
+  while (split > m->P && (size_t)2 * split * m->hd * 4 > slot) split -= m->P;
+  slot = std::max(slot, (size_t)2 * split * m->hd * 4);  // f32 KV worst case
+  slot = (slot + 127) / 128 * 128;
+  const int G_q = m->H / m->KVH;
+  const size_t xs_floats = std::max<size_t>(K2, (size_t)G_q * m->hd + 2 * m->hd + (size_t)G_q * split);
+  uint32_t off_x = 128;
+  uint32_t off_dig = off_x + (uint32_t)((xs_floats * 4 + 127) / 128 * 128);
+  uint32_t off_sx = off_dig + (uint32_t)(((size_t)K2 / 4 * 12 + 127) / 128 * 128);
+  uint32_t off_part = off_sx + (uint32_t)(((size_t)K2 / 32 * 4 + 127) / 128 * 128);
+  uint32_t off_slots = off_part + (uint32_t)((MG_CPART_ROWS * 4 * 4 + 127) / 128 * 128);
+  const size_t limit = (size_t)m->gemv_smem_optin;
+  if (off_slots + 2 * slot > limit) return TCU_OK;
+  const int nslots = (int)std::min<size_t>(MG_MAX_SLOTS, (limit - off_slots) / slot);
+  std::vector<MegaLayer> hl(m->L);
+  for (int l = 0; l < m->L; l++) {
+    const Layer& ly = m->layers[l];
+    hl[l] = MegaLayer{(const int8_t*)ly.w1.w, ly.w1.s, (const int8_t*)ly.w2.w, ly.w2.s, ly.n1w, ly.n1b};
+  }
+  void* p = nullptr;
+  TRY(dalloc(m, &p, hl.size() * sizeof(MegaLayer)));
+  CK(cudaMemcpy(p, hl.data(), hl.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice));
+  m->mega_layers = (MegaLayer*)p;
+  m->mega_slot_bytes = (uint32_t)slot;
+  m->mega_slots = nslots;
+  m->mega_split = split;
+  m->mega_off[0] = off_x;
+  m->mega_off[1] = off_dig;
+  m->mega_off[2] = off_sx;
+  m->mega_off[3] = off_part;
+  m->mega_off[4] = off_slots;
+  m->mega_smem = off_slots + (size_t)nslots * slot;
+  CK(cudaFuncSetAttribute(k_decode_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->mega_smem));
+  int occ = 0;
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_decode_mega, MG_THREADS, m->mega_smem));
+  m->mega = occ >= 1 && m->mega_split == SPLIT_PAGES * m->P;
   return TCU_OK;
 }
 
@@ -411,6 +492,7 @@ static int stablelm_load(const tcu_stablelm_config* c, const tcu_tensor* t, int 
   if ((rc = decode_vec(find_tensor(t, n, "model.norm.weight"), d, fw)) || (rc = decode_vec(find_tensor(t, n, "model.norm.bias"), d, fb)) ||
       (rc = upload_floats(m, fw, &m->fnw)) || (rc = upload_floats(m, fb, &m->fnb)))
     return bail(rc);
+  if ((rc = build_mega(m))) return bail(rc);
   *out = m;
   return TCU_OK;
 }
@@ -534,8 +616,16 @@ static int pool_get(tcu_model* m, int half, KVPool** out) {
     cudaGetLastError();
     return fail(TCU_ENOMEM, "KV pool: cannot allocate %d pages (%zu bytes)", (int)pages, 2 * half_bytes);
   }
+  // Zeroed on the legacy stream, which does not order with the sessions'
+  // non-blocking streams: wait here so no session kernel can race it.
   cudaMemset(p->k, 0, half_bytes);
   cudaMemset(p->v, 0, half_bytes);
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(p->k);
+    cudaFree(p->v);
+    delete p;
+    return fail(TCU_ECUDA, "KV pool initialisation failed: %s", cudaGetErrorString(cudaGetLastError()));
+  }
   p->ref.assign(p->num_pages, 0);
   p->free_list.reserve(p->num_pages);
   for (int i = p->num_pages - 1; i >= 0; i--) p->free_list.push_back(i);
@@ -569,8 +659,6 @@ static int page_refcount(tcu_model* m, KVPool* p, int page) {
 // Workspace for M concurrent sequences (a session: M = 1 decode or a prompt
 // chunk of up to CHUNK tokens; branches: M = count).
 
-static const int CHUNK = 512;  // prompt tokens per internal chunk (mlx.go:352-355)
-static const int SPLIT_PAGES = 2;
 
 struct Work {
   int rows = 0, seqs = 0, logits_rows = 0;
@@ -584,6 +672,10 @@ struct Work {
   int* sl_ids = nullptr;
   float* sl_vals = nullptr;
   double* sl_lse = nullptr;
+  int* err = nullptr;  // device error word of bounded waits (TCU_DEV_TIMEOUT)
+  unsigned long long* keys = nullptr;  // persistent decode: argmax per step parity
+  int* step = nullptr;
+  unsigned* bar = nullptr;  // persistent decode: grid barrier words
   std::vector<void*> allocs;
   ~Work() {
     for (void* p : allocs) cudaFree(p);
@@ -625,6 +717,12 @@ static int work_init(tcu_model* m, Work* w, int rows, int seqs, int logits_rows,
   TRY(w->get(&w->sl_ids, 256));
   TRY(w->get(&w->sl_vals, 256));
   TRY(w->get(&w->sl_lse, 1));
+  TRY(w->get(&w->err, 1));
+  TRY(w->get(&w->keys, 2));
+  TRY(w->get(&w->step, 1));
+  TRY(w->get(&w->bar, 2));
+  // The zeroing memsets ran on the legacy stream (see pool_get).
+  CK(cudaDeviceSynchronize());
   return TCU_OK;
 }
 
@@ -634,7 +732,7 @@ static int work_init(tcu_model* m, Work* w, int rows, int seqs, int logits_rows,
 // are accumulated after the stream is synchronised. With profiling off no
 // event is recorded.
 
-enum Stage { ST_EMBED = 0, ST_W1, ST_ATTN, ST_W2, ST_HEAD, ST_PF_GEMM, ST_PF_ATTN, ST_OTHER, ST_COUNT };
+enum Stage { ST_EMBED = 0, ST_W1, ST_ATTN, ST_W2, ST_HEAD, ST_PF_GEMM, ST_PF_ATTN, ST_OTHER, ST_MEGA, ST_COUNT };
 
 struct Prof {
   bool on = false;
@@ -657,12 +755,22 @@ struct Prof {
       stage.push_back(0);
     }
     stage[used] = st;
-    cudaEventRecord(ev[2 * used], s);
+    record(ev[2 * used], s);
   }
   void end(cudaStream_t s) {
     if (!on) return;
-    cudaEventRecord(ev[2 * used + 1], s);
+    record(ev[2 * used + 1], s);
     used++;
+  }
+  // Under stream capture a plain cudaEventRecord only expresses a dependency;
+  // cudaEventRecordExternal makes it an event-record node of the graph.
+  static void record(cudaEvent_t e, cudaStream_t s) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(s, &st);
+    if (st == cudaStreamCaptureStatusActive)
+      cudaEventRecordWithFlags(e, s, cudaEventRecordExternal);
+    else
+      cudaEventRecord(e, s);
   }
   // Call after the stream is synchronised.
   void collect(size_t n) {
@@ -671,6 +779,8 @@ struct Prof {
       if (cudaEventElapsedTime(&t, ev[2 * i], ev[2 * i + 1]) == cudaSuccess) {
         ms[stage[i]] += t;
         launches[stage[i]]++;
+      } else {
+        cudaGetLastError();  // an unreadable pair is skipped, not reported by the next call
       }
     }
   }
@@ -697,7 +807,9 @@ static void launch_gemv_fmt(const tcu_model* m, const GemvArgs& a, cudaStream_t 
   case MM: {                                                                                \
     auto kern = k_gemv<FMT, MM, PRO, EPI>;                                                  \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);     \
+    NOTE("cudaFuncSetAttribute(k_gemv)");                                                   \
     kern<<<blocks, GEMV_THREADS, smem, s>>>(a);                                             \
+    NOTE("k_gemv");                                                                         \
     break;                                                                                  \
   }
     TCU_GEMV_CASE(1)
@@ -706,6 +818,126 @@ static void launch_gemv_fmt(const tcu_model* m, const GemvArgs& a, cudaStream_t 
     TCU_GEMV_CASE(4)
 #undef TCU_GEMV_CASE
   }
+}
+
+// Launch with programmatic stream serialization: the kernel may start while
+// the previous one drains and synchronises with griddepcontrol.wait.
+template <typename Kern, typename Args>
+static void launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t s, const Args& args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, args);
+}
+
+static const size_t GS_SMEM_LIMIT = 227 * 1024;
+
+// Plans the streaming GEMV for W (M == 1): K chunks of at most GS_CHUNK
+// values (for EPI_RESID2 the first chunk ends exactly at k_split), rows per
+// stage and pipeline depth. Returns false when the shape does not fit.
+static bool plan_gemv_stream(const DMat& W, int epi, int k_split, GemvStreamArgs* sa, int* ks_out) {
+  int E;
+  size_t esz;
+  switch (W.fmt) {
+    case FMT_Q8_0: E = 16; esz = 1; break;
+    case FMT_BF16: case FMT_F16: E = 8; esz = 2; break;
+    case FMT_F32: E = 4; esz = 4; break;
+    default: return false;
+  }
+  const int K = W.cols;
+  if (K % E || (W.fmt == FMT_Q8_0 && K % 32)) return false;
+  int ks;
+  if (epi == EPI_RESID2) {
+    if (k_split <= 0 || k_split >= K || k_split % E || k_split > GS_CHUNK) return false;
+    const int rest = K - k_split;
+    int n = (rest + GS_CHUNK - 1) / GS_CHUNK;
+    ks = n + 1 <= 2 ? 2 : 4;
+    if (ks - 1 < n) return false;
+    sa->kc[0] = 0;
+    sa->kc[1] = k_split;
+    const int nv = rest / E;
+    for (int c = 1; c < ks; c++) sa->kc[c + 1] = k_split + (int)((long long)nv * c / (ks - 1)) * E;
+    sa->lo_chunks = 1;
+  } else {
+    const int nv = K / E;
+    ks = K <= GS_CHUNK ? 1 : (K <= 2 * GS_CHUNK ? 2 : 4);
+    if (ks == 4 && K > 4 * GS_CHUNK) return false;
+    for (int c = 0; c <= ks; c++) sa->kc[c] = (int)((long long)nv * c / ks) * E;
+    sa->lo_chunks = ks;
+    if (ks > 1 && epi != EPI_STORE && epi != EPI_RESID1) return false;  // GLU / head need whole rows per warp
+  }
+  for (int c = 0; c < ks; c++)
+    if (sa->kc[c + 1] - sa->kc[c] > GS_CHUNK) return false;
+  const int rs = 2 * (GS_CONSUMERS / ks);
+  const size_t row_bytes = (size_t)K * esz;
+  const size_t sbytes = W.fmt == FMT_Q8_0 ? (size_t)W.sstride * 2 : 0;
+  const uint32_t stage = (uint32_t)(((size_t)rs * (row_bytes + sbytes) + 127) / 128 * 128);
+  const uint32_t off_x = 128;
+  const uint32_t off_part = off_x + (uint32_t)(((size_t)K * 4 + 127) / 128 * 128);
+  const uint32_t off_stage = off_part + (uint32_t)(((size_t)GS_MAX_STAGES * rs * ks * 4 + 127) / 128 * 128);
+  if (off_stage + 2 * (size_t)stage > GS_SMEM_LIMIT) return false;
+  const int nstage = (int)std::min<size_t>(GS_MAX_STAGES, (GS_SMEM_LIMIT - off_stage) / stage);
+  sa->rs = rs;
+  sa->nstage = nstage;
+  sa->stage_bytes = stage;
+  sa->off_x = off_x;
+  sa->off_part = off_part;
+  sa->off_stage = off_stage;
+  *ks_out = ks;
+  return true;
+}
+
+template <int FMT, int PRO, int EPI, int KS>
+static void launch_gemv_stream_k(const tcu_model* m, const GemvStreamArgs& sa, cudaStream_t s) {
+  auto kern = k_gemv_stream<FMT, PRO, EPI, KS>;
+  const size_t smem = sa.off_stage + (size_t)sa.nstage * sa.stage_bytes;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  NOTE("cudaFuncSetAttribute(k_gemv_stream)");
+  const int pairs = (sa.g.W.rows + 1) / 2;
+  const int grid = std::max(1, std::min(m->sm_count, pairs));
+  launch_pdl(kern, dim3(grid), dim3(GS_THREADS), smem, s, sa);
+  NOTE("k_gemv_stream");
+}
+
+template <int FMT, int PRO, int EPI>
+static void launch_gemv_stream_fmt(const tcu_model* m, const GemvStreamArgs& sa, int ks, cudaStream_t s) {
+  if constexpr (EPI == EPI_GLU || EPI == EPI_HEAD) {
+    launch_gemv_stream_k<FMT, PRO, EPI, 1>(m, sa, s);
+  } else {
+    if (ks == 1)
+      launch_gemv_stream_k<FMT, PRO, EPI, 1>(m, sa, s);
+    else if (ks == 2)
+      launch_gemv_stream_k<FMT, PRO, EPI, 2>(m, sa, s);
+    else
+      launch_gemv_stream_k<FMT, PRO, EPI, 4>(m, sa, s);
+  }
+}
+
+// Returns true if the streaming kernel took the launch.
+template <int PRO, int EPI>
+static bool try_gemv_stream(const tcu_model* m, const GemvArgs& a, int* err, cudaStream_t s) {
+  if (a.M != 1 || m->disable_stream) return false;
+  if (EPI == EPI_RESID2 && m->arch != ARCH_STABLELM) return false;
+  GemvStreamArgs sa{};
+  sa.g = a;
+  sa.err = err;
+  int ks = 1;
+  if (!plan_gemv_stream(a.W, EPI, a.k_split, &sa, &ks)) return false;
+  if ((EPI == EPI_GLU || EPI == EPI_HEAD) && ks != 1) return false;
+  switch (a.W.fmt) {
+    case FMT_Q8_0: launch_gemv_stream_fmt<FMT_Q8_0, PRO, EPI>(m, sa, ks, s); return true;
+    case FMT_BF16: launch_gemv_stream_fmt<FMT_BF16, PRO, EPI>(m, sa, ks, s); return true;
+    case FMT_F16: launch_gemv_stream_fmt<FMT_F16, PRO, EPI>(m, sa, ks, s); return true;
+    case FMT_F32: launch_gemv_stream_fmt<FMT_F32, PRO, EPI>(m, sa, ks, s); return true;
+  }
+  return false;
 }
 
 template <int PRO, int EPI>
@@ -720,6 +952,7 @@ static void launch_gemv_generic(const tcu_model* m, const GemvArgs& a, cudaStrea
     auto kern = k_gemv_generic<MM, PRO, EPI>;                                           \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
     kern<<<blocks, GEMV_THREADS, smem, s>>>(a);                                         \
+    NOTE("k_gemv_generic");                                                             \
     break;                                                                              \
   }
     TCU_GEMV_CASE(1)
@@ -749,10 +982,12 @@ static thread_local int g_stage = ST_OTHER;  // stage charged by the next launch
 template <int PRO, int EPI>
 static void launch_gemv_impl(const tcu_model* m, const GemvArgs& a, cudaStream_t s);
 
+static thread_local int* g_err_word = nullptr;  // device error word of the enqueueing call
+
 template <int PRO, int EPI>
 static void launch_gemv(const tcu_model* m, const GemvArgs& a, cudaStream_t s) {
   PROF_BEGIN(g_stage, s);
-  launch_gemv_impl<PRO, EPI>(m, a, s);
+  if (!try_gemv_stream<PRO, EPI>(m, a, g_err_word, s)) launch_gemv_impl<PRO, EPI>(m, a, s);
   PROF_END(s);
 }
 
@@ -778,6 +1013,7 @@ static void launch_gemm(const GemmArgs& a, cudaStream_t s) {
   PROF_BEGIN(g_stage, s);
   dim3 grid((a.W.rows + SG_BN - 1) / SG_BN, (a.n + SG_BM - 1) / SG_BM);
   k_gemm_simt<EPI><<<grid, SG_THREADS, 0, s>>>(a);
+  NOTE("k_gemm_simt");
   PROF_END(s);
 }
 
@@ -785,6 +1021,7 @@ static void launch_norm_rows(const tcu_model* m, const float* in, float* out, in
   PROF_BEGIN(ST_OTHER, s);
   NormRowsArgs a{n, m->d, in, m->d, out, m->d, w, b, m->eps, m->arch == ARCH_LLAMA};
   k_norm_rows<<<n, 256, 0, s>>>(a);
+  NOTE("k_norm_rows");
   PROF_END(s);
 }
 
@@ -815,9 +1052,33 @@ static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M,
   a.out = w->ah;
   a.out_stride = m->d + m->ff;
   a.scale = (float)sqrt((double)m->hd);
-  const size_t smem = attn_decode_smem(m);
-  cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k_attn_decode<<<dim3(grid_splits, m->KVH, M), 128, smem, s>>>(a);
+  const int es = pool->half ? 2 : 4;
+  const int G = m->H / m->KVH;
+  const size_t bulk_smem =
+      128 + 2 * (size_t)a.split * m->hd * es + sizeof(float) * ((size_t)G * m->hd + (size_t)G * a.split + 2 * m->hd);
+  if (!m->disable_stream && ((size_t)m->P * m->hd * es) % 16 == 0 && bulk_smem <= GS_SMEM_LIMIT && G <= 32) {
+    DecodeAttn2Extra x{w->err};
+    cudaFuncSetAttribute(k_attn_decode_bulk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bulk_smem);
+    NOTE("cudaFuncSetAttribute(k_attn_decode_bulk)");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid_splits, m->KVH, M);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = bulk_smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, k_attn_decode_bulk, a, x);
+    NOTE("k_attn_decode_bulk");
+  } else {
+    const size_t smem = attn_decode_smem(m);
+    cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    NOTE("cudaFuncSetAttribute(k_attn_decode)");
+    k_attn_decode<<<dim3(grid_splits, m->KVH, M), 128, smem, s>>>(a);
+    NOTE("k_attn_decode");
+  }
   PROF_END(s);
 }
 
@@ -840,6 +1101,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
   ea.x_stride = d;
   PROF_BEGIN(ST_EMBED, s);
   k_embed<<<M, 256, 0, s>>>(ea);
+  NOTE("k_embed");
   PROF_END(s);
   const bool gemv = M <= GEMV_MAX_M;
   for (int l = 0; l < m->L; l++) {
@@ -1014,6 +1276,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
     launch_gemm<EPI_STORE>(g, s);
     PROF_BEGIN(ST_HEAD, s);
     k_argmax_rows<<<M, 256, 0, s>>>(w->logits, m->V, m->V, w->argmax);
+    NOTE("k_argmax_rows");
     PROF_END(s);
   }
 }
@@ -1030,6 +1293,7 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
   ea.x_stride = d;
   PROF_BEGIN(ST_EMBED, s);
   k_embed<<<n, 256, 0, s>>>(ea);
+  NOTE("k_embed");
   PROF_END(s);
   g_stage = ST_PF_GEMM;
   for (int l = 0; l < m->L; l++) {
@@ -1065,6 +1329,7 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
     r.page_table = w->pt;
     PROF_BEGIN(ST_OTHER, s);
     k_rope_store<<<n, 128, 0, s>>>(r);
+    NOTE("k_rope_store");
     PROF_END(s);
     PrefillAttnArgs pa{};
     pa.n = n;
@@ -1082,8 +1347,10 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
     pa.scale = (float)sqrt((double)m->hd);
     const size_t smem = sizeof(float) * ((size_t)PA_QT * (m->hd + 1) + 2 * (size_t)PA_KT * (m->hd + 1) + (size_t)PA_QT * PA_KT);
     cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    NOTE("cudaFuncSetAttribute(k_attn_prefill)");
     PROF_BEGIN(ST_PF_ATTN, s);
     k_attn_prefill<<<dim3((n + PA_QT - 1) / PA_QT, m->H), 128, smem, s>>>(pa);
+    NOTE("k_attn_prefill");
     PROF_END(s);
     if (m->arch == ARCH_STABLELM) {
       GemmArgs g2{};
@@ -1130,6 +1397,7 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
 // Head over the last row of a prefill chunk (prefill.go:103-109).
 static void enqueue_head_row(const tcu_model* m, Work* w, int row, float* logits, cudaStream_t s) {
   cudaMemsetAsync(w->argmax, 0, sizeof(unsigned long long), s);
+  NOTE("cudaMemsetAsync(w->argmax, 0, sizeof(uns");
   g_stage = ST_HEAD;
   GemvArgs a{};
   a.W = m->head;
@@ -1170,10 +1438,17 @@ struct tcu_session {
   Prof prof;
 };
 
-// Routes the launch helpers' stage events to a profiled session while a call runs.
+// Routes the launch helpers' stage events (when profiling) and bounded-wait
+// error word to the session whose call is enqueueing work.
 struct ProfScope {
-  explicit ProfScope(tcu_session* s) { g_prof = (s && s->prof.on) ? &s->prof : nullptr; }
-  ~ProfScope() { g_prof = nullptr; }
+  explicit ProfScope(tcu_session* s, int* err = nullptr) {
+    g_prof = (s && s->prof.on) ? &s->prof : nullptr;
+    g_err_word = err ? err : (s ? s->w.err : nullptr);
+  }
+  ~ProfScope() {
+    g_prof = nullptr;
+    g_err_word = nullptr;
+  }
 };
 
 // Accumulates recorded stage events (the stream must be synchronised).
@@ -1214,6 +1489,7 @@ static int prepare_pages(tcu_model* m, KVPool* pool, std::vector<int>& pages, in
       TRY(page_alloc(m, pool, &pg));
       const size_t page_vec = pool->page_elems() * pool->elem() / 16;
       k_copy_page<<<592, 256, 0, s>>>((uint4*)pool->k, (uint4*)pool->v, page_vec, pool->num_pages, pages[i], pg, pool->L);
+      NOTE("k_copy_page");
       CK(cudaGetLastError());
       page_unref(m, pool, pages[i]);
       pages[i] = pg;
@@ -1222,13 +1498,23 @@ static int prepare_pages(tcu_model* m, KVPool* pool, std::vector<int>& pages, in
   return TCU_OK;
 }
 
-static int session_sync(tcu_session* s) {
-  cudaError_t e = cudaStreamSynchronize(s->stream);
-  if (e != cudaSuccess) return fail(TCU_ECUDA, "device execution failed: %s", cudaGetErrorString(e));
+static int sync_stream(cudaStream_t stream, int* err_word) {
+  cudaError_t e = cudaStreamSynchronize(stream);
+  const char* site = g_err_site ? g_err_site : "?";
+  g_err_site = nullptr;
+  if (e != cudaSuccess) return fail(TCU_ECUDA, "device execution failed: %s (first failing launch: %s)", cudaGetErrorString(e), site);
   e = cudaGetLastError();
-  if (e != cudaSuccess) return fail(TCU_ECUDA, "launch failed: %s", cudaGetErrorString(e));
+  if (e != cudaSuccess) return fail(TCU_ECUDA, "launch failed: %s (at %s)", cudaGetErrorString(e), site);
+  int flag = 0;
+  if (cudaMemcpy(&flag, err_word, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && flag != 0) {
+    const int zero = 0;
+    cudaMemcpy(err_word, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    return fail(TCU_ETIMEOUT, "a bounded device wait expired (error word %d); results of this call are invalid", flag);
+  }
   return TCU_OK;
 }
+
+static int session_sync(tcu_session* s) { return sync_stream(s->stream, s->w.err); }
 
 static int upload_pt(tcu_session* s) {
   CK(cudaMemcpyAsync(s->w.pt, s->pages.data(), s->pages.size() * sizeof(int), cudaMemcpyHostToDevice, s->stream));
@@ -1473,6 +1759,73 @@ int tcu_session_forward_all(tcu_session* s, int32_t prefix, const int32_t* token
   return session_finish(s, rc, prefix + n);
 }
 
+// Launches one persistent decode step (decode_mega.cuh) as a cooperative
+// grid of one CTA per SM.
+static int launch_mega(tcu_session* s) {
+  tcu_model* m = s->m;
+  MegaArgs a{};
+  a.L = m->L;
+  a.d = m->d;
+  a.ff = m->ff;
+  a.V = m->V;
+  a.H = m->H;
+  a.KVH = m->KVH;
+  a.hd = m->hd;
+  a.s1_stride = m->layers[0].w1.sstride;
+  a.s2_stride = m->layers[0].w2.sstride;
+  a.sh_stride = m->head.sstride;
+  a.se_stride = m->embed.sstride;
+  a.eps = m->eps;
+  a.layers = m->mega_layers;
+  a.head_w = (const int8_t*)m->head.w;
+  a.head_s = m->head.s;
+  a.emb_w = (const int8_t*)m->embed.w;
+  a.emb_s = m->embed.s;
+  a.fnw = m->fnw;
+  a.fnb = m->fnb;
+  a.rope = m->rope;
+  a.kv = s->pool->view();
+  a.page_table = s->w.pt;
+  a.split = m->mega_split;
+  a.max_splits = s->w.max_splits;
+  a.scale = (float)sqrt((double)m->hd);
+  a.pos = s->w.pos;
+  a.keys = s->w.keys;
+  a.step = s->w.step;
+  a.out_tokens = s->w.out_tokens;
+  a.out_count = s->w.out_count;
+  a.logits = s->w.logits;
+  a.x_buf = s->w.x;
+  a.qkv = s->w.qkv;
+  a.ah = s->w.ah;
+  a.part = s->w.part;
+  a.counters = s->w.counters;
+  a.bar = s->w.bar;
+  a.err = s->w.err;
+  a.slot_bytes = m->mega_slot_bytes;
+  a.nslots = m->mega_slots;
+  a.off_x = m->mega_off[0];
+  a.off_dig = m->mega_off[1];
+  a.off_sx = m->mega_off[2];
+  a.off_part = m->mega_off[3];
+  a.off_slots = m->mega_off[4];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(m->sm_count);
+  cfg.blockDim = dim3(MG_THREADS);
+  cfg.dynamicSmemBytes = m->mega_smem;
+  cfg.stream = s->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PROF_BEGIN(ST_MEGA, s->stream);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_decode_mega, a);
+  PROF_END(s->stream);
+  if (e != cudaSuccess) return fail(TCU_ECUDA, "persistent decode launch: %s", cudaGetErrorString(e));
+  return TCU_OK;
+}
+
 int tcu_session_generate_greedy(tcu_session* s, int32_t prefix, const int32_t* tokens, int32_t n, int32_t steps, int32_t* out_tokens) {
   TRY(validate_forward(s, prefix, tokens, n));
   if (steps < 1 || !out_tokens) return fail(TCU_EINVAL, "invalid steps or output buffer");
@@ -1488,10 +1841,35 @@ int tcu_session_generate_greedy(tcu_session* s, int32_t prefix, const int32_t* t
   const int end = prefix + n + steps - 1;  // resident positions afterwards
   if (rc == TCU_OK) rc = prepare_pages(m, s->pool, s->pages, prefix + n, end, s->stream);
   if (rc == TCU_OK) rc = upload_pt(s);
+  if (rc == TCU_OK && m->mega && steps > 1) {
+    // Persistent decode: one cooperative launch per generated token.
+    const int first = prefix + n;
+    CK(cudaMemcpyAsync(s->w.pos, &first, sizeof(int), cudaMemcpyHostToDevice, s->stream));
+    CK(cudaMemcpyAsync(s->w.keys, s->w.argmax, sizeof(unsigned long long), cudaMemcpyDeviceToDevice, s->stream));
+    CK(cudaMemsetAsync(s->w.keys + 1, 0, sizeof(unsigned long long), s->stream));
+    CK(cudaMemsetAsync(s->w.step, 0, sizeof(int), s->stream));
+    CK(cudaMemsetAsync(s->w.out_count, 0, sizeof(int), s->stream));
+    for (int i = 1; rc == TCU_OK && i < steps; i++) {
+      rc = launch_mega(s);
+      if (rc == TCU_OK && s->prof.on) {
+        rc = session_sync(s);
+        prof_collect(s);
+      }
+    }
+    if (rc == TCU_OK) {
+      k_finish_mega<<<1, 32, 0, s->stream>>>(s->w.keys, s->w.step, s->w.out_tokens, s->w.out_count);
+      NOTE("k_finish_mega");
+      cudaError_t e = cudaMemcpyAsync(out_tokens, s->w.out_tokens, (size_t)steps * sizeof(int), cudaMemcpyDeviceToHost, s->stream);
+      if (e != cudaSuccess) rc = fail(TCU_ECUDA, "token copy: %s", cudaGetErrorString(e));
+    }
+    return session_finish(s, rc, end);
+  }
   if (rc == TCU_OK) {
     const int last = prefix + n - 1;
     cudaMemcpyAsync(s->w.pos, &last, sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    NOTE("cudaMemcpyAsync(s->w.pos, &last, sizeof(");
     cudaMemsetAsync(s->w.out_count, 0, sizeof(int), s->stream);
+    NOTE("cudaMemsetAsync(s->w.out_count, 0, sizeo");
     const int split = SPLIT_PAGES * m->P;
     int splits = (end + split - 1) / split;
     int bucket = 1;
@@ -1509,6 +1887,7 @@ int tcu_session_generate_greedy(tcu_session* s, int32_t prefix, const int32_t* t
     }
     if (rc == TCU_OK) {
       k_finish_greedy<<<1, 32, 0, s->stream>>>(s->w.argmax, s->w.out_tokens, s->w.out_cap, s->w.out_count, 1);
+      NOTE("k_finish_greedy");
       cudaError_t e = cudaMemcpyAsync(out_tokens, s->w.out_tokens, (size_t)steps * sizeof(int), cudaMemcpyDeviceToHost, s->stream);
       if (e != cudaSuccess) rc = fail(TCU_ECUDA, "token copy: %s", cudaGetErrorString(e));
     }
@@ -1525,7 +1904,9 @@ int tcu_session_shortlist(tcu_session* s, int32_t k, int32_t* ids, float* logits
   const int kk = std::min<int>(k, s->m->V);
   const size_t smem = ((size_t)s->m->V + 31) / 32 * 4;
   cudaFuncSetAttribute(k_shortlist, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  NOTE("cudaFuncSetAttribute(k_shortlist)");
   k_shortlist<<<1, 1024, smem, s->stream>>>(s->w.logits, s->m->V, kk, s->w.sl_ids, s->w.sl_vals, s->w.sl_lse);
+  NOTE("k_shortlist");
   CK(cudaGetLastError());
   CK(cudaMemcpyAsync(ids, s->w.sl_ids, kk * sizeof(int), cudaMemcpyDeviceToHost, s->stream));
   CK(cudaMemcpyAsync(logits, s->w.sl_vals, kk * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
@@ -1668,7 +2049,7 @@ int tcu_branches_forward(tcu_branches* b, const int32_t* tokens, float* rows_out
   if (b->prefix + b->step >= m->max_pos) return fail(TCU_EINVAL, "invalid branch batch or context length");
   TRY(check_tokens(m, tokens, b->count));
   CK(cudaSetDevice(m->device));
-  ProfScope ps(s);
+  ProfScope ps(s, b->w.err);
   const int pos = b->prefix + b->step;
   int rc = TCU_OK;
   std::vector<int> pt((size_t)b->count * b->w.pt_stride, 0);
@@ -1679,9 +2060,13 @@ int tcu_branches_forward(tcu_branches* b, const int32_t* tokens, float* rows_out
   if (rc == TCU_OK) {
     std::vector<int> posv(b->count, pos);
     cudaMemcpyAsync(b->w.pt, pt.data(), pt.size() * sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    NOTE("cudaMemcpyAsync(b->w.pt, pt.data(), pt.s");
     cudaMemcpyAsync(b->w.pos, posv.data(), b->count * sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    NOTE("cudaMemcpyAsync(b->w.pos, posv.data(), b");
     cudaMemcpyAsync(b->w.tokens, tokens, b->count * sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    NOTE("cudaMemcpyAsync(b->w.tokens, tokens, b->");
     cudaMemsetAsync(b->w.argmax, 0, b->count * sizeof(unsigned long long), s->stream);
+    NOTE("cudaMemsetAsync(b->w.argmax, 0, b->count");
     const int split = SPLIT_PAGES * m->P;
     enqueue_decode(m, s->pool, &b->w, b->count, false, (pos + 1 + split - 1) / split, true, s->stream);
     cudaError_t e = cudaGetLastError();
@@ -1691,7 +2076,7 @@ int tcu_branches_forward(tcu_branches* b, const int32_t* tokens, float* rows_out
       if (e != cudaSuccess) rc = fail(TCU_ECUDA, "rows copy: %s", cudaGetErrorString(e));
     }
   }
-  if (rc == TCU_OK) rc = session_sync(s);
+  if (rc == TCU_OK) rc = sync_stream(s->stream, b->w.err);
   if (rc == TCU_OK) prof_collect(s);
   s->prof.used = 0;
   if (rc != TCU_OK) {
