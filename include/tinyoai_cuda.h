@@ -185,6 +185,34 @@ int tcu_branches_argmax(tcu_branches* branches, int32_t* ids);
  * tcu_branches_forward already released the pages; close it all the same. */
 int tcu_branches_close(tcu_branches* branches);
 
+/* Sampling shortlist over a logits row the caller already holds in device
+ * memory, allocating no device memory. This entry point has no counterpart in
+ * the reference (its Go path keeps logits on the host); it serves callers that
+ * must not allocate on the device when they call, for example a host whose
+ * own caching allocator already holds the free HBM.
+ *
+ * Same kernel and results as tcu_session_shortlist: up to k (id, logit)
+ * pairs, descending, ties by lower id (sampling.go:112-143), plus the float64
+ * log-sum-exp of the whole row (logprobs.go:64-95). logits: `vocab` floats on
+ * `device`; stream: a CUDA stream of that device, or NULL for the legacy
+ * default stream. The call makes `device` current, returns after the stream
+ * has synchronised, and writes *n_out = min(k, vocab) entries to the host
+ * arrays ids and values.
+ *
+ * The kernel's results pass through one fixed device array of
+ * TCU_SHORTLIST_STATIC_SCRATCH_BYTES per device, so k is limited to
+ * TCU_SHORTLIST_STATIC_MAX_K. vocab is limited to
+ * TCU_SHORTLIST_STATIC_MAX_VOCAB (the kernel marks taken ids in shared memory).
+ * Larger values fail with TCU_EINVAL. The first call on a device does the set-up
+ * (it looks up that array's device address); make it before any stream capture.
+ * Calls on one device share the array: two calls in flight at the same time on
+ * one device, from different host threads, overwrite each other's results. */
+#define TCU_SHORTLIST_STATIC_MAX_K 256
+#define TCU_SHORTLIST_STATIC_MAX_VOCAB 1048576
+#define TCU_SHORTLIST_STATIC_SCRATCH_BYTES 4096
+int tcu_shortlist_static(int32_t device, const float* logits, int32_t vocab, int32_t k, void* stream, int32_t* ids,
+                         float* values, double* logsumexp, int32_t* n_out);
+
 #ifdef __cplusplus
 }
 #endif

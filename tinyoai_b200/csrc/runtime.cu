@@ -2109,3 +2109,93 @@ int tcu_branches_close(tcu_branches* b) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Shortlist with no device allocation (tcu_shortlist_static). No counterpart
+// in the reference.
+//
+// Some callers must not allocate device memory when they call: a host whose
+// own caching allocator already reserved the free HBM (a cudaMalloc then fails
+// or fragments that pool), or a caller on a latency budget, for which
+// cudaMalloc's cost and cudaFree's device-wide synchronisation are too much.
+// This path runs the unchanged k_shortlist kernel over a logits row the
+// caller already holds on the device. Session workspace is not used: the
+// kernel's results go to one fixed file-scope device array.
+//
+// Scratch layout (TCU_SHORTLIST_STATIC_SCRATCH_BYTES):
+//   [0, 1024)     int32  ids[TCU_SHORTLIST_STATIC_MAX_K]
+//   [1024, 2048)  float  values[TCU_SHORTLIST_STATIC_MAX_K]
+//   [2048, 2056)  double logsumexp
+// The kernel writes every word the host then reads back (ids and values
+// 0..n-1, the log-sum-exp), so nothing has to start at zero and nothing is
+// cleared. The array keeps the last call's results. Calls on one device share
+// it, so two calls in flight at the same time on one device overwrite each
+// other's results.
+
+static_assert(TCU_SHORTLIST_STATIC_MAX_K * 8 + 8 <= TCU_SHORTLIST_STATIC_SCRATCH_BYTES, "shortlist scratch too small");
+static_assert(((size_t)TCU_SHORTLIST_STATIC_MAX_VOCAB + 31) / 32 * 4 <= 200 * 1024, "taken bitmap exceeds shared memory");
+
+static __device__ __align__(256) unsigned char g_shortlist_scratch[TCU_SHORTLIST_STATIC_SCRATCH_BYTES];
+
+static const int SL_STATIC_MAX_DEVICES = 64;
+static std::mutex g_sl_static_mu;
+static unsigned char* g_sl_static_ptr[SL_STATIC_MAX_DEVICES] = {};
+
+// Once per device, with that device current: checks the architecture and
+// looks up the device address of g_shortlist_scratch.
+static int shortlist_static_setup(int device, unsigned char** out) {
+  std::lock_guard<std::mutex> g(g_sl_static_mu);
+  if (!g_sl_static_ptr[device]) {
+    int major = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    if (e != cudaSuccess) return fail(TCU_ECUDA, "shortlist set-up on device %d: %s", device, cudaGetErrorString(e));
+    if (major != 10) return fail(TCU_ENODEV, "device %d is not sm_100; this library is built for sm_100a", device);
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_shortlist_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(TCU_ECUDA, "shortlist set-up on device %d: cudaGetSymbolAddress: %s", device, cudaGetErrorString(e));
+    g_sl_static_ptr[device] = (unsigned char*)p;
+  }
+  *out = g_sl_static_ptr[device];
+  return TCU_OK;
+}
+
+extern "C" int tcu_shortlist_static(int32_t device, const float* logits, int32_t vocab, int32_t k, void* stream, int32_t* ids,
+                                    float* values, double* logsumexp, int32_t* n_out) {
+  if (!logits || !ids || !values || !logsumexp || !n_out) return fail(TCU_EINVAL, "null argument");
+  if (k < 1 || k > TCU_SHORTLIST_STATIC_MAX_K)
+    return fail(TCU_EINVAL, "shortlist size %d is outside [1, %d], the capacity of the static scratch", k, TCU_SHORTLIST_STATIC_MAX_K);
+  if (vocab < 1 || vocab > TCU_SHORTLIST_STATIC_MAX_VOCAB)
+    return fail(TCU_EINVAL, "vocabulary of %d is outside [1, %d], the largest the static shortlist handles", vocab,
+                TCU_SHORTLIST_STATIC_MAX_VOCAB);
+  if ((reinterpret_cast<uintptr_t>(logits) & 3) != 0) return fail(TCU_EINVAL, "logits pointer is not 4-byte aligned");
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return fail(TCU_ENODEV, "no CUDA device available");
+  }
+  if (device < 0 || device >= n || device >= SL_STATIC_MAX_DEVICES)
+    return fail(TCU_ENODEV, "device %d out of range (%d devices)", device, n);
+  CK(cudaSetDevice(device));
+  cudaPointerAttributes pa;
+  CK(cudaPointerGetAttributes(&pa, logits));
+  if ((pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged) || pa.device != device)
+    return fail(TCU_EINVAL, "logits must be device memory on device %d", device);
+  unsigned char* scratch = nullptr;
+  TRY(shortlist_static_setup(device, &scratch));
+  int32_t* d_ids = reinterpret_cast<int32_t*>(scratch);
+  float* d_vals = reinterpret_cast<float*>(scratch + TCU_SHORTLIST_STATIC_MAX_K * 4);
+  double* d_lse = reinterpret_cast<double*>(scratch + TCU_SHORTLIST_STATIC_MAX_K * 8);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int kk = std::min<int>(k, vocab);
+  const size_t smem = ((size_t)vocab + 31) / 32 * 4;
+  CK(cudaFuncSetAttribute(k_shortlist, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k_shortlist<<<1, 1024, smem, st>>>(logits, vocab, kk, d_ids, d_vals, d_lse);
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(ids, d_ids, kk * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(values, d_vals, kk * sizeof(float), cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(logsumexp, d_lse, sizeof(double), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  *n_out = kk;
+  return TCU_OK;
+}
