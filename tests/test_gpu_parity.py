@@ -346,9 +346,25 @@ def test_stage_profile(small):
         L = cfg["num_hidden_layers"]
         assert prof["prefill_projection"][0] == 2 * L
         assert prof["prefill_attention"][0] == L
-        assert prof["norm_qkv_gate_up"][0] == 5 * L  # five decode forwards (steps - 1)
-        assert prof["attention"][0] == 5 * L and prof["out_down_residual"][0] == 5 * L
-        assert prof["head"][0] == 6  # prefill head + five decode heads
-        assert all(ms >= 0 for _, ms in prof.values()) and prof["norm_qkv_gate_up"][1] > 0
+        if prof["decode_step"][0]:
+            # Persistent decode: one launch per decoded token (steps - 1),
+            # with layers and head inside it.
+            assert prof["decode_step"][0] == 5 and prof["decode_step"][1] > 0
+            assert prof["norm_qkv_gate_up"][0] == 0 and prof["attention"][0] == 0
+            assert prof["head"][0] == 1  # the prefill's head
+        else:
+            assert prof["norm_qkv_gate_up"][0] == 5 * L  # five decode forwards (steps - 1)
+            assert prof["attention"][0] == 5 * L and prof["out_down_residual"][0] == 5 * L
+            assert prof["head"][0] == 6  # prefill head + five decode heads
+        assert all(ms >= 0 for _, ms in prof.values())
+
+        # A single-token forward takes the per-layer kernels.
+        s.profile(True)
+        s.forward(len(ids) + 4, [int(got[-1])])
+        prof = s.profile_read(reset=True)
+        s.profile(False)
+        assert prof["norm_qkv_gate_up"][0] == L and prof["attention"][0] == L
+        assert prof["out_down_residual"][0] == L and prof["head"][0] == 1
+        assert prof["norm_qkv_gate_up"][1] > 0 and prof["decode_step"][0] == 0
     finally:
         s.close()

@@ -12,13 +12,18 @@
 // the producer keeps prefetching through it.
 //
 // Matrix-vector products use exact integer dot products (dp4a): the input
-// vector is quantised per 32-value block to 24-bit fixed point relative to the
+// vector is quantised per 16-value block to 24-bit fixed point relative to the
 // block's largest magnitude (absolute error at most half an ulp of that
 // value) and split into three byte digits, so every block sum of int8 weight
 // x digit is exact in int32; the digit sums are recombined in float32 and
-// scaled by the weight block scale (dot.go:31-40 computes the same block
-// sums in float64). LayerNorm, RoPE, attention and the parallel residual
-// follow the reference arithmetic as the separate kernels do.
+// scaled by the weight and input block scales (dot.go:31-40 computes the
+// weight-block sums in float64). LayerNorm, RoPE, attention and the parallel
+// residual follow the reference arithmetic as the separate kernels do.
+//
+// The input of the out/down rows ([attention | SwiGLU]) is quantised once,
+// by the CTA that produces each block (the attention merge, the SwiGLU rows),
+// and published as digits; every CTA then copies the digits in with one bulk
+// copy instead of quantising the whole vector itself.
 #pragma once
 #include "attention.cuh"
 #include "common.cuh"
@@ -72,7 +77,11 @@ struct MegaArgs {
   // scratch
   float* x_buf;  // [d]
   float* qkv;    // [d + 2 kvw]
-  float* ah;     // [d + ff]
+  float* ah;     // [d + ff] (SwiGLU part used)
+  uint32_t* adig;  // [(d + ff) / 16][12] digits of [attention | SwiGLU]
+  float* asx;      // [(d + ff) / 16] their block scales
+  int* bcnt;       // [ff / 16] SwiGLU block arrivals (zero between steps)
+  uint32_t dig_bytes, sx_bytes;  // phase C staging sizes (multiples of 16)
   float* part;   // [H][max_splits][hd+2]
   int* counters;  // [KVH]
   unsigned* bar;  // [2]: arrival count, generation
@@ -142,48 +151,52 @@ __device__ void mg_grid_sync(const MegaArgs& a) {
 // (two passes), float32 affine, then warp-per-block digits.
 __device__ void mg_ln_digits(const float* xs, int K, const float* nw, const float* nb, double eps, uint32_t* dig, float* sx);
 
-// Quantises one 32-value block held one value per lane: scale = max|x| /
-// (2^23 - 1) and three digit words per 4 values (low byte, middle byte,
-// signed high byte of round(x / scale)); lanes 4q write word q.
-__device__ __forceinline__ void mg_quant_block(float x, int b, uint32_t* dig, float* sx) {
-  const int lane = threadIdx.x & 31;
-  float mx = fabsf(x);
+// One thread quantises the 16 values v into 12 digit words (word 3q + k holds
+// digit k of values 4q..4q+3) and the block scale.
+__device__ __forceinline__ void mg_quant16(const float (&v)[16], uint32_t* dig12, float* sc) {
+  float mx = 0.f;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  for (int i = 0; i < 16; i++) mx = fmaxf(mx, fabsf(v[i]));
   const float inv = mx > 0.f ? __fdiv_rn(8388607.f, mx) : 0.f;
-  int xi = __float2int_rn(x * inv);
-  xi = max(-8388607, min(8388607, xi));
-  const uint32_t u = (uint32_t)xi & 0xFFFFFFu;
-  const uint32_t u1 = __shfl_down_sync(0xffffffffu, u, 1);
-  const uint32_t u2 = __shfl_down_sync(0xffffffffu, u, 2);
-  const uint32_t u3 = __shfl_down_sync(0xffffffffu, u, 3);
-  if ((lane & 3) == 0) {
-    const int q = lane >> 2;
-    uint32_t* w = dig + (b * 8 + q) * 3;
-    w[0] = (u & 0xFF) | (u1 & 0xFF) << 8 | (u2 & 0xFF) << 16 | (u3 & 0xFF) << 24;
-    w[1] = ((u >> 8) & 0xFF) | ((u1 >> 8) & 0xFF) << 8 | ((u2 >> 8) & 0xFF) << 16 | ((u3 >> 8) & 0xFF) << 24;
-    w[2] = (u >> 16) | (u1 >> 16) << 8 | (u2 >> 16) << 16 | (u3 >> 16) << 24;
+  uint32_t w[12];
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    uint32_t b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      int xi = __float2int_rn(v[4 * q + k] * inv);
+      xi = max(-8388607, min(8388607, xi));
+      const uint32_t u = (uint32_t)xi & 0xFFFFFFu;
+      b0 |= (u & 0xFFu) << (8 * k);
+      b1 |= ((u >> 8) & 0xFFu) << (8 * k);
+      b2 |= (u >> 16) << (8 * k);
+    }
+    w[3 * q] = b0;
+    w[3 * q + 1] = b1;
+    w[3 * q + 2] = b2;
   }
-  if (lane == 0) sx[b] = mx > 0.f ? __fdiv_rn(mx, 8388607.f) : 0.f;
-}
-
-// Digits of xs[0..K) (K a multiple of 32): warp w quantises blocks w, w+8, ...
-__device__ void mg_digits(const float* xs, int K, uint32_t* dig, float* sx) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int b = warp; b < K / 32; b += MG_CW) mg_quant_block(xs[b * 32 + lane], b, dig, sx);
-  named_bar_sync(1, MG_CT);
-}
-
-// Digits straight from global memory (phase C input), same layout.
-__device__ void mg_digits_global(const float* src, int K, uint32_t* dig, float* sx) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int b = warp; b < K / 32; b += MG_CW) mg_quant_block(__ldcg(src + b * 32 + lane), b, dig, sx);
-  named_bar_sync(1, MG_CT);
+  uint4* o = reinterpret_cast<uint4*>(dig12);
+  o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  o[2] = make_uint4(w[8], w[9], w[10], w[11]);
+  *sc = mx > 0.f ? __fdiv_rn(mx, 8388607.f) : 0.f;
 }
 
 __device__ void mg_ln_digits(const float* xs, int K, const float* nw, const float* nb, double eps, uint32_t* dig, float* sx) {
   __shared__ double red[2][MG_CW];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // Thread t normalises and quantises block t (K / 16 <= MG_CT); its weight
+  // and bias are fetched before the reductions.
+  const int b = threadIdx.x;
+  const bool has_blk = b < K / 16;
+  float4 wv[4], bv[4];
+  if (has_blk) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      wv[q] = __ldg(reinterpret_cast<const float4*>(nw + 16 * b) + q);
+      bv[q] = __ldg(reinterpret_cast<const float4*>(nb + 16 * b) + q);
+    }
+  }
   double s = 0;
   for (int i = threadIdx.x; i < K; i += MG_CT) s += (double)xs[i];
   s = warp_sum_d(s);
@@ -206,10 +219,21 @@ __device__ void mg_ln_digits(const float* xs, int K, const float* nw, const floa
   for (int w = 0; w < MG_CW; w++) var += red[1][w];
   const float inv = (float)(1.0 / sqrt(var / (double)K + eps));
   const float mf = (float)mean;
-  for (int b = warp; b < K / 32; b += MG_CW) {
-    const int i = b * 32 + lane;
-    const float y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xs[i], mf), inv), nw[i]), nb[i]);
-    mg_quant_block(y, b, dig, sx);
+  if (has_blk) {
+    float v[16];
+    const float* wf = reinterpret_cast<const float*>(wv);
+    const float* bf = reinterpret_cast<const float*>(bv);
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const float4 x4 = reinterpret_cast<const float4*>(xs + 16 * b)[q];
+      const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int i = 4 * q + k;
+        v[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[k], mf), inv), wf[i]), bf[i]);
+      }
+    }
+    mg_quant16(v, dig + 12 * b, sx + b);
   }
   named_bar_sync(1, MG_CT);
 }
@@ -391,9 +415,17 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
 #pragma unroll
     for (int j = 0; j < MG_NJ; j++) {
       const int v = vb + lane + 32 * j;
-#pragma unroll
-      for (int t = 0; t < 12; t++) dr[j][t] = v < ve ? dig[v * 12 + t] : 0u;
-      sxr[j] = v < ve ? sx[v >> 1] : 0.f;
+      uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0, q2 = q0;
+      if (v < ve) {
+        const uint4* p = reinterpret_cast<const uint4*>(dig + v * 12);
+        q0 = p[0];
+        q1 = p[1];
+        q2 = p[2];
+      }
+      dr[j][0] = q0.x, dr[j][1] = q0.y, dr[j][2] = q0.z, dr[j][3] = q0.w;
+      dr[j][4] = q1.x, dr[j][5] = q1.y, dr[j][6] = q1.z, dr[j][7] = q1.w;
+      dr[j][8] = q2.x, dr[j][9] = q2.y, dr[j][10] = q2.z, dr[j][11] = q2.w;
+      sxr[j] = v < ve ? sx[v] : 0.f;
     }
   };
 
@@ -432,6 +464,29 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
           if (2 * warp + 1 < nr) a.qkv[r + 1] = acc[1];
         } else {
           a.ah[d + ((r - n_plain) >> 1)] = silu_mul_stablelm(acc[0], acc[1]);
+        }
+      }
+    }
+    // Digits of this CTA's SwiGLU outputs j in [j0, j1): a 16-value block is
+    // quantised by whichever CTA completes it (blocks at the edge of a CTA's
+    // rows are shared with its neighbour).
+    {
+      const int j0 = max(0, rb1 - n_plain) >> 1, j1 = max(0, re1 - n_plain) >> 1;
+      if (j1 > j0) {
+        __threadfence();
+        named_bar_sync(1, MG_CT);
+        for (int b = j0 / 16 + threadIdx.x; b < (j1 + 15) / 16; b += MG_CT) {
+          const int cnt = min(j1, 16 * b + 16) - max(j0, 16 * b);
+          bool last = cnt == 16;
+          if (!last) last = atomicAdd(a.bcnt + b, cnt) + cnt == 16;
+          if (last) {
+            __threadfence();
+            if (cnt != 16) a.bcnt[b] = 0;
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) v[i] = __ldcg(a.ah + d + 16 * b + i);
+            mg_quant16(v, a.adig + (size_t)(d / 16 + b) * 12, a.asx + d / 16 + b);
+          }
         }
       }
     }
@@ -535,6 +590,8 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
         named_bar_sync(1, MG_CT);
         if (is_last) {
           __threadfence();
+          // Merged head outputs go to qs (no longer read), then their digits
+          // to adig: G_q * hd is a multiple of 16.
           for (int e = threadIdx.x; e < G_q * hd; e += MG_CT) {
             const int hh = e / hd, i = e % hd;
             const float* ph = pg + (size_t)hh * a.max_splits * (hd + 2);
@@ -547,7 +604,15 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
               lsum = fmaf(__ldcg(pj + hd + 1), w, lsum);
               o = fmaf(__ldcg(pj + i), w, o);
             }
-            a.ah[(g * G_q + hh) * hd + i] = __fdiv_rn(o, lsum);
+            qs[e] = __fdiv_rn(o, lsum);
+          }
+          named_bar_sync(1, MG_CT);
+          const int nb16 = G_q * hd / 16;
+          for (int b = threadIdx.x; b < nb16; b += MG_CT) {
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) v[i] = qs[16 * b + i];
+            mg_quant16(v, a.adig + (size_t)(g * nb16 + b) * 12, a.asx + g * nb16 + b);
           }
           if (threadIdx.x == 0) a.counters[g] = 0;
         }
@@ -558,8 +623,16 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
 
     // Phase C: out/down rows over [attention | SwiGLU], parallel residual
     // (stablelm.go:365-377). K chunks: [0, d) then down split in three.
-    stage_in(a.ah, K2);
-    mg_digits(xs, K2, dig, sx);
+    // The digits of [attention | SwiGLU] were published by their producers.
+    fence_proxy_async();
+    named_bar_sync(1, MG_CT);
+    if (threadIdx.x == 0) {
+      mbar_expect_tx(inbar, a.dig_bytes + a.sx_bytes);
+      bulk_g2s(dig, a.adig, a.dig_bytes, inbar);
+      bulk_g2s(sx, a.asx, a.sx_bytes, inbar);
+    }
+    mbar_wait(inbar, in_phase & 1, a.err);
+    in_phase++;
     {
       const int chunk = warp & 3, sub = warp >> 2;
       const int nvd = ff / 16;

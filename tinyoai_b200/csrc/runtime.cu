@@ -355,7 +355,7 @@ static int build_mega(tcu_model* m) {
     if (ly.w1.fmt != FMT_Q8_0 || ly.w2.fmt != FMT_Q8_0) return TCU_OK;
   const int d = m->d, ff = m->ff, K2 = d + ff;
   if (d % 32 || ff % 32 || d / 16 > 32 * MG_NJ || ff / 16 / 3 + 1 > 32 * MG_NJ || K2 > MG_MAXK) return TCU_OK;
-  if (m->H / m->KVH > 32 || m->hd % 2) return TCU_OK;
+  if (m->H / m->KVH > 32 || m->hd % 2 || (m->H / m->KVH * m->hd) % 16 || d / 16 > MG_CT) return TCU_OK;
   if (2 * ((d / 2 + m->sm_count - 1) / m->sm_count) > MG_CPART_ROWS) return TCU_OK;
   const size_t w1 = (size_t)MG_W1_RS * (d + m->layers[0].w1.sstride * 2);
   const size_t w2 = (size_t)MG_W2_RS * (K2 + m->layers[0].w2.sstride * 2);
@@ -370,7 +370,7 @@ static int build_mega(tcu_model* m) {
   uint32_t off_x = 128;
   uint32_t off_dig = off_x + (uint32_t)((xs_floats * 4 + 127) / 128 * 128);
   uint32_t off_sx = off_dig + (uint32_t)(((size_t)K2 / 4 * 12 + 127) / 128 * 128);
-  uint32_t off_part = off_sx + (uint32_t)(((size_t)K2 / 32 * 4 + 127) / 128 * 128);
+  uint32_t off_part = off_sx + (uint32_t)(((size_t)K2 / 16 * 4 + 127) / 128 * 128);
   uint32_t off_slots = off_part + (uint32_t)((MG_CPART_ROWS * 4 * 4 + 127) / 128 * 128);
   const size_t limit = (size_t)m->gemv_smem_optin;
   if (off_slots + 2 * slot > limit) return TCU_OK;
@@ -396,7 +396,7 @@ static int build_mega(tcu_model* m) {
   CK(cudaFuncSetAttribute(k_decode_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->mega_smem));
   int occ = 0;
   CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_decode_mega, MG_THREADS, m->mega_smem));
-  m->mega = occ >= 1 && m->mega_split == SPLIT_PAGES * m->P;
+  m->mega = occ >= 1;
   return TCU_OK;
 }
 
@@ -676,6 +676,9 @@ struct Work {
   unsigned long long* keys = nullptr;  // persistent decode: argmax per step parity
   int* step = nullptr;
   unsigned* bar = nullptr;  // persistent decode: grid barrier words
+  uint32_t* adig = nullptr;  // persistent decode: digits of [attention | SwiGLU]
+  float* asx = nullptr;      // and their block scales
+  int* bcnt = nullptr;       // SwiGLU block arrivals
   std::vector<void*> allocs;
   ~Work() {
     for (void* p : allocs) cudaFree(p);
@@ -697,8 +700,9 @@ static int work_init(tcu_model* m, Work* w, int rows, int seqs, int logits_rows,
   w->seqs = seqs;
   w->logits_rows = logits_rows;
   w->pt_stride = (m->max_pos + m->P - 1) / m->P;
-  const int split = SPLIT_PAGES * m->P;
-  w->max_splits = (m->max_pos + split - 1) / split;
+  // Room for the smallest history split (one page), which the persistent
+  // decode step may use; the other kernels use SPLIT_PAGES pages.
+  w->max_splits = (m->max_pos + m->P - 1) / m->P;
   w->out_cap = out_cap;
   const int qkvw = m->d + 2 * m->kvw;
   TRY(w->get(&w->x, (size_t)rows * m->d));
@@ -721,6 +725,12 @@ static int work_init(tcu_model* m, Work* w, int rows, int seqs, int logits_rows,
   TRY(w->get(&w->keys, 2));
   TRY(w->get(&w->step, 1));
   TRY(w->get(&w->bar, 2));
+  {
+    const size_t nb16 = (size_t)(m->d + m->ff) / 16;
+    TRY(w->get(&w->adig, nb16 * 12));
+    TRY(w->get(&w->asx, (nb16 + 3) / 4 * 4));
+    TRY(w->get(&w->bcnt, (size_t)m->ff / 16 + 1));
+  }
   // The zeroing memsets ran on the legacy stream (see pool_get).
   CK(cudaDeviceSynchronize());
   return TCU_OK;
@@ -1801,6 +1811,11 @@ static int launch_mega(tcu_session* s) {
   a.part = s->w.part;
   a.counters = s->w.counters;
   a.bar = s->w.bar;
+  a.adig = s->w.adig;
+  a.asx = s->w.asx;
+  a.bcnt = s->w.bcnt;
+  a.dig_bytes = (uint32_t)((m->d + m->ff) / 16 * 48);
+  a.sx_bytes = (uint32_t)(((m->d + m->ff) / 16 * 4 + 15) / 16 * 16);
   a.err = s->w.err;
   a.slot_bytes = m->mega_slot_bytes;
   a.nslots = m->mega_slots;
@@ -1849,6 +1864,11 @@ int tcu_session_generate_greedy(tcu_session* s, int32_t prefix, const int32_t* t
     CK(cudaMemsetAsync(s->w.keys + 1, 0, sizeof(unsigned long long), s->stream));
     CK(cudaMemsetAsync(s->w.step, 0, sizeof(int), s->stream));
     CK(cudaMemsetAsync(s->w.out_count, 0, sizeof(int), s->stream));
+    // Arrival counters start at zero (a run cut short by a timeout may have
+    // left them set).
+    CK(cudaMemsetAsync(s->w.bar, 0, sizeof(unsigned), s->stream));
+    CK(cudaMemsetAsync(s->w.counters, 0, (size_t)m->KVH * sizeof(int), s->stream));
+    CK(cudaMemsetAsync(s->w.bcnt, 0, ((size_t)m->ff / 16 + 1) * sizeof(int), s->stream));
     for (int i = 1; rc == TCU_OK && i < steps; i++) {
       rc = launch_mega(s);
       if (rc == TCU_OK && s->prof.on) {
