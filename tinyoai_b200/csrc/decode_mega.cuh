@@ -2,14 +2,20 @@
 // whole forward of one token (stablelm.go:332-387) in a single cooperative
 // launch.
 //
-// Grid = one CTA per SM. Warp 8 lane 0 is the producer: it walks the CTA's
-// fixed schedule for the step -- per layer its share of the fused
-// q/k/v/gate/up rows, its attention units' KV page tiles, its share of the
-// fused out/down rows; then its share of the lm_head rows -- and streams each
-// piece into a shared-memory ring of slots with cp.async.bulk, running ahead
-// across phase boundaries. Warps 0..7 consume in the same order. Phases that
-// need every CTA's results are separated by a grid barrier (bounded spin);
-// the producer keeps prefetching through it.
+// Grid = one CTA per SM. Warp 8 lane 0 is the producer, warps 0..7 consume.
+// Work is handed out dynamically: for each layer the producer takes items
+// from global counters -- tiles of the fused q/k/v/gate/up rows, attention
+// units (KV head x history split), tiles of the fused out/down rows; then
+// tiles of the lm_head rows -- and streams each item's weights or KV pages
+// into a shared-memory ring of slots with cp.async.bulk, tagging the slot
+// with the item. SMs that stream faster take more items, so the phases end
+// together. A phase's input is awaited only where it is read:
+//   - attention needs every q/k/v row (a count of finished q/k/v tiles);
+//   - the out/down rows need every published input block (SwiGLU blocks and
+//     merged attention heads);
+//   - the next layer needs every residual row.
+// Each wait is a bounded poll of one counter. Per-layer x and digit buffers
+// mean no CTA overwrites what a slower CTA may still be reading.
 //
 // Matrix-vector products use exact integer dot products (dp4a): the input
 // vector is quantised per 16-value block to 24-bit fixed point relative to the
@@ -20,10 +26,10 @@
 // weight-block sums in float64). LayerNorm, RoPE, attention and the parallel
 // residual follow the reference arithmetic as the separate kernels do.
 //
-// The input of the out/down rows ([attention | SwiGLU]) is quantised once,
-// by the CTA that produces each block (the attention merge, the SwiGLU rows),
-// and published as digits; every CTA then copies the digits in with one bulk
-// copy instead of quantising the whole vector itself.
+// Failure: every wait is bounded (%globaltimer). A wait that gives up sets the
+// error word and ends the item loop it is in. Loops over row tiles contain no
+// CTA-wide barrier (warps meet through shared-memory arrival counters), and
+// attention items are dispatched CTA-uniformly, so the kernel always ends.
 #pragma once
 #include "attention.cuh"
 #include "common.cuh"
@@ -40,7 +46,9 @@ constexpr int MG_W1_RS = 16;  // rows per stage, q/k/v/gate/up and head
 constexpr int MG_W2_RS = 4;   // rows per stage, out/down (4 K chunks x 2 row groups)
 constexpr int MG_NJ = 5;      // 16-value vectors per lane (K chunk <= 2560)
 constexpr int MG_MAXK = 10240;
-constexpr int MG_CPART_ROWS = 32;  // out/down rows per CTA (hidden <= 2 * 32 * grid)
+constexpr int MG_CTL = 4;     // control words per (launch parity, layer)
+constexpr int MG_HDR = 256;   // shared-memory header: mbarriers and slot tags
+constexpr int MG_SEQ = 8;     // in-flight tiles tracked by the arrival counters
 
 struct MegaLayer {
   const int8_t* w1;  // [n_plain + 2ff][d] quants
@@ -75,20 +83,21 @@ struct MegaArgs {
   int* out_count;
   float* logits;  // optional
   // scratch
-  float* x_buf;  // [d]
-  float* qkv;    // [d + 2 kvw]
-  float* ah;     // [d + ff] (SwiGLU part used)
-  uint32_t* adig;  // [(d + ff) / 16][12] digits of [attention | SwiGLU]
-  float* asx;      // [(d + ff) / 16] their block scales
-  int* bcnt;       // [ff / 16] SwiGLU block arrivals (zero between steps)
-  uint32_t dig_bytes, sx_bytes;  // phase C staging sizes (multiples of 16)
-  float* part;   // [H][max_splits][hd+2]
-  int* counters;  // [KVH]
-  unsigned* bar;  // [2]: arrival count, generation
+  float* xl;       // [L + 1][d]: input of layer l (xl[L]: input of the final norm)
+  float* qkv;      // [d + 2 kvw]
+  uint32_t* adig;  // [L][(d + ff) / 16][12] digits of [attention | SwiGLU]
+  float* asx;      // [L][asx_stride] their block scales
+  int asx_stride;  // floats per layer (multiple of 4)
+  int att_warp;    // floats of attention scratch per consumer warp
+  float* part;     // [H][max_splits][hd+2]
+  int* counters;   // [KVH] split arrivals per KV head (zero between layers)
+  int* grab;       // [2][L + 1][MG_CTL] work counters by launch parity
+  int* done;       // [2][L + 1][MG_CTL] completion counters by launch parity
   int* err;
+  uint32_t dig_bytes, sx_bytes;  // out/down input staging sizes (multiples of 16)
   uint32_t slot_bytes;
   int nslots;  // ring depth (<= MG_MAX_SLOTS)
-  uint32_t off_x, off_dig, off_sx, off_part, off_slots;
+  uint32_t off_x, off_att, off_dig, off_sx, off_slots;
 };
 
 __device__ __forceinline__ int dp4a_su(uint32_t a_signed, uint32_t b_unsigned, int c) {
@@ -116,43 +125,9 @@ __device__ __forceinline__ float dot16_dp4a(const uint4& w, const uint32_t* dg) 
   return fmaf((float)t2, 65536.f, (float)(t1 * 256 + t0));
 }
 
-// Grid-wide barrier among the consumer warps of all CTAs (the producer warps
-// never take part). Sense reversal on a generation word; bounded spin.
-__device__ void mg_grid_sync(const MegaArgs& a) {
-  named_bar_sync(1, MG_CT);
-  if (threadIdx.x == 0) {
-    volatile unsigned* gen = a.bar + 1;
-    const unsigned g = *gen;
-    __threadfence();
-    if (atomicAdd(a.bar, 1u) == gridDim.x - 1) {
-      atomicExch(a.bar, 0u);
-      __threadfence();
-      atomicAdd(a.bar + 1, 1u);
-    } else {
-      const unsigned long long t0 = global_ns();
-      uint32_t i = 0;
-      while (*gen == g) {
-        if ((++i & 63) == 0) {
-          if (*(volatile int*)a.err) break;
-          if (global_ns() - t0 > TCU_WAIT_NS) {
-            atomicExch(a.err, 2);
-            break;
-          }
-        }
-      }
-    }
-    __threadfence();
-  }
-  named_bar_sync(1, MG_CT);
-}
-
-// LayerNorm of xs[0..K) (stablelm.go:288-305) fused with the digit
-// quantisation of the normalised values: float64 mean and variance
-// (two passes), float32 affine, then warp-per-block digits.
-__device__ void mg_ln_digits(const float* xs, int K, const float* nw, const float* nb, double eps, uint32_t* dig, float* sx);
-
 // One thread quantises the 16 values v into 12 digit words (word 3q + k holds
-// digit k of values 4q..4q+3) and the block scale.
+// digit k of values 4q..4q+3) and the block scale: scale = max|v| / (2^23 - 1),
+// digits = low, middle and signed high byte of round(v / scale).
 __device__ __forceinline__ void mg_quant16(const float (&v)[16], uint32_t* dig12, float* sc) {
   float mx = 0.f;
 #pragma unroll
@@ -182,11 +157,63 @@ __device__ __forceinline__ void mg_quant16(const float (&v)[16], uint32_t* dig12
   *sc = mx > 0.f ? __fdiv_rn(mx, 8388607.f) : 0.f;
 }
 
+// The same quantisation by a warp: lanes 0-15 hold the 16 values (lanes
+// 16-31 take part in the shuffles only); lanes 0, 4, 8, 12 write the words.
+__device__ __forceinline__ void mg_quant16_warp(float v, uint32_t* dig12, float* sc) {
+  const int lane = threadIdx.x & 31;
+  float mx = fabsf(v);
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float inv = mx > 0.f ? __fdiv_rn(8388607.f, mx) : 0.f;
+  int xi = __float2int_rn(v * inv);
+  xi = max(-8388607, min(8388607, xi));
+  const uint32_t u = (uint32_t)xi & 0xFFFFFFu;
+  const uint32_t u1 = __shfl_down_sync(0xffffffffu, u, 1);
+  const uint32_t u2 = __shfl_down_sync(0xffffffffu, u, 2);
+  const uint32_t u3 = __shfl_down_sync(0xffffffffu, u, 3);
+  if (lane < 16 && (lane & 3) == 0) {
+    uint32_t* w = dig12 + 3 * (lane >> 2);
+    w[0] = (u & 0xFF) | (u1 & 0xFF) << 8 | (u2 & 0xFF) << 16 | (u3 & 0xFF) << 24;
+    w[1] = ((u >> 8) & 0xFF) | ((u1 >> 8) & 0xFF) << 8 | ((u2 >> 8) & 0xFF) << 16 | ((u3 >> 8) & 0xFF) << 24;
+    w[2] = (u >> 16) | (u1 >> 16) << 8 | (u2 >> 16) << 16 | (u3 >> 16) << 24;
+  }
+  if (lane == 0) *sc = mx > 0.f ? __fdiv_rn(mx, 8388607.f) : 0.f;
+}
+
+// Dot products of two rows (lr0, lr0 + 1) of a stage with the lane's digit
+// registers, over vectors v = vb + lane + 32 j (j < MG_NJ). All shared-memory
+// loads are issued before the arithmetic and nothing is branched on: a lane
+// past the input's end (ve) reads the row's last vector and adds exactly zero
+// (its digits and scale are zero); a row past nr repeats row nr - 1 and its
+// result is not used.
+__device__ __forceinline__ void mg_dot2(const uint8_t* st, size_t pitch, const __half* ss, int sstride, int lr0, int nr, int vb,
+                                        int ve, const uint32_t (&dr)[MG_NJ][12], const float (&sxr)[MG_NJ], float (&acc)[2]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int t = 0; t < 2; t++) {
+    const int lr = min(lr0 + t, nr - 1);
+    uint4 w[MG_NJ];
+    float sc[MG_NJ];
+#pragma unroll
+    for (int j = 0; j < MG_NJ; j++) {
+      const int v = min(vb + lane + 32 * j, ve - 1);
+      w[j] = *reinterpret_cast<const uint4*>(st + (size_t)lr * pitch + (size_t)v * 16);
+      sc[j] = __half2float(ss[lr * sstride + (v >> 1)]);
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < MG_NJ; j++) s = fmaf(dot16_dp4a(w[j], dr[j]), sc[j] * sxr[j], s);
+    acc[t] = warp_sum(s);
+  }
+}
+
+// LayerNorm of xs[0..K) (stablelm.go:288-305) fused with the digit
+// quantisation of the normalised values: float64 mean and variance (two
+// passes), float32 affine; thread t normalises and quantises block t
+// (K / 16 <= MG_CT), with its weight and bias fetched before the reductions.
 __device__ void mg_ln_digits(const float* xs, int K, const float* nw, const float* nb, double eps, uint32_t* dig, float* sx) {
   __shared__ double red[2][MG_CW];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // Thread t normalises and quantises block t (K / 16 <= MG_CT); its weight
-  // and bias are fetched before the reductions.
   const int b = threadIdx.x;
   const bool has_blk = b < K / 16;
   float4 wv[4], bv[4];
@@ -220,7 +247,7 @@ __device__ void mg_ln_digits(const float* xs, int K, const float* nw, const floa
   const float inv = (float)(1.0 / sqrt(var / (double)K + eps));
   const float mf = (float)mean;
   if (has_blk) {
-    float v[16];
+    float y[16];
     const float* wf = reinterpret_cast<const float*>(wv);
     const float* bf = reinterpret_cast<const float*>(bv);
 #pragma unroll
@@ -230,44 +257,81 @@ __device__ void mg_ln_digits(const float* xs, int K, const float* nw, const floa
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         const int i = 4 * q + k;
-        v[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[k], mf), inv), wf[i]), bf[i]);
+        y[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[k], mf), inv), wf[i]), bf[i]);
       }
     }
-    mg_quant16(v, dig + 12 * b, sx + b);
+    mg_quant16(y, dig + 12 * b, sx + b);
   }
   named_bar_sync(1, MG_CT);
 }
 
-// Balanced share [rb, re) of R rows in pairs for CTA c of G.
-__device__ __forceinline__ void mg_rows(int R, int c, int G, int& rb, int& re) {
-  const int pairs = (R + 1) >> 1;
-  rb = min(R, 2 * (int)(((long long)pairs * c) / G));
-  re = min(R, 2 * (int)(((long long)pairs * (c + 1)) / G));
+// Bounded wait until *ctr >= target (acquire). Called by one thread; returns
+// false (and sets *err) if it gives up or another thread already did.
+__device__ bool mg_wait_count(const int* ctr, int target, int* err) {
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 0;; i++) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return true;
+    if ((i & 31) == 31) {
+      if (*(volatile int*)err) return false;
+      if (global_ns() - t0 > TCU_WAIT_NS) {
+        atomicExch(err, 2);
+        return false;
+      }
+    }
+  }
+}
+
+// Release / acquire-release atomics at GPU scope: the release orders every
+// write this thread has made or observed (including a warp's or CTA's writes
+// it synchronised with) before the update.
+__device__ __forceinline__ int mg_atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void mg_red_add_release(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits (bounded, without touching the error word) for the phase with the
+// given parity of bar to complete: the copies of a stage landing.
+__device__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > TCU_WAIT_NS) return;
 }
 
 struct MgRing {
   uint64_t* full;
   uint64_t* empty;
+  int* tag;
   uint8_t* slots;
   uint32_t slot_bytes;
   int n;  // slots
   int i;  // running stage index
 };
 
-// Producer side: next slot, ready for writing (waits until consumers released it).
-__device__ __forceinline__ uint8_t* mg_produce(MgRing& r, uint32_t bytes, int* err) {
+// Producer: takes the next slot (waiting until the consumers released it),
+// tags it and arms its barrier for `bytes` of copies (0: a bare tag).
+// Returns nullptr if the wait failed: the producer then stops.
+__device__ __forceinline__ uint8_t* mg_produce(MgRing& r, int tag, uint32_t bytes, int* err) {
   const int slot = r.i % r.n;
-  if (r.i >= r.n) mbar_wait(&r.empty[slot], ((r.i / r.n) - 1) & 1, err);
+  if (r.i >= r.n && !mbar_wait(&r.empty[slot], ((r.i / r.n) - 1) & 1, err)) return nullptr;
+  r.tag[slot] = tag;
   mbar_expect_tx(&r.full[slot], bytes);
   return r.slots + (size_t)slot * r.slot_bytes;
 }
 __device__ __forceinline__ uint64_t* mg_full(MgRing& r) { return &r.full[r.i % r.n]; }
 
-// Consumer side.
-__device__ __forceinline__ const uint8_t* mg_consume(MgRing& r, int* err) {
+// Consumer warp: waits for the next slot; returns its tag (-1: end of the
+// phase), or -2 if the wait failed. Warp-uniform.
+__device__ __forceinline__ int mg_next_warp(MgRing& r, const uint8_t** st, int* err) {
   const int slot = r.i % r.n;
-  mbar_wait(&r.full[slot], (r.i / r.n) & 1, err);
-  return r.slots + (size_t)slot * r.slot_bytes;
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(&r.full[slot], (r.i / r.n) & 1, err));
+  *st = r.slots + (size_t)slot * r.slot_bytes;
+  return ok ? r.tag[slot] : -2;
 }
 __device__ __forceinline__ void mg_release(MgRing& r) {
   __syncwarp();
@@ -275,30 +339,55 @@ __device__ __forceinline__ void mg_release(MgRing& r) {
   r.i++;
 }
 
-// Attention units of a layer: (kv head g, chunk s) for chunks of the history.
-__device__ __forceinline__ int mg_units(const MegaArgs& a, int T) { return a.KVH * ((T + a.split - 1) / a.split); }
+// Publishes n finished items of this CTA on a completion counter, after
+// every consumer thread's global writes (the barrier, then a release).
+__device__ __forceinline__ void mg_publish(int* ctr, int n) {
+  named_bar_sync(1, MG_CT);
+  if (threadIdx.x == 0 && n > 0) mg_red_add_release(ctr, n);
+}
+
+// Waits, CTA-uniformly, until *ctr >= target. The result of a failed wait is
+// garbage but the kernel keeps going to its end.
+__device__ __forceinline__ void mg_await(const int* ctr, int target, int* err) {
+  if (threadIdx.x == 0) {
+    mg_wait_count(ctr, target, err);
+    fence_proxy_async();  // later bulk copies read what the counter covers
+  }
+  named_bar_sync(1, MG_CT);
+}
 
 __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
   extern __shared__ __align__(128) uint8_t mg_smem[];
+  __shared__ float swg[MG_SEQ][16], swu[MG_SEQ][16];  // gate / up of in-flight gate/up tiles
+  __shared__ int swcnt[MG_SEQ];
+  __shared__ float cpart[MG_SEQ][16];  // out/down chunk partials of in-flight tiles
+  __shared__ int cpcnt[MG_SEQ];
   MgRing ring;
   ring.full = reinterpret_cast<uint64_t*>(mg_smem);
   ring.empty = ring.full + MG_MAX_SLOTS;
   uint64_t* inbar = ring.full + 2 * MG_MAX_SLOTS;  // phase inputs staged by bulk copy
+  ring.tag = reinterpret_cast<int*>(mg_smem + 128);
   uint32_t in_phase = 0;
   ring.slots = mg_smem + a.off_slots;
   ring.slot_bytes = a.slot_bytes;
   ring.n = a.nslots;
   ring.i = 0;
   float* xs = reinterpret_cast<float*>(mg_smem + a.off_x);
+  float* att = reinterpret_cast<float*>(mg_smem + a.off_att);
   uint32_t* dig = reinterpret_cast<uint32_t*>(mg_smem + a.off_dig);
   float* sx = reinterpret_cast<float*>(mg_smem + a.off_sx);
-  float* cpart = reinterpret_cast<float*>(mg_smem + a.off_part);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, c = blockIdx.x;
   const int d = a.d, ff = a.ff, hd = a.hd, kvw = a.KVH * hd;
   const int n_plain = d + 2 * kvw;
-  const int R1 = n_plain + 2 * ff, K2 = d + ff;
+  const int K2 = d + ff;
   const size_t row2 = (size_t)K2;
+  const int n_pt = n_plain / MG_W1_RS;     // q/k/v tiles (16 rows)
+  const int n_w1t = n_pt + ff / 16;        // + gate/up tiles (32 rows: 16 SwiGLU values)
+  const int n_w2t = (d + MG_W2_RS - 1) / MG_W2_RS;
+  const int n_ht = (a.V + MG_W1_RS - 1) / MG_W1_RS;
+  const int nb_in = ff / 16 + a.KVH;       // published out/down input items per layer
+  const int G_q = a.H / a.KVH;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < ring.n; i++) {
@@ -308,16 +397,20 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
     mbar_init(inbar, 1);
     fence_barrier_init();
   }
+  if (threadIdx.x < MG_SEQ) {
+    swcnt[threadIdx.x] = 0;
+    cpcnt[threadIdx.x] = 0;
+  }
   __syncthreads();
 
   const int pos = *(volatile int*)a.pos;
+  const int step = *(volatile int*)a.step;
+  const int par = step & 1;
+  int* grab = a.grab + (size_t)par * (a.L + 1) * MG_CTL;
+  int* done = a.done + (size_t)par * (a.L + 1) * MG_CTL;
   const int T = pos + 1;
   const int nsplit = (T + a.split - 1) / a.split;
-  const int units = mg_units(a, T);
-  int rb1, re1, rb2, re2, rbh, reh;
-  mg_rows(R1, c, G, rb1, re1);
-  mg_rows(d, c, G, rb2, re2);
-  mg_rows(a.V, c, G, rbh, reh);
+  const int units = a.KVH * nsplit;
   const int es = a.kv.half ? 2 : 4;
   const uint32_t page_bytes = (uint32_t)(a.kv.P * hd * es);
   const int pages_per_split = a.split / a.kv.P;
@@ -325,23 +418,66 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
   // ------------------------------------------------------------------ producer
   if (warp == MG_CW) {
     if (lane == 0) {
-      for (int l = 0; l < a.L; l++) {
-        const MegaLayer& ly = a.layers[l];
-        for (int r0 = rb1; r0 < re1; r0 += MG_W1_RS) {
-          const int nr = min(MG_W1_RS, re1 - r0);
-          const uint32_t qb = (uint32_t)(nr * d), sb = (uint32_t)(nr * a.s1_stride * 2);
-          uint8_t* dst = mg_produce(ring, qb + sb, a.err);
-          bulk_g2s(dst, ly.w1 + (size_t)r0 * d, qb, mg_full(ring));
-          bulk_g2s(dst + (size_t)MG_W1_RS * d, ly.s1 + (size_t)r0 * a.s1_stride, sb, mg_full(ring));
+      bool stop = false;
+      // Ends a phase for the consumers with a bare tag.
+      auto end_phase = [&]() {
+        if (!mg_produce(ring, -1, 0, a.err))
+          stop = true;
+        else
           ring.i++;
+      };
+      for (int l = 0; l < a.L && !stop; l++) {
+        // Kept in registers: the grab atomics would otherwise force reloads.
+        const int8_t* const w1p = a.layers[l].w1;
+        const __half* const s1p = a.layers[l].s1;
+        const int8_t* const w2p = a.layers[l].w2;
+        const __half* const s2p = a.layers[l].s2;
+        int* gl = grab + l * MG_CTL;
+        // Two grabs stay in flight, so the atomic's round trip overlaps the copies.
+        int q0 = atomicAdd(gl + 0, 1), q1 = atomicAdd(gl + 0, 1);
+        while (!stop) {
+          const int t = q0;
+          q0 = q1;
+          if (t >= n_w1t) {
+            end_phase();
+            break;
+          }
+          q1 = atomicAdd(gl + 0, 1);
+          const int nst = t < n_pt ? 1 : 2;
+          const int rbase = t < n_pt ? t * MG_W1_RS : n_plain + (t - n_pt) * 2 * MG_W1_RS;
+          for (int sub = 0; sub < nst && !stop; sub++) {
+            const int r0 = rbase + sub * MG_W1_RS;
+            const uint32_t qb = (uint32_t)(MG_W1_RS * d), sb = (uint32_t)(MG_W1_RS * a.s1_stride * 2);
+            uint8_t* dst = mg_produce(ring, (t << 1) | sub, qb + sb, a.err);
+            if (!dst) {
+              stop = true;
+              break;
+            }
+            bulk_g2s(dst, w1p + (size_t)r0 * d, qb, mg_full(ring));
+            bulk_g2s(dst + (size_t)MG_W1_RS * d, s1p + (size_t)r0 * a.s1_stride, sb, mg_full(ring));
+            ring.i++;
+          }
         }
-        for (int u = c; u < units; u += G) {
+        q0 = atomicAdd(gl + 1, 1);
+        q1 = atomicAdd(gl + 1, 1);
+        while (!stop) {
+          const int u = q0;
+          q0 = q1;
+          if (u >= units) {
+            end_phase();
+            break;
+          }
+          q1 = atomicAdd(gl + 1, 1);
           const int g = u / nsplit, s = u % nsplit;
           const int t0 = s * a.split;
           const int nt = min(T, t0 + a.split) - t0;
           const int n_hist = (s == nsplit - 1) ? nt - 1 : nt;
           const int np = (n_hist + a.kv.P - 1) / a.kv.P;
-          uint8_t* dst = mg_produce(ring, 2u * np * page_bytes, a.err);
+          uint8_t* dst = mg_produce(ring, u, 2u * np * page_bytes, a.err);
+          if (!dst) {
+            stop = true;
+            break;
+          }
           for (int j = 0; j < np; j++) {
             const int page = a.page_table[t0 / a.kv.P + j];
             const size_t o = a.kv.off(l, page, g, 0) * es;
@@ -351,60 +487,95 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
           }
           ring.i++;
         }
-        for (int r0 = rb2; r0 < re2; r0 += MG_W2_RS) {
-          const int nr = min(MG_W2_RS, re2 - r0);
+        q0 = atomicAdd(gl + 2, 1);
+        q1 = atomicAdd(gl + 2, 1);
+        while (!stop) {
+          const int t = q0;
+          q0 = q1;
+          if (t >= n_w2t) {
+            end_phase();
+            break;
+          }
+          q1 = atomicAdd(gl + 2, 1);
+          const int r0 = t * MG_W2_RS, nr = min(MG_W2_RS, d - r0);
           const uint32_t qb = (uint32_t)(nr * row2), sb = (uint32_t)(nr * a.s2_stride * 2);
-          uint8_t* dst = mg_produce(ring, qb + sb, a.err);
-          bulk_g2s(dst, ly.w2 + (size_t)r0 * row2, qb, mg_full(ring));
-          bulk_g2s(dst + (size_t)MG_W2_RS * row2, ly.s2 + (size_t)r0 * a.s2_stride, sb, mg_full(ring));
+          uint8_t* dst = mg_produce(ring, t, qb + sb, a.err);
+          if (!dst) {
+            stop = true;
+            break;
+          }
+          bulk_g2s(dst, w2p + (size_t)r0 * row2, qb, mg_full(ring));
+          bulk_g2s(dst + (size_t)MG_W2_RS * row2, s2p + (size_t)r0 * a.s2_stride, sb, mg_full(ring));
           ring.i++;
         }
       }
-      for (int r0 = rbh; r0 < reh; r0 += MG_W1_RS) {
-        const int nr = min(MG_W1_RS, reh - r0);
+      int* gh = grab + a.L * MG_CTL;
+      int h0 = stop ? 0 : atomicAdd(gh, 1), h1 = stop ? 0 : atomicAdd(gh, 1);
+      while (!stop) {
+        const int t = h0;
+        h0 = h1;
+        if (t >= n_ht) {
+          end_phase();
+          break;
+        }
+        h1 = atomicAdd(gh, 1);
+        const int r0 = t * MG_W1_RS, nr = min(MG_W1_RS, a.V - r0);
         const uint32_t qb = (uint32_t)(nr * d), sb = (uint32_t)(nr * a.sh_stride * 2);
-        uint8_t* dst = mg_produce(ring, qb + sb, a.err);
+        uint8_t* dst = mg_produce(ring, t, qb + sb, a.err);
+        if (!dst) {
+          stop = true;
+          break;
+        }
         bulk_g2s(dst, a.head_w + (size_t)r0 * d, qb, mg_full(ring));
         bulk_g2s(dst + (size_t)MG_W1_RS * d, a.head_s + (size_t)r0 * a.sh_stride, sb, mg_full(ring));
         ring.i++;
+      }
+      // No copy may still be landing in this CTA's shared memory when it exits.
+      for (int k = 0; k < ring.n && k < ring.i; k++) {
+        const int last = ring.i - 1 - ((ring.i - 1 - k) % ring.n);
+        mbar_drain(&ring.full[k], (last / ring.n) & 1);
       }
     }
     return;
   }
 
   // ------------------------------------------------------------------ consumers
-  const int step = *(volatile int*)a.step;
-  const unsigned long long key_in = *(volatile unsigned long long*)(a.keys + (step & 1));
+  if (c == 0) {
+    // Control words of the next launch (the other parity) start at zero.
+    const int n = (a.L + 1) * MG_CTL;
+    int* g2 = a.grab + (size_t)(par ^ 1) * n;
+    int* d2 = a.done + (size_t)(par ^ 1) * n;
+    for (int i = threadIdx.x; i < n; i += MG_CT) {
+      g2[i] = 0;
+      d2[i] = 0;
+    }
+  }
+  // This position's RoPE row (cos, sin per pair) and KV page, for every layer.
+  __shared__ float2 rope_cs[64];
+  for (int i = threadIdx.x; i < a.rope.pairs; i += MG_CT) rope_cs[i] = a.rope.table[(size_t)pos * a.rope.pairs + i];
+  const int page_cur = a.page_table[pos / a.kv.P];
+  const unsigned long long key_in = *(volatile unsigned long long*)(a.keys + par);
   int token = argmax_index(key_in);
   token = (token >= 0 && token < a.V) ? token : 0;
-  if (c == 0 && threadIdx.x == 0) {
-    a.keys[(step + 1) & 1] = 0ull;
-    const int cnt = a.out_count[0];
-    a.out_tokens[cnt] = token;
-    a.out_count[0] = cnt + 1;
-  }
   // Embedding row (Q8_0 decode, matmul.go:24-34), computed by every CTA.
   for (int i = threadIdx.x; i < d; i += MG_CT)
     xs[i] = __fmul_rn(__half2float(a.emb_s[(size_t)token * a.se_stride + i / 32]), (float)a.emb_w[(size_t)token * d + i]);
   named_bar_sync(1, MG_CT);
-  if (c == 0)
-    for (int i = threadIdx.x; i < d; i += MG_CT) a.x_buf[i] = xs[i];
 
   uint32_t dr[MG_NJ][12];
   float sxr[MG_NJ];
   unsigned long long best = 0ull;
+  int sw_seq = 0, cp_seq = 0;  // local sequence numbers of gate/up and out/down tiles
 
-  // Copies n floats (n * 4 a multiple of 16) from global memory into xs with
-  // one bulk copy issued by consumer thread 0, and waits for it. The fence
-  // and barrier order every consumer's earlier generic accesses to xs, and
-  // the other CTAs' stores to src seen through the grid barrier, before the
-  // copy (async proxy).
-  auto stage_in = [&](const float* src, int n) {
+  // Copies n bytes from global memory into shared memory at dst with one bulk
+  // copy issued by consumer thread 0, and waits for it (all consumers).
+  auto stage_in = [&](void* dst, const void* src, uint32_t n, void* dst2, const void* src2, uint32_t n2) {
     fence_proxy_async();
     named_bar_sync(1, MG_CT);
     if (threadIdx.x == 0) {
-      mbar_expect_tx(inbar, (uint32_t)n * 4u);
-      bulk_g2s(xs, src, (uint32_t)n * 4u, inbar);
+      mbar_expect_tx(inbar, n + n2);
+      bulk_g2s(dst, src, n, inbar);
+      if (n2) bulk_g2s(dst2, src2, n2, inbar);
     }
     mbar_wait(inbar, in_phase & 1, a.err);
     in_phase++;
@@ -429,131 +600,178 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
     }
   };
 
+  // Two dot products of one 16-row stage: rows 2w and 2w+1 against the
+  // digit registers (vectors [0, d/16)).
+  auto rows16 = [&](const uint8_t* st, int nr, int sstride, float (&acc)[2]) {
+    mg_dot2(st, (size_t)d, reinterpret_cast<const __half*>(st + (size_t)MG_W1_RS * d), sstride, 2 * warp, nr, 0, d / 16, dr, sxr,
+            acc);
+  };
+
   for (int l = 0; l < a.L; l++) {
     const MegaLayer& ly = a.layers[l];
-    // Phase A: LayerNorm, then q/k/v rows and SwiGLU of (gate, up) pairs.
-    if (l > 0) stage_in(a.x_buf, d);
+    int* dl = done + l * MG_CTL;
+    uint32_t* adig_l = a.adig + (size_t)l * (K2 / 16) * 12;
+    float* asx_l = a.asx + (size_t)l * a.asx_stride;
+
+    // ---- Phase A: LayerNorm, then q/k/v tiles and gate/up tiles (SwiGLU).
+    if (l > 0) {
+      mg_await(done + (l - 1) * MG_CTL + 2, d, a.err);
+      stage_in(xs, a.xl + (size_t)l * d, (uint32_t)d * 4u, nullptr, nullptr, 0);
+    }
     mg_ln_digits(xs, d, ly.nw, ly.nb, a.eps, dig, sx);
     load_regs(0, d / 16);
-    for (int r0 = rb1; r0 < re1; r0 += MG_W1_RS) {
-      const int nr = min(MG_W1_RS, re1 - r0);
-      const uint8_t* st = mg_consume(ring, a.err);
-      const __half* ss = reinterpret_cast<const __half*>(st + (size_t)MG_W1_RS * d);
-      float acc[2];
-#pragma unroll
-      for (int t = 0; t < 2; t++) {
-        const int lr = 2 * warp + t;
-        float s = 0.f;
-        if (lr < nr) {
-#pragma unroll
-          for (int j = 0; j < MG_NJ; j++) {
-            const int v = lane + 32 * j;
-            if (v < d / 16) {
-              const uint4 w = *reinterpret_cast<const uint4*>(st + (size_t)lr * d + (size_t)v * 16);
-              s = fmaf(dot16_dp4a(w, dr[j]), __half2float(ss[(size_t)lr * a.s1_stride + (v >> 1)]) * sxr[j], s);
-            }
-          }
+    {
+      int n_plain_done = 0, n_blocks = 0;
+      bool plain_open = true;
+      for (;;) {
+        const uint8_t* st;
+        const int tag = mg_next_warp(ring, &st, a.err);
+        if (tag == -2) break;
+        const bool is_plain = tag >= 0 && (tag >> 1) < n_pt;
+        if (!is_plain && plain_open) {
+          // This warp's q/k/v rows are written (by its lane 0): publish them.
+          plain_open = false;
+          if (lane == 0 && n_plain_done > 0) mg_red_add_release(dl + 0, 2 * n_plain_done);
         }
-        acc[t] = warp_sum(s);
-      }
-      mg_release(ring);
-      if (lane == 0 && 2 * warp < nr) {
-        const int r = r0 + 2 * warp;
-        if (r < n_plain) {
-          a.qkv[r] = acc[0];
-          if (2 * warp + 1 < nr) a.qkv[r + 1] = acc[1];
+        if (tag == -1) {
+          mg_release(ring);
+          break;
+        }
+        const int t = tag >> 1, sub = tag & 1;
+        float acc[2];
+        rows16(st, MG_W1_RS, a.s1_stride, acc);
+        mg_release(ring);
+        if (is_plain) {
+          if (lane == 0) {
+            a.qkv[t * MG_W1_RS + 2 * warp] = acc[0];
+            a.qkv[t * MG_W1_RS + 2 * warp + 1] = acc[1];
+          }
+          n_plain_done++;
         } else {
-          a.ah[d + ((r - n_plain) >> 1)] = silu_mul_stablelm(acc[0], acc[1]);
-        }
-      }
-    }
-    // Digits of this CTA's SwiGLU outputs j in [j0, j1): a 16-value block is
-    // quantised by whichever CTA completes it (blocks at the edge of a CTA's
-    // rows are shared with its neighbour).
-    {
-      const int j0 = max(0, rb1 - n_plain) >> 1, j1 = max(0, re1 - n_plain) >> 1;
-      if (j1 > j0) {
-        __threadfence();
-        named_bar_sync(1, MG_CT);
-        for (int b = j0 / 16 + threadIdx.x; b < (j1 + 15) / 16; b += MG_CT) {
-          const int cnt = min(j1, 16 * b + 16) - max(j0, 16 * b);
-          bool last = cnt == 16;
-          if (!last) last = atomicAdd(a.bcnt + b, cnt) + cnt == 16;
-          if (last) {
-            __threadfence();
-            if (cnt != 16) a.bcnt[b] = 0;
-            float v[16];
-#pragma unroll
-            for (int i = 0; i < 16; i++) v[i] = __ldcg(a.ah + d + 16 * b + i);
-            mg_quant16(v, a.adig + (size_t)(d / 16 + b) * 12, a.asx + d / 16 + b);
+          // Gate/up pair j = 16 (t - n_pt) + 8 sub + warp. The last warp to
+          // finish a tile forms its 16 SwiGLU values (one per lane) and
+          // quantises them.
+          const int e = sw_seq % MG_SEQ;
+          if (lane == 0) {
+            swg[e][8 * sub + warp] = acc[0];
+            swu[e][8 * sub + warp] = acc[1];
+          }
+          if (sub == 1) {
+            __threadfence_block();
+            int last = 0;
+            if (lane == 0) last = atomicAdd(&swcnt[e], 1) == MG_CW - 1;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+              __threadfence_block();
+              const float v = lane < 16 ? silu_mul_stablelm(swg[e][lane], swu[e][lane]) : 0.f;
+              const int b = d / 16 + (t - n_pt);
+              mg_quant16_warp(v, adig_l + (size_t)b * 12, asx_l + b);
+              if (lane == 0) swcnt[e] = 0;
+              n_blocks++;
+            }
+            sw_seq++;
           }
         }
       }
+      // The gate/up blocks this warp quantised are read in phase C only:
+      // published once, outside the streaming loop.
+      __syncwarp();
+      if (lane == 0 && n_blocks > 0) mg_red_add_release(dl + 1, n_blocks);
     }
-    mg_grid_sync(a);
 
-    // Phase B: attention units (stablelm.go:401-427), split over the history.
+    // ---- Phase B: attention units (stablelm.go:401-427), split over the
+    // history. The k-th unit this CTA receives goes to warp k % 8, so up to
+    // one unit per ring slot runs at once; the other warps release its slot.
     {
-      const int G_q = a.H / a.KVH;
-      float* qs = xs;                         // [G_q][hd]
-      float* cur = xs + G_q * hd;             // [2][hd]
-      float* sc = cur + 2 * hd;               // [G_q][split]
-      __shared__ int is_last;
-      __shared__ float mloc[32], lloc[32];
-      for (int u = c; u < units; u += G) {
+      const int ghd = G_q * hd;
+      float* wq = att + (size_t)warp * a.att_warp;  // [G_q][hd] rotated queries
+      float* cur = wq + ghd;                         // [2][hd] this position's k, v
+      float* sc = cur + 2 * hd;                      // [G_q][split] scores / weights
+      float* wo = sc + G_q * a.split;                // [G_q][hd] merged outputs
+      bool s1 = false;
+      int k_unit = 0;
+      for (;;) {
+        const uint8_t* st;
+        const int u = mg_next_warp(ring, &st, a.err);
+        if (u < 0) {
+          if (u == -1) mg_release(ring);
+          break;
+        }
+        const bool mine = (k_unit % MG_CW) == warp;
+        k_unit++;
+        if (!mine) {
+          mg_release(ring);
+          continue;
+        }
+        if (!s1) {
+          if (lane == 0) mg_wait_count(dl + 0, n_plain, a.err);
+          __syncwarp();
+          s1 = true;
+        }
         const int g = u / nsplit, s = u % nsplit;
         const int t0 = s * a.split;
         const int nt = min(T, t0 + a.split) - t0;
         const bool has_cur = (s == nsplit - 1);
         const int n_hist = has_cur ? nt - 1 : nt;
-        for (int e = threadIdx.x; e < G_q * hd; e += MG_CT) qs[e] = __ldcg(a.qkv + (g * G_q) * hd + e);
+        const int pairs = a.rope.pairs;
+        for (int e = lane; e < ghd; e += 32) wq[e] = __ldcg(a.qkv + (g * G_q) * hd + e);
         if (has_cur)
-          for (int e = threadIdx.x; e < hd; e += MG_CT) {
+          for (int e = lane; e < hd; e += 32) {
             cur[e] = __ldcg(a.qkv + a.H * hd + g * hd + e);
             cur[hd + e] = __ldcg(a.qkv + (a.H + a.KVH) * hd + g * hd + e);
           }
-        named_bar_sync(1, MG_CT);
-        for (int e = threadIdx.x; e < G_q * a.rope.pairs; e += MG_CT) rope_pair(qs + (e / a.rope.pairs) * hd, e % a.rope.pairs, a.rope, pos);
-        if (has_cur)
-          for (int e = threadIdx.x; e < a.rope.pairs; e += MG_CT) rope_pair(cur, e, a.rope, pos);
-        named_bar_sync(1, MG_CT);
+        __syncwarp();
+        // Split-half RoPE (stablelm.go:309-326) with this position's row.
+        for (int e = lane; e < (G_q + (has_cur ? 1 : 0)) * pairs; e += 32) {
+          const int hh = e / pairs, i = e % pairs;
+          float* x = hh < G_q ? wq + hh * hd : cur;
+          const float2 cs = rope_cs[i];
+          const float x0 = x[i], x1 = x[i + pairs];
+          x[i] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+          x[i + pairs] = __fadd_rn(__fmul_rn(x1, cs.x), __fmul_rn(x0, cs.y));
+        }
+        __syncwarp();
         if (has_cur) {
-          for (int e = threadIdx.x; e < 2 * hd; e += MG_CT) cur[e] = kv_round(cur[e], a.kv.half);
-          named_bar_sync(1, MG_CT);
-          const int page = a.page_table[pos / a.kv.P], row = pos % a.kv.P;
-          const size_t o = a.kv.off(l, page, g, row);
-          for (int e = threadIdx.x; e < hd; e += MG_CT) {
+          for (int e = lane; e < 2 * hd; e += 32) cur[e] = kv_round(cur[e], a.kv.half);
+          __syncwarp();
+          const size_t o = a.kv.off(l, page_cur, g, pos % a.kv.P);
+          for (int e = lane; e < hd; e += 32) {
             kv_store(a.kv, a.kv.k, o + e, cur[e]);
             kv_store(a.kv, a.kv.v, o + e, cur[hd + e]);
           }
         }
-        const uint8_t* st = mg_consume(ring, a.err);
         const uint8_t* ktile = st;
         const uint8_t* vtile = st + (size_t)pages_per_split * page_bytes;
-        for (int e = threadIdx.x; e < G_q * a.split; e += MG_CT) {
-          const int hh = e / a.split, t = e % a.split;
-          if (t < nt) {
-            const float* q = qs + hh * hd;
-            float acc = 0.f;
-            const int i0 = t % hd;
-            if (has_cur && t == nt - 1) {
-              for (int i = 0; i < hd; i++) {
-                int ii = i0 + i;
-                ii -= ii >= hd ? hd : 0;
-                acc = fmaf(q[ii], cur[ii], acc);
-              }
-            } else {
-              for (int i = 0; i < hd; i++) {
-                int ii = i0 + i;
-                ii -= ii >= hd ? hd : 0;
-                acc = fmaf(q[ii], kv_ld(ktile, a.kv.half, (size_t)t * hd + ii), acc);
-              }
+        // Scores: lane per token, four partial sums over the dimensions from a
+        // token-dependent starting offset (conflict-free shared-memory reads).
+        for (int t = lane; t < nt; t += 32) {
+          const bool is_cur = has_cur && t == nt - 1;
+          for (int hh = 0; hh < G_q; hh++) {
+            const float* q = wq + hh * hd;
+            const uint8_t* krow = ktile + (size_t)t * hd * (a.kv.half ? 2 : 4);
+            auto kat = [&](int i) { return is_cur ? cur[i] : kv_ld(krow, a.kv.half, i); };
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+            int i = t % hd, j = 0;
+            for (; j + 4 <= hd; j += 4) {
+              a0 = fmaf(q[i], kat(i), a0);
+              i = i + 1 == hd ? 0 : i + 1;
+              a1 = fmaf(q[i], kat(i), a1);
+              i = i + 1 == hd ? 0 : i + 1;
+              a2 = fmaf(q[i], kat(i), a2);
+              i = i + 1 == hd ? 0 : i + 1;
+              a3 = fmaf(q[i], kat(i), a3);
+              i = i + 1 == hd ? 0 : i + 1;
             }
-            sc[hh * a.split + t] = __fdiv_rn(acc, a.scale);
+            for (; j < hd; j++) {
+              a0 = fmaf(q[i], kat(i), a0);
+              i = i + 1 == hd ? 0 : i + 1;
+            }
+            sc[hh * a.split + t] = __fdiv_rn((a0 + a1) + (a2 + a3), a.scale);
           }
         }
-        named_bar_sync(1, MG_CT);
-        for (int hh = warp; hh < G_q; hh += MG_CW) {
+        __syncwarp();
+        float mloc = 0.f, lloc = 0.f;  // lane hh holds head hh's max and sum
+        for (int hh = 0; hh < G_q; hh++) {
           float mx = -INFINITY;
           for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, sc[hh * a.split + t]);
 #pragma unroll
@@ -565,34 +783,43 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
             lsum += p;
           }
           lsum = warp_sum(lsum);
-          if (lane == 0) {
-            mloc[hh] = mx;
-            lloc[hh] = lsum;
+          if (lane == hh) {
+            mloc = mx;
+            lloc = lsum;
           }
         }
-        named_bar_sync(1, MG_CT);
+        __syncwarp();
+        // Weighted values: lane per dimension, four partial sums over tokens.
         float* pg = a.part + (size_t)(g * G_q) * a.max_splits * (hd + 2);
-        for (int e = threadIdx.x; e < G_q * hd; e += MG_CT) {
+        for (int e = lane; e < ghd; e += 32) {
           const int hh = e / hd, i = e % hd;
-          float o = 0.f;
-          for (int t = 0; t < n_hist; t++) o = fmaf(sc[hh * a.split + t], kv_ld(vtile, a.kv.half, (size_t)t * hd + i), o);
-          if (has_cur) o = fmaf(sc[hh * a.split + nt - 1], cur[hd + i], o);
-          pg[((size_t)hh * a.max_splits + s) * (hd + 2) + i] = o;
+          const float* p = sc + hh * a.split;
+          float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+          int t = 0;
+          for (; t + 4 <= n_hist; t += 4) {
+            a0 = fmaf(p[t], kv_ld(vtile, a.kv.half, (size_t)t * hd + i), a0);
+            a1 = fmaf(p[t + 1], kv_ld(vtile, a.kv.half, (size_t)(t + 1) * hd + i), a1);
+            a2 = fmaf(p[t + 2], kv_ld(vtile, a.kv.half, (size_t)(t + 2) * hd + i), a2);
+            a3 = fmaf(p[t + 3], kv_ld(vtile, a.kv.half, (size_t)(t + 3) * hd + i), a3);
+          }
+          for (; t < n_hist; t++) a0 = fmaf(p[t], kv_ld(vtile, a.kv.half, (size_t)t * hd + i), a0);
+          if (has_cur) a1 = fmaf(p[nt - 1], cur[hd + i], a1);
+          pg[((size_t)hh * a.max_splits + s) * (hd + 2) + i] = (a0 + a1) + (a2 + a3);
         }
-        if (threadIdx.x < G_q) {
-          pg[((size_t)threadIdx.x * a.max_splits + s) * (hd + 2) + hd] = mloc[threadIdx.x];
-          pg[((size_t)threadIdx.x * a.max_splits + s) * (hd + 2) + hd + 1] = lloc[threadIdx.x];
+        if (lane < G_q) {
+          pg[((size_t)lane * a.max_splits + s) * (hd + 2) + hd] = mloc;
+          pg[((size_t)lane * a.max_splits + s) * (hd + 2) + hd + 1] = lloc;
         }
         mg_release(ring);
-        __threadfence();
-        named_bar_sync(1, MG_CT);
-        if (threadIdx.x == 0) is_last = (atomicAdd(a.counters + g, 1) == nsplit - 1);
-        named_bar_sync(1, MG_CT);
-        if (is_last) {
-          __threadfence();
-          // Merged head outputs go to qs (no longer read), then their digits
-          // to adig: G_q * hd is a multiple of 16.
-          for (int e = threadIdx.x; e < G_q * hd; e += MG_CT) {
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = mg_atom_add_acq_rel(a.counters + g, 1) == nsplit - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          // Merge the splits of KV head g (fp32 max / sum), then publish the
+          // digits of its G_q * hd outputs (a multiple of 16).
+          __syncwarp();
+          for (int e = lane; e < ghd; e += 32) {
             const int hh = e / hd, i = e % hd;
             const float* ph = pg + (size_t)hh * a.max_splits * (hd + 2);
             float mx = -INFINITY;
@@ -604,35 +831,30 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
               lsum = fmaf(__ldcg(pj + hd + 1), w, lsum);
               o = fmaf(__ldcg(pj + i), w, o);
             }
-            qs[e] = __fdiv_rn(o, lsum);
+            wo[e] = __fdiv_rn(o, lsum);
           }
-          named_bar_sync(1, MG_CT);
-          const int nb16 = G_q * hd / 16;
-          for (int b = threadIdx.x; b < nb16; b += MG_CT) {
+          __syncwarp();
+          const int nb16 = ghd / 16;
+          for (int b = lane; b < nb16; b += 32) {
             float v[16];
 #pragma unroll
-            for (int i = 0; i < 16; i++) v[i] = qs[16 * b + i];
-            mg_quant16(v, a.adig + (size_t)(g * nb16 + b) * 12, a.asx + g * nb16 + b);
+            for (int i = 0; i < 16; i++) v[i] = wo[16 * b + i];
+            mg_quant16(v, adig_l + (size_t)(g * nb16 + b) * 12, asx_l + g * nb16 + b);
           }
-          if (threadIdx.x == 0) a.counters[g] = 0;
+          __syncwarp();
+          if (lane == 0) {
+            a.counters[g] = 0;
+            mg_red_add_release(dl + 1, 1);
+          }
         }
-        named_bar_sync(1, MG_CT);
+        __syncwarp();
       }
     }
-    mg_grid_sync(a);
 
-    // Phase C: out/down rows over [attention | SwiGLU], parallel residual
-    // (stablelm.go:365-377). K chunks: [0, d) then down split in three.
-    // The digits of [attention | SwiGLU] were published by their producers.
-    fence_proxy_async();
-    named_bar_sync(1, MG_CT);
-    if (threadIdx.x == 0) {
-      mbar_expect_tx(inbar, a.dig_bytes + a.sx_bytes);
-      bulk_g2s(dig, a.adig, a.dig_bytes, inbar);
-      bulk_g2s(sx, a.asx, a.sx_bytes, inbar);
-    }
-    mbar_wait(inbar, in_phase & 1, a.err);
-    in_phase++;
+    // ---- Phase C: out/down rows over [attention | SwiGLU] with the parallel
+    // residual (stablelm.go:365-377). K chunks: [0, d) then down split in three.
+    mg_await(dl + 1, nb_in, a.err);
+    stage_in(dig, adig_l, a.dig_bytes, sx, asx_l, a.sx_bytes);
     {
       const int chunk = warp & 3, sub = warp >> 2;
       const int nvd = ff / 16;
@@ -645,72 +867,64 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
         ve = d / 16 + (nvd * chunk) / 3;
       }
       load_regs(vb, ve);
-      for (int r0 = rb2; r0 < re2; r0 += MG_W2_RS) {
-        const int nr = min(MG_W2_RS, re2 - r0);
-        const uint8_t* st = mg_consume(ring, a.err);
-        const __half* ss = reinterpret_cast<const __half*>(st + (size_t)MG_W2_RS * row2);
+      float* xo = a.xl + (size_t)(l + 1) * d;
+      int rows = 0;
+      for (;;) {
+        const uint8_t* st;
+        const int tag = mg_next_warp(ring, &st, a.err);
+        if (tag < 0) {
+          if (tag == -1) mg_release(ring);
+          break;
+        }
+        const int r0 = tag * MG_W2_RS, nr = min(MG_W2_RS, d - r0);
         float acc[2];
-#pragma unroll
-        for (int t = 0; t < 2; t++) {
-          const int lr = 2 * sub + t;
-          float s = 0.f;
-          if (lr < nr) {
-#pragma unroll
-            for (int j = 0; j < MG_NJ; j++) {
-              const int v = vb + lane + 32 * j;
-              if (v < ve) {
-                const uint4 w = *reinterpret_cast<const uint4*>(st + (size_t)lr * row2 + (size_t)v * 16);
-                s = fmaf(dot16_dp4a(w, dr[j]), __half2float(ss[(size_t)lr * a.s2_stride + (v >> 1)]) * sxr[j], s);
-              }
-            }
-          }
-          acc[t] = warp_sum(s);
-        }
+        mg_dot2(st, row2, reinterpret_cast<const __half*>(st + (size_t)MG_W2_RS * row2), a.s2_stride, 2 * sub, nr, vb, ve, dr, sxr,
+                acc);
         mg_release(ring);
-        // Chunk partials of each row stay in shared memory until the phase
-        // ends; one fixed-order reduction per row follows the loop.
+        // The last warp to finish this tile adds its rows' partials in a
+        // fixed order and writes the residual.
+        const int e = cp_seq % MG_SEQ;
         if (lane == 0) {
-#pragma unroll
-          for (int t = 0; t < 2; t++)
-            if (2 * sub + t < nr) cpart[(r0 - rb2 + 2 * sub + t) * 4 + chunk] = acc[t];
+          cpart[e][(2 * sub) * 4 + chunk] = acc[0];
+          cpart[e][(2 * sub + 1) * 4 + chunk] = acc[1];
         }
+        __threadfence_block();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&cpcnt[e], 1) == MG_CW - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence_block();
+          if (lane < nr) {
+            const float lo = cpart[e][lane * 4 + 0];
+            const float hi = (cpart[e][lane * 4 + 1] + cpart[e][lane * 4 + 2]) + cpart[e][lane * 4 + 3];
+            const int r = r0 + lane;
+            xo[r] = __fadd_rn(__fadd_rn(xs[r], lo), hi);
+          }
+          __syncwarp();
+          if (lane == 0) cpcnt[e] = 0;
+        }
+        cp_seq++;
+        rows += nr;
       }
-      named_bar_sync(1, MG_CT);
-      for (int l = threadIdx.x; l < re2 - rb2; l += MG_CT) {
-        const float lo = cpart[l * 4 + 0];
-        const float hi = (cpart[l * 4 + 1] + cpart[l * 4 + 2]) + cpart[l * 4 + 3];
-        const int r = rb2 + l;
-        a.x_buf[r] = __fadd_rn(__fadd_rn(__ldcg(a.x_buf + r), lo), hi);
-      }
+      mg_publish(dl + 2, warp == 0 ? rows : 0);
     }
-    mg_grid_sync(a);
   }
 
-  // Final LayerNorm and lm_head with argmax (stablelm.go:380-385, model.go:622-630).
-  stage_in(a.x_buf, d);
+  // ---- Final LayerNorm and lm_head with argmax (stablelm.go:380-385, model.go:622-630).
+  mg_await(done + (a.L - 1) * MG_CTL + 2, d, a.err);
+  stage_in(xs, a.xl + (size_t)a.L * d, (uint32_t)d * 4u, nullptr, nullptr, 0);
   mg_ln_digits(xs, d, a.fnw, a.fnb, a.eps, dig, sx);
   load_regs(0, d / 16);
-  for (int r0 = rbh; r0 < reh; r0 += MG_W1_RS) {
-    const int nr = min(MG_W1_RS, reh - r0);
-    const uint8_t* st = mg_consume(ring, a.err);
-    const __half* ss = reinterpret_cast<const __half*>(st + (size_t)MG_W1_RS * d);
-    float acc[2];
-#pragma unroll
-    for (int t = 0; t < 2; t++) {
-      const int lr = 2 * warp + t;
-      float s = 0.f;
-      if (lr < nr) {
-#pragma unroll
-        for (int j = 0; j < MG_NJ; j++) {
-          const int v = lane + 32 * j;
-          if (v < d / 16) {
-            const uint4 w = *reinterpret_cast<const uint4*>(st + (size_t)lr * d + (size_t)v * 16);
-            s = fmaf(dot16_dp4a(w, dr[j]), __half2float(ss[(size_t)lr * a.sh_stride + (v >> 1)]) * sxr[j], s);
-          }
-        }
-      }
-      acc[t] = warp_sum(s);
+  for (;;) {
+    const uint8_t* st;
+    const int tag = mg_next_warp(ring, &st, a.err);
+    if (tag < 0) {
+      if (tag == -1) mg_release(ring);
+      break;
     }
+    const int r0 = tag * MG_W1_RS, nr = min(MG_W1_RS, a.V - r0);
+    float acc[2];
+    rows16(st, nr, a.sh_stride, acc);
     mg_release(ring);
     if (lane == 0) {
 #pragma unroll
@@ -731,21 +945,30 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
   if (threadIdx.x == 0) {
     unsigned long long b = 0;
     for (int w = 0; w < MG_CW; w++) b = bred[w] > b ? bred[w] : b;
-    atomicMax(a.keys + ((step + 1) & 1), b);
-  }
-  // The next launch reads pos and step after this one completes.
-  if (c == 0 && threadIdx.x == 0) {
-    *a.pos = pos + 1;
-    *a.step = step + 1;
+    if (b) atomicMax(a.keys + (par ^ 1), b);
+    // The last CTA to finish logs the token this step consumed, clears its key
+    // (the next step's argmax target) and advances the position; every CTA has
+    // read pos, step and the key by then.
+    __threadfence();
+    if (atomicAdd(done + a.L * MG_CTL + 3, 1) == G - 1) {
+      __threadfence();
+      const int cnt = a.out_count[0];
+      a.out_tokens[cnt] = token;
+      a.out_count[0] = cnt + 1;
+      a.keys[par] = 0ull;
+      *a.pos = pos + 1;
+      *a.step = step + 1;
+    }
+    if (in_phase > 0) mbar_drain(inbar, (in_phase - 1) & 1);
   }
 }
 
-// Logs the argmax of the last step (the final generated token).
+// Logs the argmax of the last persistent step (keys[step & 1]).
 __global__ void k_finish_mega(const unsigned long long* keys, const int* step, int* out_tokens, int* out_count) {
-  if (threadIdx.x == 0 && blockIdx.x == 0) {
-    const int c = out_count[0];
-    out_tokens[c] = argmax_index(keys[step[0] & 1]);
-    out_count[0] = c + 1;
+  if (threadIdx.x == 0) {
+    const int cnt = out_count[0];
+    out_tokens[cnt] = argmax_index(keys[step[0] & 1]);
+    out_count[0] = cnt + 1;
   }
 }
 

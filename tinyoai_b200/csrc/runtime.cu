@@ -121,7 +121,7 @@ struct tcu_model {
   bool mega = false;
   MegaLayer* mega_layers = nullptr;  // device array
   uint32_t mega_slot_bytes = 0, mega_off[5] = {0, 0, 0, 0, 0};
-  int mega_slots = 0, mega_split = 0;
+  int mega_slots = 0, mega_split = 0, mega_att_warp = 0;
   size_t mega_smem = 0;
 };
 
@@ -354,9 +354,11 @@ static int build_mega(tcu_model* m) {
   for (const Layer& ly : m->layers)
     if (ly.w1.fmt != FMT_Q8_0 || ly.w2.fmt != FMT_Q8_0) return TCU_OK;
   const int d = m->d, ff = m->ff, K2 = d + ff;
-  if (d % 32 || ff % 32 || d / 16 > 32 * MG_NJ || ff / 16 / 3 + 1 > 32 * MG_NJ || K2 > MG_MAXK) return TCU_OK;
-  if (m->H / m->KVH > 32 || m->hd % 2 || (m->H / m->KVH * m->hd) % 16 || d / 16 > MG_CT) return TCU_OK;
-  if (2 * ((d / 2 + m->sm_count - 1) / m->sm_count) > MG_CPART_ROWS) return TCU_OK;
+  const int G_q = m->H / m->KVH, n_plain = d + 2 * m->kvw;
+  if (d % 32 || ff % 32 || n_plain % MG_W1_RS || d / 16 > 32 * MG_NJ || ff / 16 / 3 + 1 > 32 * MG_NJ || K2 > MG_MAXK) return TCU_OK;
+  if (d / 16 > MG_CT || G_q > 32 || m->hd % 2 || (G_q * m->hd) % 16 || m->rope.pairs > 64 || m->rope.mode != 0) return TCU_OK;
+  cudaFuncAttributes fa;
+  CK(cudaFuncGetAttributes(&fa, k_decode_mega));
   const size_t w1 = (size_t)MG_W1_RS * (d + m->layers[0].w1.sstride * 2);
   const size_t w2 = (size_t)MG_W2_RS * (K2 + m->layers[0].w2.sstride * 2);
   const size_t hb = (size_t)MG_W1_RS * (d + m->head.sstride * 2);
@@ -365,14 +367,16 @@ static int build_mega(tcu_model* m) {
   while (split > m->P && (size_t)2 * split * m->hd * 4 > slot) split -= m->P;
   slot = std::max(slot, (size_t)2 * split * m->hd * 4);  // f32 KV worst case
   slot = (slot + 127) / 128 * 128;
-  const int G_q = m->H / m->KVH;
-  const size_t xs_floats = std::max<size_t>(K2, (size_t)G_q * m->hd + 2 * m->hd + (size_t)G_q * split);
-  uint32_t off_x = 128;
-  uint32_t off_dig = off_x + (uint32_t)((xs_floats * 4 + 127) / 128 * 128);
-  uint32_t off_sx = off_dig + (uint32_t)(((size_t)K2 / 4 * 12 + 127) / 128 * 128);
-  uint32_t off_part = off_sx + (uint32_t)(((size_t)K2 / 16 * 4 + 127) / 128 * 128);
-  uint32_t off_slots = off_part + (uint32_t)((MG_CPART_ROWS * 4 * 4 + 127) / 128 * 128);
-  const size_t limit = (size_t)m->gemv_smem_optin;
+  const size_t ghd = (size_t)G_q * m->hd;
+  const size_t att_warp = (2 * ghd + 2 * m->hd + (size_t)G_q * split + 3) / 4 * 4;  // q, k/v, scores, outputs
+  const size_t att_floats = att_warp * MG_CW;
+  auto r128 = [](size_t b) { return (uint32_t)((b + 127) / 128 * 128); };
+  const uint32_t off_x = MG_HDR;
+  const uint32_t off_att = off_x + r128((size_t)d * 4);
+  const uint32_t off_dig = off_att + r128(att_floats * 4);
+  const uint32_t off_sx = off_dig + r128((size_t)K2 / 16 * 48);
+  const uint32_t off_slots = off_sx + r128((size_t)K2 / 16 * 4);
+  const size_t limit = (size_t)m->gemv_smem_optin - fa.sharedSizeBytes;
   if (off_slots + 2 * slot > limit) return TCU_OK;
   const int nslots = (int)std::min<size_t>(MG_MAX_SLOTS, (limit - off_slots) / slot);
   std::vector<MegaLayer> hl(m->L);
@@ -387,16 +391,20 @@ static int build_mega(tcu_model* m) {
   m->mega_slot_bytes = (uint32_t)slot;
   m->mega_slots = nslots;
   m->mega_split = split;
+  m->mega_att_warp = (int)att_warp;
   m->mega_off[0] = off_x;
-  m->mega_off[1] = off_dig;
-  m->mega_off[2] = off_sx;
-  m->mega_off[3] = off_part;
+  m->mega_off[1] = off_att;
+  m->mega_off[2] = off_dig;
+  m->mega_off[3] = off_sx;
   m->mega_off[4] = off_slots;
   m->mega_smem = off_slots + (size_t)nslots * slot;
   CK(cudaFuncSetAttribute(k_decode_mega, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->mega_smem));
   int occ = 0;
   CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_decode_mega, MG_THREADS, m->mega_smem));
   m->mega = occ >= 1;
+  if (getenv("TCU_VERBOSE"))
+    fprintf(stderr, "tinyoai_b200: persistent decode %s (blocks/SM %d, regs %d, static smem %zu, dynamic smem %zu, slots %d x %u, split %d)\n",
+            m->mega ? "on" : "off", occ, fa.numRegs, (size_t)fa.sharedSizeBytes, m->mega_smem, nslots, (unsigned)slot, split);
   return TCU_OK;
 }
 
@@ -675,10 +683,14 @@ struct Work {
   int* err = nullptr;  // device error word of bounded waits (TCU_DEV_TIMEOUT)
   unsigned long long* keys = nullptr;  // persistent decode: argmax per step parity
   int* step = nullptr;
-  unsigned* bar = nullptr;  // persistent decode: grid barrier words
-  uint32_t* adig = nullptr;  // persistent decode: digits of [attention | SwiGLU]
-  float* asx = nullptr;      // and their block scales
-  int* bcnt = nullptr;       // SwiGLU block arrivals
+  // Persistent decode (decode_mega.cuh): per-layer inputs, published digits
+  // of [attention | SwiGLU] and their scales, work and completion counters.
+  float* xl = nullptr;
+  uint32_t* adig = nullptr;
+  float* asx = nullptr;
+  int asx_stride = 0;
+  int* grab = nullptr;
+  int* done = nullptr;
   std::vector<void*> allocs;
   ~Work() {
     for (void* p : allocs) cudaFree(p);
@@ -724,12 +736,14 @@ static int work_init(tcu_model* m, Work* w, int rows, int seqs, int logits_rows,
   TRY(w->get(&w->err, 1));
   TRY(w->get(&w->keys, 2));
   TRY(w->get(&w->step, 1));
-  TRY(w->get(&w->bar, 2));
-  {
+  if (m->mega) {
     const size_t nb16 = (size_t)(m->d + m->ff) / 16;
-    TRY(w->get(&w->adig, nb16 * 12));
-    TRY(w->get(&w->asx, (nb16 + 3) / 4 * 4));
-    TRY(w->get(&w->bcnt, (size_t)m->ff / 16 + 1));
+    w->asx_stride = (int)((nb16 + 3) / 4 * 4);
+    TRY(w->get(&w->xl, (size_t)(m->L + 1) * m->d));
+    TRY(w->get(&w->adig, (size_t)m->L * nb16 * 12));
+    TRY(w->get(&w->asx, (size_t)m->L * w->asx_stride));
+    TRY(w->get(&w->grab, (size_t)2 * (m->L + 1) * MG_CTL));
+    TRY(w->get(&w->done, (size_t)2 * (m->L + 1) * MG_CTL));
   }
   // The zeroing memsets ran on the legacy stream (see pool_get).
   CK(cudaDeviceSynchronize());
@@ -1805,24 +1819,25 @@ static int launch_mega(tcu_session* s) {
   a.out_tokens = s->w.out_tokens;
   a.out_count = s->w.out_count;
   a.logits = s->w.logits;
-  a.x_buf = s->w.x;
+  a.xl = s->w.xl;
   a.qkv = s->w.qkv;
-  a.ah = s->w.ah;
   a.part = s->w.part;
   a.counters = s->w.counters;
-  a.bar = s->w.bar;
   a.adig = s->w.adig;
   a.asx = s->w.asx;
-  a.bcnt = s->w.bcnt;
+  a.asx_stride = s->w.asx_stride;
+  a.att_warp = m->mega_att_warp;
+  a.grab = s->w.grab;
+  a.done = s->w.done;
   a.dig_bytes = (uint32_t)((m->d + m->ff) / 16 * 48);
   a.sx_bytes = (uint32_t)(((m->d + m->ff) / 16 * 4 + 15) / 16 * 16);
   a.err = s->w.err;
   a.slot_bytes = m->mega_slot_bytes;
   a.nslots = m->mega_slots;
   a.off_x = m->mega_off[0];
-  a.off_dig = m->mega_off[1];
-  a.off_sx = m->mega_off[2];
-  a.off_part = m->mega_off[3];
+  a.off_att = m->mega_off[1];
+  a.off_dig = m->mega_off[2];
+  a.off_sx = m->mega_off[3];
   a.off_slots = m->mega_off[4];
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(m->sm_count);
@@ -1864,11 +1879,12 @@ int tcu_session_generate_greedy(tcu_session* s, int32_t prefix, const int32_t* t
     CK(cudaMemsetAsync(s->w.keys + 1, 0, sizeof(unsigned long long), s->stream));
     CK(cudaMemsetAsync(s->w.step, 0, sizeof(int), s->stream));
     CK(cudaMemsetAsync(s->w.out_count, 0, sizeof(int), s->stream));
-    // Arrival counters start at zero (a run cut short by a timeout may have
-    // left them set).
-    CK(cudaMemsetAsync(s->w.bar, 0, sizeof(unsigned), s->stream));
+    // Work and arrival counters start at zero (a run cut short by a timeout
+    // may have left them set).
+    const size_t nctl = (size_t)2 * (m->L + 1) * MG_CTL * sizeof(int);
+    CK(cudaMemsetAsync(s->w.grab, 0, nctl, s->stream));
+    CK(cudaMemsetAsync(s->w.done, 0, nctl, s->stream));
     CK(cudaMemsetAsync(s->w.counters, 0, (size_t)m->KVH * sizeof(int), s->stream));
-    CK(cudaMemsetAsync(s->w.bcnt, 0, ((size_t)m->ff / 16 + 1) * sizeof(int), s->stream));
     for (int i = 1; rc == TCU_OK && i < steps; i++) {
       rc = launch_mega(s);
       if (rc == TCU_OK && s->prof.on) {
