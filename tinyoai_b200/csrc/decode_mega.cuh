@@ -356,6 +356,124 @@ __device__ __forceinline__ void mg_await(const int* ctr, int target, int* err) {
   named_bar_sync(1, MG_CT);
 }
 
+// Scores, softmax and weighted values of one attention unit, by one warp
+// (stablelm.go:401-427 with the history split): K and V tiles of n_hist
+// tokens in shared memory (float32 or binary16 rows of hd values), this
+// position's k, v (float32, already rounded to the KV precision) in cur.
+// Writes the unit's partial (hd outputs, max, sum) per query head to pg.
+// Scores: a lane per token reads its K row in 16-byte chunks from a
+// token-dependent starting chunk (conflict-free); values: a lane per chunk
+// of dimensions with one accumulator per dimension.
+template <bool HALF>
+__device__ __forceinline__ void mg_unit_core(const MegaArgs& a, const uint8_t* ktile, uint32_t vofs, const float* wq, const float* cur,
+                                             float* sc, int G_q, int hd, int n_hist, int nt, bool has_cur, float* pg, int s) {
+  constexpr int CE = HALF ? 8 : 4;  // values per 16-byte chunk
+  const int lane = threadIdx.x & 31;
+  const int nch = hd / CE;
+  const size_t row_bytes = (size_t)hd * (HALF ? 2 : 4);
+  const uint8_t* vtile = ktile + vofs;
+  for (int t = lane; t < n_hist; t += 32) {
+    const uint8_t* krow = ktile + (size_t)t * row_bytes;
+    for (int hh = 0; hh < G_q; hh++) {
+      const float* q = wq + hh * hd;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      int c = t % nch;
+      for (int j = 0; j < nch; j++) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(krow + (size_t)c * 16);
+        if (HALF) {
+          const __half2* h = reinterpret_cast<const __half2*>(&raw);
+          const float4 q0 = *reinterpret_cast<const float4*>(q + 8 * c);
+          const float4 q1 = *reinterpret_cast<const float4*>(q + 8 * c + 4);
+          const float2 k0 = __half22float2(h[0]), k1 = __half22float2(h[1]), k2 = __half22float2(h[2]), k3 = __half22float2(h[3]);
+          a0 = fmaf(q0.x, k0.x, a0);
+          a1 = fmaf(q0.y, k0.y, a1);
+          a2 = fmaf(q0.z, k1.x, a2);
+          a3 = fmaf(q0.w, k1.y, a3);
+          a0 = fmaf(q1.x, k2.x, a0);
+          a1 = fmaf(q1.y, k2.y, a1);
+          a2 = fmaf(q1.z, k3.x, a2);
+          a3 = fmaf(q1.w, k3.y, a3);
+        } else {
+          const float4 k4 = *reinterpret_cast<const float4*>(&raw);
+          const float4 q4 = *reinterpret_cast<const float4*>(q + 4 * c);
+          a0 = fmaf(q4.x, k4.x, a0);
+          a1 = fmaf(q4.y, k4.y, a1);
+          a2 = fmaf(q4.z, k4.z, a2);
+          a3 = fmaf(q4.w, k4.w, a3);
+        }
+        c = c + 1 == nch ? 0 : c + 1;
+      }
+      sc[hh * a.split + t] = __fdiv_rn((a0 + a1) + (a2 + a3), a.scale);
+    }
+  }
+  if (has_cur)
+    for (int hh = 0; hh < G_q; hh++) {
+      float acc = 0.f;
+      for (int i = lane; i < hd; i += 32) acc = fmaf(wq[hh * hd + i], cur[i], acc);
+      acc = warp_sum(acc);
+      if (lane == 0) sc[hh * a.split + nt - 1] = __fdiv_rn(acc, a.scale);
+    }
+  __syncwarp();
+  float mloc = 0.f, lloc = 0.f;  // lane hh holds head hh's max and sum
+  for (int hh = 0; hh < G_q; hh++) {
+    float mx = -INFINITY;
+    for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, sc[hh * a.split + t]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float lsum = 0.f;
+    for (int t = lane; t < nt; t += 32) {
+      const float p = expf(sc[hh * a.split + t] - mx);
+      sc[hh * a.split + t] = p;
+      lsum += p;
+    }
+    lsum = warp_sum(lsum);
+    if (lane == hh) {
+      mloc = mx;
+      lloc = lsum;
+    }
+  }
+  __syncwarp();
+  for (int hh = 0; hh < G_q; hh++) {
+    const float* p = sc + hh * a.split;
+    float* po = pg + ((size_t)hh * a.max_splits + s) * (hd + 2);
+    for (int c = lane; c < nch; c += 32) {
+      float acc[CE];
+#pragma unroll
+      for (int k = 0; k < CE; k++) acc[k] = 0.f;
+      for (int t = 0; t < n_hist; t++) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(vtile + (size_t)t * row_bytes + (size_t)c * 16);
+        const float pt = p[t];
+        if (HALF) {
+          const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const float2 v2 = __half22float2(h[k]);
+            acc[2 * k] = fmaf(pt, v2.x, acc[2 * k]);
+            acc[2 * k + 1] = fmaf(pt, v2.y, acc[2 * k + 1]);
+          }
+        } else {
+          const float4 v4 = *reinterpret_cast<const float4*>(&raw);
+          acc[0] = fmaf(pt, v4.x, acc[0]);
+          acc[1] = fmaf(pt, v4.y, acc[1]);
+          acc[2] = fmaf(pt, v4.z, acc[2]);
+          acc[3] = fmaf(pt, v4.w, acc[3]);
+        }
+      }
+      if (has_cur) {
+        const float pt = p[nt - 1];
+#pragma unroll
+        for (int k = 0; k < CE; k++) acc[k] = fmaf(pt, cur[hd + c * CE + k], acc[k]);
+      }
+#pragma unroll
+      for (int k = 0; k < CE; k++) po[c * CE + k] = acc[k];
+    }
+    if (lane == hh) {
+      po[hd] = mloc;
+      po[hd + 1] = lloc;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
   extern __shared__ __align__(128) uint8_t mg_smem[];
   __shared__ float swg[MG_SEQ][16], swu[MG_SEQ][16];  // gate / up of in-flight gate/up tiles
@@ -740,76 +858,11 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
             kv_store(a.kv, a.kv.v, o + e, cur[hd + e]);
           }
         }
-        const uint8_t* ktile = st;
-        const uint8_t* vtile = st + (size_t)pages_per_split * page_bytes;
-        // Scores: lane per token, four partial sums over the dimensions from a
-        // token-dependent starting offset (conflict-free shared-memory reads).
-        for (int t = lane; t < nt; t += 32) {
-          const bool is_cur = has_cur && t == nt - 1;
-          for (int hh = 0; hh < G_q; hh++) {
-            const float* q = wq + hh * hd;
-            const uint8_t* krow = ktile + (size_t)t * hd * (a.kv.half ? 2 : 4);
-            auto kat = [&](int i) { return is_cur ? cur[i] : kv_ld(krow, a.kv.half, i); };
-            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-            int i = t % hd, j = 0;
-            for (; j + 4 <= hd; j += 4) {
-              a0 = fmaf(q[i], kat(i), a0);
-              i = i + 1 == hd ? 0 : i + 1;
-              a1 = fmaf(q[i], kat(i), a1);
-              i = i + 1 == hd ? 0 : i + 1;
-              a2 = fmaf(q[i], kat(i), a2);
-              i = i + 1 == hd ? 0 : i + 1;
-              a3 = fmaf(q[i], kat(i), a3);
-              i = i + 1 == hd ? 0 : i + 1;
-            }
-            for (; j < hd; j++) {
-              a0 = fmaf(q[i], kat(i), a0);
-              i = i + 1 == hd ? 0 : i + 1;
-            }
-            sc[hh * a.split + t] = __fdiv_rn((a0 + a1) + (a2 + a3), a.scale);
-          }
-        }
-        __syncwarp();
-        float mloc = 0.f, lloc = 0.f;  // lane hh holds head hh's max and sum
-        for (int hh = 0; hh < G_q; hh++) {
-          float mx = -INFINITY;
-          for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, sc[hh * a.split + t]);
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-          float lsum = 0.f;
-          for (int t = lane; t < nt; t += 32) {
-            const float p = expf(sc[hh * a.split + t] - mx);
-            sc[hh * a.split + t] = p;
-            lsum += p;
-          }
-          lsum = warp_sum(lsum);
-          if (lane == hh) {
-            mloc = mx;
-            lloc = lsum;
-          }
-        }
-        __syncwarp();
-        // Weighted values: lane per dimension, four partial sums over tokens.
         float* pg = a.part + (size_t)(g * G_q) * a.max_splits * (hd + 2);
-        for (int e = lane; e < ghd; e += 32) {
-          const int hh = e / hd, i = e % hd;
-          const float* p = sc + hh * a.split;
-          float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-          int t = 0;
-          for (; t + 4 <= n_hist; t += 4) {
-            a0 = fmaf(p[t], kv_ld(vtile, a.kv.half, (size_t)t * hd + i), a0);
-            a1 = fmaf(p[t + 1], kv_ld(vtile, a.kv.half, (size_t)(t + 1) * hd + i), a1);
-            a2 = fmaf(p[t + 2], kv_ld(vtile, a.kv.half, (size_t)(t + 2) * hd + i), a2);
-            a3 = fmaf(p[t + 3], kv_ld(vtile, a.kv.half, (size_t)(t + 3) * hd + i), a3);
-          }
-          for (; t < n_hist; t++) a0 = fmaf(p[t], kv_ld(vtile, a.kv.half, (size_t)t * hd + i), a0);
-          if (has_cur) a1 = fmaf(p[nt - 1], cur[hd + i], a1);
-          pg[((size_t)hh * a.max_splits + s) * (hd + 2) + i] = (a0 + a1) + (a2 + a3);
-        }
-        if (lane < G_q) {
-          pg[((size_t)lane * a.max_splits + s) * (hd + 2) + hd] = mloc;
-          pg[((size_t)lane * a.max_splits + s) * (hd + 2) + hd + 1] = lloc;
-        }
+        if (a.kv.half)
+          mg_unit_core<true>(a, st, pages_per_split * page_bytes, wq, cur, sc, G_q, hd, n_hist, nt, has_cur, pg, s);
+        else
+          mg_unit_core<false>(a, st, pages_per_split * page_bytes, wq, cur, sc, G_q, hd, n_hist, nt, has_cur, pg, s);
         mg_release(ring);
         __syncwarp();
         int last = 0;
