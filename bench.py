@@ -190,9 +190,9 @@ def run_b200(args):
     import torch
     import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    from tinyoai_b200 import replicas
+
+    world, rank, local = replicas.world()
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
@@ -231,8 +231,7 @@ def run_b200(args):
         step()
     torch.cuda.synchronize()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
+    replicas.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
         start = torch.cuda.Event(enable_timing=True)
@@ -242,15 +241,12 @@ def run_b200(args):
             toks = step(evs[i])
         end.record(stream)
         torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    replicas.barrier()
     total_ms = start.elapsed_time(end)
     pf_ms = sum(e[0].elapsed_time(e[1]) for e in evs)
     dc_ms = sum(e[1].elapsed_time(e[2]) for e in evs)
-    t = torch.tensor([total_ms, pf_ms, dc_ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, pf_ms, dc_ms = t.tolist()
+    # Whole-job time = the slowest replica's (max over ranks, on the device).
+    total_ms, pf_ms, dc_ms = replicas.max_over_ranks([total_ms, pf_ms, dc_ms], device="cuda")
 
     # End to end through the public API: host prompt in, host tokens out,
     # one call per step (tcu_session_generate_greedy), host-timed.
@@ -260,9 +256,7 @@ def run_b200(args):
         t0 = time.perf_counter()
         sess.generate_greedy(0, prompt, GEN)
         e2e_ms.append((time.perf_counter() - t0) * 1e3)
-    e2e = torch.tensor([statistics.median(e2e_ms)], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+    (e2e_med,) = replicas.max_over_ranks([statistics.median(e2e_ms)], device="cuda")
 
     # Stage profile of one more step (CUDA events around every kernel, on the
     # stream the kernels run on): launch counts and the dominant kernel's time.
@@ -272,13 +266,12 @@ def run_b200(args):
     prof = sess.profile_read(reset=True)
     sess.profile(False)
 
-    if world > 1:
-        dist.barrier()
+    replicas.barrier()
     line = None
     if rank == 0:
         hbm, peak_kind = peaks()
         tok_per_step = PROMPT + GEN
-        value = world * tok_per_step * args.steps / (total_ms / 1e3)
+        value = replicas.aggregate_rate(tok_per_step * args.steps, world, total_ms / 1e3)
         launches = sum(v[0] for v in prof.values())
         avg_T = PROMPT + GEN / 2
         step_bytes, w1_bytes = decode_bytes(cfg, avg_T)
@@ -310,7 +303,7 @@ def run_b200(args):
                          "decode_step_gbs": dec_gbs, "decode_step_frac": dec_gbs / hbm},
             "profile": {k: {"launches": v[0], "ms": round(v[1], 3)} for k, v in prof.items()},
             "clocks": clocks.summary(),
-            "e2e": {"value": world * tok_per_step / (e2e.item() / 1e3), "unit": "tok/s",
+            "e2e": {"value": replicas.aggregate_rate(tok_per_step, world, e2e_med / 1e3), "unit": "tok/s",
                     "h2d_bytes_per_step": PROMPT * 4, "d2h_bytes_per_step": GEN * 4},
             "gpu_launches": int(launches * args.steps),
             "last_tokens": [int(x) for x in toks[:8]],
