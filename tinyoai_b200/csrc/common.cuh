@@ -21,7 +21,8 @@ struct DMat {
   int rows, cols;
   const uint8_t* w;
   const __half* s;
-  int sstride;  // Q8_0 scale row stride in halves
+  int sstride;    // Q8_0 scale row stride in halves
+  int tc_sw = 0;  // Q8_0: power of two applied before the tensor-core split (gemm_tc.cuh)
 };
 
 __device__ __forceinline__ float bf16_bits_to_float(uint32_t b) { return __uint_as_float(b << 16); }

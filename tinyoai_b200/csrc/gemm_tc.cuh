@@ -1,0 +1,377 @@
+// Prefill / batched projection on the 5th-generation tensor cores:
+// D[r][t] = sum_k W[r][k] * X[t][k] for a tile of 128 weight rows and up to
+// 256 tokens, accumulated in tensor memory (TMEM) by tcgen05.mma.
+//
+// Replaces weightTensor.mulBatch (matmul.go:55-95) for Q8_0 weights with the
+// epilogues of the CUDA-core path (gemm_simt.cuh). Exactness: a Q8_0 weight
+// s*q has at most 19 significant bits and an activation 24, more than one
+// binary16 operand holds, so both sides are split into an exact binary16
+// pair -- W' = W * 2^sw = Wh + Wl (Wh = fp16(s'q), Wl = fp16(fma(s', q, -Wh)))
+// and X' = X * 2^sx(t) = Xh + Xl -- and three products Wh.Xh + Wh.Xl + Wl.Xh
+// are accumulated in float32; the dropped terms are ~2^-22 of the result. The
+// power-of-two scales keep the low halves out of the subnormal range and are
+// removed exactly in the epilogue.
+//
+// Warps: 0-3 dequantise the weight tile (then run the epilogue from TMEM),
+// warp 4 owns TMEM and issues the MMAs (one thread), warp 5 issues the TMA
+// loads of the activation tiles. Two shared-memory buffers; every wait is
+// bounded. All copies read this GPU's own memory into this CTA's shared
+// memory.
+#pragma once
+#include <cuda.h>
+#include "common.cuh"
+#include "gemv.cuh"
+#include "tma.cuh"
+
+namespace tcu {
+
+constexpr int TC_BM = 128;     // weight rows per tile (MMA M)
+constexpr int TC_BK = 64;      // K per stage (one 128-byte swizzle atom of binary16)
+constexpr int TC_MAXN = 256;   // tokens per tile (MMA N)
+constexpr int TC_THREADS = 192;
+constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;      // 16 KB per binary16 weight tile
+constexpr int TC_B_BYTES = TC_MAXN * TC_BK * 2;    // 32 KB per binary16 activation tile
+constexpr int TC_BUF_BYTES = 2 * TC_A_BYTES + 2 * TC_B_BYTES;
+constexpr int TC_SMEM = 2 * TC_BUF_BYTES + 1024 + 256;  // two buffers, 1 KB alignment slack, barriers
+
+struct TcArgs {
+  DMat W;             // Q8_0 weights [rows][cols]
+  int n;              // tokens
+  int n_tile;         // tokens per CTA tile (multiple of 16, <= TC_MAXN)
+  int n_pad;          // rows of one half of the activation split (hi rows, then lo rows)
+  const int* sx;      // [n] per-token power of two of the split
+  int sw;             // power of two of the weight split
+  // epilogue (as GemmArgs)
+  float* out;
+  int out_stride;
+  int n_plain;
+  float* glu_out;
+  int glu_stride;
+  int glu_act;
+  float* resid;
+  int resid_stride;
+  int k_split;        // EPI_RESID2: K where the second accumulator starts (multiple of TC_BK)
+  float* part;        // split K: partial sums [gridDim.z][n][rows] (nullptr: apply the epilogue)
+  int k_per_z;        // split K: columns per z slice (multiple of TC_BK)
+  int* err;
+};
+
+// 2^e exactly, for e in [-126, 127].
+__device__ __forceinline__ float tc_pow2(int e) { return __int_as_float((e + 127) << 23); }
+
+__device__ __forceinline__ uint64_t tc_smem_desc(uint32_t saddr) {
+  // K-major operand, 128-byte swizzle: 8-row groups 1024 bytes apart (SBO),
+  // LBO unused (1), descriptor version 1, layout type 2 (SWIZZLE_128B).
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor: float32 accumulator, binary16 A and B, both
+// K-major, N = n, M = 128.
+__device__ __forceinline__ uint32_t tc_idesc(int n) { return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24); }
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// 2-D TMA load of a box at (x = k, y = row) into shared memory, completing on bar.
+__device__ __forceinline__ void tc_tma_load(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                   smem_u32(dst)),
+               "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Byte offset of element (row, k) (k < 64) in a K-major 128-byte-swizzled
+// tile: rows in 8-row groups of 1024 bytes, 16-byte chunk c of row r stored
+// at chunk c ^ (r % 8).
+__device__ __forceinline__ uint32_t tc_sw128(int row, int k) {
+  return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k * 2) >> 4) ^ (row & 7)) << 4) + ((k * 2) & 15));
+}
+
+// Binary16 pair of 8 int8 weights times the scale s' (binary16): the eight
+// values 1024 + (q ^ 0x80) are built by byte permutation and 1152 subtracted,
+// which is exact; Wh = q * s' rounded, Wl = fma(q, s', -Wh) rounded (exact).
+__device__ __forceinline__ void tc_dequant8(uint2 q, __half2 s2, uint4& hi, uint4& lo) {
+  const uint32_t w[2] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u};
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const uint32_t p = __byte_perm(w[i], 0x64646464u, j == 0 ? 0x7170 : 0x7372);  // bytes (2j, 2j+1) as 0x64xx
+      const __half2 qv = __hsub2(*reinterpret_cast<const __half2*>(&p), bias);
+      const __half2 wh = __hmul2(qv, s2);
+      const __half2 wl = __hfma2(qv, s2, __hneg2(wh));
+      h[2 * i + j] = *reinterpret_cast<const uint32_t*>(&wh);
+      l[2 * i + j] = *reinterpret_cast<const uint32_t*>(&wl);
+    }
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
+  extern __shared__ uint8_t tc_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * TC_BUF_BYTES);
+  uint64_t* x_full = bars;         // [2] activation tiles landed
+  uint64_t* w_full = bars + 2;     // [2] weight tiles written
+  uint64_t* mma_done = bars + 4;   // [2] MMAs reading the buffer finished
+  uint64_t* acc_full = bars + 6;   // accumulators final
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int R = a.W.rows, K = a.W.cols;
+  const int r0 = blockIdx.x * TC_BM, t0 = blockIdx.y * a.n_tile;
+  const int k_begin = a.part ? blockIdx.z * a.k_per_z : 0;
+  const int k_end = a.part ? min(K, k_begin + a.k_per_z) : K;
+  const int iters = (k_end - k_begin + TC_BK - 1) / TC_BK;
+  const int NT = a.n_tile;
+  const bool two_acc = (EPI == EPI_RESID2) && !a.part;
+  const uint32_t tmem_cols = two_acc ? 2 * TC_MAXN : TC_MAXN;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&w_full[i], 128);
+      mbar_init(&mma_done[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+
+  auto buf = [&](int b) { return smem + (size_t)b * TC_BUF_BYTES; };
+
+  if (warp == 5) {
+    // ---- activation tiles: Xh rows [t0, t0 + NT), Xl rows n_pad + the same
+    if (lane == 0) {
+      const uint32_t bytes = (uint32_t)(2 * NT * TC_BK * 2);
+      for (int i = 0; i < iters; i++) {
+        const int b = i & 1;
+        if (i >= 2) mbar_wait(&mma_done[b], ((i >> 1) - 1) & 1, a.err);
+        mbar_expect_tx(&x_full[b], bytes);
+        const int k = k_begin + i * TC_BK;
+        tc_tma_load(buf(b) + 2 * TC_A_BYTES, &xmap, k, t0, &x_full[b]);
+        tc_tma_load(buf(b) + 2 * TC_A_BYTES + TC_B_BYTES, &xmap, k, a.n_pad + t0, &x_full[b]);
+      }
+    }
+  } else if (warp == 4) {
+    // ---- MMA issue (one thread): 4 K16 steps x (Wh.Xh, Wh.Xl, Wl.Xh) per stage
+    if (lane == 0) {
+      const uint32_t idesc = tc_idesc(NT);
+      bool first0 = true, first1 = true;
+      for (int i = 0; i < iters; i++) {
+        const int b = i & 1;
+        mbar_wait(&x_full[b], (i >> 1) & 1, a.err);
+        mbar_wait(&w_full[b], (i >> 1) & 1, a.err);
+        tc_fence_after();
+        const int k = k_begin + i * TC_BK;
+        const bool second = two_acc && k >= a.k_split;
+        const uint32_t d = tmem + (second ? TC_MAXN : 0);
+        bool& first = second ? first1 : first0;
+        const uint32_t sa = smem_u32(buf(b)), sb = sa + 2 * TC_A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < TC_BK / 16; kk++) {
+          const uint32_t off = kk * 32;  // 16 binary16 columns
+          const uint64_t wh = tc_smem_desc(sa + off), wl = tc_smem_desc(sa + TC_A_BYTES + off);
+          const uint64_t xh = tc_smem_desc(sb + off), xl = tc_smem_desc(sb + TC_B_BYTES + off);
+          tc_mma(d, wh, xh, idesc, first ? 0u : 1u);
+          first = false;
+          tc_mma(d, wh, xl, idesc, 1u);
+          tc_mma(d, wl, xh, idesc, 1u);
+        }
+        tc_commit(&mma_done[b]);
+      }
+      tc_commit(acc_full);
+    }
+  } else {
+    // ---- weight tiles (warps 0-3): 4 threads per row, 16 bytes each
+    const int tid = threadIdx.x;  // 0..127
+    const int kc = (tid & 3) * 16;
+    const float wscale = tc_pow2(a.sw);
+    for (int i = 0; i < iters; i++) {
+      const int b = i & 1;
+      if (i >= 2) mbar_wait(&mma_done[b], ((i >> 1) - 1) & 1, a.err);
+      uint8_t* ah = buf(b);
+      uint8_t* al = ah + TC_A_BYTES;
+      const int k0 = k_begin + i * TC_BK + kc;
+      for (int rr = tid >> 2; rr < TC_BM; rr += 32) {
+        const int r = r0 + rr;
+        uint4 h0 = make_uint4(0, 0, 0, 0), l0 = h0, h1 = h0, l1 = h0;
+        if (r < R && k0 < k_end) {
+          const uint4 q = *reinterpret_cast<const uint4*>(a.W.w + (size_t)r * K + k0);
+          const float s = __half2float(a.W.s[(size_t)r * a.W.sstride + k0 / 32]) * wscale;
+          const __half2 s2 = __float2half2_rn(s);
+          tc_dequant8(make_uint2(q.x, q.y), s2, h0, l0);
+          tc_dequant8(make_uint2(q.z, q.w), s2, h1, l1);
+          if (k0 + 8 > k_end) h0 = l0 = make_uint4(0, 0, 0, 0);
+          if (k0 + 16 > k_end) h1 = l1 = make_uint4(0, 0, 0, 0);
+        }
+        *reinterpret_cast<uint4*>(ah + tc_sw128(rr, kc)) = h0;
+        *reinterpret_cast<uint4*>(ah + tc_sw128(rr, kc + 8)) = h1;
+        *reinterpret_cast<uint4*>(al + tc_sw128(rr, kc)) = l0;
+        *reinterpret_cast<uint4*>(al + tc_sw128(rr, kc + 8)) = l1;
+      }
+      // Generic writes must be visible to the tensor core (async proxy).
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&w_full[b]);
+    }
+    // ---- epilogue: warp w reads TMEM lanes 32w..32w+31 (weight rows)
+    mbar_wait(acc_full, 0, a.err);
+    tc_fence_after();
+    const int rr = warp * 32 + lane, r = r0 + rr;
+    const float wunscale = tc_pow2(-a.sw);
+    for (int c0 = 0; c0 < NT; c0 += 16) {
+      float v[16], v2[16];
+      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + c0;
+      tc_ld16(taddr, v);
+      if (two_acc) tc_ld16(taddr + TC_MAXN, v2);
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const int t = t0 + c0 + j;
+        const bool ok = t < a.n && r < R;
+        const float sc = ok ? wunscale * tc_pow2(-a.sx[t]) : 0.f;
+        const float lo = v[j] * sc;
+        if (a.part) {
+          if (ok) a.part[((size_t)blockIdx.z * a.n + t) * R + r] = lo;
+          continue;
+        }
+        if constexpr (EPI == EPI_STORE) {
+          if (ok) a.out[(size_t)t * a.out_stride + r] = lo;
+        } else if constexpr (EPI == EPI_GLU) {
+          const float up = __shfl_xor_sync(0xffffffffu, lo, 1);
+          if (ok) {
+            if (r < a.n_plain)
+              a.out[(size_t)t * a.out_stride + r] = lo;
+            else if (((r - a.n_plain) & 1) == 0)
+              a.glu_out[(size_t)t * a.glu_stride + ((r - a.n_plain) >> 1)] =
+                  a.glu_act ? silu_mul_llama(lo, up) : silu_mul_stablelm(lo, up);
+          }
+        } else if constexpr (EPI == EPI_RESID1) {
+          if (ok) {
+            float* x = a.resid + (size_t)t * a.resid_stride + r;
+            *x = __fadd_rn(*x, lo);
+          }
+        } else if constexpr (EPI == EPI_RESID2) {
+          if (ok) {
+            float* x = a.resid + (size_t)t * a.resid_stride + r;
+            *x = __fadd_rn(__fadd_rn(*x, lo), v2[j] * sc);
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols));
+  }
+}
+
+// Exact binary16 split of activation rows for the tensor-core GEMM: per
+// token t, sx(t) = 13 - exponent of max|X[t]| (a power of two), then
+// Xh = fp16(X * 2^sx), Xl = fp16(X * 2^sx - Xh). out: [2][n_pad][K] binary16
+// (rows >= n are left as they are; the TMA loads zeros past the map).
+__global__ void k_split_f16(const float* X, int ldx, int n, int K, int n_pad, __half* out, int* sx) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const float* x = X + (size_t)t * ldx;
+  float mx = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(x[k]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0) {
+      int e = 0;
+      if (m > 0.f) frexpf(m, &e);  // m in [2^(e-1), 2^e)
+      red[0] = (float)(m > 0.f ? 13 - e : 0);
+    }
+  }
+  __syncthreads();
+  const int s = (int)red[0];
+  if (threadIdx.x == 0) sx[t] = s;
+  const float scale = tc_pow2(s);
+  __half* hi = out + (size_t)t * K;
+  __half* lo = out + ((size_t)n_pad + t) * K;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const float v = x[k] * scale;
+    const __half h = __float2half_rn(v);
+    hi[k] = h;
+    lo[k] = __float2half_rn(v - __half2float(h));
+  }
+}
+
+// Largest |scale| of a Q8_0 scale plane (rows x nb valid blocks), as the
+// bits of a non-negative float (their unsigned order is the float order).
+__global__ void k_scale_absmax(const __half* s, int rows, int sstride, int nb, unsigned* out) {
+  unsigned m = 0;
+  const size_t total = (size_t)rows * nb;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const float v = fabsf(__half2float(s[(i / nb) * sstride + i % nb]));
+    if (v == v) m = max(m, __float_as_uint(v));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(out, m);
+}
+
+// Split-K reduction of the out/down rows with the parallel residual
+// (stablelm.go:365-377): slices [0, z_lo) cover the attention columns, the
+// rest the SwiGLU columns; x = (x + lo) + hi, each sum in slice order.
+__global__ void k_splitk_resid(const float* part, int z_lo, int z_n, int n, int R, float* resid, int stride) {
+  const size_t total = (size_t)n * R;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / R), r = (int)(i % R);
+    float lo = 0.f, hi = 0.f;
+    for (int z = 0; z < z_lo; z++) lo += part[(size_t)z * total + i];
+    for (int z = z_lo; z < z_n; z++) hi += part[(size_t)z * total + i];
+    float* x = resid + (size_t)t * stride + r;
+    *x = z_lo < z_n ? __fadd_rn(__fadd_rn(*x, lo), hi) : __fadd_rn(*x, lo);
+  }
+}
+
+}  // namespace tcu

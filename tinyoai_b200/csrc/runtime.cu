@@ -26,6 +26,8 @@
 #include "gemv.cuh"
 #include "gemv_stream.cuh"
 #include "decode_mega.cuh"
+#include "gemm_tc.cuh"
+#include <cudaTypedefs.h>
 #include "misc.cuh"
 
 using namespace tcu;
@@ -117,6 +119,8 @@ struct tcu_model {
   int sm_count = 148;
   int gemv_smem_optin = 0;
   bool disable_stream = false;  // TCU_DECODE_KERNELS=portable selects the non-TMA kernels
+  bool use_tc = true;           // tensor-core prefill GEMM (TCU_GEMM=simt selects the CUDA-core one)
+  unsigned* scratch_u32 = nullptr;
   // Persistent decode step (decode_mega.cuh): Q8_0 StableLM shapes that fit.
   bool mega = false;
   MegaLayer* mega_layers = nullptr;  // device array
@@ -295,6 +299,8 @@ static void init_common(tcu_model* m, const tcu_load_options* o) {
   cudaDeviceGetAttribute(&m->gemv_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
   const char* k = getenv("TCU_DECODE_KERNELS");
   m->disable_stream = k && strcmp(k, "portable") == 0;
+  const char* g = getenv("TCU_GEMM");
+  m->use_tc = !(g && strcmp(g, "simt") == 0);
 }
 
 // StableLM rotary table (stablelm.go:309-326): per position and rotary pair,
@@ -347,6 +353,8 @@ static int check_tensor(const tcu_tensor* t, const std::string& name, int64_t ro
 // its shared memory: Q8_0 weights everywhere, hidden <= 2560 (one register
 // chunk per warp), intermediate <= 3 * 2560, head_dim such that an attention
 // unit's K and V tiles fit one ring slot.
+static int set_tc_shifts(tcu_model* m);
+
 static int build_mega(tcu_model* m) {
   m->mega = false;
   if (m->disable_stream || m->arch != ARCH_STABLELM) return TCU_OK;
@@ -500,6 +508,7 @@ static int stablelm_load(const tcu_stablelm_config* c, const tcu_tensor* t, int 
   if ((rc = decode_vec(find_tensor(t, n, "model.norm.weight"), d, fw)) || (rc = decode_vec(find_tensor(t, n, "model.norm.bias"), d, fb)) ||
       (rc = upload_floats(m, fw, &m->fnw)) || (rc = upload_floats(m, fb, &m->fnb)))
     return bail(rc);
+  if ((rc = set_tc_shifts(m))) return bail(rc);
   if ((rc = build_mega(m))) return bail(rc);
   *out = m;
   return TCU_OK;
@@ -586,6 +595,7 @@ static int llama_load(const void* ck, uint64_t nbytes, const tcu_load_options* o
   m->rope.table = (const float2*)p;
   m->rope.pairs = (int)(hs / 2);
   m->rope.mode = 1;
+  if ((rc = set_tc_shifts(m))) return bail(rc);
   *out = m;
   return TCU_OK;
 }
@@ -691,9 +701,19 @@ struct Work {
   int asx_stride = 0;
   int* grab = nullptr;
   int* done = nullptr;
+  // Tensor-core GEMM workspace (allocated on first use): binary16 split of
+  // the activations [2][tc_npad][tc_kmax], their shifts, split-K partials.
+  __half* tc_split = nullptr;
+  int* tc_sx = nullptr;
+  float* tc_part = nullptr;
+  int tc_npad = 0, tc_kmax = 0;
+  size_t tc_part_floats = 0;
   std::vector<void*> allocs;
   ~Work() {
     for (void* p : allocs) cudaFree(p);
+    if (tc_split) cudaFree(tc_split);
+    if (tc_sx) cudaFree(tc_sx);
+    if (tc_part) cudaFree(tc_part);
   }
   template <class T>
   int get(T** p, size_t n) {
@@ -1032,8 +1052,157 @@ static void launch_gemv_impl(const tcu_model* m, const GemvArgs& a, cudaStream_t
   launch_gemv_generic<PRO, EPI>(m, a, s);
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core GEMM (gemm_tc.cuh)
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library); nullptr if unavailable.
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  std::call_once(g_encode_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    cudaGetLastError();
+  });
+  return g_encode;
+}
+
+// Power of two for the tensor-core split of a Q8_0 matrix: the largest
+// |s * q| (q <= 128) scaled below 2^13.
+static int set_tc_shift(tcu_model* m, DMat* W) {
+  if (W->fmt != FMT_Q8_0) return TCU_OK;
+  if (!m->scratch_u32) TRY(dalloc(m, (void**)&m->scratch_u32, sizeof(unsigned)));
+  CK(cudaMemset(m->scratch_u32, 0, sizeof(unsigned)));
+  k_scale_absmax<<<m->sm_count * 4, 256>>>(W->s, W->rows, W->sstride, W->cols / 32, m->scratch_u32);
+  CK(cudaGetLastError());
+  unsigned bits = 0;
+  CK(cudaMemcpy(&bits, m->scratch_u32, sizeof(unsigned), cudaMemcpyDeviceToHost));
+  float mx;
+  memcpy(&mx, &bits, sizeof(mx));
+  int e = 0;
+  if (mx > 0.f) frexpf(mx * 128.f, &e);
+  W->tc_sw = mx > 0.f ? std::max(-100, std::min(100, 13 - e)) : 0;
+  return TCU_OK;
+}
+
+static int set_tc_shifts(tcu_model* m) {
+  for (Layer& ly : m->layers) {
+    TRY(set_tc_shift(m, &ly.w1));
+    TRY(set_tc_shift(m, &ly.w2));
+    TRY(set_tc_shift(m, &ly.w3));
+    TRY(set_tc_shift(m, &ly.w4));
+  }
+  TRY(set_tc_shift(m, &m->head));
+  return TCU_OK;
+}
+
+static int work_reserve(void** p, size_t bytes) {
+  if (cudaMalloc(p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    *p = nullptr;
+    return TCU_ENOMEM;
+  }
+  cudaMemset(*p, 0, bytes);
+  return TCU_OK;
+}
+
+// Enqueues a Q8_0 product on the tensor cores; false if this shape or format
+// takes the CUDA-core path.
 template <int EPI>
-static void launch_gemm(const GemmArgs& a, cudaStream_t s) {
+static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaStream_t s) {
+  const DMat& W = g.W;
+  const int K = W.cols, R = W.rows, n = g.n;
+  if (!m->use_tc || !w || W.fmt != FMT_Q8_0 || K % 16 || n < 1 || R < 1) return false;
+  if (EPI == EPI_RESID2 && g.k_split % TC_BK) return false;
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return false;
+  const int n_tile = std::min(TC_MAXN, (n + 15) / 16 * 16);
+  const int n_pad = (n + n_tile - 1) / n_tile * n_tile;
+  const int row_tiles = (R + TC_BM - 1) / TC_BM;
+  // Too few tiles to fill the GPU: split K into slices (out/down rows only).
+  int z = 1, k_per_z = K, z_lo = 0;
+  if (EPI == EPI_RESID2 && row_tiles * (n_pad / n_tile) < m->sm_count / 2) {
+    k_per_z = TC_BK;
+    for (int c = 20; c >= 1; c--)
+      if (g.k_split % (c * TC_BK) == 0) {
+        k_per_z = c * TC_BK;
+        break;
+      }
+    z_lo = g.k_split / k_per_z;
+    z = z_lo + (K - g.k_split + k_per_z - 1) / k_per_z;
+  }
+  // Workspace: grows on first use (not during stream capture).
+  if (n_pad > w->tc_npad || K > w->tc_kmax) {
+    const int np = std::max(n_pad, w->tc_npad), kk = std::max(K, w->tc_kmax);
+    if (w->tc_split) cudaFree(w->tc_split);
+    if (w->tc_sx) cudaFree(w->tc_sx);
+    w->tc_split = nullptr;
+    w->tc_sx = nullptr;
+    w->tc_npad = w->tc_kmax = 0;
+    if (work_reserve((void**)&w->tc_split, (size_t)2 * np * kk * 2) || work_reserve((void**)&w->tc_sx, (size_t)np * 4)) return false;
+    w->tc_npad = np;
+    w->tc_kmax = kk;
+  }
+  if (z > 1 && (size_t)z * n * R > w->tc_part_floats) {
+    if (w->tc_part) cudaFree(w->tc_part);
+    w->tc_part = nullptr;
+    w->tc_part_floats = 0;
+    if (work_reserve((void**)&w->tc_part, (size_t)z * n * R * 4)) return false;
+    w->tc_part_floats = (size_t)z * n * R;
+  }
+  CUtensorMap map;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)(2 * n_pad)};
+    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)n_tile};
+    cuuint32_t estr[2] = {1, 1};
+    if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w->tc_split, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  if (cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  PROF_BEGIN(g_stage, s);
+  k_split_f16<<<n, 256, 0, s>>>(g.A, g.lda, n, K, n_pad, w->tc_split, w->tc_sx);
+  NOTE("k_split_f16");
+  TcArgs a{};
+  a.W = W;
+  a.n = n;
+  a.n_tile = n_tile;
+  a.n_pad = n_pad;
+  a.sx = w->tc_sx;
+  a.sw = W.tc_sw;
+  a.out = g.out;
+  a.out_stride = g.out_stride;
+  a.n_plain = g.n_plain;
+  a.glu_out = g.glu_out;
+  a.glu_stride = g.glu_stride;
+  a.glu_act = g.glu_act;
+  a.resid = g.resid;
+  a.resid_stride = g.resid_stride;
+  a.k_split = g.k_split;
+  a.part = z > 1 ? w->tc_part : nullptr;
+  a.k_per_z = k_per_z;
+  a.err = w->err;
+  k_gemm_tc<EPI><<<dim3(row_tiles, n_pad / n_tile, z), TC_THREADS, TC_SMEM, s>>>(map, a);
+  NOTE("k_gemm_tc");
+  if (z > 1) {
+    k_splitk_resid<<<m->sm_count * 4, 256, 0, s>>>(w->tc_part, z_lo, z, n, R, g.resid, g.resid_stride);
+    NOTE("k_splitk_resid");
+  }
+  PROF_END(s);
+  return true;
+}
+
+template <int EPI>
+static void launch_gemm(const tcu_model* m, Work* w, const GemmArgs& a, cudaStream_t s) {
+  if (launch_gemm_tc<EPI>(m, w, a, s)) return;
   PROF_BEGIN(g_stage, s);
   dim3 grid((a.W.rows + SG_BN - 1) / SG_BN, (a.n + SG_BM - 1) / SG_BM);
   k_gemm_simt<EPI><<<grid, SG_THREADS, 0, s>>>(a);
@@ -1161,7 +1330,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
         g.glu_out = w->ah + d;
         g.glu_stride = d + ff;
         g.glu_act = 0;
-        launch_gemm<EPI_GLU>(g, s);
+        launch_gemm<EPI_GLU>(m, w, g, s);
       }
       launch_attn_decode(m, pool, w, M, l, grid_splits, s);
       g_stage = ST_W2;
@@ -1184,7 +1353,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
         g.resid = w->x;
         g.resid_stride = d;
         g.k_split = d;
-        launch_gemm<EPI_RESID2>(g, s);
+        launch_gemm<EPI_RESID2>(m, w, g, s);
       }
     } else {
       g_stage = ST_W1;
@@ -1207,7 +1376,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
         g.lda = d;
         g.out = w->qkv;
         g.out_stride = qkvw;
-        launch_gemm<EPI_STORE>(g, s);
+        launch_gemm<EPI_STORE>(m, w, g, s);
       }
       launch_attn_decode(m, pool, w, M, l, grid_splits, s);
       g_stage = ST_W2;
@@ -1247,7 +1416,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
         g.lda = d + ff;
         g.resid = w->x;
         g.resid_stride = d;
-        launch_gemm<EPI_RESID1>(g, s);
+        launch_gemm<EPI_RESID1>(m, w, g, s);
         launch_norm_rows(m, w->x, w->xn, M, ly.n2w, nullptr, s);
         GemmArgs g3{};
         g3.W = ly.w3;
@@ -1258,7 +1427,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
         g3.glu_out = w->ah + d;
         g3.glu_stride = d + ff;
         g3.glu_act = 1;
-        launch_gemm<EPI_GLU>(g3, s);
+        launch_gemm<EPI_GLU>(m, w, g3, s);
         GemmArgs g4{};
         g4.W = ly.w4;
         g4.n = M;
@@ -1266,7 +1435,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
         g4.lda = d + ff;
         g4.resid = w->x;
         g4.resid_stride = d;
-        launch_gemm<EPI_RESID1>(g4, s);
+        launch_gemm<EPI_RESID1>(m, w, g4, s);
       }
     }
   }
@@ -1297,7 +1466,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
     g.lda = d;
     g.out = w->logits;
     g.out_stride = m->V;
-    launch_gemm<EPI_STORE>(g, s);
+    launch_gemm<EPI_STORE>(m, w, g, s);
     PROF_BEGIN(ST_HEAD, s);
     k_argmax_rows<<<M, 256, 0, s>>>(w->logits, m->V, m->V, w->argmax);
     NOTE("k_argmax_rows");
@@ -1335,9 +1504,9 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
       g.glu_out = w->ah + d;
       g.glu_stride = d + ff;
       g.glu_act = 0;
-      launch_gemm<EPI_GLU>(g, s);
+      launch_gemm<EPI_GLU>(m, w, g, s);
     } else {
-      launch_gemm<EPI_STORE>(g, s);
+      launch_gemm<EPI_STORE>(m, w, g, s);
     }
     RopeStoreArgs r{};
     r.n = n;
@@ -1385,7 +1554,7 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
       g2.resid = w->x;
       g2.resid_stride = d;
       g2.k_split = d;
-      launch_gemm<EPI_RESID2>(g2, s);
+      launch_gemm<EPI_RESID2>(m, w, g2, s);
     } else {
       GemmArgs g2{};
       g2.W = ly.w2;
@@ -1394,7 +1563,7 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
       g2.lda = d + ff;
       g2.resid = w->x;
       g2.resid_stride = d;
-      launch_gemm<EPI_RESID1>(g2, s);
+      launch_gemm<EPI_RESID1>(m, w, g2, s);
       launch_norm_rows(m, w->x, w->xn, n, ly.n2w, nullptr, s);
       GemmArgs g3{};
       g3.W = ly.w3;
@@ -1405,7 +1574,7 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
       g3.glu_out = w->ah + d;
       g3.glu_stride = d + ff;
       g3.glu_act = 1;
-      launch_gemm<EPI_GLU>(g3, s);
+      launch_gemm<EPI_GLU>(m, w, g3, s);
       GemmArgs g4{};
       g4.W = ly.w4;
       g4.n = n;
@@ -1413,7 +1582,7 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
       g4.lda = d + ff;
       g4.resid = w->x;
       g4.resid_stride = d;
-      launch_gemm<EPI_RESID1>(g4, s);
+      launch_gemm<EPI_RESID1>(m, w, g4, s);
     }
   }
 }
