@@ -71,6 +71,15 @@ __device__ __forceinline__ float silu_mul_stablelm(float v, float up) {
   float s = __fdiv_rn(v, den);
   return __fmul_rn(s, up);
 }
+// The same with exp evaluated in float32 (expf, within 2 ulp of the rounded
+// float64 value): for the persistent decode step, where the float64 exp sits
+// on the critical path of every gate/up tile.
+__device__ __forceinline__ float silu_mul_stablelm_f32(float v, float up) {
+  float e = expf(-v);
+  float den = __fadd_rn(1.0f, e);
+  float s = __fdiv_rn(v, den);
+  return __fmul_rn(s, up);
+}
 // SwiGLU of the llama2.c MLP (model.go:470-473): v * (1/(1+exp(-v))) * up.
 __device__ __forceinline__ float silu_mul_llama(float v, float up) {
   float e = (float)exp(-(double)v);

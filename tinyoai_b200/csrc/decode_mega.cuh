@@ -49,6 +49,7 @@ constexpr int MG_MAXK = 10240;
 constexpr int MG_CTL = 4;     // control words per (launch parity, layer)
 constexpr int MG_HDR = 256;   // shared-memory header: mbarriers and slot tags
 constexpr int MG_SEQ = 8;     // in-flight tiles tracked by the arrival counters
+constexpr int MG_SWT = 24;    // W1 tiles per CTA and layer (gate/up values kept for quantisation after the loop)
 
 struct MegaLayer {
   const int8_t* w1;  // [n_plain + 2ff][d] quants
@@ -476,8 +477,8 @@ __device__ __forceinline__ void mg_unit_core(const MegaArgs& a, const uint8_t* k
 
 __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
   extern __shared__ __align__(128) uint8_t mg_smem[];
-  __shared__ float swg[MG_SEQ][16], swu[MG_SEQ][16];  // gate / up of in-flight gate/up tiles
-  __shared__ int swcnt[MG_SEQ];
+  __shared__ float swg[MG_SWT][16], swu[MG_SWT][16];  // gate / up of this layer's gate/up tiles
+  __shared__ int swtile[MG_SWT];
   __shared__ float cpart[MG_SEQ][16];  // out/down chunk partials of in-flight tiles
   __shared__ int cpcnt[MG_SEQ];
   MgRing ring;
@@ -515,10 +516,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
     mbar_init(inbar, 1);
     fence_barrier_init();
   }
-  if (threadIdx.x < MG_SEQ) {
-    swcnt[threadIdx.x] = 0;
-    cpcnt[threadIdx.x] = 0;
-  }
+  if (threadIdx.x < MG_SEQ) cpcnt[threadIdx.x] = 0;
   __syncthreads();
 
   const int pos = *(volatile int*)a.pos;
@@ -552,7 +550,9 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
         const __half* const s2p = a.layers[l].s2;
         int* gl = grab + l * MG_CTL;
         // Two grabs stay in flight, so the atomic's round trip overlaps the copies.
-        int q0 = atomicAdd(gl + 0, 1), q1 = atomicAdd(gl + 0, 1);
+        // At most MG_SWT tiles per layer (the row warps keep their gate/up
+        // values in shared memory until the phase ends); others take the rest.
+        int q0 = atomicAdd(gl + 0, 1), q1 = atomicAdd(gl + 0, 1), grabs = 2;
         while (!stop) {
           const int t = q0;
           q0 = q1;
@@ -560,7 +560,12 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
             end_phase();
             break;
           }
-          q1 = atomicAdd(gl + 0, 1);
+          if (grabs < MG_SWT) {
+            q1 = atomicAdd(gl + 0, 1);
+            grabs++;
+          } else {
+            q1 = n_w1t;
+          }
           const int nst = t < n_pt ? 1 : 2;
           const int rbase = t < n_pt ? t * MG_W1_RS : n_plain + (t - n_pt) * 2 * MG_W1_RS;
           for (int sub = 0; sub < nst && !stop; sub++) {
@@ -739,7 +744,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
     mg_ln_digits(xs, d, ly.nw, ly.nb, a.eps, dig, sx);
     load_regs(0, d / 16);
     {
-      int n_plain_done = 0, n_blocks = 0;
+      int n_plain_done = 0;
       bool plain_open = true;
       for (;;) {
         const uint8_t* st;
@@ -766,35 +771,27 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
           }
           n_plain_done++;
         } else {
-          // Gate/up pair j = 16 (t - n_pt) + 8 sub + warp. The last warp to
-          // finish a tile forms its 16 SwiGLU values (one per lane) and
-          // quantises them.
-          const int e = sw_seq % MG_SEQ;
+          // Gate/up pair j = 16 (t - n_pt) + 8 sub + warp; its tile is
+          // quantised after the loop (kept off the streaming path).
+          // (The producer takes at most MG_SWT W1 tiles per layer.)
           if (lane == 0) {
-            swg[e][8 * sub + warp] = acc[0];
-            swu[e][8 * sub + warp] = acc[1];
+            swg[sw_seq][8 * sub + warp] = acc[0];
+            swu[sw_seq][8 * sub + warp] = acc[1];
+            if (warp == 0 && sub == 1) swtile[sw_seq] = t;
           }
-          if (sub == 1) {
-            __threadfence_block();
-            int last = 0;
-            if (lane == 0) last = atomicAdd(&swcnt[e], 1) == MG_CW - 1;
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (last) {
-              __threadfence_block();
-              const float v = lane < 16 ? silu_mul_stablelm(swg[e][lane], swu[e][lane]) : 0.f;
-              const int b = d / 16 + (t - n_pt);
-              mg_quant16_warp(v, adig_l + (size_t)b * 12, asx_l + b);
-              if (lane == 0) swcnt[e] = 0;
-              n_blocks++;
-            }
-            sw_seq++;
-          }
+          if (sub == 1) sw_seq++;
         }
       }
-      // The gate/up blocks this warp quantised are read in phase C only:
-      // published once, outside the streaming loop.
-      __syncwarp();
-      if (lane == 0 && n_blocks > 0) mg_red_add_release(dl + 1, n_blocks);
+      // SwiGLU values and digits of this layer's gate/up tiles: warp w takes
+      // tiles w, w + 8, ... (lane i: value i); read in phase C only.
+      named_bar_sync(1, MG_CT);
+      for (int q = warp; q < sw_seq; q += MG_CW) {
+        const float v = lane < 16 ? silu_mul_stablelm_f32(swg[q][lane], swu[q][lane]) : 0.f;
+        const int b = d / 16 + (swtile[q] - n_pt);
+        mg_quant16_warp(v, adig_l + (size_t)b * 12, asx_l + b);
+      }
+      mg_publish(dl + 1, threadIdx.x == 0 ? sw_seq : 0);
+      sw_seq = 0;
     }
 
     // ---- Phase B: attention units (stablelm.go:401-427), split over the
