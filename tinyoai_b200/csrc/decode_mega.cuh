@@ -479,8 +479,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
   extern __shared__ __align__(128) uint8_t mg_smem[];
   __shared__ float swg[MG_SWT][16], swu[MG_SWT][16];  // gate / up of this layer's gate/up tiles
   __shared__ int swtile[MG_SWT];
-  __shared__ float cpart[MG_SEQ][16];  // out/down chunk partials of in-flight tiles
-  __shared__ int cpcnt[MG_SEQ];
+  float(*cpart)[16] = swg;  // out/down chunk partials of this layer's tiles (phase C)
   MgRing ring;
   ring.full = reinterpret_cast<uint64_t*>(mg_smem);
   ring.empty = ring.full + MG_MAX_SLOTS;
@@ -516,7 +515,6 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
     mbar_init(inbar, 1);
     fence_barrier_init();
   }
-  if (threadIdx.x < MG_SEQ) cpcnt[threadIdx.x] = 0;
   __syncthreads();
 
   const int pos = *(volatile int*)a.pos;
@@ -610,8 +608,10 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
           }
           ring.i++;
         }
+        // At most MG_SWT out/down tiles per layer, as for the W1 tiles.
         q0 = atomicAdd(gl + 2, 1);
         q1 = atomicAdd(gl + 2, 1);
+        grabs = 2;
         while (!stop) {
           const int t = q0;
           q0 = q1;
@@ -619,7 +619,12 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
             end_phase();
             break;
           }
-          q1 = atomicAdd(gl + 2, 1);
+          if (grabs < MG_SWT) {
+            q1 = atomicAdd(gl + 2, 1);
+            grabs++;
+          } else {
+            q1 = n_w2t;
+          }
           const int r0 = t * MG_W2_RS, nr = min(MG_W2_RS, d - r0);
           const uint32_t qb = (uint32_t)(nr * row2), sb = (uint32_t)(nr * a.s2_stride * 2);
           uint8_t* dst = mg_produce(ring, t, qb + sb, a.err);
@@ -918,7 +923,6 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
       }
       load_regs(vb, ve);
       float* xo = a.xl + (size_t)(l + 1) * d;
-      int rows = 0;
       for (;;) {
         const uint8_t* st;
         const int tag = mg_next_warp(ring, &st, a.err);
@@ -931,32 +935,33 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
         mg_dot2(st, row2, reinterpret_cast<const __half*>(st + (size_t)MG_W2_RS * row2), a.s2_stride, 2 * sub, nr, vb, ve, dr, sxr,
                 acc);
         mg_release(ring);
-        // The last warp to finish this tile adds its rows' partials in a
-        // fixed order and writes the residual.
-        const int e = cp_seq % MG_SEQ;
+        // Chunk partials of the tile's rows wait in shared memory (the
+        // gate/up buffer, free in this phase) until the loop ends. (The
+        // producer takes at most MG_SWT out/down tiles per layer.)
         if (lane == 0) {
-          cpart[e][(2 * sub) * 4 + chunk] = acc[0];
-          cpart[e][(2 * sub + 1) * 4 + chunk] = acc[1];
-        }
-        __threadfence_block();
-        int last = 0;
-        if (lane == 0) last = atomicAdd(&cpcnt[e], 1) == MG_CW - 1;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-          __threadfence_block();
-          if (lane < nr) {
-            const float lo = cpart[e][lane * 4 + 0];
-            const float hi = (cpart[e][lane * 4 + 1] + cpart[e][lane * 4 + 2]) + cpart[e][lane * 4 + 3];
-            const int r = r0 + lane;
-            xo[r] = __fadd_rn(__fadd_rn(xs[r], lo), hi);
-          }
-          __syncwarp();
-          if (lane == 0) cpcnt[e] = 0;
+          cpart[cp_seq][(2 * sub) * 4 + chunk] = acc[0];
+          cpart[cp_seq][(2 * sub + 1) * 4 + chunk] = acc[1];
+          if (warp == 0) swtile[cp_seq] = tag;
         }
         cp_seq++;
-        rows += nr;
       }
-      mg_publish(dl + 2, warp == 0 ? rows : 0);
+      // The parallel residual of every row of this CTA's tiles, partials
+      // added in a fixed order.
+      named_bar_sync(1, MG_CT);
+      int rows = 0;
+      for (int i = threadIdx.x; i < cp_seq * MG_W2_RS; i += MG_CT) {
+        const int q = i / MG_W2_RS, lr = i % MG_W2_RS;
+        const int r = swtile[q] * MG_W2_RS + lr;
+        if (r < d) {
+          const float lo = cpart[q][lr * 4 + 0];
+          const float hi = (cpart[q][lr * 4 + 1] + cpart[q][lr * 4 + 2]) + cpart[q][lr * 4 + 3];
+          xo[r] = __fadd_rn(__fadd_rn(xs[r], lo), hi);
+        }
+      }
+      if (threadIdx.x == 0)
+        for (int q = 0; q < cp_seq; q++) rows += min(MG_W2_RS, d - swtile[q] * MG_W2_RS);
+      mg_publish(dl + 2, rows);
+      cp_seq = 0;
     }
   }
 

@@ -367,6 +367,7 @@ static int build_mega(tcu_model* m) {
   if (d / 16 > MG_CT || G_q > 32 || m->hd % 8 || (G_q * m->hd) % 16 || m->rope.pairs > 64 || m->rope.mode != 0) return TCU_OK;
   // Every W1 tile must fit under the per-CTA cap of the persistent step.
   if ((size_t)(n_plain / MG_W1_RS + ff / 16) > (size_t)m->sm_count * MG_SWT) return TCU_OK;
+  if ((size_t)(d + MG_W2_RS - 1) / MG_W2_RS > (size_t)m->sm_count * MG_SWT) return TCU_OK;
   cudaFuncAttributes fa;
   CK(cudaFuncGetAttributes(&fa, k_decode_mega));
   const size_t w1 = (size_t)MG_W1_RS * (d + m->layers[0].w1.sstride * 2);
