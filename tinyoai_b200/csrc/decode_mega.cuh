@@ -357,6 +357,61 @@ __device__ __forceinline__ void mg_await(const int* ctr, int target, int* err) {
   named_bar_sync(1, MG_CT);
 }
 
+// Merges the nsplit partials (rows of hd outputs, max, sum) of each of the
+// G_q query heads of one KV head into wo[G_q][hd], by one warp: the fp32
+// maximum over the splits, weights expf(max_j - max), then the sum and the
+// outputs accumulated in split order. Lane j holds split j's max, sum and
+// weight; output rows are loaded 8 splits at a time before any is used, so
+// the merge costs a few L2 round trips rather than one per split.
+__device__ __forceinline__ void mg_merge_head(const float* pg, int max_splits, int hd, int G_q, int nsplit, int lane, float* wo) {
+  const int rs = hd + 2;
+  for (int hh = 0; hh < G_q; hh++) {
+    const float* ph = pg + (size_t)hh * max_splits * rs;
+    float mx = -INFINITY;
+    for (int jb = 0; jb < nsplit; jb += 32)
+      if (jb + lane < nsplit) mx = fmaxf(mx, __ldcg(ph + (size_t)(jb + lane) * rs + hd));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int ib = 0; ib < hd; ib += 128) {
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
+      float lsum = 0.f;
+      for (int jb = 0; jb < nsplit; jb += 32) {
+        const int jl = jb + lane, n = min(32, nsplit - jb);
+        float wj = 0.f, sj = 0.f;
+        if (jl < nsplit) {
+          wj = expf(__ldcg(ph + (size_t)jl * rs + hd) - mx);
+          sj = __ldcg(ph + (size_t)jl * rs + hd + 1);
+        }
+        for (int j8 = 0; j8 < n; j8 += 8) {
+          float pv[8][4];
+#pragma unroll
+          for (int jj = 0; jj < 8; jj++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+              const int i = ib + lane + 32 * k;
+              pv[jj][k] = (j8 + jj < n && i < hd) ? __ldcg(ph + (size_t)(jb + j8 + jj) * rs + i) : 0.f;
+            }
+#pragma unroll
+          for (int jj = 0; jj < 8; jj++) {
+            const float w = __shfl_sync(0xffffffffu, wj, (j8 + jj) & 31);
+            const float sv = __shfl_sync(0xffffffffu, sj, (j8 + jj) & 31);
+            if (j8 + jj < n) {
+              lsum = fmaf(sv, w, lsum);
+#pragma unroll
+              for (int k = 0; k < 4; k++) o[k] = fmaf(pv[jj][k], w, o[k]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int i = ib + lane + 32 * k;
+        if (i < hd) wo[hh * hd + i] = __fdiv_rn(o[k], lsum);
+      }
+    }
+  }
+}
+
 // Scores, softmax and weighted values of one attention unit, by one warp
 // (stablelm.go:401-427 with the history split): K and V tiles of n_hist
 // tokens in shared memory (float32 or binary16 rows of hd values), this
@@ -874,20 +929,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
           // Merge the splits of KV head g (fp32 max / sum), then publish the
           // digits of its G_q * hd outputs (a multiple of 16).
           __syncwarp();
-          for (int e = lane; e < ghd; e += 32) {
-            const int hh = e / hd, i = e % hd;
-            const float* ph = pg + (size_t)hh * a.max_splits * (hd + 2);
-            float mx = -INFINITY;
-            for (int j = 0; j < nsplit; j++) mx = fmaxf(mx, __ldcg(ph + (size_t)j * (hd + 2) + hd));
-            float lsum = 0.f, o = 0.f;
-            for (int j = 0; j < nsplit; j++) {
-              const float* pj = ph + (size_t)j * (hd + 2);
-              const float w = expf(__ldcg(pj + hd) - mx);
-              lsum = fmaf(__ldcg(pj + hd + 1), w, lsum);
-              o = fmaf(__ldcg(pj + i), w, o);
-            }
-            wo[e] = __fdiv_rn(o, lsum);
-          }
+          mg_merge_head(pg, a.max_splits, hd, G_q, nsplit, lane, wo);
           __syncwarp();
           const int nb16 = ghd / 16;
           for (int b = lane; b < nb16; b += 32) {
