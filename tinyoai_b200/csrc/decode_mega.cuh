@@ -5,15 +5,17 @@
 // Grid = one CTA per SM. Warp 8 lane 0 is the producer, warps 0..7 consume.
 // Work is handed out dynamically: for each layer the producer takes items
 // from global counters -- tiles of the fused q/k/v/gate/up rows, attention
-// units (KV head x history split), tiles of the fused out/down rows; then
-// tiles of the lm_head rows -- and streams each item's weights or KV pages
-// into a shared-memory ring of slots with cp.async.bulk, tagging the slot
-// with the item. SMs that stream faster take more items, so the phases end
-// together. A phase's input is awaited only where it is read:
+// units (KV head x history split), tiles of the down-projection rows (the
+// SwiGLU columns of the fused out/down matrix), tiles of the out-projection
+// rows (its attention columns); then tiles of the lm_head rows -- and streams
+// each item's weights or KV pages into a shared-memory ring of slots with
+// cp.async.bulk, tagging the slot with the item. SMs that stream faster take
+// more items, so the phases end together. A phase's input is awaited only
+// where it is read:
 //   - attention needs every q/k/v row (a count of finished q/k/v tiles);
-//   - the out/down rows need every published input block (SwiGLU blocks and
-//     merged attention heads);
-//   - the next layer needs every residual row.
+//   - the down rows need every SwiGLU block, so they run while attention
+//     does; the out rows need every merged attention head;
+//   - a residual row needs its down sum; the next layer needs every row.
 // Each wait is a bounded poll of one counter. Per-layer x and digit buffers
 // mean no CTA overwrites what a slower CTA may still be reading.
 //
@@ -43,10 +45,15 @@ constexpr int MG_THREADS = (MG_CW + 1) * 32;  // + producer warp
 constexpr int MG_CT = MG_CW * 32;
 constexpr int MG_MAX_SLOTS = 6;
 constexpr int MG_W1_RS = 16;  // rows per stage, q/k/v/gate/up and head
-constexpr int MG_W2_RS = 4;   // rows per stage, out/down (4 K chunks x 2 row groups)
+constexpr int MG_DN_RS = 4;   // rows per stage, down projection (4 K chunks x 2 row groups)
+constexpr int MG_O_RS = 16;   // rows per stage, out projection (2 rows per warp)
 constexpr int MG_NJ = 5;      // 16-value vectors per lane (K chunk <= 2560)
 constexpr int MG_MAXK = 10240;
-constexpr int MG_CTL = 4;     // control words per (launch parity, layer)
+// Control words per (launch parity, layer). grab: 0 q/k/v/gate/up tiles,
+// 1 attention units, 2 down tiles, 3 out tiles; grab[L][0]: lm_head tiles.
+// done: 0 q/k/v rows, 1 gate/up tiles, 2 residual rows, 3 merged heads,
+// 4 down rows; done[L][3] counts the CTAs that finished the launch.
+constexpr int MG_CTL = 8;
 constexpr int MG_HDR = 256;   // shared-memory header: mbarriers and slot tags
 constexpr int MG_SEQ = 8;     // in-flight tiles tracked by the arrival counters
 constexpr int MG_SWT = 24;    // W1 tiles per CTA and layer (gate/up values kept for quantisation after the loop)
@@ -65,6 +72,8 @@ struct MegaArgs {
   int s1_stride, s2_stride, sh_stride, se_stride;
   double eps;
   const MegaLayer* layers;
+  int dn_sstride;  // scale halves per row in a down tile (staged segment)
+  int dn_soff;     // first scale of the down segment within that staged run
   const int8_t* head_w;
   const __half* head_s;
   const int8_t* emb_w;
@@ -85,6 +94,7 @@ struct MegaArgs {
   float* logits;  // optional
   // scratch
   float* xl;       // [L + 1][d]: input of layer l (xl[L]: input of the final norm)
+  float* xdn;      // [L][d]: down-projection sums of layer l
   float* qkv;      // [d + 2 kvw]
   uint32_t* adig;  // [L][(d + ff) / 16][12] digits of [attention | SwiGLU]
   float* asx;      // [L][asx_stride] their block scales
@@ -95,7 +105,6 @@ struct MegaArgs {
   int* grab;       // [2][L + 1][MG_CTL] work counters by launch parity
   int* done;       // [2][L + 1][MG_CTL] completion counters by launch parity
   int* err;
-  uint32_t dig_bytes, sx_bytes;  // out/down input staging sizes (multiples of 16)
   uint32_t slot_bytes;
   int nslots;  // ring depth (<= MG_MAX_SLOTS)
   uint32_t off_x, off_att, off_dig, off_sx, off_slots;
@@ -557,9 +566,10 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
   const size_t row2 = (size_t)K2;
   const int n_pt = n_plain / MG_W1_RS;     // q/k/v tiles (16 rows)
   const int n_w1t = n_pt + ff / 16;        // + gate/up tiles (32 rows: 16 SwiGLU values)
-  const int n_w2t = (d + MG_W2_RS - 1) / MG_W2_RS;
+  const int n_dnt = (d + MG_DN_RS - 1) / MG_DN_RS;
+  const int n_ot = (d + MG_O_RS - 1) / MG_O_RS;
+  const int osc = (d / 32 + 7) / 8 * 8;  // scale halves per row in an out tile
   const int n_ht = (a.V + MG_W1_RS - 1) / MG_W1_RS;
-  const int nb_in = ff / 16 + a.KVH;       // published out/down input items per layer
   const int G_q = a.H / a.KVH;
 
   if (threadIdx.x == 0) {
@@ -663,33 +673,45 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
           }
           ring.i++;
         }
-        // At most MG_SWT out/down tiles per layer, as for the W1 tiles.
-        q0 = atomicAdd(gl + 2, 1);
-        q1 = atomicAdd(gl + 2, 1);
-        grabs = 2;
-        while (!stop) {
-          const int t = q0;
-          q0 = q1;
-          if (t >= n_w2t) {
-            end_phase();
-            break;
+        // Down tiles, then out tiles: at most MG_SWT of each per layer, as for
+        // the W1 tiles. Each row's segment of the fused matrix is one copy
+        // (quants), plus one for its scales.
+        for (int ph = 0; ph < 2 && !stop; ph++) {
+          const int nt = ph == 0 ? n_dnt : n_ot;
+          const int rs = ph == 0 ? MG_DN_RS : MG_O_RS;
+          const int qoff = ph == 0 ? d : 0, qlen = ph == 0 ? ff : d;
+          const int soff = ph == 0 ? d / 32 - a.dn_soff : 0, slen = ph == 0 ? a.dn_sstride : osc;
+          int* gc = gl + 2 + ph;
+          q0 = atomicAdd(gc, 1);
+          q1 = atomicAdd(gc, 1);
+          grabs = 2;
+          while (!stop) {
+            const int t = q0;
+            q0 = q1;
+            if (t >= nt) {
+              end_phase();
+              break;
+            }
+            if (grabs < MG_SWT) {
+              q1 = atomicAdd(gc, 1);
+              grabs++;
+            } else {
+              q1 = nt;
+            }
+            const int r0 = t * rs, nr = min(rs, d - r0);
+            uint8_t* dst = mg_produce(ring, t, (uint32_t)nr * (qlen + 2 * slen), a.err);
+            if (!dst) {
+              stop = true;
+              break;
+            }
+            for (int lr = 0; lr < nr; lr++) {
+              const size_t r = (size_t)(r0 + lr);
+              bulk_g2s(dst + (size_t)lr * qlen, w2p + r * row2 + qoff, (uint32_t)qlen, mg_full(ring));
+              bulk_g2s(dst + (size_t)rs * qlen + (size_t)lr * slen * 2, s2p + r * a.s2_stride + soff, (uint32_t)slen * 2u,
+                       mg_full(ring));
+            }
+            ring.i++;
           }
-          if (grabs < MG_SWT) {
-            q1 = atomicAdd(gl + 2, 1);
-            grabs++;
-          } else {
-            q1 = n_w2t;
-          }
-          const int r0 = t * MG_W2_RS, nr = min(MG_W2_RS, d - r0);
-          const uint32_t qb = (uint32_t)(nr * row2), sb = (uint32_t)(nr * a.s2_stride * 2);
-          uint8_t* dst = mg_produce(ring, t, qb + sb, a.err);
-          if (!dst) {
-            stop = true;
-            break;
-          }
-          bulk_g2s(dst, w2p + (size_t)r0 * row2, qb, mg_full(ring));
-          bulk_g2s(dst + (size_t)MG_W2_RS * row2, s2p + (size_t)r0 * a.s2_stride, sb, mg_full(ring));
-          ring.i++;
         }
       }
       int* gh = grab + a.L * MG_CTL;
@@ -941,30 +963,24 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
           __syncwarp();
           if (lane == 0) {
             a.counters[g] = 0;
-            mg_red_add_release(dl + 1, 1);
+            mg_red_add_release(dl + 3, 1);
           }
         }
         __syncwarp();
       }
     }
 
-    // ---- Phase C: out/down rows over [attention | SwiGLU] with the parallel
-    // residual (stablelm.go:365-377). K chunks: [0, d) then down split in three.
-    mg_await(dl + 1, nb_in, a.err);
-    stage_in(dig, adig_l, a.dig_bytes, sx, asx_l, a.sx_bytes);
+    // ---- Phase C: down-projection rows over the SwiGLU blocks (4 K chunks x
+    // 2 row pairs per tile); their sums go to xdn for the residual.
+    mg_await(dl + 1, ff / 16, a.err);
     {
+      const int sb = (d / 16) & ~3, se = (K2 / 16 + 3) & ~3;  // sx staged in 16-byte units
+      stage_in(dig + (d / 16) * 12, adig_l + (size_t)(d / 16) * 12, (uint32_t)(ff / 16) * 48u, sx + sb, asx_l + sb,
+               (uint32_t)(se - sb) * 4u);
       const int chunk = warp & 3, sub = warp >> 2;
       const int nvd = ff / 16;
-      int vb, ve;
-      if (chunk == 0) {
-        vb = 0;
-        ve = d / 16;
-      } else {
-        vb = d / 16 + (nvd * (chunk - 1)) / 3;
-        ve = d / 16 + (nvd * chunk) / 3;
-      }
+      const int vb = d / 16 + (nvd * chunk) / 4, ve = d / 16 + (nvd * (chunk + 1)) / 4;
       load_regs(vb, ve);
-      float* xo = a.xl + (size_t)(l + 1) * d;
       for (;;) {
         const uint8_t* st;
         const int tag = mg_next_warp(ring, &st, a.err);
@@ -972,14 +988,14 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
           if (tag == -1) mg_release(ring);
           break;
         }
-        const int r0 = tag * MG_W2_RS, nr = min(MG_W2_RS, d - r0);
+        const int nr = min(MG_DN_RS, d - tag * MG_DN_RS);
         float acc[2];
-        mg_dot2(st, row2, reinterpret_cast<const __half*>(st + (size_t)MG_W2_RS * row2), a.s2_stride, 2 * sub, nr, vb, ve, dr, sxr,
-                acc);
+        mg_dot2(st, (size_t)ff, reinterpret_cast<const __half*>(st + (size_t)MG_DN_RS * ff) + a.dn_soff, a.dn_sstride, 2 * sub, nr,
+                vb - d / 16, ve - d / 16, dr, sxr, acc);
         mg_release(ring);
-        // Chunk partials of the tile's rows wait in shared memory (the
-        // gate/up buffer, free in this phase) until the loop ends. (The
-        // producer takes at most MG_SWT out/down tiles per layer.)
+        // Chunk partials wait in shared memory (the gate/up buffer, free in
+        // this phase) until the loop ends. (The producer takes at most MG_SWT
+        // down tiles per layer.)
         if (lane == 0) {
           cpart[cp_seq][(2 * sub) * 4 + chunk] = acc[0];
           cpart[cp_seq][(2 * sub + 1) * 4 + chunk] = acc[1];
@@ -987,21 +1003,58 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
         }
         cp_seq++;
       }
-      // The parallel residual of every row of this CTA's tiles, partials
-      // added in a fixed order.
+      // Down sums of this CTA's rows, chunk partials added in a fixed order.
       named_bar_sync(1, MG_CT);
+      float* xd = a.xdn + (size_t)l * d;
       int rows = 0;
-      for (int i = threadIdx.x; i < cp_seq * MG_W2_RS; i += MG_CT) {
-        const int q = i / MG_W2_RS, lr = i % MG_W2_RS;
-        const int r = swtile[q] * MG_W2_RS + lr;
-        if (r < d) {
-          const float lo = cpart[q][lr * 4 + 0];
-          const float hi = (cpart[q][lr * 4 + 1] + cpart[q][lr * 4 + 2]) + cpart[q][lr * 4 + 3];
-          xo[r] = __fadd_rn(__fadd_rn(xs[r], lo), hi);
-        }
+      for (int i = threadIdx.x; i < cp_seq * MG_DN_RS; i += MG_CT) {
+        const int q = i / MG_DN_RS, lr = i % MG_DN_RS;
+        const int r = swtile[q] * MG_DN_RS + lr;
+        if (r < d) xd[r] = ((cpart[q][lr * 4 + 0] + cpart[q][lr * 4 + 1]) + cpart[q][lr * 4 + 2]) + cpart[q][lr * 4 + 3];
       }
       if (threadIdx.x == 0)
-        for (int q = 0; q < cp_seq; q++) rows += min(MG_W2_RS, d - swtile[q] * MG_W2_RS);
+        for (int q = 0; q < cp_seq; q++) rows += min(MG_DN_RS, d - swtile[q] * MG_DN_RS);
+      mg_publish(dl + 4, rows);
+      cp_seq = 0;
+    }
+
+    // ---- Phase D: out-projection rows over the merged attention heads (2
+    // rows per warp, all of K), then the parallel residual
+    // x + attn_o + mlp_down in the reference's order (stablelm.go:365-377).
+    mg_await(dl + 3, a.KVH, a.err);
+    {
+      stage_in(dig, adig_l, (uint32_t)(d / 16) * 48u, sx, asx_l, (uint32_t)((d / 16 + 3) & ~3) * 4u);
+      load_regs(0, d / 16);
+      for (;;) {
+        const uint8_t* st;
+        const int tag = mg_next_warp(ring, &st, a.err);
+        if (tag < 0) {
+          if (tag == -1) mg_release(ring);
+          break;
+        }
+        const int nr = min(MG_O_RS, d - tag * MG_O_RS);
+        float acc[2];
+        mg_dot2(st, (size_t)d, reinterpret_cast<const __half*>(st + (size_t)MG_O_RS * d), osc, 2 * warp, nr, 0, d / 16, dr, sxr, acc);
+        mg_release(ring);
+        if (lane == 0) {
+          cpart[cp_seq][2 * warp] = acc[0];
+          cpart[cp_seq][2 * warp + 1] = acc[1];
+          if (warp == 0) swtile[cp_seq] = tag;
+        }
+        cp_seq++;
+      }
+      // Every down sum is written (usually long before).
+      mg_await(dl + 4, d, a.err);
+      const float* xd = a.xdn + (size_t)l * d;
+      float* xo = a.xl + (size_t)(l + 1) * d;
+      int rows = 0;
+      for (int i = threadIdx.x; i < cp_seq * MG_O_RS; i += MG_CT) {
+        const int q = i / MG_O_RS, lr = i % MG_O_RS;
+        const int r = swtile[q] * MG_O_RS + lr;
+        if (r < d) xo[r] = __fadd_rn(__fadd_rn(xs[r], cpart[q][lr]), __ldcg(xd + r));
+      }
+      if (threadIdx.x == 0)
+        for (int q = 0; q < cp_seq; q++) rows += min(MG_O_RS, d - swtile[q] * MG_O_RS);
       mg_publish(dl + 2, rows);
       cp_seq = 0;
     }

@@ -355,6 +355,15 @@ static int check_tensor(const tcu_tensor* t, const std::string& name, int64_t ro
 // unit's K and V tiles fit one ring slot.
 static int set_tc_shifts(tcu_model* m);
 
+// Scale layout of a staged down-projection row: the scales of its SwiGLU
+// columns alone when they start 16-byte aligned in the row, else the whole
+// scale row with the down segment starting at *soff.
+static void mega_dn_scales(const tcu_model* m, int* sstride, int* soff) {
+  const bool aligned = (m->d / 32) % 8 == 0;
+  *sstride = aligned ? (m->ff / 32 + 7) / 8 * 8 : m->layers[0].w2.sstride;
+  *soff = aligned ? 0 : m->d / 32;
+}
+
 static int build_mega(tcu_model* m) {
   m->mega = false;
   if (m->disable_stream || m->arch != ARCH_STABLELM) return TCU_OK;
@@ -363,15 +372,18 @@ static int build_mega(tcu_model* m) {
     if (ly.w1.fmt != FMT_Q8_0 || ly.w2.fmt != FMT_Q8_0) return TCU_OK;
   const int d = m->d, ff = m->ff, K2 = d + ff;
   const int G_q = m->H / m->KVH, n_plain = d + 2 * m->kvw;
-  if (d % 32 || ff % 32 || n_plain % MG_W1_RS || d / 16 > 32 * MG_NJ || ff / 16 / 3 + 1 > 32 * MG_NJ || K2 > MG_MAXK) return TCU_OK;
+  if (d % 32 || ff % 32 || n_plain % MG_W1_RS || d / 16 > 32 * MG_NJ || (ff / 16 + 3) / 4 > 32 * MG_NJ || K2 > MG_MAXK) return TCU_OK;
   if (d / 16 > MG_CT || G_q > 32 || m->hd % 8 || (G_q * m->hd) % 16 || m->rope.pairs > 64 || m->rope.mode != 0) return TCU_OK;
   // Every W1 tile must fit under the per-CTA cap of the persistent step.
   if ((size_t)(n_plain / MG_W1_RS + ff / 16) > (size_t)m->sm_count * MG_SWT) return TCU_OK;
-  if ((size_t)(d + MG_W2_RS - 1) / MG_W2_RS > (size_t)m->sm_count * MG_SWT) return TCU_OK;
+  if ((size_t)(d + MG_DN_RS - 1) / MG_DN_RS > (size_t)m->sm_count * MG_SWT) return TCU_OK;
+  if ((size_t)(d + MG_O_RS - 1) / MG_O_RS > (size_t)m->sm_count * MG_SWT) return TCU_OK;
   cudaFuncAttributes fa;
   CK(cudaFuncGetAttributes(&fa, k_decode_mega));
   const size_t w1 = (size_t)MG_W1_RS * (d + m->layers[0].w1.sstride * 2);
-  const size_t w2 = (size_t)MG_W2_RS * (K2 + m->layers[0].w2.sstride * 2);
+  int dn_sstride = 0, dn_soff = 0;
+  mega_dn_scales(m, &dn_sstride, &dn_soff);
+  const size_t w2 = std::max((size_t)MG_DN_RS * (ff + dn_sstride * 2), (size_t)MG_O_RS * (d + (d / 32 + 7) / 8 * 8 * 2));
   const size_t hb = (size_t)MG_W1_RS * (d + m->head.sstride * 2);
   size_t slot = std::max(w1, std::max(w2, hb));
   int split = 2 * m->P;
@@ -697,8 +709,10 @@ struct Work {
   unsigned long long* keys = nullptr;  // persistent decode: argmax per step parity
   int* step = nullptr;
   // Persistent decode (decode_mega.cuh): per-layer inputs, published digits
-  // of [attention | SwiGLU] and their scales, work and completion counters.
+  // of [attention | SwiGLU] and their scales, down-projection sums, work and
+  // completion counters.
   float* xl = nullptr;
+  float* xdn = nullptr;
   uint32_t* adig = nullptr;
   float* asx = nullptr;
   int asx_stride = 0;
@@ -763,6 +777,7 @@ static int work_init(tcu_model* m, Work* w, int rows, int seqs, int logits_rows,
     const size_t nb16 = (size_t)(m->d + m->ff) / 16;
     w->asx_stride = (int)((nb16 + 3) / 4 * 4);
     TRY(w->get(&w->xl, (size_t)(m->L + 1) * m->d));
+    TRY(w->get(&w->xdn, (size_t)m->L * m->d));
     TRY(w->get(&w->adig, (size_t)m->L * nb16 * 12));
     TRY(w->get(&w->asx, (size_t)m->L * w->asx_stride));
     TRY(w->get(&w->grab, (size_t)2 * (m->L + 1) * MG_CTL));
@@ -2001,8 +2016,8 @@ static int launch_mega(tcu_session* s) {
   a.att_warp = m->mega_att_warp;
   a.grab = s->w.grab;
   a.done = s->w.done;
-  a.dig_bytes = (uint32_t)((m->d + m->ff) / 16 * 48);
-  a.sx_bytes = (uint32_t)(((m->d + m->ff) / 16 * 4 + 15) / 16 * 16);
+  mega_dn_scales(m, &a.dn_sstride, &a.dn_soff);
+  a.xdn = s->w.xdn;
   a.err = s->w.err;
   a.slot_bytes = m->mega_slot_bytes;
   a.nslots = m->mega_slots;
