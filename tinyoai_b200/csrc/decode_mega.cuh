@@ -2,7 +2,8 @@
 // whole forward of one token (stablelm.go:332-387) in a single cooperative
 // launch.
 //
-// Grid = one CTA per SM. Warp 8 lane 0 is the producer, warps 0..7 consume.
+// Grid = one CTA per SM. Warp 8 lane 0 is the producer, warps 0..7 consume,
+// warp 9 of CTA g merges the history splits of KV head g (g < KV heads).
 // Work is handed out dynamically: for each layer the producer takes items
 // from global counters -- tiles of the fused q/k/v/gate/up rows, attention
 // units (KV head x history split), tiles of the down-projection rows (the
@@ -41,7 +42,11 @@
 namespace tcu {
 
 constexpr int MG_CW = 8;                      // consumer warps
-constexpr int MG_THREADS = (MG_CW + 1) * 32;  // + producer warp
+constexpr int MG_THREADS = (MG_CW + 2) * 32;  // + producer warp + merge warp
+constexpr int MG_MW = MG_CW + 1;              // the merge warp
+// Register bound: 10 warps put 3 on two of the four SM sub-partitions, whose
+// register files hold 16,384 each, so a thread may use at most 170.
+constexpr int MG_REG_THREADS = 384;
 constexpr int MG_CT = MG_CW * 32;
 constexpr int MG_MAX_SLOTS = 6;
 constexpr int MG_W1_RS = 16;  // rows per stage, q/k/v/gate/up and head
@@ -374,6 +379,43 @@ __device__ __forceinline__ void mg_await(const int* ctr, int target, int* err) {
 // the merge costs a few L2 round trips rather than one per split.
 __device__ __forceinline__ void mg_merge_head(const float* pg, int max_splits, int hd, int G_q, int nsplit, int lane, float* wo) {
   const int rs = hd + 2;
+  if (nsplit <= 16 && hd <= 128) {
+    // Up to 16 splits: every load of a head is issued before any is used.
+    for (int hh = 0; hh < G_q; hh++) {
+      const float* ph = pg + (size_t)hh * max_splits * rs;
+      float pv[16][4];
+#pragma unroll
+      for (int j = 0; j < 16; j++)
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const int i = lane + 32 * k;
+          pv[j][k] = (j < nsplit && i < hd) ? __ldcg(ph + (size_t)j * rs + i) : 0.f;
+        }
+      const float mj = lane < nsplit ? __ldcg(ph + (size_t)lane * rs + hd) : -INFINITY;
+      const float sj = lane < nsplit ? __ldcg(ph + (size_t)lane * rs + hd + 1) : 0.f;
+      float mx = mj;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float wj = lane < nsplit ? expf(mj - mx) : 0.f;
+      float o4[4] = {0.f, 0.f, 0.f, 0.f}, lsum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const float w = __shfl_sync(0xffffffffu, wj, j);
+        const float sv = __shfl_sync(0xffffffffu, sj, j);
+        if (j < nsplit) {
+          lsum = fmaf(sv, w, lsum);
+#pragma unroll
+          for (int k = 0; k < 4; k++) o4[k] = fmaf(pv[j][k], w, o4[k]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const int i = lane + 32 * k;
+        if (i < hd) wo[hh * hd + i] = __fdiv_rn(o4[k], lsum);
+      }
+    }
+    return;
+  }
   for (int hh = 0; hh < G_q; hh++) {
     const float* ph = pg + (size_t)hh * max_splits * rs;
     float mx = -INFINITY;
@@ -539,7 +581,7 @@ __device__ __forceinline__ void mg_unit_core(const MegaArgs& a, const uint8_t* k
   }
 }
 
-__global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
+__global__ void __launch_bounds__(MG_REG_THREADS, 1) k_decode_mega(MegaArgs a) {
   extern __shared__ __align__(128) uint8_t mg_smem[];
   __shared__ float swg[MG_SWT][16], swu[MG_SWT][16];  // gate / up of this layer's gate/up tiles
   __shared__ int swtile[MG_SWT];
@@ -744,6 +786,40 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
     return;
   }
 
+  // ------------------------------------------------------------ merge warp
+  // Waits until every split of its KV heads has written its partial, merges
+  // them (fp32 max / sum) and publishes the digits of the heads' outputs.
+  if (warp == MG_MW) {
+    float* wo = att + (size_t)MG_CW * a.att_warp;  // [G_q][hd], after the consumer warps' scratch
+    const int ghd = G_q * hd, nb16 = ghd / 16;
+    for (int l = 0; l < a.L; l++) {
+      int* dl = done + l * MG_CTL;
+      uint32_t* adig_l = a.adig + (size_t)l * (K2 / 16) * 12;
+      float* asx_l = a.asx + (size_t)l * a.asx_stride;
+      for (int g = c; g < a.KVH; g += G) {
+        int ok = 1;
+        if (lane == 0) ok = mg_wait_count(a.counters + g, nsplit, a.err);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+        const float* pg = a.part + (size_t)(g * G_q) * a.max_splits * (hd + 2);
+        mg_merge_head(pg, a.max_splits, hd, G_q, nsplit, lane, wo);
+        __syncwarp();
+        for (int b = lane; b < nb16; b += 32) {
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; i++) v[i] = wo[16 * b + i];
+          mg_quant16(v, adig_l + (size_t)(g * nb16 + b) * 12, asx_l + g * nb16 + b);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          a.counters[g] = 0;  // the next layer's splits count from zero
+          mg_red_add_release(dl + 3, 1);
+        }
+        __syncwarp();
+      }
+    }
+    return;
+  }
+
   // ------------------------------------------------------------------ consumers
   if (c == 0) {
     // Control words of the next launch (the other parity) start at zero.
@@ -879,6 +955,8 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
     // ---- Phase B: attention units (stablelm.go:401-427), split over the
     // history. The k-th unit this CTA receives goes to warp k % 8, so up to
     // one unit per ring slot runs at once; the other warps release its slot.
+    // Each unit writes its partial (outputs, max, sum); the merge warp of the
+    // KV head's CTA combines them.
     {
       const int ghd = G_q * hd;
       float* wq = att + (size_t)warp * a.att_warp;  // [G_q][hd] rotated queries
@@ -944,28 +1022,8 @@ __global__ void __launch_bounds__(MG_THREADS, 1) k_decode_mega(MegaArgs a) {
           mg_unit_core<false>(a, st, pages_per_split * page_bytes, wq, cur, sc, G_q, hd, n_hist, nt, has_cur, pg, s);
         mg_release(ring);
         __syncwarp();
-        int last = 0;
-        if (lane == 0) last = mg_atom_add_acq_rel(a.counters + g, 1) == nsplit - 1;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-          // Merge the splits of KV head g (fp32 max / sum), then publish the
-          // digits of its G_q * hd outputs (a multiple of 16).
-          __syncwarp();
-          mg_merge_head(pg, a.max_splits, hd, G_q, nsplit, lane, wo);
-          __syncwarp();
-          const int nb16 = ghd / 16;
-          for (int b = lane; b < nb16; b += 32) {
-            float v[16];
-#pragma unroll
-            for (int i = 0; i < 16; i++) v[i] = wo[16 * b + i];
-            mg_quant16(v, adig_l + (size_t)(g * nb16 + b) * 12, asx_l + g * nb16 + b);
-          }
-          __syncwarp();
-          if (lane == 0) {
-            a.counters[g] = 0;
-            mg_red_add_release(dl + 3, 1);
-          }
-        }
+        // This split's partial is written: count it for the merge warp.
+        if (lane == 0) mg_red_add_release(a.counters + g, 1);
         __syncwarp();
       }
     }

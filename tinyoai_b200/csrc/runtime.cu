@@ -392,7 +392,7 @@ static int build_mega(tcu_model* m) {
   slot = (slot + 127) / 128 * 128;
   const size_t ghd = (size_t)G_q * m->hd;
   const size_t att_warp = (2 * ghd + 2 * m->hd + (size_t)G_q * split + 3) / 4 * 4;  // q, k/v, scores, outputs
-  const size_t att_floats = att_warp * MG_CW;
+  const size_t att_floats = att_warp * MG_CW + (ghd + 3) / 4 * 4;  // consumer warps, then the merge warp's outputs
   auto r128 = [](size_t b) { return (uint32_t)((b + 127) / 128 * 128); };
   const uint32_t off_x = MG_HDR;
   const uint32_t off_att = off_x + r128((size_t)d * 4);
