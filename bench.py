@@ -49,6 +49,14 @@ def q8_bytes(n):
     return n * 34 // 32
 
 
+# DRAM traffic of one k_decode_mega launch relative to its algorithmic bytes,
+# from the ncu capture of the 4-layer profiling case at T = 532
+# (dram__bytes_read.sum + dram__bytes_write.sum = 560.187904 + 4.362240 MB
+# against 558,942,880 algorithmic bytes). Traffic grows with layers and history
+# in proportion, so the bench launch's traffic is this ratio times its bytes.
+MEGA_TRAFFIC_RATIO = (560.187904e6 + 4.362240e6) / 558942880
+
+
 def decode_bytes(c, T):
     d, ff, L, V = c["hidden_size"], c["intermediate_size"], c["num_hidden_layers"], c["vocab_size"]
     kvw = d // c["num_attention_heads"] * c["num_key_value_heads"]
@@ -281,9 +289,12 @@ def run_b200(args):
         if prof["decode_step"][0]:
             dom_n, dom_ms = prof["decode_step"]
             dom_bytes, dom_kernel = step_bytes, "k_decode_mega (persistent decode step: all layers, lm_head, argmax)"
+            dom_traffic = MEGA_TRAFFIC_RATIO * step_bytes
+            dom_traffic_src = "ncu 4-layer capture (profiles/k_decode_mega_3b_4layer.md), scaled by algorithmic bytes"
         else:
             dom_n, dom_ms = prof["norm_qkv_gate_up"]
             dom_bytes, dom_kernel = w1_bytes, "k_gemv<Q8_0, LayerNorm prologue, q/k/v + SwiGLU epilogue>"
+            dom_traffic, dom_traffic_src = None, None
         achieved = dom_bytes / (dom_ms / dom_n / 1e3) / 1e9 if dom_n else None
         workload = WORKLOAD if not args.layers else WORKLOAD + f" [PROFILING CASE: {args.layers} layers, not a bench line]"
         line = {
@@ -298,7 +309,7 @@ def run_b200(args):
             "roofline": {"bound": "hbm", "kernel": dom_kernel,
                          "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": (achieved / hbm) if achieved else None, "peak_kind": peak_kind,
-                         "traffic": None, "bytes_per_launch": dom_bytes,
+                         "traffic": dom_traffic, "traffic_source": dom_traffic_src, "bytes_per_launch": dom_bytes,
                          "avg_launch_us": (dom_ms / dom_n * 1e3) if dom_n else None,
                          "decode_step_gbs": dec_gbs, "decode_step_frac": dec_gbs / hbm},
             "profile": {k: {"launches": v[0], "ms": round(v[1], 3)} for k, v in prof.items()},
