@@ -379,33 +379,38 @@ __device__ __forceinline__ void mg_await(const int* ctr, int target, int* err) {
 // the merge costs a few L2 round trips rather than one per split.
 __device__ __forceinline__ void mg_merge_head(const float* pg, int max_splits, int hd, int G_q, int nsplit, int lane, float* wo) {
   const int rs = hd + 2;
-  if (nsplit <= 16 && hd <= 128) {
-    // Up to 16 splits: every load of a head is issued before any is used.
+  if (nsplit <= 32 && hd <= 128) {
+    // Up to 32 splits (lane j holds split j's max, sum, weight): the output
+    // rows load 16 splits at a time, every load of a batch before any use.
     for (int hh = 0; hh < G_q; hh++) {
       const float* ph = pg + (size_t)hh * max_splits * rs;
-      float pv[16][4];
-#pragma unroll
-      for (int j = 0; j < 16; j++)
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-          const int i = lane + 32 * k;
-          pv[j][k] = (j < nsplit && i < hd) ? __ldcg(ph + (size_t)j * rs + i) : 0.f;
-        }
       const float mj = lane < nsplit ? __ldcg(ph + (size_t)lane * rs + hd) : -INFINITY;
       const float sj = lane < nsplit ? __ldcg(ph + (size_t)lane * rs + hd + 1) : 0.f;
-      float mx = mj;
+      float o4[4] = {0.f, 0.f, 0.f, 0.f}, lsum = 0.f, wj = 0.f;
+      for (int jb = 0; jb < nsplit; jb += 16) {
+        float pv[16][4];
 #pragma unroll
-      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float wj = lane < nsplit ? expf(mj - mx) : 0.f;
-      float o4[4] = {0.f, 0.f, 0.f, 0.f}, lsum = 0.f;
+        for (int j = 0; j < 16; j++)
 #pragma unroll
-      for (int j = 0; j < 16; j++) {
-        const float w = __shfl_sync(0xffffffffu, wj, j);
-        const float sv = __shfl_sync(0xffffffffu, sj, j);
-        if (j < nsplit) {
-          lsum = fmaf(sv, w, lsum);
+          for (int k = 0; k < 4; k++) {
+            const int i = lane + 32 * k;
+            pv[j][k] = (jb + j < nsplit && i < hd) ? __ldcg(ph + (size_t)(jb + j) * rs + i) : 0.f;
+          }
+        if (jb == 0) {
+          float mx = mj;
 #pragma unroll
-          for (int k = 0; k < 4; k++) o4[k] = fmaf(pv[j][k], w, o4[k]);
+          for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          wj = lane < nsplit ? expf(mj - mx) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const float w = __shfl_sync(0xffffffffu, wj, (jb + j) & 31);
+          const float sv = __shfl_sync(0xffffffffu, sj, (jb + j) & 31);
+          if (jb + j < nsplit) {
+            lsum = fmaf(sv, w, lsum);
+#pragma unroll
+            for (int k = 0; k < 4; k++) o4[k] = fmaf(pv[j][k], w, o4[k]);
+          }
         }
       }
 #pragma unroll
