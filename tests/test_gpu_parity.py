@@ -370,11 +370,14 @@ def test_stage_profile(small):
         s.close()
 
 
-def test_tensor_core_prefill_matches_cuda_core_prefill(monkeypatch):
-    """The tcgen05 prefill GEMM (exact binary16 splits, float32 accumulation)
-    against the CUDA-core GEMM on the same Q8_0 model: logits of a 96-token
-    prefill within 1e-4 of the logit range, identical greedy continuations."""
-    cfg, tensors = synth_stablelm(SMALL, "Q8_0", seed=23)
+@pytest.mark.parametrize("fmt", ["Q8_0", "BF16"])
+def test_tensor_core_prefill_matches_cuda_core_prefill(monkeypatch, fmt):
+    """The tcgen05 prefill GEMM (exact binary16 splits of Q8_0 weights, or
+    bfloat16 weights against a three-piece bfloat16 split of the activations;
+    float32 accumulation) against the CUDA-core GEMM on the same model:
+    logits of a 96-token prefill within 1e-4 of the logit range, identical
+    greedy continuations."""
+    cfg, tensors = synth_stablelm(SMALL, fmt, seed=23)
     ids = prompt_ids(96, cfg["vocab_size"], seed=5)
     out = {}
     for mode in ("simt", "tc"):

@@ -2,8 +2,17 @@
 // D[r][t] = sum_k W[r][k] * X[t][k] for a tile of 128 weight rows and up to
 // 256 tokens, accumulated in tensor memory (TMEM) by tcgen05.mma.
 //
-// Replaces weightTensor.mulBatch (matmul.go:55-95) for Q8_0 weights with the
-// epilogues of the CUDA-core path (gemm_simt.cuh). Exactness: a Q8_0 weight
+// Replaces weightTensor.mulBatch (matmul.go:55-95) for Q8_0 and BF16 weights
+// with the epilogues of the CUDA-core path (gemm_simt.cuh).
+//
+// BF16 weights are tensor-core operands as stored: TMA brings the weight tile
+// with the activation tiles, and the float32 activations are split exactly
+// into three bfloat16 pieces X' = X0 + X1 + X2 (8 + 8 + 8 significant bits),
+// so W.X0 + W.X1 + W.X2 (exact products, float32 accumulation) is the
+// float32 product. Tiles of up to 128 tokens keep the three pieces within
+// one stage buffer.
+//
+// Q8_0 exactness: a Q8_0 weight
 // s*q has at most 19 significant bits and an activation 24, more than one
 // binary16 operand holds, so both sides are split into an exact binary16
 // pair -- W' = W * 2^sw = Wh + Wl (Wh = fp16(s'q), Wl = fp16(fma(s', q, -Wh)))
@@ -19,6 +28,7 @@
 // memory.
 #pragma once
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include "common.cuh"
 #include "gemv.cuh"
 #include "tma.cuh"
@@ -71,9 +81,11 @@ __device__ __forceinline__ uint64_t tc_smem_desc(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor: float32 accumulator, binary16 A and B, both
-// K-major, N = n, M = 128.
-__device__ __forceinline__ uint32_t tc_idesc(int n) { return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24); }
+// Instruction descriptor: float32 accumulator, A and B both binary16 (or
+// both bfloat16), both K-major, N = n, M = 128.
+__device__ __forceinline__ uint32_t tc_idesc(int n, bool bf16) {
+  return (1u << 4) | (bf16 ? (1u << 7) | (1u << 10) : 0u) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+}
 
 __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -140,8 +152,11 @@ __device__ __forceinline__ void tc_dequant8(uint2 q, __half2 s2, uint4& hi, uint
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-template <int EPI>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
+// WB: bfloat16 weights through wmap (else Q8_0 weights dequantised by warps
+// 0-3; wmap unused).
+template <int EPI, bool WB>
+__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap xmap,
+                                                           const __grid_constant__ CUtensorMap wmap, TcArgs a) {
   extern __shared__ uint8_t tc_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * TC_BUF_BYTES);
@@ -181,27 +196,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
   auto buf = [&](int b) { return smem + (size_t)b * TC_BUF_BYTES; };
 
   if (warp == 5) {
-    // ---- activation tiles: Xh rows [t0, t0 + NT), Xl rows n_pad + the same
+    // ---- activation tiles: Xh rows [t0, t0 + NT), Xl rows n_pad + the same.
+    // BF16: the weight tile, then pieces X0, X1, X2 (rows p * n_pad + t0).
     if (lane == 0) {
-      const uint32_t bytes = (uint32_t)(2 * NT * TC_BK * 2);
+      const uint32_t bytes = WB ? (uint32_t)(TC_A_BYTES + 3 * NT * TC_BK * 2) : (uint32_t)(2 * NT * TC_BK * 2);
       for (int i = 0; i < iters; i++) {
         const int b = i & 1;
         if (i >= 2) mbar_wait(&mma_done[b], ((i >> 1) - 1) & 1, a.err);
         mbar_expect_tx(&x_full[b], bytes);
         const int k = k_begin + i * TC_BK;
-        tc_tma_load(buf(b) + 2 * TC_A_BYTES, &xmap, k, t0, &x_full[b]);
-        tc_tma_load(buf(b) + 2 * TC_A_BYTES + TC_B_BYTES, &xmap, k, a.n_pad + t0, &x_full[b]);
+        if (WB) {
+          tc_tma_load(buf(b), &wmap, k, r0, &x_full[b]);
+#pragma unroll
+          for (int p = 0; p < 3; p++) tc_tma_load(buf(b) + 2 * TC_A_BYTES + p * NT * TC_BK * 2, &xmap, k, p * a.n_pad + t0, &x_full[b]);
+        } else {
+          tc_tma_load(buf(b) + 2 * TC_A_BYTES, &xmap, k, t0, &x_full[b]);
+          tc_tma_load(buf(b) + 2 * TC_A_BYTES + TC_B_BYTES, &xmap, k, a.n_pad + t0, &x_full[b]);
+        }
       }
     }
   } else if (warp == 4) {
     // ---- MMA issue (one thread): 4 K16 steps x (Wh.Xh, Wh.Xl, Wl.Xh) per stage
     if (lane == 0) {
-      const uint32_t idesc = tc_idesc(NT);
+      const uint32_t idesc = tc_idesc(NT, WB);
       bool first0 = true, first1 = true;
       for (int i = 0; i < iters; i++) {
         const int b = i & 1;
         mbar_wait(&x_full[b], (i >> 1) & 1, a.err);
-        mbar_wait(&w_full[b], (i >> 1) & 1, a.err);
+        if (!WB) mbar_wait(&w_full[b], (i >> 1) & 1, a.err);
         tc_fence_after();
         const int k = k_begin + i * TC_BK;
         const bool second = two_acc && k >= a.k_split;
@@ -210,13 +232,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         const uint32_t sa = smem_u32(buf(b)), sb = sa + 2 * TC_A_BYTES;
 #pragma unroll
         for (int kk = 0; kk < TC_BK / 16; kk++) {
-          const uint32_t off = kk * 32;  // 16 binary16 columns
-          const uint64_t wh = tc_smem_desc(sa + off), wl = tc_smem_desc(sa + TC_A_BYTES + off);
-          const uint64_t xh = tc_smem_desc(sb + off), xl = tc_smem_desc(sb + TC_B_BYTES + off);
-          tc_mma(d, wh, xh, idesc, first ? 0u : 1u);
-          first = false;
-          tc_mma(d, wh, xl, idesc, 1u);
-          tc_mma(d, wl, xh, idesc, 1u);
+          const uint32_t off = kk * 32;  // 16 columns of 2 bytes
+          if (WB) {
+            const uint64_t w = tc_smem_desc(sa + off);
+#pragma unroll
+            for (int p = 0; p < 3; p++) {
+              tc_mma(d, w, tc_smem_desc(sb + p * NT * TC_BK * 2 + off), idesc, first ? 0u : 1u);
+              first = false;
+            }
+          } else {
+            const uint64_t wh = tc_smem_desc(sa + off), wl = tc_smem_desc(sa + TC_A_BYTES + off);
+            const uint64_t xh = tc_smem_desc(sb + off), xl = tc_smem_desc(sb + TC_B_BYTES + off);
+            tc_mma(d, wh, xh, idesc, first ? 0u : 1u);
+            first = false;
+            tc_mma(d, wh, xl, idesc, 1u);
+            tc_mma(d, wl, xh, idesc, 1u);
+          }
         }
         tc_commit(&mma_done[b]);
       }
@@ -227,7 +258,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     const int tid = threadIdx.x;  // 0..127
     const int kc = (tid & 3) * 16;
     const float wscale = tc_pow2(a.sw);
-    for (int i = 0; i < iters; i++) {
+    for (int i = 0; i < (WB ? 0 : iters); i++) {
       const int b = i & 1;
       if (i >= 2) mbar_wait(&mma_done[b], ((i >> 1) - 1) & 1, a.err);
       uint8_t* ah = buf(b);
@@ -342,6 +373,48 @@ __global__ void k_split_f16(const float* X, int ldx, int n, int K, int n_pad, __
     const __half h = __float2half_rn(v);
     hi[k] = h;
     lo[k] = __float2half_rn(v - __half2float(h));
+  }
+}
+
+// Exact bfloat16 split of activation rows: per token t the power of two sx(t)
+// as in k_split_f16, then X' = X * 2^sx = X0 + X1 + X2 with each piece the
+// bfloat16 rounding of what the previous pieces leave (both differences are
+// exact in float32). out: [3][n_pad][K] bfloat16.
+__global__ void k_split_bf16(const float* X, int ldx, int n, int K, int n_pad, __nv_bfloat16* out, int* sx) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const float* x = X + (size_t)t * ldx;
+  float mx = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(x[k]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0) {
+      int e = 0;
+      if (m > 0.f) frexpf(m, &e);
+      red[0] = (float)(m > 0.f ? 13 - e : 0);
+    }
+  }
+  __syncthreads();
+  const int s = (int)red[0];
+  if (threadIdx.x == 0) sx[t] = s;
+  const float scale = tc_pow2(s);
+  __nv_bfloat16* p0 = out + (size_t)t * K;
+  __nv_bfloat16* p1 = out + ((size_t)n_pad + t) * K;
+  __nv_bfloat16* p2 = out + ((size_t)2 * n_pad + t) * K;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const float v = x[k] * scale;
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    const float r1 = v - __bfloat162float(h);
+    const __nv_bfloat16 m1 = __float2bfloat16_rn(r1);
+    p0[k] = h;
+    p1[k] = m1;
+    p2[k] = __float2bfloat16_rn(r1 - __bfloat162float(m1));
   }
 }
 

@@ -1128,17 +1128,20 @@ static int work_reserve(void** p, size_t bytes) {
   return TCU_OK;
 }
 
-// Enqueues a Q8_0 product on the tensor cores; false if this shape or format
-// takes the CUDA-core path.
+// Enqueues a Q8_0 or BF16 product on the tensor cores; false if this shape
+// or format takes the CUDA-core path.
 template <int EPI>
 static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaStream_t s) {
   const DMat& W = g.W;
   const int K = W.cols, R = W.rows, n = g.n;
-  if (!m->use_tc || !w || W.fmt != FMT_Q8_0 || K % 16 || n < 1 || R < 1) return false;
+  const bool wb = W.fmt == FMT_BF16;
+  if (!m->use_tc || !w || !(W.fmt == FMT_Q8_0 || wb) || K % 16 || n < 1 || R < 1) return false;
+  if (wb && ((uintptr_t)W.w % 16)) return false;
   if (EPI == EPI_RESID2 && g.k_split % TC_BK) return false;
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (!encode) return false;
-  const int n_tile = std::min(TC_MAXN, (n + 15) / 16 * 16);
+  const int pieces = wb ? 3 : 2;  // activation split: bfloat16 x3 or binary16 x2
+  const int n_tile = std::min(wb ? 128 : TC_MAXN, (n + 15) / 16 * 16);
   const int n_pad = (n + n_tile - 1) / n_tile * n_tile;
   const int row_tiles = (R + TC_BM - 1) / TC_BM;
   // Too few tiles to fill the GPU: split K into slices (out/down rows only).
@@ -1161,7 +1164,7 @@ static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaS
     w->tc_split = nullptr;
     w->tc_sx = nullptr;
     w->tc_npad = w->tc_kmax = 0;
-    if (work_reserve((void**)&w->tc_split, (size_t)2 * np * kk * 2) || work_reserve((void**)&w->tc_sx, (size_t)np * 4)) return false;
+    if (work_reserve((void**)&w->tc_split, (size_t)3 * np * kk * 2) || work_reserve((void**)&w->tc_sx, (size_t)np * 4)) return false;
     w->tc_npad = np;
     w->tc_kmax = kk;
   }
@@ -1172,30 +1175,48 @@ static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaS
     if (work_reserve((void**)&w->tc_part, (size_t)z * n * R * 4)) return false;
     w->tc_part_floats = (size_t)z * n * R;
   }
-  CUtensorMap map;
+  const CUtensorMapDataType dt = wb ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap map, wmap;
   {
-    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)(2 * n_pad)};
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)(pieces * n_pad)};
     cuuint64_t strides[1] = {(cuuint64_t)K * 2};
     cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)n_tile};
     cuuint32_t estr[2] = {1, 1};
-    if (encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w->tc_split, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+    if (encode(&map, dt, 2, w->tc_split, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  wmap = map;
+  if (wb) {
+    // bfloat16 weights [R][K], tiles of 128 rows x 64 columns.
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)R};
+    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)TC_BM};
+    cuuint32_t estr[2] = {1, 1};
+    if (encode(&wmap, dt, 2, const_cast<uint8_t*>(W.w), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return false;
   }
-  if (cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess) {
+  auto kern = wb ? k_gemm_tc<EPI, true> : k_gemm_tc<EPI, false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess) {
     cudaGetLastError();
     return false;
   }
   PROF_BEGIN(g_stage, s);
-  k_split_f16<<<n, 256, 0, s>>>(g.A, g.lda, n, K, n_pad, w->tc_split, w->tc_sx);
-  NOTE("k_split_f16");
+  if (wb) {
+    k_split_bf16<<<n, 256, 0, s>>>(g.A, g.lda, n, K, n_pad, reinterpret_cast<__nv_bfloat16*>(w->tc_split), w->tc_sx);
+    NOTE("k_split_bf16");
+  } else {
+    k_split_f16<<<n, 256, 0, s>>>(g.A, g.lda, n, K, n_pad, w->tc_split, w->tc_sx);
+    NOTE("k_split_f16");
+  }
   TcArgs a{};
   a.W = W;
   a.n = n;
   a.n_tile = n_tile;
   a.n_pad = n_pad;
   a.sx = w->tc_sx;
-  a.sw = W.tc_sw;
+  a.sw = wb ? 0 : W.tc_sw;
   a.out = g.out;
   a.out_stride = g.out_stride;
   a.n_plain = g.n_plain;
@@ -1208,7 +1229,7 @@ static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaS
   a.part = z > 1 ? w->tc_part : nullptr;
   a.k_per_z = k_per_z;
   a.err = w->err;
-  k_gemm_tc<EPI><<<dim3(row_tiles, n_pad / n_tile, z), TC_THREADS, TC_SMEM, s>>>(map, a);
+  kern<<<dim3(row_tiles, n_pad / n_tile, z), TC_THREADS, TC_SMEM, s>>>(map, wmap, a);
   NOTE("k_gemm_tc");
   if (z > 1) {
     k_splitk_resid<<<m->sm_count * 4, 256, 0, s>>>(w->tc_part, z_lo, z, n, R, g.resid, g.resid_stride);
