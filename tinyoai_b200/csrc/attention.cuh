@@ -314,111 +314,154 @@ struct PrefillAttnArgs {
   float scale;
 };
 
-constexpr int PA_QT = 16;  // queries per CTA
-constexpr int PA_KT = 64;  // keys per tile
+constexpr int PA_QT = 64;       // queries per CTA
+constexpr int PA_KT = 64;       // keys per tile
+constexpr int PA_THREADS = 256;  // 16 row groups (4 queries) x 16 column groups
+constexpr int PA_KTS = PA_KT + 4;  // row stride of the transposed key tile (floats)
 
-__global__ void __launch_bounds__(128) k_attn_prefill(PrefillAttnArgs a) {
+// Dynamic shared memory of k_attn_prefill for head size hd.
+__host__ __device__ inline size_t pa_smem_bytes(int hd) {
+  return sizeof(float) * ((size_t)hd * PA_QT + (size_t)hd * PA_KTS + (size_t)PA_KT * hd + (size_t)PA_KT * PA_QT);
+}
+
+// Causal attention of a prefill chunk (attention.go:6-45 semantics: every
+// query attends to the history and to the chunk up to itself), flash style on
+// CUDA cores. One CTA per (64-query tile, query head). Thread (rg, cg) holds
+// the scores of queries 4rg..4rg+3 against keys 4cg..4cg+3 of the current
+// 64-key tile, each a float32 dot product in dimension order divided by
+// sqrt(hd) (stablelm.go:401-431), and the outputs of the same four queries
+// at dimensions cg, cg + 16, ... . Queries and keys sit transposed in shared
+// memory, so each step of a dot product is two float4 loads and 16 FMAs. The
+// softmax runs online over the key tiles (fp32 max, expf, sum), the weighted
+// values accumulate in key order.
+__global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(PrefillAttnArgs a) {
   extern __shared__ __align__(16) float pa_smem[];
   const int hd = a.hd, h = blockIdx.y, g = h / (a.H / a.KVH);
   const int q0 = blockIdx.x * PA_QT;
   const int nq = min(PA_QT, a.n - q0);
-  float* qs = pa_smem;                    // [QT][hd+1]
-  float* ks = qs + PA_QT * (hd + 1);      // [KT][hd+1]
-  float* vs = ks + PA_KT * (hd + 1);      // [KT][hd+1]
-  float* ps = vs + PA_KT * (hd + 1);      // [QT][KT]
-  __shared__ float mrow[PA_QT], lrow[PA_QT], alpha[PA_QT];
-  for (int e = threadIdx.x; e < PA_QT * hd; e += blockDim.x) {
+  float* qT = pa_smem;               // [hd][QT]
+  float* kT = qT + hd * PA_QT;       // [hd][KTS]
+  float* vs = kT + hd * PA_KTS;      // [KT][hd]
+  float* ps = vs + PA_KT * hd;       // [KT][QT] softmax weights
+  const int tid = threadIdx.x, rg = tid >> 4, cg = tid & 15;
+  for (int e = tid; e < PA_QT * hd; e += PA_THREADS) {
     const int qi = e / hd, i = e % hd;
-    qs[qi * (hd + 1) + i] = qi < nq ? a.qkv[(size_t)(q0 + qi) * a.qkv_stride + h * hd + i] : 0.f;
+    qT[i * PA_QT + qi] = qi < nq ? a.qkv[(size_t)(q0 + qi) * a.qkv_stride + h * hd + i] : 0.f;
   }
-  if (threadIdx.x < PA_QT) {
-    mrow[threadIdx.x] = -INFINITY;
-    lrow[threadIdx.x] = 0.f;
-  }
-  // Output accumulators: thread owns (qi, i) pairs e = tid + 128*j.
-  constexpr int MAXO = (PA_QT * 128 + 127) / 128;  // supports hd <= 128
-  float acc[MAXO];
+  constexpr int MAXC = 8;  // output columns per thread: hd <= 128
+  const int ncol = (hd + 15) / 16;
+  float o[4][MAXC];
 #pragma unroll
-  for (int j = 0; j < MAXO; j++) acc[j] = 0.f;
+  for (int r = 0; r < 4; r++)
+#pragma unroll
+    for (int j = 0; j < MAXC; j++) o[r][j] = 0.f;
+  float m[4], l[4];
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+  }
   const int last_pos = a.start + q0 + nq - 1;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int t0 = 0; t0 <= last_pos; t0 += PA_KT) {
     const int nt = min(PA_KT, last_pos + 1 - t0);
-    __syncthreads();
+    __syncthreads();  // the previous tile's keys, values and weights are read
     for (int t = 0; t < nt;) {
       const int ta = t0 + t;
       const int page = a.page_table[ta / a.kv.P], row = ta % a.kv.P;
       const int n = min(nt - t, a.kv.P - row);
-      const size_t o = a.kv.off(a.layer, page, g, row);
-      for (int e = threadIdx.x; e < n * hd; e += blockDim.x) {
+      const size_t off = a.kv.off(a.layer, page, g, row);
+      for (int e = tid; e < n * hd; e += PA_THREADS) {
         const int r = e / hd, c = e % hd;
         float kk, vv;
         if (a.kv.half) {
-          kk = __half2float(reinterpret_cast<const __half*>(a.kv.k)[o + e]);
-          vv = __half2float(reinterpret_cast<const __half*>(a.kv.v)[o + e]);
+          kk = __half2float(reinterpret_cast<const __half*>(a.kv.k)[off + e]);
+          vv = __half2float(reinterpret_cast<const __half*>(a.kv.v)[off + e]);
         } else {
-          kk = reinterpret_cast<const float*>(a.kv.k)[o + e];
-          vv = reinterpret_cast<const float*>(a.kv.v)[o + e];
+          kk = reinterpret_cast<const float*>(a.kv.k)[off + e];
+          vv = reinterpret_cast<const float*>(a.kv.v)[off + e];
         }
-        ks[(t + r) * (hd + 1) + c] = kk;
-        vs[(t + r) * (hd + 1) + c] = vv;
+        kT[c * PA_KTS + t + r] = kk;
+        vs[(t + r) * hd + c] = vv;
       }
       t += n;
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < PA_QT * PA_KT; e += blockDim.x) {
-      const int qi = e / PA_KT, t = e % PA_KT;
-      float sv = -INFINITY;
-      if (qi < nq && t < nt && t0 + t <= a.start + q0 + qi) {
-        const float* q = qs + qi * (hd + 1);
-        const float* k = ks + t * (hd + 1);
-        float d = 0.f;
-        for (int i = 0; i < hd; i++) d = fmaf(q[i], k[i], d);
-        sv = __fdiv_rn(d, a.scale);
-      }
-      ps[qi * PA_KT + t] = sv;
+    // Scores of 4 queries x 4 keys.
+    float sc[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) sc[r][c] = 0.f;
+    for (int i = 0; i < hd; i++) {
+      const float4 qv = *reinterpret_cast<const float4*>(qT + i * PA_QT + 4 * rg);
+      const float4 kv = *reinterpret_cast<const float4*>(kT + i * PA_KTS + 4 * cg);
+      const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int r = 0; r < 4; r++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) sc[r][c] = fmaf(qa[r], ka[c], sc[r][c]);
     }
-    __syncthreads();
-    for (int qi = warp; qi < PA_QT; qi += 4) {
+    float alpha[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int qi = 4 * rg + r;
+      const int qpos = a.start + q0 + qi;
       float mx = -INFINITY;
-      for (int t = lane; t < PA_KT; t += 32) mx = fmaxf(mx, ps[qi * PA_KT + t]);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float mnew = fmaxf(mrow[qi], mx);
-      float l = 0.f;
-      for (int t = lane; t < PA_KT; t += 32) {
-        float sv = ps[qi * PA_KT + t];
-        float p = (sv == -INFINITY) ? 0.f : expf(sv - mnew);
-        ps[qi * PA_KT + t] = p;
-        l += p;
+      for (int c = 0; c < 4; c++) {
+        const int t = 4 * cg + c;
+        const bool ok = qi < nq && t < nt && t0 + t <= qpos;
+        sc[r][c] = ok ? __fdiv_rn(sc[r][c], a.scale) : -INFINITY;
+        mx = fmaxf(mx, sc[r][c]);
       }
-      l = warp_sum(l);
-      if (lane == 0) {
-        float al = (mrow[qi] == -INFINITY) ? 0.f : expf(mrow[qi] - mnew);
-        alpha[qi] = al;
-        lrow[qi] = lrow[qi] * al + l;
-        mrow[qi] = mnew;
+#pragma unroll
+      for (int x = 1; x < 16; x <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, x));
+      const float mnew = fmaxf(m[r], mx);
+      float ls = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        const float p = sc[r][c] == -INFINITY ? 0.f : expf(sc[r][c] - mnew);
+        sc[r][c] = p;
+        ls += p;
       }
+#pragma unroll
+      for (int x = 1; x < 16; x <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, x);
+      alpha[r] = m[r] == -INFINITY ? 0.f : expf(m[r] - mnew);
+      l[r] = l[r] * alpha[r] + ls;
+      m[r] = mnew;
     }
-    __syncthreads();
 #pragma unroll
-    for (int j = 0; j < MAXO; j++) {
-      const int e = threadIdx.x + 128 * j;
-      if (e < PA_QT * hd) {
-        const int qi = e / hd, i = e % hd;
-        float o = acc[j] * alpha[qi];
-        for (int t = 0; t < nt; t++) o = fmaf(ps[qi * PA_KT + t], vs[t * (hd + 1) + i], o);
-        acc[j] = o;
+    for (int c = 0; c < 4; c++)
+      *reinterpret_cast<float4*>(ps + (4 * cg + c) * PA_QT + 4 * rg) = make_float4(sc[0][c], sc[1][c], sc[2][c], sc[3][c]);
+    __syncthreads();
+    // Outputs of the same 4 queries at dimensions cg + 16 j, keys in order.
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+#pragma unroll
+      for (int j = 0; j < MAXC; j++) o[r][j] *= alpha[r];
+    for (int t = 0; t < nt; t++) {
+      const float4 pv = *reinterpret_cast<const float4*>(ps + t * PA_QT + 4 * rg);
+      const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+      const float* vr = vs + t * hd;
+#pragma unroll
+      for (int j = 0; j < MAXC; j++) {
+        const int c = cg + 16 * j;
+        if (j < ncol && c < hd) {
+          const float vv = vr[c];
+#pragma unroll
+          for (int r = 0; r < 4; r++) o[r][j] = fmaf(pa[r], vv, o[r][j]);
+        }
       }
     }
   }
-  __syncthreads();
 #pragma unroll
-  for (int j = 0; j < MAXO; j++) {
-    const int e = threadIdx.x + 128 * j;
-    if (e < PA_QT * hd) {
-      const int qi = e / hd, i = e % hd;
-      if (qi < nq) a.out[(size_t)(q0 + qi) * a.out_stride + h * hd + i] = __fdiv_rn(acc[j], lrow[qi]);
+  for (int r = 0; r < 4; r++) {
+    const int qi = 4 * rg + r;
+    if (qi >= nq) continue;
+#pragma unroll
+    for (int j = 0; j < MAXC; j++) {
+      const int c = cg + 16 * j;
+      if (j < ncol && c < hd) a.out[(size_t)(q0 + qi) * a.out_stride + h * hd + c] = __fdiv_rn(o[r][j], l[r]);
     }
   }
 }
