@@ -127,7 +127,7 @@ class ClockSampler:
                 "samples": len(self.samples), "reasons": sorted(self.reasons)}
 
 
-def cpu_sample(cfg, tensors, prompt, budget_s=20.0):
+def cpu_sample(cfg, tensors, prompt, budget_s=20.0, fmt="Q8_0", extrapolation=None):
     """Times the CPU oracle (a C restatement of the reference's Go scalar path,
     OpenMP over rows and heads on every host core) on a bounded sample of the
     workload: a short prompt prefill and a few decode forwards of the same 3B
@@ -149,9 +149,9 @@ def cpu_sample(cfg, tensors, prompt, budget_s=20.0):
             n_dec += 1
     finally:
         m.close()
+    extrapolation = extrapolation or f"{PROMPT}/prefill_rate + {GEN}/decode_rate"
     sample = (f"oracle (C port of the Go scalar path, {oc.threads()} OpenMP threads): prefill of {n_pf} prompt tokens "
-              f"and {n_dec} decode forwards of the full 3B Q8_0 model; step time extrapolated as "
-              f"{PROMPT}/prefill_rate + {GEN}/decode_rate")
+              f"and {n_dec} decode forwards of the full 3B {fmt} model; step time extrapolated as {extrapolation}")
     return n_pf / t_pf, n_dec / t_dec, oc.threads(), sample
 
 
@@ -332,6 +332,175 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+# Supplementary workloads: BASELINE.json configs 3 and 4 on the same 3B shape.
+CONFIGS = {
+    3: dict(fmt="BF16", kv="f16", prompt=8129, gen=64,
+            metric="prefill & decode tok/s, 3B StableLM BF16, 8129-token prompt + 64 greedy, f16 KV",
+            workload="config 3: 3B StableLM BF16, prompt 8129 + greedy 64 (8192 context), f16 KV, 512-token prefill chunks, "
+                     "one sequence per GPU (head-parallel sharding not built: replicas)"),
+    4: dict(fmt="Q6_K", kv="f16", prefix=4043, branches=64, suffix_max=64, gen=32,
+            metric="prefix prefill & branch tok/s, 3B StableLM K-quant, 4043-token prefix + 64 ragged branches x 32 greedy",
+            workload="config 4: 3B StableLM {fmt}, f16 KV, shared prefix 4043, 64 branches with suffix lengths U[1,64] "
+                     "(seeded), 32 greedy tokens each; branches split across GPUs"),
+}
+
+
+def kquant_bytes(fmt, n):
+    return n * (210 if fmt == "Q6_K" else 176 if fmt == "Q5_K" else 2) // (256 if fmt in ("Q6_K", "Q5_K") else 1)
+
+
+def run_config(args):
+    """One step of config 3 (prefill of 8129 tokens in 512-token chunks, then
+    64 greedy tokens) or config 4 (prefill of the shared 4043-token prefix,
+    then 64 branches at the same absolute position: each is fed its own
+    suffix, then its own greedy argmax, until it has 32 generated tokens;
+    counted tokens are the prefix plus every branch's suffix and generated
+    tokens). Device time with CUDA events on the library's stream, max over
+    ranks; e2e is the host clock around the same public calls."""
+    import torch
+    import torch.distributed as dist
+
+    from tinyoai_b200 import Model, replicas
+    from tinyoai_b200.synth import CLIO_3B, prompt_ids, synth_stablelm
+
+    c = dict(CONFIGS[args.config])
+    if args.fmt:
+        c["fmt"] = args.fmt
+    world, rank, local = replicas.world()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=torch.device("cuda", local))
+    cfg = dict(CLIO_3B)
+    if args.layers:
+        cfg["num_hidden_layers"] = args.layers
+    cfg, tensors = synth_stablelm(cfg, c["fmt"], seed=0, device=f"cuda:{local}")
+    model = Model.load_stablelm(cfg, tensors, device=local, kv_pool_bytes=args.kv_pool_mb << 20)
+    torch.cuda.empty_cache()
+    cpu_tensors = tensors if (rank == 0 and world == 1 and args.cpu_baseline) else None
+    del tensors
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    V = cfg["vocab_size"]
+    if args.config == 3:
+        prompt = prompt_ids(c["prompt"], V, seed=rank)
+        units = c["prompt"] + c["gen"]
+
+        def step(ev):
+            sess = model.session(c["kv"])
+            sess.set_stream(stream.cuda_stream)
+            try:
+                ev[0].record(stream)
+                sess.forward(0, prompt[:-1], want_logits=False)
+                ev[1].record(stream)
+                out = sess.generate_greedy(len(prompt) - 1, prompt[-1:], c["gen"])
+                ev[2].record(stream)
+            finally:
+                sess.close()
+            return out
+    else:
+        rng = np.random.default_rng(1234)
+        suffix_len = rng.integers(1, c["suffix_max"] + 1, c["branches"])
+        lo, hi = replicas.shard(c["branches"], world, rank)
+        mine = suffix_len[lo:hi]
+        suffixes = [prompt_ids(int(n), V, seed=1000 + lo + b) for b, n in enumerate(mine)]
+        prefix = prompt_ids(c["prefix"], V, seed=0)
+        units = c["prefix"] + int(mine.sum()) + len(mine) * c["gen"]
+
+        def step(ev):
+            sess = model.session(c["kv"])
+            sess.set_stream(stream.cuda_stream)
+            try:
+                ev[0].record(stream)
+                sess.forward(0, prefix, want_logits=False)
+                ev[1].record(stream)
+                br = sess.new_branches(len(prefix), len(mine))
+                try:
+                    nxt = np.zeros(len(mine), np.int32)
+                    for t in range(int(mine.max()) + c["gen"]):
+                        toks = np.array([suffixes[b][t] if t < mine[b] else nxt[b] for b in range(len(mine))], np.int32)
+                        br.forward(toks, want_rows=False)
+                        nxt = br.argmax()
+                finally:
+                    br.close()
+                ev[2].record(stream)
+            finally:
+                sess.close()
+            return nxt
+
+    for _ in range(args.warmup):
+        step([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    host = []
+    replicas.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            t0 = time.perf_counter()
+            step(evs[i])
+            torch.cuda.synchronize()
+            host.append((time.perf_counter() - t0) * 1e3)
+    replicas.barrier()
+    total_ms = sum(e[0].elapsed_time(e[2]) for e in evs)
+    pf_ms = sum(e[0].elapsed_time(e[1]) for e in evs)
+    rest_ms = sum(e[1].elapsed_time(e[2]) for e in evs)
+    total_ms, pf_ms, rest_ms, host_ms = replicas.max_over_ranks([total_ms, pf_ms, rest_ms, sum(host)], device="cuda")
+    if rank == 0:
+        hbm, peak_kind = peaks()
+        peaks_f = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        tflops_peak = peaks_f.get("bf16_tflops", 1590.0)
+        d, ff, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"]
+        kvw = d // cfg["num_attention_heads"] * cfg["num_key_value_heads"]
+        per_tok = L * ((d + 2 * kvw + 2 * ff) * d + d * (d + ff))  # matrix weights touched per token
+        n_pf = (c["prompt"] - 1) if args.config == 3 else c["prefix"]
+        # Prefill work: projections 2 * weights * n plus causal attention 2 * 2 * L * d * n^2 / 2.
+        pf_flop = 2.0 * per_tok * n_pf + 2.0 * L * d * float(n_pf) ** 2
+        pf_tfs = pf_flop / (pf_ms / args.steps / 1e3) / 1e12
+        if args.config == 3:
+            T = c["prompt"] + c["gen"] / 2
+            step_bytes = kquant_bytes(c["fmt"], per_tok + cfg["vocab_size"] * d) + 2 * L * kvw * 2 * (T + 1)
+            rest_units = c["gen"]
+            rest_gbs = step_bytes * rest_units / (rest_ms / args.steps / 1e3) / 1e9
+            rest_name = "decode (per token: all weights + f16 KV history)"
+        else:
+            n_steps = int(suffix_len.max()) + c["gen"]
+            rows = hi - lo
+            # per branch step: every weight once + the shared prefix KV once + each branch's suffix KV
+            step_bytes = kquant_bytes(c["fmt"], per_tok + cfg["vocab_size"] * d) + 2 * L * kvw * 2 * c["prefix"]
+            rest_units = n_steps
+            rest_gbs = step_bytes * rest_units / (rest_ms / args.steps / 1e3) / 1e9
+            rest_name = f"branch steps ({rows} rows each: weights once + shared prefix KV once)"
+        dominant = "prefill" if pf_ms >= rest_ms else "rest"
+        roof = ({"bound": "tensor", "stage": "prefill (projections + causal attention)", "achieved": pf_tfs, "peak": tflops_peak,
+                 "unit": "TFLOP/s", "frac": pf_tfs / tflops_peak, "peak_kind": peak_kind, "traffic": None}
+                if dominant == "prefill" else
+                {"bound": "hbm", "stage": rest_name, "achieved": rest_gbs, "peak": hbm, "unit": "GB/s", "frac": rest_gbs / hbm,
+                 "peak_kind": peak_kind, "traffic": None})
+        value = replicas.aggregate_rate(units * args.steps, world, total_ms / 1e3)
+        line = {"metric": c["metric"], "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": f"{c['fmt']} weights, f32 activations, f16 KV",
+                "data": "synthetic (seeded N(0,0.02) weights quantised to the format, uniform ids)",
+                "config": {"workload": c["workload"].format(fmt=c["fmt"]) + (f" [PROFILING CASE: {args.layers} layers]" if args.layers else ""),
+                           "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (GBs of weights per step)"},
+                "prefill_tok_s": world * n_pf * args.steps / (pf_ms / 1e3), "prefill_tflops": pf_tfs,
+                "rest_ms_per_step": rest_ms / args.steps, "rest_gbs": rest_gbs,
+                "roofline": roof, "clocks": clocks.summary(),
+                "e2e": {"value": replicas.aggregate_rate(units * args.steps, world, host_ms / 1e3), "unit": "tok/s",
+                        "h2d_bytes_per_step": 4 * units, "d2h_bytes_per_step": 4 * (c["gen"] if args.config == 3 else rest_units * (hi - lo))}}
+        if cpu_tensors is not None:
+            prompt0 = prompt_ids(512, V, seed=0)
+            pf, dc, cores, sample = cpu_sample(cfg, cpu_tensors, prompt0, budget_s=12.0, fmt=c["fmt"],
+                                               extrapolation=f"{n_pf}/prefill_rate + {units - n_pf}/decode_rate "
+                                                             "(short-context rates: attention over long histories not included)")
+            line["cpu_baseline"] = {"value": units / (n_pf / pf + (units - n_pf) / dc), "unit": "tok/s", "cores": cores,
+                                    "kind": "port", "sample": sample}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -342,8 +511,13 @@ def main():
     ap.add_argument("--kv-pool-mb", type=int, default=2048, help="KV page pool per GPU (config 2 needs ~0.5 GB)")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: fewer layers of the 3B shape (a bench line always uses all 32)")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
+                    help="2: the bench line (default); 3, 4: BASELINE.json's long-context and branch workloads")
+    ap.add_argument("--fmt", default=None, help="config 4 weight format: Q6_K (default) or Q5_K")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.config != 2 and args.impl == "b200":
+        run_config(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

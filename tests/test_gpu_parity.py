@@ -159,6 +159,74 @@ def test_bf16_model():
         ora16.close()
 
 
+# K-quant super-blocks span 256 columns: hidden and MLP widths are multiples.
+KQ_SMALL = dict(SMALL, hidden_size=256, intermediate_size=768)
+
+
+@pytest.mark.parametrize("fmt", ["Q6_K", "Q5_K"])
+@pytest.mark.parametrize("kv", ["f32", "f16"])
+def test_kquant_model_vs_oracle(fmt, kv):
+    """Q6_K / Q5_K weights (config 4's formats, quant_k.go:47-85) through the
+    prefill GEMM and the per-token GEMV: logits against the oracle's
+    decode-then-multiply at the north-star tolerance, then identical greedy
+    streams."""
+    cfg, tensors = synth_stablelm(KQ_SMALL, fmt, seed=31)
+    m = Model.load_stablelm(cfg, tensors)
+    ids = prompt_ids(120, cfg["vocab_size"], seed=13)
+    ora = oc.StableLM(cfg, tensors, half_kv=(kv == "f16"), capacity=cfg["max_position_embeddings"])
+    tol = 2e-3 if kv == "f32" else 1e-2
+    s = m.session(kv)
+    try:
+        assert rel_err(s.forward(0, ids[:96]), ora.prefill(ids[:96])) <= tol
+        for pos in range(96, 120):
+            assert rel_err(s.forward(pos, [ids[pos]]), ora.forward(ids[pos], pos)) <= tol, pos
+    finally:
+        s.close()
+        ora.close()
+    ora = oc.StableLM(cfg, tensors, half_kv=(kv == "f16"), capacity=cfg["max_position_embeddings"])
+    s = m.session(kv)
+    try:
+        want, margins = ora.greedy(ids[:64], 24, chunk=128)
+        got = s.generate_greedy(0, ids[:64], 24)
+    finally:
+        s.close()
+        ora.close()
+        m.close()
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, f"first divergence at step {bad[0]} (oracle top-2 margin {margins[bad[0]]:.3g})"
+
+
+@pytest.mark.parametrize("fmt", ["Q6_K", "Q5_K"])
+def test_kquant_branches_match_sequential(fmt):
+    """Config 4's shape in small: branches over a shared prefix with K-quant
+    weights and f16 KV (batched rows) equal sessions that evaluated prefix +
+    their own suffix."""
+    cfg, tensors = synth_stablelm(KQ_SMALL, fmt, seed=37)
+    m = Model.load_stablelm(cfg, tensors)
+    count = 8
+    ids = prompt_ids(70, cfg["vocab_size"], seed=43)
+    rng = np.random.default_rng(7)
+    steps = [rng.integers(3, cfg["vocab_size"], count).astype(np.int32) for _ in range(5)]
+    s = m.session("f16")
+    try:
+        s.forward(0, ids, want_logits=False)
+        br = s.new_branches(70, count)
+        try:
+            rows = [br.forward(t) for t in steps]
+        finally:
+            br.close()
+        for b in range(count):
+            ref = m.session("f16")
+            try:
+                want = ref.forward(0, np.concatenate([ids, [st[b] for st in steps]]))
+            finally:
+                ref.close()
+            assert rel_err(rows[-1][b], want) <= 1e-4
+    finally:
+        s.close()
+        m.close()
+
+
 def test_prefix_reuse_matches_cold(small):
     """prefill_test.go:68-109: extending or replacing a resident suffix gives
     the same logits as a cold evaluation."""

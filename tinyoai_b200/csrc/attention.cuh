@@ -333,8 +333,11 @@ __host__ __device__ inline size_t pa_smem_bytes(int hd) {
 // at dimensions cg, cg + 16, ... . Queries and keys sit transposed in shared
 // memory, so each step of a dot product is two float4 loads and 16 FMAs. The
 // softmax runs online over the key tiles (fp32 max, expf, sum), the weighted
-// values accumulate in key order.
-__global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(PrefillAttnArgs a) {
+// values accumulate in key order. The next tile's keys and values are loaded
+// into registers (4 values per load) while the current tile is computed.
+// NC = ceil(hd / 16): output columns and 4-value load chunks per thread.
+template <int NC>
+__global__ void __launch_bounds__(PA_THREADS, NC <= 5 ? 2 : 1) k_attn_prefill(PrefillAttnArgs a) {
   extern __shared__ __align__(16) float pa_smem[];
   const int hd = a.hd, h = blockIdx.y, g = h / (a.H / a.KVH);
   const int q0 = blockIdx.x * PA_QT;
@@ -348,7 +351,7 @@ __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(PrefillAttnArgs a) 
     const int qi = e / hd, i = e % hd;
     qT[i * PA_QT + qi] = qi < nq ? a.qkv[(size_t)(q0 + qi) * a.qkv_stride + h * hd + i] : 0.f;
   }
-  constexpr int MAXC = 8;  // output columns per thread: hd <= 128
+  constexpr int MAXC = NC;
   const int ncol = (hd + 15) / 16;
   float o[4][MAXC];
 #pragma unroll
@@ -362,30 +365,50 @@ __global__ void __launch_bounds__(PA_THREADS) k_attn_prefill(PrefillAttnArgs a) 
     l[r] = 0.f;
   }
   const int last_pos = a.start + q0 + nq - 1;
+  // Chunk e = tid + PA_THREADS * j of a tile: key e / (hd/4), values
+  // 4 (e % (hd/4)) .. +3 (hd % 4 == 0; a tile is 64 * hd / 4 <= 256 * NC chunks).
+  const int cpk = hd / 4;
+  float4 kr[NC], vr[NC];
+  auto fetch = [&](int t0) {
+    const int nt = min(PA_KT, last_pos + 1 - t0);
+#pragma unroll
+    for (int j = 0; j < NC; j++) {
+      const int e = tid + PA_THREADS * j, r = e / cpk, c4 = e % cpk;
+      kr[j] = vr[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r < nt) {
+        const int ta = t0 + r;
+        const size_t off = a.kv.off(a.layer, a.page_table[ta / a.kv.P], g, ta % a.kv.P) + 4 * c4;
+        if (a.kv.half) {
+          const uint2 kb = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(a.kv.k) + off);
+          const uint2 vb = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(a.kv.v) + off);
+          const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kb.x)), k1 = __half22float2(*reinterpret_cast<const __half2*>(&kb.y));
+          const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vb.x)), v1 = __half22float2(*reinterpret_cast<const __half2*>(&vb.y));
+          kr[j] = make_float4(k0.x, k0.y, k1.x, k1.y);
+          vr[j] = make_float4(v0.x, v0.y, v1.x, v1.y);
+        } else {
+          kr[j] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.kv.k) + off);
+          vr[j] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.kv.v) + off);
+        }
+      }
+    }
+  };
+  fetch(0);
   for (int t0 = 0; t0 <= last_pos; t0 += PA_KT) {
     const int nt = min(PA_KT, last_pos + 1 - t0);
     __syncthreads();  // the previous tile's keys, values and weights are read
-    for (int t = 0; t < nt;) {
-      const int ta = t0 + t;
-      const int page = a.page_table[ta / a.kv.P], row = ta % a.kv.P;
-      const int n = min(nt - t, a.kv.P - row);
-      const size_t off = a.kv.off(a.layer, page, g, row);
-      for (int e = tid; e < n * hd; e += PA_THREADS) {
-        const int r = e / hd, c = e % hd;
-        float kk, vv;
-        if (a.kv.half) {
-          kk = __half2float(reinterpret_cast<const __half*>(a.kv.k)[off + e]);
-          vv = __half2float(reinterpret_cast<const __half*>(a.kv.v)[off + e]);
-        } else {
-          kk = reinterpret_cast<const float*>(a.kv.k)[off + e];
-          vv = reinterpret_cast<const float*>(a.kv.v)[off + e];
-        }
-        kT[c * PA_KTS + t + r] = kk;
-        vs[(t + r) * hd + c] = vv;
+#pragma unroll
+    for (int j = 0; j < NC; j++) {
+      const int e = tid + PA_THREADS * j, r = e / cpk, c4 = e % cpk;
+      if (r < PA_KT) {
+        kT[(4 * c4 + 0) * PA_KTS + r] = kr[j].x;
+        kT[(4 * c4 + 1) * PA_KTS + r] = kr[j].y;
+        kT[(4 * c4 + 2) * PA_KTS + r] = kr[j].z;
+        kT[(4 * c4 + 3) * PA_KTS + r] = kr[j].w;
+        *reinterpret_cast<float4*>(vs + r * hd + 4 * c4) = vr[j];
       }
-      t += n;
     }
     __syncthreads();
+    if (t0 + PA_KT <= last_pos) fetch(t0 + PA_KT);
     // Scores of 4 queries x 4 keys.
     float sc[4][4];
 #pragma unroll

@@ -466,7 +466,7 @@ static int stablelm_load(const tcu_stablelm_config* c, const tcu_tensor* t, int 
     return code;
   };
   // The prefill attention kernel holds up to 128 output dimensions per query.
-  if (m->hd < 1 || m->hd > 128) return bail(fail(TCU_EINVAL, "head size %d outside 1..128", m->hd));
+  if (m->hd < 4 || m->hd > 128 || m->hd % 4) return bail(fail(TCU_EINVAL, "head size %d: a multiple of 4 in 4..128 is supported", m->hd));
   // Validate every tensor before allocating (loadStableWeights, stablelm.go:167-199).
   std::vector<std::string> names;
   auto chk = [&](const std::string& name, int64_t r, int64_t cc) { return check_tensor(find_tensor(t, n, name), name, r, cc); };
@@ -567,7 +567,7 @@ static int llama_load(const void* ck, uint64_t nbytes, const tcu_load_options* o
     return code;
   };
   // The prefill attention kernel holds up to 128 output dimensions per query.
-  if (m->hd < 1 || m->hd > 128) return bail(fail(TCU_EINVAL, "head size %d outside 1..128", m->hd));
+  if (m->hd < 4 || m->hd > 128 || m->hd % 4) return bail(fail(TCU_EINVAL, "head size %d: a multiple of 4 in 4..128 is supported", m->hd));
   const float* f = (const float*)((const uint8_t*)ck + 28);
   const float* ptr[13];
   {
@@ -1582,10 +1582,12 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
     pa.out_stride = d + ff;
     pa.scale = (float)sqrt((double)m->hd);
     const size_t smem = pa_smem_bytes(m->hd);
-    cudaFuncSetAttribute(k_attn_prefill, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int nc = (m->hd + 15) / 16;
+    auto kern = nc <= 2 ? k_attn_prefill<2> : nc <= 4 ? k_attn_prefill<4> : nc <= 5 ? k_attn_prefill<5> : k_attn_prefill<8>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     NOTE("cudaFuncSetAttribute(k_attn_prefill)");
     PROF_BEGIN(ST_PF_ATTN, s);
-    k_attn_prefill<<<dim3((n + PA_QT - 1) / PA_QT, m->H), PA_THREADS, smem, s>>>(pa);
+    kern<<<dim3((n + PA_QT - 1) / PA_QT, m->H), PA_THREADS, smem, s>>>(pa);
     NOTE("k_attn_prefill");
     PROF_END(s);
     if (m->arch == ARCH_STABLELM) {

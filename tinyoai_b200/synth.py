@@ -57,6 +57,68 @@ def _q8_0_torch(x):
     return out.reshape(-1)
 
 
+def _q6_k_torch(x):
+    """Q6_K super-blocks of 256 values (the layout quant_k.go:47-62 decodes):
+    ql[128] low nibbles, qh[64] high bit pairs, 16 int8 group scales, f16 d;
+    value = d * scale[group] * (q - 32). Any valid encoding serves: both the
+    library and the oracle decode these same bytes."""
+    import torch
+    rows, cols = x.shape
+    b = x.reshape(-1, 16, 16)                                    # [blocks, group, 16]
+    gs = b.abs().amax(-1) / 31.0                                 # group scale in weight units
+    d = (gs.amax(-1) / 127.0).to(torch.float16).float()          # [blocks]
+    inv_d = torch.where(d == 0, torch.zeros_like(d), 1.0 / d)
+    sc = torch.round(gs * inv_d[:, None]).clamp_(-128, 127)      # int8 group scales
+    step = d[:, None] * sc                                       # [blocks, group]
+    inv = torch.where(step == 0, torch.zeros_like(step), 1.0 / step)
+    q = (torch.round(b * inv[..., None]) + 32).clamp_(0, 63).to(torch.int32).reshape(-1, 256)
+    n = q.shape[0]
+    out = torch.empty(n, 210, dtype=torch.uint8, device=x.device)
+    for h in range(2):
+        sub = q[:, h * 128:(h + 1) * 128]
+        lo, hi = sub & 15, sub >> 4
+        out[:, h * 64:(h + 1) * 64] = (lo[:, :64] | (lo[:, 64:] << 4)).to(torch.uint8)
+        out[:, 128 + h * 32:128 + (h + 1) * 32] = (hi[:, :32] | (hi[:, 32:64] << 2) | (hi[:, 64:96] << 4)
+                                                    | (hi[:, 96:] << 6)).to(torch.uint8)
+    out[:, 192:208] = sc.to(torch.int8).view(torch.uint8)
+    out[:, 208:210] = d.to(torch.float16).view(torch.uint8).reshape(n, 2)
+    return out.reshape(-1)
+
+
+def _q5_k_torch(x):
+    """Q5_K super-blocks of 256 values (the layout quant_k.go:63-85 decodes):
+    f16 d and dmin, twelve bytes of packed 6-bit group scales and minima,
+    qh[32] fifth bits, qs[128] nibbles; value = d * sc * q - dmin * mn."""
+    import torch
+    b = x.reshape(-1, 8, 32)                                     # [blocks, group, 32]
+    lo = torch.clamp(b.amin(-1), max=0.0)                        # group minimum (<= 0)
+    gs = (b.amax(-1) - lo) / 31.0
+    d = (gs.amax(-1) / 63.0).to(torch.float16).float()
+    dmin = ((-lo).amax(-1) / 63.0).to(torch.float16).float()
+    inv_d = torch.where(d == 0, torch.zeros_like(d), 1.0 / d)
+    inv_m = torch.where(dmin == 0, torch.zeros_like(dmin), 1.0 / dmin)
+    sc = torch.round(gs * inv_d[:, None]).clamp_(0, 63)
+    mn = torch.round(-lo * inv_m[:, None]).clamp_(0, 63)
+    step = d[:, None] * sc
+    inv = torch.where(step == 0, torch.zeros_like(step), 1.0 / step)
+    q = torch.round((b + (dmin[:, None] * mn)[..., None]) * inv[..., None]).clamp_(0, 31).to(torch.int32)
+    sc, mn = sc.to(torch.int32), mn.to(torch.int32)
+    n = q.shape[0]
+    out = torch.empty(n, 176, dtype=torch.uint8, device=x.device)
+    out[:, 0:2] = d.to(torch.float16).view(torch.uint8).reshape(n, 2)
+    out[:, 2:4] = dmin.to(torch.float16).view(torch.uint8).reshape(n, 2)
+    out[:, 4:8] = (sc[:, :4] | ((sc[:, 4:] >> 4) << 6)).to(torch.uint8)
+    out[:, 8:12] = (mn[:, :4] | ((mn[:, 4:] >> 4) << 6)).to(torch.uint8)
+    out[:, 12:16] = ((sc[:, 4:] & 15) | ((mn[:, 4:] & 15) << 4)).to(torch.uint8)
+    qh = torch.zeros(n, 32, dtype=torch.int32, device=x.device)
+    for g in range(8):
+        qh |= ((q[:, g] >> 4) & 1) << g
+    out[:, 16:48] = qh.to(torch.uint8)
+    for p in range(4):
+        out[:, 48 + p * 32:48 + (p + 1) * 32] = ((q[:, 2 * p] & 15) | ((q[:, 2 * p + 1] & 15) << 4)).to(torch.uint8)
+    return out.reshape(-1)
+
+
 def synth_stablelm(config=None, dtype="Q8_0", seed=0, std=0.02, device="cpu"):
     """Returns {name: (dtype, shape, numpy uint8 payload)} for a random model.
 
@@ -78,6 +140,10 @@ def synth_stablelm(config=None, dtype="Q8_0", seed=0, std=0.02, device="cpu"):
         x = torch.randn(s, generator=g, device=device, dtype=torch.float32) * std
         if dtype == "Q8_0":
             payload = _q8_0_torch(x)
+        elif dtype == "Q6_K":
+            payload = _q6_k_torch(x)
+        elif dtype == "Q5_K":
+            payload = _q5_k_torch(x)
         elif dtype == "BF16":
             payload = x.to(torch.bfloat16).view(torch.int16).view(torch.uint8).reshape(-1)
         elif dtype == "F32":
