@@ -313,6 +313,39 @@ def test_branches_match_sequential(small, count):
         s.close()
 
 
+@pytest.mark.parametrize("kv", ["f32", "f16"])
+@pytest.mark.parametrize("gqa", [False, True])
+def test_branches_long_prefix(kv, gqa):
+    """Branches over a 300-token prefix: the whole 64-position splits inside
+    the shared pages are attended once for all branches (k_attn_shared), the
+    rest per branch; each branch still equals a session that evaluated
+    prefix + its own suffix."""
+    cfg, tensors = synth_stablelm(SMALL_GQA if gqa else SMALL, "Q8_0", seed=19)
+    m = Model.load_stablelm(cfg, tensors)
+    count = 12
+    ids = prompt_ids(300, cfg["vocab_size"], seed=47)
+    rng = np.random.default_rng(3)
+    steps = [rng.integers(3, cfg["vocab_size"], count).astype(np.int32) for _ in range(40)]
+    s = m.session(kv)
+    try:
+        s.forward(0, ids, want_logits=False)
+        br = s.new_branches(300, count)
+        try:
+            rows = [br.forward(t) for t in steps]
+        finally:
+            br.close()
+        for b in (0, 5, count - 1):
+            ref = m.session(kv)
+            try:
+                want = ref.forward(0, np.concatenate([ids, [st[b] for st in steps]]))
+            finally:
+                ref.close()
+            assert rel_err(rows[-1][b], want) <= 1e-4
+    finally:
+        s.close()
+        m.close()
+
+
 def test_shortlist_matches_oracle(small):
     """sampling.go:112-143 ordering and logprobs.go:64-95 normaliser on device."""
     cfg, tensors, m = small

@@ -119,11 +119,12 @@ struct DecodeAttnArgs {
   float* out;     // out[m*out_stride + h*hd + i]
   int out_stride;
   float scale;  // float32(sqrt(hd))
+  int s_begin;  // splits below this are computed for all rows by k_attn_shared
 };
 
 __global__ void __launch_bounds__(128) k_attn_decode(DecodeAttnArgs a) {
   extern __shared__ __align__(16) float att_smem[];
-  const int s = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
+  const int s = blockIdx.x + a.s_begin, g = blockIdx.y, m = blockIdx.z;
   const int hd = a.hd, G = a.H / a.KVH, split = a.split;
   const int pos = a.pos[m];
   const int T = pos + 1;
@@ -246,7 +247,7 @@ __global__ void __launch_bounds__(128) k_attn_decode(DecodeAttnArgs a) {
   __syncthreads();
   if (threadIdx.x == 0) {
     int prev = atomicAdd(a.counters + m * a.KVH + g, 1);
-    is_last = (prev == nsplit - 1);
+    is_last = (prev == nsplit - a.s_begin - 1);
   }
   __syncthreads();
   if (!is_last) return;
@@ -489,6 +490,140 @@ __global__ void __launch_bounds__(PA_THREADS, NC <= 5 ? 2 : 1) k_attn_prefill(Pr
   }
 }
 
+// Attention over history splits that every row shares (branches of one
+// prefix: mlx_branches.go:98-114 reads the prefix read-only for all of them).
+// One CTA per (shared split of 64 positions, KV head, tile of 64 query rows):
+// the split's keys and values are loaded once for all rows, query qi is head
+// g * G + qi % G of row qi / G, rotated at that row's position. Scores,
+// softmax and weighted values as in k_attn_prefill (no causal mask: every
+// position precedes every row's own). Writes each row's split partial
+// (sum_t exp(s_t - m) v_t, m, sum_t exp(s_t - m)) where the per-row kernels
+// expect it; they handle the later splits and merge all of them.
+template <int NC>
+__global__ void __launch_bounds__(PA_THREADS, NC <= 5 ? 2 : 1) k_attn_shared(DecodeAttnArgs a) {
+  extern __shared__ __align__(16) float pa_smem[];
+  const int hd = a.hd, s = blockIdx.x, g = blockIdx.y, G = a.H / a.KVH;
+  const int nrow = a.M * G;
+  const int q0 = blockIdx.z * PA_QT;
+  const int nq = min(PA_QT, nrow - q0);
+  float* qT = pa_smem;           // [hd][QT]
+  float* kT = qT + hd * PA_QT;   // [hd][KTS]
+  float* vs = kT + hd * PA_KTS;  // [KT][hd]; first holds the query rows for RoPE
+  float* ps = vs + PA_KT * hd;   // [KT][QT]
+  const int tid = threadIdx.x, rg = tid >> 4, cg = tid & 15;
+  for (int e = tid; e < PA_QT * hd; e += PA_THREADS) {
+    const int qi = e / hd, i = e % hd, row = q0 + qi;
+    vs[e] = qi < nq ? a.qkv[(size_t)(row / G) * a.qkv_stride + (g * G + row % G) * hd + i] : 0.f;
+  }
+  __syncthreads();
+  for (int e = tid; e < nq * a.rope.pairs; e += PA_THREADS) {
+    const int qi = e / a.rope.pairs;
+    rope_pair(vs + qi * hd, e % a.rope.pairs, a.rope, a.pos[(q0 + qi) / G]);
+  }
+  __syncthreads();
+  for (int e = tid; e < PA_QT * hd; e += PA_THREADS) qT[(e % hd) * PA_QT + e / hd] = vs[e];
+  __syncthreads();
+  // Keys and values of the split (pages of row 0's table: shared by all rows).
+  const int t0 = s * PA_KT;
+  for (int t = 0; t < PA_KT;) {
+    const int ta = t0 + t;
+    const int page = a.page_table[ta / a.kv.P], row = ta % a.kv.P;
+    const int n = min(PA_KT - t, a.kv.P - row);
+    const size_t off = a.kv.off(a.layer, page, g, row);
+    for (int e = tid; e < n * hd; e += PA_THREADS) {
+      const int r = e / hd, c = e % hd;
+      float kk, vv;
+      if (a.kv.half) {
+        kk = __half2float(reinterpret_cast<const __half*>(a.kv.k)[off + e]);
+        vv = __half2float(reinterpret_cast<const __half*>(a.kv.v)[off + e]);
+      } else {
+        kk = reinterpret_cast<const float*>(a.kv.k)[off + e];
+        vv = reinterpret_cast<const float*>(a.kv.v)[off + e];
+      }
+      kT[c * PA_KTS + t + r] = kk;
+      vs[(t + r) * hd + c] = vv;
+    }
+    t += n;
+  }
+  __syncthreads();
+  float sc[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; r++)
+#pragma unroll
+    for (int c = 0; c < 4; c++) sc[r][c] = 0.f;
+  for (int i = 0; i < hd; i++) {
+    const float4 qv = *reinterpret_cast<const float4*>(qT + i * PA_QT + 4 * rg);
+    const float4 kv = *reinterpret_cast<const float4*>(kT + i * PA_KTS + 4 * cg);
+    const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+#pragma unroll
+      for (int c = 0; c < 4; c++) sc[r][c] = fmaf(qa[r], ka[c], sc[r][c]);
+  }
+  float mrow[4], lrow[4];
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      sc[r][c] = __fdiv_rn(sc[r][c], a.scale);
+      mx = fmaxf(mx, sc[r][c]);
+    }
+#pragma unroll
+    for (int x = 1; x < 16; x <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, x));
+    float ls = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      sc[r][c] = expf(sc[r][c] - mx);
+      ls += sc[r][c];
+    }
+#pragma unroll
+    for (int x = 1; x < 16; x <<= 1) ls += __shfl_xor_sync(0xffffffffu, ls, x);
+    mrow[r] = mx;
+    lrow[r] = ls;
+  }
+#pragma unroll
+  for (int c = 0; c < 4; c++)
+    *reinterpret_cast<float4*>(ps + (4 * cg + c) * PA_QT + 4 * rg) = make_float4(sc[0][c], sc[1][c], sc[2][c], sc[3][c]);
+  __syncthreads();
+  const int ncol = (hd + 15) / 16;
+  float o[4][NC];
+#pragma unroll
+  for (int r = 0; r < 4; r++)
+#pragma unroll
+    for (int j = 0; j < NC; j++) o[r][j] = 0.f;
+  for (int t = 0; t < PA_KT; t++) {
+    const float4 pv = *reinterpret_cast<const float4*>(ps + t * PA_QT + 4 * rg);
+    const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+    const float* vr = vs + t * hd;
+#pragma unroll
+    for (int j = 0; j < NC; j++) {
+      const int c = cg + 16 * j;
+      if (j < ncol && c < hd) {
+        const float vv = vr[c];
+#pragma unroll
+        for (int r = 0; r < 4; r++) o[r][j] = fmaf(pa[r], vv, o[r][j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const int qi = 4 * rg + r;
+    if (qi >= nq) continue;
+    const int row = q0 + qi, m = row / G;
+    float* part = a.part + (((size_t)m * a.H + g * G + row % G) * a.max_splits + s) * (hd + 2);
+#pragma unroll
+    for (int j = 0; j < NC; j++) {
+      const int c = cg + 16 * j;
+      if (j < ncol && c < hd) part[c] = o[r][j];
+    }
+    if (cg == 0) {
+      part[hd] = mrow[r];
+      part[hd + 1] = lrow[r];
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Embedding rows (stablelm.go:338, prefill.go:58-60, model.go:419). In step
 // mode the token of sequence m is the argmax of the previous step
@@ -557,7 +692,7 @@ struct DecodeAttn2Extra {
 
 __global__ void __launch_bounds__(128) k_attn_decode_bulk(DecodeAttnArgs a, DecodeAttn2Extra x) {
   extern __shared__ __align__(128) uint8_t ab_smem[];
-  const int s = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
+  const int s = blockIdx.x + a.s_begin, g = blockIdx.y, m = blockIdx.z;
   const int hd = a.hd, G = a.H / a.KVH, split = a.split, P = a.kv.P;
   const int es = a.kv.half ? 2 : 4;
   pdl_launch_dependents();
@@ -684,7 +819,7 @@ __global__ void __launch_bounds__(128) k_attn_decode_bulk(DecodeAttnArgs a, Deco
   __syncthreads();
   if (threadIdx.x == 0) {
     int prev = atomicAdd(a.counters + m * a.KVH + g, 1);
-    is_last = (prev == nsplit - 1);
+    is_last = (prev == nsplit - a.s_begin - 1);
   }
   __syncthreads();
   if (!is_last) return;

@@ -129,6 +129,50 @@ __device__ __forceinline__ float kquant_at(const uint8_t* block, int i, int fmt)
 __host__ __device__ inline int kquant_block_bytes(int fmt) { return fmt == FMT_Q5_1 ? 24 : fmt == FMT_Q6_K ? 210 : 176; }
 __host__ __device__ inline int kquant_block_width(int fmt) { return fmt == FMT_Q5_1 ? 32 : 256; }
 
+// Eight values W[r][k0 .. k0 + 8) of a Q6_K or Q5_K matrix whose rows are
+// whole super-blocks (cols % 256 == 0, k0 % 8 == 0, so the eight share one
+// scale group): the block address and the group's scale are computed once,
+// each value exactly as kquant_at computes it (quant_k.go:47-85).
+__device__ __forceinline__ void kquant_decode8(const DMat& W, int r, int k0, float* dst) {
+  const int K = W.cols;
+  const int i0 = k0 & 255;
+  const uint8_t* blk = W.w + ((size_t)r * (K >> 8) + (k0 >> 8)) * (W.fmt == FMT_Q6_K ? 210 : 176);
+  if (W.fmt == FMT_Q6_K) {
+    const float d = __half2float(__ushort_as_half((unsigned short)(blk[208] | (blk[209] << 8))));
+    const float scale = __fmul_rn(d, (float)(int8_t)blk[192 + i0 / 16]);
+    const uint8_t* ql = blk + (i0 / 128) * 64 + i0 % 64;
+    const uint8_t* qh = blk + 128 + (i0 / 128) * 32 + i0 % 32;
+    const int ls = (i0 % 128) / 64 * 4, hs = (i0 % 128) / 32 * 2;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int q = ((ql[i] >> ls) & 15) | (((qh[i] >> hs) & 3) << 4);
+      dst[i] = __fmul_rn(scale, (float)(q - 32));
+    }
+  } else {
+    const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(blk[2] | (blk[3] << 8))));
+    const uint8_t* sc = blk + 4;
+    const int group = i0 / 32, j0 = i0 % 32;
+    int scale, minimum;
+    if (group < 4) {
+      scale = sc[group] & 63;
+      minimum = sc[group + 4] & 63;
+    } else {
+      scale = (sc[group + 4] & 15) | ((sc[group - 4] >> 6) << 4);
+      minimum = (sc[group + 4] >> 4) | ((sc[group] >> 6) << 4);
+    }
+    const float ds = __fmul_rn(d, (float)scale), dm = __fmul_rn(dmin, (float)minimum);
+    const uint8_t* qs = blk + 48 + (group / 2) * 32 + j0;
+    const uint8_t* qh = blk + 16 + j0;
+    const int ls = group % 2 * 4;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int q = ((qs[i] >> ls) & 15) | (((qh[i] >> group) & 1) << 4);
+      dst[i] = __fsub_rn(__fmul_rn(ds, (float)q), dm);
+    }
+  }
+}
+
 // Element (r, c) of a device matrix, decoded exactly as the reference does.
 __device__ __forceinline__ float dmat_at(const DMat& m, int r, int c) {
   switch (m.fmt) {

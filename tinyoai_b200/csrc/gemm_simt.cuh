@@ -27,6 +27,11 @@ struct GemmArgs {
   float* resid;
   int resid_stride;
   int k_split;
+  // Split K (out/down rows with few row tiles): slice blockIdx.z covers
+  // columns [z * k_per_z, (z + 1) * k_per_z) and writes its sums to
+  // part[z][n][rows] instead of applying the epilogue (nullptr: no split).
+  float* part;
+  int k_per_z;
 };
 
 // Decodes W[r][k0 .. k0+8) into dst (zeros outside the matrix).
@@ -57,6 +62,10 @@ __device__ __forceinline__ void decode8(const DMat& W, int r, int k0, float* dst
     }
     return;
   }
+  if ((W.fmt == FMT_Q6_K || W.fmt == FMT_Q5_K) && (K & 255) == 0 && k0 + 8 <= K) {
+    kquant_decode8(W, r, k0, dst);
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < 8; i++) dst[i] = (k0 + i < K) ? dmat_at(W, r, k0 + i) : 0.f;
 }
@@ -75,7 +84,9 @@ __global__ void __launch_bounds__(SG_THREADS) k_gemm_simt(GemmArgs a) {
 #pragma unroll
     for (int j = 0; j < 4; j++) lo[i][j] = hi[i][j] = 0.f;
   const int lr = tid / 4, lk = (tid % 4) * 8;  // loader: row/token lr, columns lk..lk+7
-  for (int k0 = 0; k0 < K; k0 += SG_BK) {
+  const int k_begin = a.part ? blockIdx.z * a.k_per_z : 0;
+  const int k_end = a.part ? min(K, k_begin + a.k_per_z) : K;
+  for (int k0 = k_begin; k0 < k_end; k0 += SG_BK) {
     {
       const int tok = m0 + lr;
       const float* ap = a.A + (size_t)tok * a.lda + k0 + lk;
@@ -116,6 +127,12 @@ __global__ void __launch_bounds__(SG_THREADS) k_gemm_simt(GemmArgs a) {
       const int r = r0 + tx * 4 + j;
       if (r >= a.W.rows) continue;
       const bool has1 = r + 1 < a.W.rows;
+      if (a.part) {  // a slice lies wholly before or after k_split: one of lo, hi is zero
+        float* pp = a.part + ((size_t)blockIdx.z * a.n + tok) * a.W.rows + r;
+        pp[0] = lo[i][j] + hi[i][j];
+        if (has1) pp[1] = lo[i][j + 1] + hi[i][j + 1];
+        continue;
+      }
       if constexpr (EPI == EPI_STORE) {
         a.out[(size_t)tok * a.out_stride + r] = lo[i][j];
         if (has1) a.out[(size_t)tok * a.out_stride + r + 1] = lo[i][j + 1];

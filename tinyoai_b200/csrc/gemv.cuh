@@ -353,6 +353,34 @@ __global__ void __launch_bounds__(GEMV_THREADS) k_gemv_generic(GemvArgs a) {
     float lo[M][2], hi[M][2];
 #pragma unroll
     for (int m = 0; m < M; m++) lo[m][0] = lo[m][1] = hi[m][0] = hi[m][1] = 0.f;
+    if ((a.W.fmt == FMT_Q6_K || a.W.fmt == FMT_Q5_K) && (K & 255) == 0 && (EPI != EPI_RESID2 || (a.k_split & 7) == 0)) {
+      // K-quant rows of whole super-blocks: a lane takes 8 values of one
+      // scale group per step (the block address and scale once).
+      for (int k0 = lane * 8; k0 < K; k0 += 256) {
+        float w0[8], w1[8];
+        kquant_decode8(a.W, r0, k0, w0);
+        if (has1)
+          kquant_decode8(a.W, r0 + 1, k0, w1);
+        else
+#pragma unroll
+          for (int i = 0; i < 8; i++) w1[i] = 0.f;
+        const bool second = EPI == EPI_RESID2 && k0 >= a.k_split;
+#pragma unroll
+        for (int m = 0; m < M; m++) {
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const float x = xs[(size_t)m * K + k0 + i];
+            if (second) {
+              hi[m][0] = fmaf(w0[i], x, hi[m][0]);
+              hi[m][1] = fmaf(w1[i], x, hi[m][1]);
+            } else {
+              lo[m][0] = fmaf(w0[i], x, lo[m][0]);
+              lo[m][1] = fmaf(w1[i], x, lo[m][1]);
+            }
+          }
+        }
+      }
+    } else
     for (int k = lane; k < K; k += 32) {
       float w0 = dmat_at(a.W, r0, k);
       float w1 = has1 ? dmat_at(a.W, r0 + 1, k) : 0.f;

@@ -717,6 +717,8 @@ struct Work {
   // completion counters.
   float* xl = nullptr;
   float* xdn = nullptr;
+  // Branch steps: leading history splits whose pages every row shares.
+  int shared_splits = 0;
   uint32_t* adig = nullptr;
   float* asx = nullptr;
   int asx_stride = 0;
@@ -1248,8 +1250,35 @@ static void launch_gemm(const tcu_model* m, Work* w, const GemmArgs& a, cudaStre
   if (launch_gemm_tc<EPI>(m, w, a, s)) return;
   PROF_BEGIN(g_stage, s);
   dim3 grid((a.W.rows + SG_BN - 1) / SG_BN, (a.n + SG_BM - 1) / SG_BM);
-  k_gemm_simt<EPI><<<grid, SG_THREADS, 0, s>>>(a);
+  GemmArgs g = a;
+  g.part = nullptr;
+  g.k_per_z = a.W.cols;
+  int z = 1, z_lo = 0;
+  // Too few output tiles to fill the GPU (out/down rows of a branch batch):
+  // split K into 256-column slices, reduced with the residual in slice order.
+  if (EPI == EPI_RESID2 && w && (int)(grid.x * grid.y) < m->sm_count / 2 && a.k_split % 256 == 0) {
+    const int kz = 256, K = a.W.cols;
+    const int zz = a.k_split / kz + (K - a.k_split + kz - 1) / kz;
+    if ((size_t)zz * a.n * a.W.rows > w->tc_part_floats) {
+      if (w->tc_part) cudaFree(w->tc_part);
+      w->tc_part = nullptr;
+      w->tc_part_floats = 0;
+      if (work_reserve((void**)&w->tc_part, (size_t)zz * a.n * a.W.rows * 4) == TCU_OK) w->tc_part_floats = (size_t)zz * a.n * a.W.rows;
+    }
+    if (w->tc_part) {
+      z = zz;
+      z_lo = a.k_split / kz;
+      g.part = w->tc_part;
+      g.k_per_z = kz;
+      grid.z = z;
+    }
+  }
+  k_gemm_simt<EPI><<<grid, SG_THREADS, 0, s>>>(g);
   NOTE("k_gemm_simt");
+  if (z > 1) {
+    k_splitk_resid<<<m->sm_count * 4, 256, 0, s>>>(w->tc_part, z_lo, z, a.n, a.W.rows, a.resid, a.resid_stride);
+    NOTE("k_splitk_resid");
+  }
   PROF_END(s);
 }
 
@@ -1288,8 +1317,21 @@ static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M,
   a.out = w->ah;
   a.out_stride = m->d + m->ff;
   a.scale = (float)sqrt((double)m->hd);
+  a.s_begin = 0;
   const int es = pool->half ? 2 : 4;
   const int G = m->H / m->KVH;
+  // Splits every row shares (branches): keys and values read once for all
+  // rows; the per-row kernels start after them.
+  if (w->shared_splits > 0 && a.split == PA_KT && w->shared_splits < grid_splits) {
+    const int nc = (m->hd + 15) / 16;
+    auto kern = nc <= 2 ? k_attn_shared<2> : nc <= 4 ? k_attn_shared<4> : nc <= 5 ? k_attn_shared<5> : k_attn_shared<8>;
+    const size_t smem = pa_smem_bytes(m->hd);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    NOTE("cudaFuncSetAttribute(k_attn_shared)");
+    kern<<<dim3(w->shared_splits, m->KVH, (M * G + PA_QT - 1) / PA_QT), PA_THREADS, smem, s>>>(a);
+    NOTE("k_attn_shared");
+    a.s_begin = w->shared_splits;
+  }
   const size_t bulk_smem =
       128 + 2 * (size_t)a.split * m->hd * es + sizeof(float) * ((size_t)G * m->hd + (size_t)G * a.split + 2 * m->hd);
   if (!m->disable_stream && ((size_t)m->P * m->hd * es) % 16 == 0 && bulk_smem <= GS_SMEM_LIMIT && G <= 32) {
@@ -1297,7 +1339,7 @@ static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M,
     cudaFuncSetAttribute(k_attn_decode_bulk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bulk_smem);
     NOTE("cudaFuncSetAttribute(k_attn_decode_bulk)");
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid_splits, m->KVH, M);
+    cfg.gridDim = dim3(grid_splits - a.s_begin, m->KVH, M);
     cfg.blockDim = dim3(128);
     cfg.dynamicSmemBytes = bulk_smem;
     cfg.stream = s;
@@ -1312,7 +1354,7 @@ static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M,
     const size_t smem = attn_decode_smem(m);
     cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     NOTE("cudaFuncSetAttribute(k_attn_decode)");
-    k_attn_decode<<<dim3(grid_splits, m->KVH, M), 128, smem, s>>>(a);
+    k_attn_decode<<<dim3(grid_splits - a.s_begin, m->KVH, M), 128, smem, s>>>(a);
     NOTE("k_attn_decode");
   }
   PROF_END(s);
@@ -2318,6 +2360,8 @@ int tcu_branches_forward(tcu_branches* b, const int32_t* tokens, float* rows_out
     cudaMemsetAsync(b->w.argmax, 0, b->count * sizeof(unsigned long long), s->stream);
     NOTE("cudaMemsetAsync(b->w.argmax, 0, b->count");
     const int split = SPLIT_PAGES * m->P;
+    // Whole splits inside the prefix's full pages are shared by every branch.
+    b->w.shared_splits = (b->prefix / m->P) / SPLIT_PAGES;
     enqueue_decode(m, s->pool, &b->w, b->count, false, (pos + 1 + split - 1) / split, true, s->stream);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) rc = fail(TCU_ECUDA, "launch: %s", cudaGetErrorString(e));
