@@ -471,14 +471,15 @@ def test_stage_profile(small):
         s.close()
 
 
-@pytest.mark.parametrize("fmt", ["Q8_0", "BF16"])
+@pytest.mark.parametrize("fmt", ["Q8_0", "BF16", "Q6_K", "Q5_K"])
 def test_tensor_core_prefill_matches_cuda_core_prefill(monkeypatch, fmt):
-    """The tcgen05 prefill GEMM (exact binary16 splits of Q8_0 weights, or
-    bfloat16 weights against a three-piece bfloat16 split of the activations;
-    float32 accumulation) against the CUDA-core GEMM on the same model:
-    logits of a 96-token prefill within 1e-4 of the logit range, identical
-    greedy continuations."""
-    cfg, tensors = synth_stablelm(SMALL, fmt, seed=23)
+    """The tcgen05 prefill GEMM against the CUDA-core GEMM on the same model:
+    Q8_0 weights as an exact binary16 pair, BF16 weights against a
+    three-piece bfloat16 split of the activations, K-quant weights decoded in
+    float32 and split into a binary16 pair (22 significant bits); float32
+    accumulation. Logits of a 96-token prefill within 1e-4 of the logit
+    range, identical greedy continuations."""
+    cfg, tensors = synth_stablelm(KQ_SMALL if fmt in ("Q6_K", "Q5_K") else SMALL, fmt, seed=23)
     ids = prompt_ids(96, cfg["vocab_size"], seed=5)
     out = {}
     for mode in ("simt", "tc"):

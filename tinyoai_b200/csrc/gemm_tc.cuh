@@ -12,6 +12,11 @@
 // float32 product. Tiles of up to 128 tokens keep the three pieces within
 // one stage buffer.
 //
+// Q6_K / Q5_K weights go through the same split: warps 0-3 decode each value
+// as the reference does (float32, quant_k.go:47-85), scale it by 2^sw and
+// split it into a binary16 pair, which keeps 22 of its up to 24 significant
+// bits (at most 2^-22 relative per weight).
+//
 // Q8_0 exactness: a Q8_0 weight
 // s*q has at most 19 significant bits and an activation 24, more than one
 // binary16 operand holds, so both sides are split into an exact binary16
@@ -267,7 +272,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
       for (int rr = tid >> 2; rr < TC_BM; rr += 32) {
         const int r = r0 + rr;
         uint4 h0 = make_uint4(0, 0, 0, 0), l0 = h0, h1 = h0, l1 = h0;
-        if (r < R && k0 < k_end) {
+        if (a.W.fmt != FMT_Q8_0) {
+          // K-quant rows of whole super-blocks (K % 256 == 0, k_end too).
+          if (r < R && k0 < k_end) {
+            float v[16];
+            kquant_decode8(a.W, r, k0, v);
+            kquant_decode8(a.W, r, k0 + 8, v + 8);
+            uint32_t hh[8], ll[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+              const float x0 = v[2 * i] * wscale, x1 = v[2 * i + 1] * wscale;
+              const __half2 h = __floats2half2_rn(x0, x1);
+              const float2 hf = __half22float2(h);
+              const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+              hh[i] = *reinterpret_cast<const uint32_t*>(&h);
+              ll[i] = *reinterpret_cast<const uint32_t*>(&l);
+            }
+            h0 = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+            h1 = make_uint4(hh[4], hh[5], hh[6], hh[7]);
+            l0 = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+            l1 = make_uint4(ll[4], ll[5], ll[6], ll[7]);
+          }
+        } else if (r < R && k0 < k_end) {
           const uint4 q = *reinterpret_cast<const uint4*>(a.W.w + (size_t)r * K + k0);
           const float s = __half2float(a.W.s[(size_t)r * a.W.sstride + k0 / 32]) * wscale;
           const __half2 s2 = __float2half2_rn(s);
@@ -425,6 +451,31 @@ __global__ void k_scale_absmax(const __half* s, int rows, int sstride, int nb, u
   const size_t total = (size_t)rows * nb;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const float v = fabsf(__half2float(s[(i / nb) * sstride + i % nb]));
+    if (v == v) m = max(m, __float_as_uint(v));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(out, m);
+}
+
+// Upper bound of |value| over a Q6_K or Q5_K matrix (nblocks super-blocks),
+// as the bits of a non-negative float: Q6_K |d| * max|scale| * 32, Q5_K
+// max(|d| * 63 * 31, |dmin| * 63).
+__global__ void k_kquant_absmax(const uint8_t* w, size_t nblocks, int fmt, unsigned* out) {
+  unsigned m = 0;
+  for (size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x; b < nblocks; b += (size_t)gridDim.x * blockDim.x) {
+    float v;
+    if (fmt == FMT_Q6_K) {
+      const uint8_t* blk = w + b * 210;
+      int ms = 0;
+      for (int g = 0; g < 16; g++) ms = max(ms, abs((int)(int8_t)blk[192 + g]));
+      v = fabsf(__half2float(__ushort_as_half((unsigned short)(blk[208] | (blk[209] << 8))))) * (float)ms * 32.f;
+    } else {
+      const uint8_t* blk = w + b * 176;
+      const float d = fabsf(__half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)))));
+      const float dm = fabsf(__half2float(__ushort_as_half((unsigned short)(blk[2] | (blk[3] << 8)))));
+      v = fmaxf(d * 63.f * 31.f, dm * 63.f);
+    }
     if (v == v) m = max(m, __float_as_uint(v));
   }
 #pragma unroll

@@ -1098,15 +1098,20 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // Power of two for the tensor-core split of a Q8_0 matrix: the largest
 // |s * q| (q <= 128) scaled below 2^13.
 static int set_tc_shift(tcu_model* m, DMat* W) {
-  if (W->fmt != FMT_Q8_0) return TCU_OK;
+  const bool kq = (W->fmt == FMT_Q6_K || W->fmt == FMT_Q5_K) && W->cols % 256 == 0;
+  if (W->fmt != FMT_Q8_0 && !kq) return TCU_OK;
   if (!m->scratch_u32) TRY(dalloc(m, (void**)&m->scratch_u32, sizeof(unsigned)));
   CK(cudaMemset(m->scratch_u32, 0, sizeof(unsigned)));
-  k_scale_absmax<<<m->sm_count * 4, 256>>>(W->s, W->rows, W->sstride, W->cols / 32, m->scratch_u32);
+  if (kq)
+    k_kquant_absmax<<<m->sm_count * 4, 256>>>(W->w, (size_t)W->rows * (W->cols / 256), W->fmt, m->scratch_u32);
+  else
+    k_scale_absmax<<<m->sm_count * 4, 256>>>(W->s, W->rows, W->sstride, W->cols / 32, m->scratch_u32);
   CK(cudaGetLastError());
   unsigned bits = 0;
   CK(cudaMemcpy(&bits, m->scratch_u32, sizeof(unsigned), cudaMemcpyDeviceToHost));
   float mx;
   memcpy(&mx, &bits, sizeof(mx));
+  if (kq) mx /= 128.f;  // the bound below is for |scale| * 128
   int e = 0;
   if (mx > 0.f) frexpf(mx * 128.f, &e);
   W->tc_sw = mx > 0.f ? std::max(-100, std::min(100, 13 - e)) : 0;
@@ -1141,7 +1146,9 @@ static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaS
   const DMat& W = g.W;
   const int K = W.cols, R = W.rows, n = g.n;
   const bool wb = W.fmt == FMT_BF16;
-  if (!m->use_tc || !w || !(W.fmt == FMT_Q8_0 || wb) || K % 16 || n < 1 || R < 1) return false;
+  const bool kq = W.fmt == FMT_Q6_K || W.fmt == FMT_Q5_K;
+  if (!m->use_tc || !w || !(W.fmt == FMT_Q8_0 || wb || kq) || K % 16 || n < 1 || R < 1) return false;
+  if (kq && (K % 256 || (EPI == EPI_RESID2 && g.k_split % 256))) return false;
   if (wb && ((uintptr_t)W.w % 16)) return false;
   if (EPI == EPI_RESID2 && g.k_split % TC_BK) return false;
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
