@@ -122,6 +122,61 @@ struct DecodeAttnArgs {
   int s_begin;  // splits below this are computed for all rows by k_attn_shared
 };
 
+// Merges the nsplit partials (hd outputs, max, sum) of each of the G heads
+// of one (row, KV head) into out[G][hd], by the whole CTA: fp32 maximum over
+// the splits, weights expf(max_j - max), the sum and the outputs accumulated
+// in split order. The splits' maxima and sums load in parallel into shared
+// memory (wsm: cap floats, at least 2 * nsplit); each output loads its
+// partials 16 splits at a time, so the merge costs a few L2 round trips
+// rather than one per split. Longer merges (2 * nsplit > cap) read the
+// partials one split at a time.
+__device__ void attn_merge_splits(const float* part, int max_splits, int hd, int G, int nsplit, float* wsm, int cap, float* out) {
+  const int rs = hd + 2;
+  for (int hh = 0; hh < G; hh++) {
+    const float* ph = part + (size_t)hh * max_splits * rs;
+    if (2 * nsplit > cap) {
+      for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+        float mx = -INFINITY;
+        for (int j = 0; j < nsplit; j++) mx = fmaxf(mx, __ldcg(ph + (size_t)j * rs + hd));
+        float l = 0.f, o = 0.f;
+        for (int j = 0; j < nsplit; j++) {
+          const float* pj = ph + (size_t)j * rs;
+          const float w = expf(__ldcg(pj + hd) - mx);
+          l = fmaf(__ldcg(pj + hd + 1), w, l);
+          o = fmaf(__ldcg(pj + i), w, o);
+        }
+        out[hh * hd + i] = __fdiv_rn(o, l);
+      }
+      continue;
+    }
+    __syncthreads();  // wsm is free (previous head or the attention tiles)
+    for (int j = threadIdx.x; j < nsplit; j += blockDim.x) {
+      wsm[j] = __ldcg(ph + (size_t)j * rs + hd);
+      wsm[nsplit + j] = __ldcg(ph + (size_t)j * rs + hd + 1);
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = 0; j < nsplit; j++) mx = fmaxf(mx, wsm[j]);
+    __syncthreads();
+    for (int j = threadIdx.x; j < nsplit; j += blockDim.x) wsm[j] = expf(wsm[j] - mx);
+    __syncthreads();
+    float l = 0.f;
+    for (int j = 0; j < nsplit; j++) l = fmaf(wsm[nsplit + j], wsm[j], l);
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+      float o = 0.f;
+      for (int j0 = 0; j0 < nsplit; j0 += 16) {
+        float pv[16];
+#pragma unroll
+        for (int jj = 0; jj < 16; jj++) pv[jj] = j0 + jj < nsplit ? __ldcg(ph + (size_t)(j0 + jj) * rs + i) : 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 16; jj++)
+          if (j0 + jj < nsplit) o = fmaf(pv[jj], wsm[j0 + jj], o);
+      }
+      out[hh * hd + i] = __fdiv_rn(o, l);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(128) k_attn_decode(DecodeAttnArgs a) {
   extern __shared__ __align__(16) float att_smem[];
   const int s = blockIdx.x + a.s_begin, g = blockIdx.y, m = blockIdx.z;
@@ -253,20 +308,7 @@ __global__ void __launch_bounds__(128) k_attn_decode(DecodeAttnArgs a) {
   if (!is_last) return;
   __threadfence();
   // Merge the nsplit partial states of each head in the group.
-  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
-    const int hh = e / hd, i = e % hd;
-    const float* ph = part + (size_t)hh * a.max_splits * (hd + 2);
-    float mx = -INFINITY;
-    for (int j = 0; j < nsplit; j++) mx = fmaxf(mx, __ldcg(ph + (size_t)j * (hd + 2) + hd));
-    float l = 0.f, o = 0.f;
-    for (int j = 0; j < nsplit; j++) {
-      const float* pj = ph + (size_t)j * (hd + 2);
-      float w = expf(__ldcg(pj + hd) - mx);
-      l = fmaf(__ldcg(pj + hd + 1), w, l);
-      o = fmaf(__ldcg(pj + i), w, o);
-    }
-    a.out[(size_t)m * a.out_stride + (g * G + hh) * hd + i] = __fdiv_rn(o, l);
-  }
+  attn_merge_splits(part, a.max_splits, hd, G, nsplit, ks, split * (hd + 1), a.out + (size_t)m * a.out_stride + g * G * hd);
   if (threadIdx.x == 0) a.counters[m * a.KVH + g] = 0;
 }
 
@@ -824,20 +866,10 @@ __global__ void __launch_bounds__(128) k_attn_decode_bulk(DecodeAttnArgs a, Deco
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
-    const int hh = e / hd, i = e % hd;
-    const float* ph = part + (size_t)hh * a.max_splits * (hd + 2);
-    float mx = -INFINITY;
-    for (int j = 0; j < nsplit; j++) mx = fmaxf(mx, __ldcg(ph + (size_t)j * (hd + 2) + hd));
-    float l = 0.f, o = 0.f;
-    for (int j = 0; j < nsplit; j++) {
-      const float* pj = ph + (size_t)j * (hd + 2);
-      float w = expf(__ldcg(pj + hd) - mx);
-      l = fmaf(__ldcg(pj + hd + 1), w, l);
-      o = fmaf(__ldcg(pj + i), w, o);
-    }
-    a.out[(size_t)m * a.out_stride + (g * G + hh) * hd + i] = __fdiv_rn(o, l);
-  }
+  // Merge the nsplit partial states of each head in the group (the key
+  // tile's shared memory is free by now).
+  attn_merge_splits(part, a.max_splits, hd, G, nsplit, reinterpret_cast<float*>(ktile), split * hd * es / 4,
+                    a.out + (size_t)m * a.out_stride + g * G * hd);
   if (threadIdx.x == 0) a.counters[m * a.KVH + g] = 0;
 }
 
