@@ -729,6 +729,10 @@ __global__ void __launch_bounds__(MG_REG_THREADS, 1) k_decode_mega(MegaArgs a) {
           const int qoff = ph == 0 ? d : 0, qlen = ph == 0 ? ff : d;
           const int soff = ph == 0 ? d / 32 - a.dn_soff : 0, slen = ph == 0 ? a.dn_sstride : osc;
           int* gc = gl + 2 + ph;
+          // A fair share per CTA (one more for down tiles): producers grab
+          // ahead of their consumers, so an uncapped early CTA would take
+          // tiles that later CTAs could start sooner. G * cap covers nt.
+          const int cap = min(MG_SWT, max(2, (nt + G - 1) / G + (ph == 0 ? 1 : 0)));
           q0 = atomicAdd(gc, 1);
           q1 = atomicAdd(gc, 1);
           grabs = 2;
@@ -739,7 +743,7 @@ __global__ void __launch_bounds__(MG_REG_THREADS, 1) k_decode_mega(MegaArgs a) {
               end_phase();
               break;
             }
-            if (grabs < MG_SWT) {
+            if (grabs < cap) {
               q1 = atomicAdd(gc, 1);
               grabs++;
             } else {
