@@ -185,6 +185,25 @@ int tcu_branches_argmax(tcu_branches* branches, int32_t* ids);
  * tcu_branches_forward already released the pages; close it all the same. */
 int tcu_branches_close(tcu_branches* branches);
 
+/* Continuous batching (BASELINE config 5's serving load). The reference's
+ * Go server runs one request at a time per model (the request gate,
+ * mlx.go:291-296); a batching scheduler instead advances all active
+ * sessions together. tcu_batch_open reserves a workspace and stream for up
+ * to max_rows rows (1..1024) so that steps allocate no device memory. */
+typedef struct tcu_batch tcu_batch;
+int tcu_batch_open(tcu_model* model, int32_t max_rows, tcu_batch** out);
+/* One decode step for n sessions of the batch's model that share one KV
+ * precision: tokens[i] is appended to sessions[i] at its current length
+ * (which must be >= 1) and its logits row computed, exactly as
+ * tcu_session_forward(sessions[i], length, &tokens[i], 1, 1, row) would.
+ * Writes n x vocab logits (rows_out may be NULL) and each row's greedy
+ * argmax (ids_out may be NULL); each session's length then grows by one.
+ * Sessions with open branches, repeated or closed sessions are rejected.
+ * Work already queued on a session's own stream completes first. */
+int tcu_batch_forward(tcu_batch* batch, tcu_session* const* sessions, const int32_t* tokens, int32_t n, float* rows_out,
+                      int32_t* ids_out);
+int tcu_batch_close(tcu_batch* batch);
+
 /* Sampling shortlist over a logits row the caller already holds in device
  * memory, allocating no device memory. This entry point has no counterpart in
  * the reference (its Go path keeps logits on the host); it serves callers that

@@ -346,6 +346,44 @@ def test_branches_long_prefix(kv, gqa):
         m.close()
 
 
+@pytest.mark.parametrize("kv", ["f32", "f16"])
+def test_batch_step_matches_single_sessions(small, kv):
+    """Continuous batching: sessions at different positions (one a fork
+    sharing its parent's pages) advance together through tcu_batch_forward;
+    every row equals the same session stepped alone, for 6 greedy steps."""
+    cfg, tensors, m = small
+    lens = [9, 37, 64, 100, 131]
+    prompts = [prompt_ids(n, cfg["vocab_size"], seed=60 + i) for i, n in enumerate(lens)]
+    batch_s, alone = [], []
+    try:
+        for p in prompts:
+            a, b = m.session(kv), m.session(kv)
+            a.forward(0, p, want_logits=False)
+            b.forward(0, p, want_logits=False)
+            batch_s.append(a)
+            alone.append(b)
+        batch_s.append(batch_s[3].fork())  # shares the parent's pages until written
+        alone_f = m.session(kv)
+        alone_f.forward(0, prompts[3], want_logits=False)
+        alone.append(alone_f)
+        toks = np.array([p[-1] for p in prompts] + [prompts[3][-1]], np.int32)
+        bt = m.batch(8)
+        try:
+            for step in range(6):
+                rows, ids = bt.forward(batch_s, toks)
+                for i, s in enumerate(alone):
+                    want = s.forward(s.length, [toks[i]])
+                    assert rel_err(rows[i], want) <= 1e-4, (step, i)
+                    assert ids[i] == int(np.argmax(want))
+                assert [s.length for s in batch_s] == [s.length for s in alone]
+                toks = ids.astype(np.int32)
+        finally:
+            bt.close()
+    finally:
+        for s in batch_s + alone:
+            s.close()
+
+
 def test_shortlist_matches_oracle(small):
     """sampling.go:112-143 ordering and logprobs.go:64-95 normaliser on device."""
     cfg, tensors, m = small

@@ -98,6 +98,12 @@ class Model:
         check(lib().tcu_model_memory(self._h, C.byref(w), C.byref(p), C.byref(u)))
         return {"weights": w.value, "kv_pool": p.value, "kv_used": u.value}
 
+    def batch(self, max_rows):
+        """A continuous-batching step runner for up to max_rows sessions."""
+        h = C.c_void_p()
+        check(lib().tcu_batch_open(self._h, int(max_rows), C.byref(h)))
+        return Batch(self, h.value, int(max_rows))
+
     def session(self, kv="f32"):
         return Session(self, kv)
 
@@ -239,3 +245,37 @@ class Branches:
         if self._h:
             check(lib().tcu_branches_close(self._h))
             self._h = None
+
+
+class Batch:
+    """One decode step for several sessions of one model at their own
+    positions (tcu_batch_forward): a batching server's step."""
+
+    def __init__(self, model, handle, max_rows):
+        self.model = model
+        self.max_rows = max_rows
+        self._h = C.c_void_p(handle)
+
+    def forward(self, sessions, tokens, want_rows=True):
+        """Appends tokens[i] to sessions[i]; returns (rows or None, argmax ids)."""
+        t, tp = _i32(tokens)
+        n = len(sessions)
+        if len(t) != n:
+            raise ValueError("one token per session")
+        hs = (C.c_void_p * n)(*[s._h.value for s in sessions])
+        ids = np.empty(n, np.int32)
+        rows = np.empty((n, self.model.vocab_size), np.float32) if want_rows else None
+        check(lib().tcu_batch_forward(self._h, hs, tp, n, rows.ctypes.data_as(C.POINTER(C.c_float)) if want_rows else None,
+                                      ids.ctypes.data_as(C.POINTER(C.c_int32))))
+        return rows, ids
+
+    def close(self):
+        if self._h:
+            check(lib().tcu_batch_close(self._h))
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

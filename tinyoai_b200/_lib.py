@@ -17,7 +17,7 @@ EXPORTS = [
     "tcu_session_length", "tcu_session_forward", "tcu_session_forward_all", "tcu_session_generate_greedy",
     "tcu_session_shortlist", "tcu_session_fork", "tcu_session_limit", "tcu_session_set_kv_dtype",
     "tcu_session_reset", "tcu_session_set_stream", "tcu_session_profile", "tcu_session_profile_read", "tcu_branches_open", "tcu_branches_forward", "tcu_branches_argmax", "tcu_branches_close",
-    "tcu_shortlist_static",
+    "tcu_batch_open", "tcu_batch_forward", "tcu_batch_close", "tcu_shortlist_static",
 ]
 
 
@@ -79,6 +79,9 @@ def lib():
         "tcu_branches_forward": ([P, i32p, f32p], C.c_int),
         "tcu_branches_argmax": ([P, i32p], C.c_int),
         "tcu_branches_close": ([P], C.c_int),
+        "tcu_batch_open": ([P, C.c_int32, C.POINTER(P)], C.c_int),
+        "tcu_batch_forward": ([P, C.POINTER(P), i32p, C.c_int32, f32p, i32p], C.c_int),
+        "tcu_batch_close": ([P], C.c_int),
         "tcu_shortlist_static": ([C.c_int32, P, C.c_int32, C.c_int32, P, i32p, f32p, C.POINTER(C.c_double), i32p], C.c_int),
     }
     for name, (args, res) in sig.items():

@@ -2412,6 +2412,111 @@ int tcu_branches_close(tcu_branches* b) {
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
+// Continuous batching: one decode step for several independent sessions of
+// one model, each at its own position (a server's active requests). The
+// per-row kernels take each row's position and page table, so the step is
+// the branch step with unrelated rows.
+struct tcu_batch {
+  tcu_model* m = nullptr;
+  int max_rows = 0;
+  Work w;
+  cudaStream_t stream = nullptr;
+};
+
+extern "C" {
+
+int tcu_batch_open(tcu_model* m, int32_t max_rows, tcu_batch** out) {
+  if (!m || !out) return fail(TCU_EINVAL, "null argument");
+  if (max_rows < 1 || max_rows > 1024) return fail(TCU_EINVAL, "batch size %d outside 1..1024", max_rows);
+  CK(cudaSetDevice(m->device));
+  tcu_batch* b = new tcu_batch();
+  b->m = m;
+  b->max_rows = max_rows;
+  int rc = work_init(m, &b->w, max_rows, max_rows, max_rows, 2);
+  if (rc == TCU_OK && cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking) != cudaSuccess)
+    rc = fail(TCU_ECUDA, "stream creation failed");
+  if (rc != TCU_OK) {
+    if (b->stream) cudaStreamDestroy(b->stream);
+    delete b;
+    return rc;
+  }
+  *out = b;
+  return TCU_OK;
+}
+
+int tcu_batch_forward(tcu_batch* b, tcu_session* const* sessions, const int32_t* tokens, int32_t n, float* rows_out,
+                      int32_t* ids_out) {
+  if (!b || !sessions || !tokens) return fail(TCU_EINVAL, "null argument");
+  if (n < 1 || n > b->max_rows) return fail(TCU_EINVAL, "batch of %d rows outside 1..%d", n, b->max_rows);
+  tcu_model* m = b->m;
+  KVPool* pool = nullptr;
+  for (int i = 0; i < n; i++) {
+    tcu_session* s = sessions[i];
+    if (!s || s->m != m) return fail(TCU_EINVAL, "row %d: not a session of this model", i);
+    if (s->closed) return fail(TCU_ECLOSED, "row %d: session is closed", i);
+    if (s->branches_open) return fail(TCU_EINVAL, "row %d: session has open branches", i);
+    if (s->length < 1 || s->length >= m->max_pos) return fail(TCU_EINVAL, "row %d: invalid position %d", i, s->length);
+    if (pool && s->pool != pool) return fail(TCU_EINVAL, "rows mix KV precisions");
+    pool = s->pool;
+    for (int j = 0; j < i; j++)
+      if (sessions[j] == s) return fail(TCU_EINVAL, "session appears twice in the batch");
+  }
+  TRY(check_tokens(m, tokens, n));
+  CK(cudaSetDevice(m->device));
+  ProfScope ps(nullptr, b->w.err);
+  // Each session's earlier work precedes this step.
+  for (int i = 0; i < n; i++) CK(cudaStreamSynchronize(sessions[i]->stream));
+  int rc = TCU_OK, max_len = 0;
+  std::vector<int> pt((size_t)n * b->w.pt_stride, 0), posv(n);
+  for (int i = 0; rc == TCU_OK && i < n; i++) {
+    tcu_session* s = sessions[i];
+    rc = prepare_pages(m, pool, s->pages, s->length, s->length + 1, b->stream);
+    std::copy(s->pages.begin(), s->pages.end(), pt.begin() + (size_t)i * b->w.pt_stride);
+    posv[i] = s->length;
+    max_len = std::max(max_len, s->length + 1);
+  }
+  if (rc == TCU_OK) {
+    cudaMemcpyAsync(b->w.pt, pt.data(), pt.size() * sizeof(int), cudaMemcpyHostToDevice, b->stream);
+    cudaMemcpyAsync(b->w.pos, posv.data(), n * sizeof(int), cudaMemcpyHostToDevice, b->stream);
+    cudaMemcpyAsync(b->w.tokens, tokens, n * sizeof(int), cudaMemcpyHostToDevice, b->stream);
+    cudaMemsetAsync(b->w.argmax, 0, n * sizeof(unsigned long long), b->stream);
+    const int split = SPLIT_PAGES * m->P;
+    b->w.shared_splits = 0;
+    enqueue_decode(m, pool, &b->w, n, false, (max_len + split - 1) / split, true, b->stream);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) rc = fail(TCU_ECUDA, "launch: %s", cudaGetErrorString(e));
+    if (rc == TCU_OK && rows_out) {
+      e = cudaMemcpyAsync(rows_out, b->w.logits, (size_t)n * m->V * 4, cudaMemcpyDeviceToHost, b->stream);
+      if (e != cudaSuccess) rc = fail(TCU_ECUDA, "rows copy: %s", cudaGetErrorString(e));
+    }
+  }
+  std::vector<unsigned long long> keys(n);
+  if (rc == TCU_OK && ids_out) {
+    cudaError_t e = cudaMemcpyAsync(keys.data(), b->w.argmax, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost, b->stream);
+    if (e != cudaSuccess) rc = fail(TCU_ECUDA, "argmax copy: %s", cudaGetErrorString(e));
+  }
+  if (rc == TCU_OK) rc = sync_stream(b->stream, b->w.err);
+  if (rc != TCU_OK) return rc;  // lengths unchanged: the new positions are rewritten next time
+  if (ids_out)
+    for (int i = 0; i < n; i++) ids_out[i] = (int)(0xffffffffu - (uint32_t)(keys[i] & 0xffffffffu));
+  for (int i = 0; i < n; i++) sessions[i]->length++;
+  return TCU_OK;
+}
+
+int tcu_batch_close(tcu_batch* b) {
+  if (!b) return TCU_OK;
+  if (b->stream) {
+    cudaSetDevice(b->m->device);
+    cudaStreamSynchronize(b->stream);
+    cudaStreamDestroy(b->stream);
+  }
+  delete b;
+  return TCU_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
 // Shortlist with no device allocation (tcu_shortlist_static). No counterpart
 // in the reference.
 //
