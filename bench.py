@@ -51,10 +51,10 @@ def q8_bytes(n):
 
 # DRAM traffic of one k_decode_mega launch relative to its algorithmic bytes,
 # from the ncu capture of the 4-layer profiling case at T = 532
-# (dram__bytes_read.sum + dram__bytes_write.sum = 560.187904 + 4.362240 MB
+# (dram__bytes_read.sum + dram__bytes_write.sum = 560.224256 + 5.593088 MB
 # against 558,942,880 algorithmic bytes). Traffic grows with layers and history
 # in proportion, so the bench launch's traffic is this ratio times its bytes.
-MEGA_TRAFFIC_RATIO = (560.187904e6 + 4.362240e6) / 558942880
+MEGA_TRAFFIC_RATIO = (560.224256e6 + 5.593088e6) / 558942880
 
 
 def decode_bytes(c, T):
