@@ -506,9 +506,10 @@ def run_config5(args):
     f16 paged KV: sessions arrive as a seeded Poisson process (8 req/s),
     prompt lengths lognormal around 1024 clipped to [16, 8000], output lengths
     uniform in [32, 512], 25 % of arrivals fork a live session's context and
-    continue it with a short suffix of their own. Each arrival is prefilled
-    when it arrives (time to first token = first token ready - arrival); all
-    active sessions then advance together, one tcu_batch_forward per step.
+    continue it with a short suffix of their own. Every step spends a budget
+    of prompt tokens on the waiting prompts in chunks, shortest remaining
+    first (time to first token = first token ready - arrival), then all
+    sessions with finished prompts advance together, one tcu_batch_forward.
     Tokens are the greedy argmax (the reference's seeded top-k / top-p draw
     runs on the host over the device shortlist and does not change the device
     work per token). Under torchrun every rank serves its own share of the
@@ -544,36 +545,47 @@ def run_config5(args):
         fork = rng.random(n) < 0.25
         return [(float(arrive[i]), int(plen[i]), int(olen[i]), bool(fork[i]), i) for i in range(n)]
 
-    def serve(reqs, max_rows=256):
+    def serve(reqs, max_rows=256, budget=1024):
+        """Each tick: admit arrivals, spend up to `budget` prompt tokens on
+        the waiting prompts in chunks (shortest remaining first, so a long
+        prompt does not hold up short ones), then one batched decode step
+        for every session whose prompt is done."""
         batch = model.batch(max_rows)
         pending = list(reqs)
-        active, done_ttft, tokens = [], [], 0
+        waiting, active, done_ttft, tokens = [], [], [], 0
         t0 = time.perf_counter()
         rng = np.random.default_rng(99)
         try:
-            while pending or active:
+            while pending or waiting or active:
                 now = time.perf_counter() - t0
-                if not active and pending and pending[0][0] > now:
+                if not active and not waiting and pending and pending[0][0] > now:
                     time.sleep(pending[0][0] - now)  # idle until the next arrival
                     now = time.perf_counter() - t0
-                while pending and pending[0][0] <= now and len(active) < max_rows:
+                while pending and pending[0][0] <= now and len(active) + len(waiting) < max_rows:
                     arr, plen, olen, fork, i = pending.pop(0)
-                    parent = None
-                    if fork and active:
-                        parent = active[int(rng.integers(0, len(active)))]
-                    if parent is not None and parent["s"].length + 257 + olen < ctx:
-                        s = parent["s"].fork()
+                    parents = [r for r in active if r["s"].length + 257 + olen < ctx]
+                    if fork and parents:
+                        s = parents[int(rng.integers(0, len(parents)))]["s"].fork()
                         ids = prompt_ids(int(rng.integers(16, 257)), V, seed=10_000 + i)
-                        prefix = s.length
                     else:
                         s = model.session("f16")
                         ids = prompt_ids(plen, V, seed=10_000 + i)
-                        prefix = 0
-                    row = s.forward(prefix, ids)
-                    tokens += len(ids)
-                    done_ttft.append(time.perf_counter() - t0 - arr)
-                    active.append({"s": s, "left": olen - 1, "tok": int(np.argmax(row))})
-                    tokens += 1
+                    waiting.append({"s": s, "ids": ids, "done": 0, "base": s.length, "arr": arr, "olen": olen})
+                left = budget
+                for r in sorted(waiting, key=lambda r: len(r["ids"]) - r["done"]):
+                    if left <= 0:
+                        break
+                    k = min(left, len(r["ids"]) - r["done"])
+                    last = r["done"] + k == len(r["ids"])
+                    row = r["s"].forward(r["base"] + r["done"], r["ids"][r["done"]:r["done"] + k], want_logits=last)
+                    r["done"] += k
+                    left -= k
+                    tokens += k
+                    if last:
+                        done_ttft.append(time.perf_counter() - t0 - r["arr"])
+                        active.append({"s": r["s"], "left": r["olen"] - 1, "tok": int(np.argmax(row))})
+                        tokens += 1
+                waiting = [r for r in waiting if r["done"] < len(r["ids"])]
                 if active:
                     _, out = batch.forward([r["s"] for r in active], np.array([r["tok"] for r in active], np.int32), want_rows=False)
                     tokens += len(active)
@@ -586,7 +598,7 @@ def run_config5(args):
                             r["s"].close()
                     active = keep
         finally:
-            for r in active:
+            for r in active + waiting:
                 r["s"].close()
             batch.close()
         return tokens, time.perf_counter() - t0, done_ttft
