@@ -530,8 +530,12 @@ def run_config5(args):
         cfg["num_hidden_layers"] = args.layers
     cfg, tensors = synth_stablelm(cfg, "Q8_0", seed=0, device=f"cuda:{local}")
     # Tens of concurrent sessions of ~1-2K positions (f16 KV: 320 KB per
-    # position on the 3B shape): a pool of at least 64 GB.
-    model = Model.load_stablelm(cfg, tensors, device=local, kv_pool_bytes=max(args.kv_pool_mb, 65536) << 20)
+    # position on the 3B shape): a pool of 140 GB by default, and admission
+    # control below keeps the admitted sessions' positions inside 90 % of it.
+    pool_mb = max(args.kv_pool_mb, 143360)
+    model = Model.load_stablelm(cfg, tensors, device=local, kv_pool_bytes=pool_mb << 20)
+    kvw = cfg["hidden_size"] // cfg["num_attention_heads"] * cfg["num_key_value_heads"]
+    pos_budget = int(0.9 * (pool_mb << 20) / (cfg["num_hidden_layers"] * 2 * kvw * 2))
     del tensors
     torch.cuda.empty_cache()
     V = cfg["vocab_size"]
@@ -561,8 +565,13 @@ def run_config5(args):
                 if not active and not waiting and pending and pending[0][0] > now:
                     time.sleep(pending[0][0] - now)  # idle until the next arrival
                     now = time.perf_counter() - t0
-                while pending and pending[0][0] <= now and len(active) + len(waiting) < max_rows:
+                # Positions the admitted sessions will hold at most (forks share
+                # their parents' pages, so this over-counts).
+                held = sum(r["s"].length + r["left"] for r in active) + sum(r["base"] + len(r["ids"]) + r["olen"] for r in waiting)
+                while (pending and pending[0][0] <= now and len(active) + len(waiting) < max_rows
+                       and held + pending[0][1] + 256 + pending[0][2] <= pos_budget):
                     arr, plen, olen, fork, i = pending.pop(0)
+                    held += plen + 256 + olen
                     parents = [r for r in active if r["s"].length + 257 + olen < ctx]
                     if fork and parents:
                         s = parents[int(rng.integers(0, len(parents)))]["s"].fork()
