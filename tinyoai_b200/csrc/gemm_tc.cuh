@@ -68,6 +68,7 @@ struct TcArgs {
   int k_split;        // EPI_RESID2: K where the second accumulator starts (multiple of TC_BK)
   float* part;        // split K: partial sums [gridDim.z][n][rows] (nullptr: apply the epilogue)
   int k_per_z;        // split K: columns per z slice (multiple of TC_BK)
+  int tok_fast;       // grid x = token tiles (else x = weight-row tiles)
   int* err;
 };
 
@@ -172,7 +173,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int R = a.W.rows, K = a.W.cols;
-  const int r0 = blockIdx.x * TC_BM, t0 = blockIdx.y * a.n_tile;
+  // tok_fast: token tiles are the fastest grid index, so the CTAs that share
+  // a weight tile run together and read it from L2 rather than HBM.
+  const int r0 = (a.tok_fast ? blockIdx.y : blockIdx.x) * TC_BM, t0 = (a.tok_fast ? blockIdx.x : blockIdx.y) * a.n_tile;
   const int k_begin = a.part ? blockIdx.z * a.k_per_z : 0;
   const int k_end = a.part ? min(K, k_begin + a.k_per_z) : K;
   const int iters = (k_end - k_begin + TC_BK - 1) / TC_BK;

@@ -1242,7 +1242,12 @@ static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaS
   a.part = z > 1 ? w->tc_part : nullptr;
   a.k_per_z = k_per_z;
   a.err = w->err;
-  kern<<<dim3(row_tiles, n_pad / n_tile, z), TC_THREADS, TC_SMEM, s>>>(map, wmap, a);
+  // BF16 and K-quant weights: the token tiles of a weight tile run together
+  // (their weight reads hit L2). Q8_0 is bound by its dequantising warps and
+  // measured faster with row tiles first.
+  a.tok_fast = (wb || kq) ? 1 : 0;
+  const dim3 grid = a.tok_fast ? dim3(n_pad / n_tile, row_tiles, z) : dim3(row_tiles, n_pad / n_tile, z);
+  kern<<<grid, TC_THREADS, TC_SMEM, s>>>(map, wmap, a);
   NOTE("k_gemm_tc");
   if (z > 1) {
     k_splitk_resid<<<m->sm_count * 4, 256, 0, s>>>(w->tc_part, z_lo, z, n, R, g.resid, g.resid_stride);
