@@ -12,7 +12,7 @@
 // float32 product. Tiles of up to 128 tokens keep the three pieces within
 // one stage buffer.
 //
-// Q6_K / Q5_K weights go through the same split: warps 0-3 decode each value
+// Q6_K / Q5_K weights go through the same split: warps 0-7 decode each value
 // as the reference does (float32, quant_k.go:47-85), scale it by 2^sw and
 // split it into a binary16 pair, which keeps 22 of its up to 24 significant
 // bits (at most 2^-22 relative per weight).
@@ -26,9 +26,11 @@
 // power-of-two scales keep the low halves out of the subnormal range and are
 // removed exactly in the epilogue.
 //
-// Warps: 0-3 dequantise the weight tile (then run the epilogue from TMEM),
-// warp 4 owns TMEM and issues the MMAs (one thread), warp 5 issues the TMA
-// loads of the activation tiles. Two shared-memory buffers; every wait is
+// Warps: 0-7 dequantise the weight tile (then run the epilogue from TMEM:
+// warps w and w + 4 share TMEM lanes 32(w % 4).. and split the columns),
+// warp 8 owns TMEM and issues the MMAs (one thread), warp 9 issues the TMA
+// loads of the activation tiles. Decoding is the pace-setter for quantised
+// weights; two decoding warps per SM sub-partition hide its load latency. Two shared-memory buffers; every wait is
 // bounded. All copies read this GPU's own memory into this CTA's shared
 // memory.
 #pragma once
@@ -43,7 +45,9 @@ namespace tcu {
 constexpr int TC_BM = 128;     // weight rows per tile (MMA M)
 constexpr int TC_BK = 64;      // K per stage (one 128-byte swizzle atom of binary16)
 constexpr int TC_MAXN = 256;   // tokens per tile (MMA N)
-constexpr int TC_THREADS = 192;
+constexpr int TC_DQW = 8;      // weight-decoding warps (a multiple of 4)
+constexpr int TC_MMA_WARP = TC_DQW, TC_TMA_WARP = TC_DQW + 1;
+constexpr int TC_THREADS = TC_DQW * 32 + 64;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;      // 16 KB per binary16 weight tile
 constexpr int TC_B_BYTES = TC_MAXN * TC_BK * 2;    // 32 KB per binary16 activation tile
 constexpr int TC_BUF_BYTES = 2 * TC_A_BYTES + 2 * TC_B_BYTES;
@@ -159,7 +163,7 @@ __device__ __forceinline__ void tc_dequant8(uint2 q, __half2 s2, uint4& hi, uint
 }
 
 // WB: bfloat16 weights through wmap (else Q8_0 weights dequantised by warps
-// 0-3; wmap unused).
+// 0-7; wmap unused).
 template <int EPI, bool WB>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap xmap,
                                                            const __grid_constant__ CUtensorMap wmap, TcArgs a) {
@@ -186,13 +190,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; i++) {
       mbar_init(&x_full[i], 1);
-      mbar_init(&w_full[i], 128);
+      mbar_init(&w_full[i], TC_DQW * 32);
       mbar_init(&mma_done[i], 1);
     }
     mbar_init(acc_full, 1);
     fence_barrier_init();
   }
-  if (warp == 4) {
+  if (warp == TC_MMA_WARP) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(tmem_cols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
@@ -203,7 +207,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
 
   auto buf = [&](int b) { return smem + (size_t)b * TC_BUF_BYTES; };
 
-  if (warp == 5) {
+  if (warp == TC_TMA_WARP) {
     // ---- activation tiles: Xh rows [t0, t0 + NT), Xl rows n_pad + the same.
     // BF16: the weight tile, then pieces X0, X1, X2 (rows p * n_pad + t0).
     if (lane == 0) {
@@ -223,7 +227,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         }
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == TC_MMA_WARP) {
     // ---- MMA issue (one thread): 4 K16 steps x (Wh.Xh, Wh.Xl, Wl.Xh) per stage
     if (lane == 0) {
       const uint32_t idesc = tc_idesc(NT, WB);
@@ -262,8 +266,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
       tc_commit(acc_full);
     }
   } else {
-    // ---- weight tiles (warps 0-3): 4 threads per row, 16 bytes each
-    const int tid = threadIdx.x;  // 0..127
+    // ---- weight tiles (warps 0-7): 4 threads per row, 16 bytes each
+    const int tid = threadIdx.x;  // 0..255
     const int kc = (tid & 3) * 16;
     const float wscale = tc_pow2(a.sw);
     for (int i = 0; i < (WB ? 0 : iters); i++) {
@@ -272,7 +276,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
       uint8_t* ah = buf(b);
       uint8_t* al = ah + TC_A_BYTES;
       const int k0 = k_begin + i * TC_BK + kc;
-      for (int rr = tid >> 2; rr < TC_BM; rr += 32) {
+      for (int rr = tid >> 2; rr < TC_BM; rr += TC_DQW * 8) {
         const int r = r0 + rr;
         uint4 h0 = make_uint4(0, 0, 0, 0), l0 = h0, h1 = h0, l1 = h0;
         if (a.W.fmt != FMT_Q8_0) {
@@ -314,14 +318,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&w_full[b]);
     }
-    // ---- epilogue: warp w reads TMEM lanes 32w..32w+31 (weight rows)
+    // ---- epilogue: warp w reads TMEM lanes 32(w % 4).. (weight rows),
+    // column chunks w / 4, w / 4 + TC_DQW / 4, ...
     mbar_wait(acc_full, 0, a.err);
     tc_fence_after();
-    const int rr = warp * 32 + lane, r = r0 + rr;
+    const int quad = warp & 3;
+    const int rr = quad * 32 + lane, r = r0 + rr;
     const float wunscale = tc_pow2(-a.sw);
-    for (int c0 = 0; c0 < NT; c0 += 16) {
+    for (int c0 = (warp >> 2) * 16; c0 < NT; c0 += 16 * (TC_DQW / 4)) {
       float v[16], v2[16];
-      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + c0;
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + c0;
       tc_ld16(taddr, v);
       if (two_acc) tc_ld16(taddr + TC_MAXN, v2);
 #pragma unroll
@@ -361,7 +367,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     tc_fence_before();
   }
   __syncthreads();
-  if (warp == 4) {
+  if (warp == TC_MMA_WARP) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols));
   }
