@@ -12,7 +12,7 @@
 // float32 product. Tiles of up to 128 tokens keep the three pieces within
 // one stage buffer.
 //
-// Q6_K / Q5_K weights go through the same split: warps 0-7 decode each value
+// Q6_K / Q5_K weights go through the same split: warps 0-15 decode each value
 // as the reference does (float32, quant_k.go:47-85), scale it by 2^sw and
 // split it into a binary16 pair, which keeps 22 of its up to 24 significant
 // bits (at most 2^-22 relative per weight).
@@ -26,11 +26,13 @@
 // power-of-two scales keep the low halves out of the subnormal range and are
 // removed exactly in the epilogue.
 //
-// Warps: 0-7 dequantise the weight tile (then run the epilogue from TMEM:
-// warps w and w + 4 share TMEM lanes 32(w % 4).. and split the columns),
-// warp 8 owns TMEM and issues the MMAs (one thread), warp 9 issues the TMA
-// loads of the activation tiles. Decoding is the pace-setter for quantised
-// weights; two decoding warps per SM sub-partition hide its load latency. Two shared-memory buffers; every wait is
+// Warps: 0-15 dequantise the weight tile, one row per thread group of 4
+// (then run the epilogue from TMEM: the warps with the same w % 4 share TMEM
+// lanes 32(w % 4).. and split the columns), warp 16 owns TMEM and issues the
+// MMAs (one thread), warp 17 issues the TMA loads of the activation tiles.
+// Decoding sets the pace for quantised weights; four decoding warps per SM
+// sub-partition hide its load latency (4 -> 8 -> 16 warps: config-4 step
+// 2797 -> 2297 -> 2192 ms). Two shared-memory buffers; every wait is
 // bounded. All copies read this GPU's own memory into this CTA's shared
 // memory.
 #pragma once
@@ -45,7 +47,7 @@ namespace tcu {
 constexpr int TC_BM = 128;     // weight rows per tile (MMA M)
 constexpr int TC_BK = 64;      // K per stage (one 128-byte swizzle atom of binary16)
 constexpr int TC_MAXN = 256;   // tokens per tile (MMA N)
-constexpr int TC_DQW = 8;      // weight-decoding warps (a multiple of 4)
+constexpr int TC_DQW = 16;     // weight-decoding warps (a multiple of 4)
 constexpr int TC_MMA_WARP = TC_DQW, TC_TMA_WARP = TC_DQW + 1;
 constexpr int TC_THREADS = TC_DQW * 32 + 64;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;      // 16 KB per binary16 weight tile
@@ -163,7 +165,7 @@ __device__ __forceinline__ void tc_dequant8(uint2 q, __half2 s2, uint4& hi, uint
 }
 
 // WB: bfloat16 weights through wmap (else Q8_0 weights dequantised by warps
-// 0-7; wmap unused).
+// 0-15; wmap unused).
 template <int EPI, bool WB>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap xmap,
                                                            const __grid_constant__ CUtensorMap wmap, TcArgs a) {
@@ -266,8 +268,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
       tc_commit(acc_full);
     }
   } else {
-    // ---- weight tiles (warps 0-7): 4 threads per row, 16 bytes each
-    const int tid = threadIdx.x;  // 0..255
+    // ---- weight tiles (warps 0-15): 4 threads per row, 16 bytes each
+    const int tid = threadIdx.x;  // 0..511
     const int kc = (tid & 3) * 16;
     const float wscale = tc_pow2(a.sw);
     for (int i = 0; i < (WB ? 0 : iters); i++) {
