@@ -131,11 +131,22 @@ __global__ void __launch_bounds__(1024) k_shortlist(const float* logits, int V, 
 
 // Per-row argmax of a logits matrix (batched branch steps).
 __global__ void k_argmax_rows(const float* logits, int V, int stride, unsigned long long* out) {
-  const int r = blockIdx.x;
+  // One CTA per row; each thread keeps four loads in flight. The packed
+  // (value, index) maximum does not depend on the visiting order.
+  const int r = blockIdx.x, nt = blockDim.x;
+  const float* row = logits + (size_t)r * stride;
   unsigned long long b = 0;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    unsigned long long key = argmax_pack(logits[(size_t)r * stride + i], i);
-    b = key > b ? key : b;
+  for (int i0 = threadIdx.x; i0 < V; i0 += 4 * nt) {
+    float v[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) v[u] = i0 + u * nt < V ? row[i0 + u * nt] : 0.f;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      if (i0 + u * nt < V) {
+        const unsigned long long key = argmax_pack(v[u], i0 + u * nt);
+        b = key > b ? key : b;
+      }
+    }
   }
   __shared__ unsigned long long red[32];
 #pragma unroll

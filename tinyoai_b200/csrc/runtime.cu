@@ -1565,7 +1565,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
     g.out_stride = m->V;
     launch_gemm<EPI_STORE>(m, w, g, s);
     PROF_BEGIN(ST_HEAD, s);
-    k_argmax_rows<<<M, 256, 0, s>>>(w->logits, m->V, m->V, w->argmax);
+    k_argmax_rows<<<M, 1024, 0, s>>>(w->logits, m->V, m->V, w->argmax);
     NOTE("k_argmax_rows");
     PROF_END(s);
   }
