@@ -227,6 +227,46 @@ def test_kquant_branches_match_sequential(fmt):
         m.close()
 
 
+WIDE = dict(SMALL, hidden_size=512, intermediate_size=1024, num_hidden_layers=2)
+
+
+@pytest.mark.parametrize("fmt", ["Q8_0", "Q6_K"])
+def test_split_k_products_vs_oracle(fmt):
+    """Tensor-core products with too few tiles for the GPU split K into slices
+    summed in order (W1 with the GLU epilogue, the lm_head with the store
+    epilogue; K = 512 is 8 stages): prefill and branch-step rows against the
+    oracle at the north-star tolerance."""
+    cfg, tensors = synth_stablelm(WIDE, fmt, seed=41)
+    m = Model.load_stablelm(cfg, tensors)
+    ids = prompt_ids(96, cfg["vocab_size"], seed=47)
+    rng = np.random.default_rng(11)
+    count = 24
+    steps = [rng.integers(3, cfg["vocab_size"], count).astype(np.int32) for _ in range(2)]
+    cap = cfg["max_position_embeddings"]
+    s = m.session()
+    try:
+        ora = oc.StableLM(cfg, tensors, half_kv=False, capacity=cap)
+        try:
+            assert rel_err(s.forward(0, ids), ora.prefill(ids)) <= 2e-3
+        finally:
+            ora.close()
+        br = s.new_branches(96, count)
+        try:
+            rows = [br.forward(t) for t in steps]
+        finally:
+            br.close()
+        for b in (0, 11, 23):
+            ora = oc.StableLM(cfg, tensors, half_kv=False, capacity=cap)
+            try:
+                want = ora.prefill(np.concatenate([ids, [st[b] for st in steps]]).astype(np.int32))
+            finally:
+                ora.close()
+            assert rel_err(rows[-1][b], want) <= 2e-3, b
+    finally:
+        s.close()
+        m.close()
+
+
 def test_prefix_reuse_matches_cold(small):
     """prefill_test.go:68-109: extending or replacing a resident suffix gives
     the same logits as a cold evaluation."""

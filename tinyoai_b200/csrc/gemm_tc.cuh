@@ -509,4 +509,27 @@ __global__ void k_splitk_resid(const float* part, int z_lo, int z_n, int n, int 
   }
 }
 
+// Split-K sum for the GLU and STORE epilogues: part [z][n][R] is summed in
+// slice order from 0, then stored (STORE rows, GLU rows below n_plain) or
+// paired into act(gate) * up (GLU rows n_plain + 2j and n_plain + 2j + 1),
+// as the single-pass epilogue of k_gemm_tc does.
+template <int EPI>
+__global__ void k_splitk_epi(const float* part, int z_n, int n, int R, float* out, int out_stride, int n_plain,
+                             float* glu_out, int glu_stride, int glu_act) {
+  const size_t total = (size_t)n * R;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / R), r = (int)(i % R);
+    if (EPI == EPI_GLU && r >= n_plain && ((r - n_plain) & 1)) continue;
+    float v = 0.f;
+    for (int z = 0; z < z_n; z++) v += part[(size_t)z * total + i];
+    if (EPI == EPI_STORE || r < n_plain) {
+      out[(size_t)t * out_stride + r] = v;
+      continue;
+    }
+    float up = 0.f;
+    for (int z = 0; z < z_n; z++) up += part[(size_t)z * total + i + 1];
+    glu_out[(size_t)t * glu_stride + ((r - n_plain) >> 1)] = glu_act ? silu_mul_llama(v, up) : silu_mul_stablelm(v, up);
+  }
+}
+
 }  // namespace tcu

@@ -1169,6 +1169,21 @@ static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaS
     z_lo = g.k_split / k_per_z;
     z = z_lo + (K - g.k_split + k_per_z - 1) / k_per_z;
   }
+  // GLU and STORE products whose last wave is ragged (a 64-row branch batch's
+  // W1: 168 tiles on 148 SMs) split K into z slices when the model
+  // waves(z) * (stages per slice + 3) drops by 15 % or more. Slices are summed
+  // in order by k_splitk_epi, which then runs the epilogue.
+  if ((EPI == EPI_GLU || EPI == EPI_STORE) && n >= 16) {
+    const int tiles = row_tiles * (n_pad / n_tile), sms = m->sm_count, iters = (K + TC_BK - 1) / TC_BK;
+    auto cost = [&](int zz) { return (double)((tiles * zz + sms - 1) / sms) * ((iters + zz - 1) / zz + 3); };
+    int best = 1;
+    for (int zz = 2; zz <= 8; zz++)
+      if (iters / zz >= 4 && cost(zz) < cost(best)) best = zz;
+    if (best > 1 && cost(best) <= 0.85 * cost(1)) {
+      k_per_z = (iters + best - 1) / best * TC_BK;
+      z = (K + k_per_z - 1) / k_per_z;
+    }
+  }
   // Workspace: grows on first use (not during stream capture).
   if (n_pad > w->tc_npad || K > w->tc_kmax) {
     const int np = std::max(n_pad, w->tc_npad), kk = std::max(K, w->tc_kmax);
@@ -1250,8 +1265,14 @@ static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaS
   kern<<<grid, TC_THREADS, TC_SMEM, s>>>(map, wmap, a);
   NOTE("k_gemm_tc");
   if (z > 1) {
-    k_splitk_resid<<<m->sm_count * 4, 256, 0, s>>>(w->tc_part, z_lo, z, n, R, g.resid, g.resid_stride);
-    NOTE("k_splitk_resid");
+    if constexpr (EPI == EPI_RESID2) {
+      k_splitk_resid<<<m->sm_count * 4, 256, 0, s>>>(w->tc_part, z_lo, z, n, R, g.resid, g.resid_stride);
+      NOTE("k_splitk_resid");
+    } else {
+      k_splitk_epi<EPI><<<m->sm_count * 4, 256, 0, s>>>(w->tc_part, z, n, R, g.out, g.out_stride, g.n_plain, g.glu_out,
+                                                         g.glu_stride, g.glu_act);
+      NOTE("k_splitk_epi");
+    }
   }
   PROF_END(s);
   return true;
