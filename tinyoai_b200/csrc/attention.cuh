@@ -367,6 +367,13 @@ __host__ __device__ inline size_t pa_smem_bytes(int hd) {
   return sizeof(float) * ((size_t)hd * PA_QT + (size_t)hd * PA_KTS + (size_t)PA_KT * hd + (size_t)PA_KT * PA_QT);
 }
 
+// Dynamic shared memory of k_attn_shared: its softmax weights reuse the key
+// tile once the scores are done (61 KB at hd = 80: three CTAs per SM).
+__host__ __device__ inline size_t pa_shared_smem_bytes(int hd) {
+  const size_t kt = (size_t)hd * PA_KTS, ps = (size_t)PA_KT * PA_QT;
+  return sizeof(float) * ((size_t)hd * PA_QT + (kt > ps ? kt : ps) + (size_t)PA_KT * hd);
+}
+
 // Causal attention of a prefill chunk (attention.go:6-45 semantics: every
 // query attends to the history and to the chunk up to itself), flash style on
 // CUDA cores. One CTA per (64-query tile, query head). Thread (rg, cg) holds
@@ -548,10 +555,10 @@ __global__ void __launch_bounds__(PA_THREADS, NC <= 5 ? 2 : 1) k_attn_shared(Dec
   const int nrow = a.M * G;
   const int q0 = blockIdx.z * PA_QT;
   const int nq = min(PA_QT, nrow - q0);
-  float* qT = pa_smem;           // [hd][QT]
-  float* kT = qT + hd * PA_QT;   // [hd][KTS]
-  float* vs = kT + hd * PA_KTS;  // [KT][hd]; first holds the query rows for RoPE
-  float* ps = vs + PA_KT * hd;   // [KT][QT]
+  float* qT = pa_smem;                                       // [hd][QT]
+  float* kT = qT + hd * PA_QT;                               // [hd][KTS]
+  float* vs = kT + max(hd * PA_KTS, PA_KT * PA_QT);          // [KT][hd]; first holds the query rows for RoPE
+  float* ps = kT;                                            // [KT][QT], over the key tile after the scores
   const int tid = threadIdx.x, rg = tid >> 4, cg = tid & 15;
   for (int e = tid; e < PA_QT * hd; e += PA_THREADS) {
     const int qi = e / hd, i = e % hd, row = q0 + qi;
@@ -624,6 +631,7 @@ __global__ void __launch_bounds__(PA_THREADS, NC <= 5 ? 2 : 1) k_attn_shared(Dec
     mrow[r] = mx;
     lrow[r] = ls;
   }
+  __syncthreads();  // every thread's reads of the key tile are done
 #pragma unroll
   for (int c = 0; c < 4; c++)
     *reinterpret_cast<float4*>(ps + (4 * cg + c) * PA_QT + 4 * rg) = make_float4(sc[0][c], sc[1][c], sc[2][c], sc[3][c]);

@@ -1358,7 +1358,7 @@ static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M,
   if (w->shared_splits > 0 && a.split == PA_KT && w->shared_splits < grid_splits) {
     const int nc = (m->hd + 15) / 16;
     auto kern = nc <= 2 ? k_attn_shared<2> : nc <= 4 ? k_attn_shared<4> : nc <= 5 ? k_attn_shared<5> : k_attn_shared<8>;
-    const size_t smem = pa_smem_bytes(m->hd);
+    const size_t smem = pa_shared_smem_bytes(m->hd);
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     NOTE("cudaFuncSetAttribute(k_attn_shared)");
     kern<<<dim3(w->shared_splits, m->KVH, (M * G + PA_QT - 1) / PA_QT), PA_THREADS, smem, s>>>(a);
