@@ -1235,7 +1235,9 @@ static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaS
     k_split_bf16<<<n, 256, 0, s>>>(g.A, g.lda, n, K, n_pad, reinterpret_cast<__nv_bfloat16*>(w->tc_split), w->tc_sx);
     NOTE("k_split_bf16");
   } else {
-    k_split_f16<<<n, 256, 0, s>>>(g.A, g.lda, n, K, n_pad, w->tc_split, w->tc_sx);
+    // One CTA per token row; 1024 threads keep a 64-row branch batch's split
+    // from being bound by the latency of one CTA's two passes over its row.
+    k_split_f16<<<n, 1024, 0, s>>>(g.A, g.lda, n, K, n_pad, w->tc_split, w->tc_sx);
     NOTE("k_split_f16");
   }
   TcArgs a{};
