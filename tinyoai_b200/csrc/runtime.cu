@@ -1320,7 +1320,7 @@ static void launch_gemm(const tcu_model* m, Work* w, const GemmArgs& a, cudaStre
 static void launch_norm_rows(const tcu_model* m, const float* in, float* out, int n, const float* w, const float* b, cudaStream_t s) {
   PROF_BEGIN(ST_OTHER, s);
   NormRowsArgs a{n, m->d, in, m->d, out, m->d, w, b, m->eps, m->arch == ARCH_LLAMA};
-  k_norm_rows<<<n, 256, 0, s>>>(a);
+  k_norm_rows<<<n, 1024, 0, s>>>(a);  // one CTA per row: 1024 threads hide a short batch's load latency
   NOTE("k_norm_rows");
   PROF_END(s);
 }
