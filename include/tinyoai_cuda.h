@@ -104,6 +104,27 @@ int tcu_model_memory(const tcu_model* model, uint64_t* weight_bytes, uint64_t* k
 /* Releases weights and the KV pool. Every session must be closed first. */
 int tcu_model_free(tcu_model* model);
 
+/* weightTensor.readValues (matmul.go:12-50, decodeKBlock quant_k.go:31-86) on
+ * the device: decodes n values, starting at row-major element `offset`, of a
+ * rows x cols tensor given in its file encoding (host bytes, checked against
+ * the format's size), into out (n host floats). `decoder` names which of the
+ * device decoders produces them:
+ *   TCU_DECODE_ELEMENT  the per-element decoder of the matrix-vector kernels
+ *                       (every format);
+ *   TCU_DECODE_GROUP8   the 8-value decoder of the batched products (Q6_K,
+ *                       Q5_K);
+ *   TCU_DECODE_TC       the tensor-core operand: the binary16 pieces the
+ *                       tcgen05 GEMM multiplies, summed back and unscaled
+ *                       (Q8_0, Q6_K, Q5_K).
+ * Each returns the reference's float32 values bit for bit, which is what this
+ * entry point lets a host check (quant_k_test.go:14-48 checks the Go decoder
+ * the same way). It allocates and frees its own device buffers. */
+#define TCU_DECODE_ELEMENT 0
+#define TCU_DECODE_GROUP8 1
+#define TCU_DECODE_TC 2
+int tcu_read_values(int32_t device, int32_t dtype, const void* data, uint64_t nbytes, int32_t rows, int32_t cols,
+                    int64_t offset, int64_t n, int32_t decoder, float* out);
+
 /* A generation session: the resident token prefix of one request stream and
  * its paged KV (the state nativeMLX keeps per model, mlx_native.go:24-45).
  * kv_dtype is TCU_F32 or TCU_F16 (StableLMOptions.KVCache, kv_cache.go:8-24). */
@@ -139,6 +160,43 @@ int tcu_session_generate_greedy(tcu_session* session, int32_t prefix, const int3
  * the full-vocabulary log-sum-exp (logprobs.go:64-95). */
 int tcu_session_shortlist(tcu_session* session, int32_t k, int32_t* ids, float* logits, double* logsumexp,
                           int32_t* n_out);
+
+/* mlxProbabilityForwarder.ForwardWithLogprobs (mlx.go:53-57,
+ * mlx_native.go:303-313 and 436-478) with summarizeLogits semantics
+ * (logprobs.go:64-95): evaluates tokens[0..n) after `prefix` as
+ * tcu_session_forward does, and for every input position i writes
+ *   chosen[i]                          log P(targets[i]) after position i,
+ *   top_ids[i * count .. + count)      the count most likely next ids,
+ *   top_logprobs[i * count .. + count) their log probabilities,
+ * descending, ties by lower id, all normalised over the full vocabulary in
+ * float64. logits_out (vocab floats, may be NULL) receives the final row.
+ * targets pair one-for-one with tokens; 1 <= count <= min(256, vocab).
+ * On failure the resident prefix is discarded, as for tcu_session_forward. */
+int tcu_session_forward_logprobs(tcu_session* session, int32_t prefix, const int32_t* tokens, const int32_t* targets, int32_t n,
+                                 int32_t count, double* chosen, int32_t* top_ids, double* top_logprobs, float* logits_out);
+
+/* SamplingOptions' penalties (sampling.go:12-58), validated as Validate does:
+ * finite, repetition_penalty >= 1, repetition_range >= 0 (0: the whole
+ * history), repetition_slope >= 0. Neutral: {1, 0, 0, 0, 0}. */
+typedef struct {
+  double repetition_penalty;
+  double presence_penalty;
+  double frequency_penalty;
+  double repetition_slope;
+  int32_t repetition_range;
+} tcu_penalties;
+
+/* samplingCandidates(penalizedLogits(logits, history, opts), k)
+ * (sampling.go:76-143) over the logits of the session's last forward, on
+ * the device: float64 scores with recency-weighted frequency, presence and
+ * logarithmic repetition penalties from `history` (the story's token ids,
+ * oldest first), then the k best (id, score) pairs, descending, ties by
+ * lower id (1 <= k <= 256). ids[0] is the greedy choice of sampleWithOptions
+ * (sampling.go:155-163). The caller draws from the pairs with its own RNG
+ * (temperature, top-p and tail-free filtering run on these k scores). At most
+ * 16384 distinct ids may carry a penalty. */
+int tcu_session_sample_candidates(tcu_session* session, const int32_t* history, int32_t n_history, const tcu_penalties* penalties,
+                                  int32_t k, int32_t* ids, double* scores, int32_t* n_out);
 
 /* mlxForker.Fork (sessions.go:26-30, mlx_sessions.go:10-71): the child shares
  * every full KV page copy-free (reference counted) and copies only the
@@ -202,6 +260,12 @@ int tcu_batch_open(tcu_model* model, int32_t max_rows, tcu_batch** out);
  * Work already queued on a session's own stream completes first. */
 int tcu_batch_forward(tcu_batch* batch, tcu_session* const* sessions, const int32_t* tokens, int32_t n, float* rows_out,
                       int32_t* ids_out);
+/* tcu_session_sample_candidates for every row of the batch's last step
+ * (n = that step's row count): row i's history is history[off_i ..
+ * off_i + history_len[i]) with off_i the sum of the earlier lengths, its
+ * penalties penalties[i]; writes n x k ids and scores. */
+int tcu_batch_sample_candidates(tcu_batch* batch, int32_t n, const int32_t* history, const int32_t* history_len,
+                                const tcu_penalties* penalties, int32_t k, int32_t* ids, double* scores);
 int tcu_batch_close(tcu_batch* batch);
 
 /* Sampling shortlist over a logits row the caller already holds in device

@@ -24,7 +24,7 @@ from . import _lib
 from ._lib import BackendError, check, lib
 from .checkpoint import as_bytes, dtype_code
 
-__all__ = ["Model", "Session", "Branches", "BackendError", "device_count"]
+__all__ = ["Model", "Session", "Branches", "BackendError", "device_count", "read_values"]
 
 
 def _i32(a):
@@ -36,6 +36,27 @@ def device_count():
     n = C.c_int32()
     check(lib().tcu_device_count(C.byref(n)))
     return n.value
+
+
+_DECODERS = {"element": _lib.DECODE_ELEMENT, "group8": _lib.DECODE_GROUP8, "tc": _lib.DECODE_TC}
+
+
+def read_values(dtype, payload, rows, cols, offset=0, n=None, decoder="element", device=0):
+    """weightTensor.readValues (matmul.go:12-50) through one of the device
+    decoders: "element" (matrix-vector kernels), "group8" (batched products,
+    Q6_K/Q5_K) or "tc" (the tcgen05 GEMM operand, Q8_0/Q6_K/Q5_K). payload is
+    the tensor in its file encoding; returns n float32 values."""
+    buf = np.ascontiguousarray(np.frombuffer(bytes(as_bytes(payload)), dtype=np.uint8))
+    n = rows * cols - offset if n is None else n
+    out = np.empty(max(n, 1), np.float32)
+    check(lib().tcu_read_values(device, dtype_code(dtype), buf.ctypes.data_as(C.c_void_p), buf.nbytes, rows, cols, offset, n,
+                                _DECODERS[decoder], out.ctypes.data_as(C.POINTER(C.c_float))))
+    return out[:n]
+
+
+def penalties_struct(repetition_penalty=1.0, presence_penalty=0.0, frequency_penalty=0.0, repetition_slope=0.0,
+                     repetition_range=0):
+    return _lib.Penalties(repetition_penalty, presence_penalty, frequency_penalty, repetition_slope, repetition_range)
 
 
 def _options(device, kv_page_tokens, kv_pool_bytes):
@@ -154,6 +175,39 @@ class Session:
         check(lib().tcu_session_generate_greedy(self._h, prefix, tp, len(t), steps, out.ctypes.data_as(C.POINTER(C.c_int32))))
         return out
 
+    def forward_logprobs(self, prefix, tokens, targets, count, want_logits=True):
+        """mlxProbabilityForwarder.ForwardWithLogprobs (mlx.go:53-57): per
+        input position the target's log probability and `count` top (id,
+        log probability) pairs (summarizeLogits, logprobs.go:64-95). Returns
+        (chosen [n], top_ids [n, count], top_logprobs [n, count], final logits
+        or None)."""
+        t, tp = _i32(tokens)
+        g, gp = _i32(targets)
+        n = len(t)
+        chosen = np.empty(n, np.float64)
+        ids = np.empty((n, count), np.int32)
+        vals = np.empty((n, count), np.float64)
+        logits = np.empty(self.model.vocab_size, np.float32) if want_logits else None
+        check(lib().tcu_session_forward_logprobs(
+            self._h, prefix, tp, gp, n, count, chosen.ctypes.data_as(C.POINTER(C.c_double)),
+            ids.ctypes.data_as(C.POINTER(C.c_int32)), vals.ctypes.data_as(C.POINTER(C.c_double)),
+            logits.ctypes.data_as(C.POINTER(C.c_float)) if want_logits else None))
+        return chosen, ids, vals, logits
+
+    def sample_candidates(self, history, k, **penalties):
+        """samplingCandidates(penalizedLogits(...), k) (sampling.go:76-143)
+        over the last forward's logits: (ids, float64 scores); ids[0] is the
+        greedy choice. penalties: repetition_penalty, presence_penalty,
+        frequency_penalty, repetition_slope, repetition_range."""
+        h, hp = _i32(history)
+        ids = np.empty(k, np.int32)
+        scores = np.empty(k, np.float64)
+        n = C.c_int32()
+        check(lib().tcu_session_sample_candidates(self._h, hp, len(h), C.byref(penalties_struct(**penalties)), k,
+                                                  ids.ctypes.data_as(C.POINTER(C.c_int32)),
+                                                  scores.ctypes.data_as(C.POINTER(C.c_double)), C.byref(n)))
+        return ids[:n.value], scores[:n.value]
+
     def shortlist(self, k):
         ids = np.empty(k, np.int32)
         vals = np.empty(k, np.float32)
@@ -268,6 +322,23 @@ class Batch:
         check(lib().tcu_batch_forward(self._h, hs, tp, n, rows.ctypes.data_as(C.POINTER(C.c_float)) if want_rows else None,
                                       ids.ctypes.data_as(C.POINTER(C.c_int32))))
         return rows, ids
+
+    def sample_candidates(self, histories, k, penalties=None):
+        """tcu_batch_sample_candidates over the last step's rows: histories is
+        one id list per row, penalties one dict per row (or None: neutral).
+        Returns (ids [n, k], scores [n, k])."""
+        n = len(histories)
+        lens = np.array([len(h) for h in histories], np.int32)
+        flat = np.concatenate([np.asarray(h, np.int32) for h in histories]) if lens.sum() else np.zeros(1, np.int32)
+        flat = np.ascontiguousarray(flat, np.int32)
+        ps = (_lib.Penalties * n)(*[penalties_struct(**(penalties[i] if penalties else {})) for i in range(n)])
+        ids = np.empty((n, k), np.int32)
+        scores = np.empty((n, k), np.float64)
+        check(lib().tcu_batch_sample_candidates(self._h, n, flat.ctypes.data_as(C.POINTER(C.c_int32)),
+                                                lens.ctypes.data_as(C.POINTER(C.c_int32)), ps, k,
+                                                ids.ctypes.data_as(C.POINTER(C.c_int32)),
+                                                scores.ctypes.data_as(C.POINTER(C.c_double))))
+        return ids, scores
 
     def close(self):
         if self._h:

@@ -6,6 +6,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libtinyoai_cuda.so"
 
+DECODE_ELEMENT, DECODE_GROUP8, DECODE_TC = 0, 1, 2
 TCU_OK, TCU_EINVAL, TCU_ENODEV, TCU_ENOMEM, TCU_ECUDA, TCU_ECLOSED, TCU_EUNSUP, TCU_ETIMEOUT = 0, -1, -2, -3, -4, -5, -6, -7
 F32, F16, Q5_1, Q8_0, Q5_K, Q6_K, BF16 = 0, 1, 7, 8, 13, 14, 30
 DTYPE_CODES = {"F32": F32, "F16": F16, "Q5_1": Q5_1, "Q8_0": Q8_0, "Q5_K": Q5_K, "Q6_K": Q6_K, "BF16": BF16}
@@ -17,7 +18,8 @@ EXPORTS = [
     "tcu_session_length", "tcu_session_forward", "tcu_session_forward_all", "tcu_session_generate_greedy",
     "tcu_session_shortlist", "tcu_session_fork", "tcu_session_limit", "tcu_session_set_kv_dtype",
     "tcu_session_reset", "tcu_session_set_stream", "tcu_session_profile", "tcu_session_profile_read", "tcu_branches_open", "tcu_branches_forward", "tcu_branches_argmax", "tcu_branches_close",
-    "tcu_batch_open", "tcu_batch_forward", "tcu_batch_close", "tcu_shortlist_static",
+    "tcu_batch_open", "tcu_batch_forward", "tcu_batch_close", "tcu_shortlist_static", "tcu_read_values",
+    "tcu_session_forward_logprobs", "tcu_session_sample_candidates", "tcu_batch_sample_candidates",
 ]
 
 
@@ -32,6 +34,12 @@ class StableLMConfig(C.Structure):
                 ("num_key_value_heads", C.c_int32), ("max_position_embeddings", C.c_int32),
                 ("bos_token_id", C.c_int32), ("eos_token_id", C.c_int32), ("layer_norm_eps", C.c_double),
                 ("rope_theta", C.c_double), ("partial_rotary_factor", C.c_double)]
+
+
+class Penalties(C.Structure):
+    """tcu_penalties: SamplingOptions' penalty fields (sampling.go:12-58)."""
+    _fields_ = [("repetition_penalty", C.c_double), ("presence_penalty", C.c_double), ("frequency_penalty", C.c_double),
+                ("repetition_slope", C.c_double), ("repetition_range", C.c_int32)]
 
 
 class LoadOptions(C.Structure):
@@ -52,6 +60,7 @@ def lib():
     P = C.c_void_p
     i32p = C.POINTER(C.c_int32)
     f32p = C.POINTER(C.c_float)
+    f64p = C.POINTER(C.c_double)
     sig = {
         "tcu_abi_version": ([], C.c_int),
         "tcu_last_error": ([], C.c_char_p),
@@ -83,6 +92,11 @@ def lib():
         "tcu_batch_forward": ([P, C.POINTER(P), i32p, C.c_int32, f32p, i32p], C.c_int),
         "tcu_batch_close": ([P], C.c_int),
         "tcu_shortlist_static": ([C.c_int32, P, C.c_int32, C.c_int32, P, i32p, f32p, C.POINTER(C.c_double), i32p], C.c_int),
+        "tcu_read_values": ([C.c_int32, C.c_int32, P, C.c_uint64, C.c_int32, C.c_int32, C.c_int64, C.c_int64, C.c_int32, f32p],
+                            C.c_int),
+        "tcu_session_forward_logprobs": ([P, C.c_int32, i32p, i32p, C.c_int32, C.c_int32, f64p, i32p, f64p, f32p], C.c_int),
+        "tcu_session_sample_candidates": ([P, i32p, C.c_int32, C.POINTER(Penalties), C.c_int32, i32p, f64p, i32p], C.c_int),
+        "tcu_batch_sample_candidates": ([P, C.c_int32, i32p, i32p, C.POINTER(Penalties), C.c_int32, i32p, f64p], C.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -12,10 +12,16 @@
 // float32 product. Tiles of up to 128 tokens keep the three pieces within
 // one stage buffer.
 //
-// Q6_K / Q5_K weights go through the same split: warps 0-15 decode each value
-// as the reference does (float32, quant_k.go:47-85), scale it by 2^sw and
-// split it into a binary16 pair, which keeps 22 of its up to 24 significant
-// bits (at most 2^-22 relative per weight).
+// Q6_K / Q5_K weights: warps 0-15 decode each value as the reference does
+// (float32, quant_k.go:47-85), scale it by 2^sw and split it into three
+// binary16 pieces W' = Wh + Wm + Wl, each the rounding of what the previous
+// pieces leave (both differences are exact in float32). Eleven significant
+// bits per piece cover the decoded value's 24, so the operand is the
+// reference's float32 weight exactly whenever its lowest bit lands at or
+// above 2^-24 after scaling: every value within 2^14 of the matrix bound
+// 2^13 (tcu_read_values with TCU_DECODE_TC checks this bit for bit). Four
+// products Wh.Xh + Wh.Xl + Wm.Xh + Wl.Xh are accumulated; the dropped
+// Wm.Xl and Wl.Xl are ~2^-22 of the result, as for Q8_0 below.
 //
 // Q8_0 exactness: a Q8_0 weight
 // s*q has at most 19 significant bits and an activation 24, more than one
@@ -52,8 +58,16 @@ constexpr int TC_MMA_WARP = TC_DQW, TC_TMA_WARP = TC_DQW + 1;
 constexpr int TC_THREADS = TC_DQW * 32 + 64;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;      // 16 KB per binary16 weight tile
 constexpr int TC_B_BYTES = TC_MAXN * TC_BK * 2;    // 32 KB per binary16 activation tile
-constexpr int TC_BUF_BYTES = 2 * TC_A_BYTES + 2 * TC_B_BYTES;
-constexpr int TC_SMEM = 2 * TC_BUF_BYTES + 1024 + 256;  // two buffers, 1 KB alignment slack, barriers
+// Weight operand of a GEMM: Q8_0 decoded into a binary16 pair, Q6_K / Q5_K
+// into three binary16 pieces, BF16 brought by TMA as stored.
+enum TcWeights : int { TCW_Q8 = 0, TCW_KQ = 1, TCW_BF16 = 2 };
+// Binary16 weight pieces a stage buffer holds (BF16 uses the first).
+__host__ __device__ constexpr int tc_pieces(int wm) { return wm == TCW_KQ ? 3 : 2; }
+__host__ __device__ constexpr int tc_buf_bytes(int wm) { return tc_pieces(wm) * TC_A_BYTES + 2 * TC_B_BYTES; }
+// Two stage buffers, 1 KB alignment slack, barriers: 193.25 KB (Q8_0, BF16)
+// or 225.25 KB (K-quants) of the 227 KB a CTA may hold.
+__host__ __device__ constexpr int tc_smem_bytes(int wm) { return 2 * tc_buf_bytes(wm) + 1024 + 256; }
+static_assert(tc_smem_bytes(TCW_KQ) <= 227 * 1024, "tensor-core GEMM stage buffers exceed shared memory");
 
 struct TcArgs {
   DMat W;             // Q8_0 weights [rows][cols]
@@ -164,11 +178,65 @@ __device__ __forceinline__ void tc_dequant8(uint2 q, __half2 s2, uint4& hi, uint
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// WB: bfloat16 weights through wmap (else Q8_0 weights dequantised by warps
-// 0-15; wmap unused).
-template <int EPI, bool WB>
+// The tensor-core operand of sixteen weights W[r][k0 .. k0 + 16), scaled by
+// wscale = 2^sw, as binary16 pieces p[piece][half] (eight values per uint4):
+//   Q8_0 (WM = TCW_Q8): the exact pair of tc_dequant8; values at or past
+//     k_end are zero;
+//   Q6_K / Q5_K (WM = TCW_KQ): each value decoded as kquant_decode8 does
+//     (the reference's float32 arithmetic), then split into three pieces,
+//     h = fp16(v), m = fp16(v - h), l = fp16(v - h - m). Rows are whole
+//     super-blocks (K % 256 == 0, k_end too), so k0 < k_end covers all 16.
+// Rows r >= R give zeros. The GEMM's decoding warps and tcu_read_values
+// (TCU_DECODE_TC) both call this.
+template <int WM>
+__device__ __forceinline__ void tc_weight_pieces(const DMat& W, int r, int k0, int k_end, float wscale,
+                                                 uint4 (&p)[tc_pieces(WM)][2]) {
+#pragma unroll
+  for (int j = 0; j < tc_pieces(WM); j++) p[j][0] = p[j][1] = make_uint4(0, 0, 0, 0);
+  if (r >= W.rows || k0 >= k_end) return;
+  if constexpr (WM == TCW_KQ) {
+    float v[16];
+    kquant_decode8(W, r, k0, v);
+    kquant_decode8(W, r, k0 + 8, v + 8);
+    uint32_t hh[8], mm[8], ll[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float x0 = v[2 * i] * wscale, x1 = v[2 * i + 1] * wscale;
+      const __half2 h = __floats2half2_rn(x0, x1);
+      const float2 hf = __half22float2(h);
+      const float r0 = __fsub_rn(x0, hf.x), r1 = __fsub_rn(x1, hf.y);
+      const __half2 m = __floats2half2_rn(r0, r1);
+      const float2 mf = __half22float2(m);
+      const __half2 l = __floats2half2_rn(__fsub_rn(r0, mf.x), __fsub_rn(r1, mf.y));
+      hh[i] = *reinterpret_cast<const uint32_t*>(&h);
+      mm[i] = *reinterpret_cast<const uint32_t*>(&m);
+      ll[i] = *reinterpret_cast<const uint32_t*>(&l);
+    }
+    p[0][0] = make_uint4(hh[0], hh[1], hh[2], hh[3]);
+    p[0][1] = make_uint4(hh[4], hh[5], hh[6], hh[7]);
+    p[1][0] = make_uint4(mm[0], mm[1], mm[2], mm[3]);
+    p[1][1] = make_uint4(mm[4], mm[5], mm[6], mm[7]);
+    p[2][0] = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+    p[2][1] = make_uint4(ll[4], ll[5], ll[6], ll[7]);
+  } else {
+    const uint4 q = *reinterpret_cast<const uint4*>(W.w + (size_t)r * W.cols + k0);
+    const float s = __half2float(W.s[(size_t)r * W.sstride + k0 / 32]) * wscale;
+    const __half2 s2 = __float2half2_rn(s);
+    tc_dequant8(make_uint2(q.x, q.y), s2, p[0][0], p[1][0]);
+    tc_dequant8(make_uint2(q.z, q.w), s2, p[0][1], p[1][1]);
+    if (k0 + 8 > k_end) p[0][0] = p[1][0] = make_uint4(0, 0, 0, 0);
+    if (k0 + 16 > k_end) p[0][1] = p[1][1] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// WM: TCW_BF16 takes bfloat16 weight tiles through wmap; TCW_Q8 and TCW_KQ
+// weights are decoded by warps 0-15 (wmap unused).
+template <int EPI, int WM>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap xmap,
                                                            const __grid_constant__ CUtensorMap wmap, TcArgs a) {
+  constexpr bool WB = WM == TCW_BF16;
+  constexpr int NP = tc_pieces(WM);
+  constexpr int TC_BUF_BYTES = tc_buf_bytes(WM);
   extern __shared__ uint8_t tc_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * TC_BUF_BYTES);
@@ -222,10 +290,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         if (WB) {
           tc_tma_load(buf(b), &wmap, k, r0, &x_full[b]);
 #pragma unroll
-          for (int p = 0; p < 3; p++) tc_tma_load(buf(b) + 2 * TC_A_BYTES + p * NT * TC_BK * 2, &xmap, k, p * a.n_pad + t0, &x_full[b]);
+          for (int p = 0; p < 3; p++) tc_tma_load(buf(b) + NP * TC_A_BYTES + p * NT * TC_BK * 2, &xmap, k, p * a.n_pad + t0, &x_full[b]);
         } else {
-          tc_tma_load(buf(b) + 2 * TC_A_BYTES, &xmap, k, t0, &x_full[b]);
-          tc_tma_load(buf(b) + 2 * TC_A_BYTES + TC_B_BYTES, &xmap, k, a.n_pad + t0, &x_full[b]);
+          tc_tma_load(buf(b) + NP * TC_A_BYTES, &xmap, k, t0, &x_full[b]);
+          tc_tma_load(buf(b) + NP * TC_A_BYTES + TC_B_BYTES, &xmap, k, a.n_pad + t0, &x_full[b]);
         }
       }
     }
@@ -243,7 +311,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         const bool second = two_acc && k >= a.k_split;
         const uint32_t d = tmem + (second ? TC_MAXN : 0);
         bool& first = second ? first1 : first0;
-        const uint32_t sa = smem_u32(buf(b)), sb = sa + 2 * TC_A_BYTES;
+        const uint32_t sa = smem_u32(buf(b)), sb = sa + NP * TC_A_BYTES;
 #pragma unroll
         for (int kk = 0; kk < TC_BK / 16; kk++) {
           const uint32_t off = kk * 32;  // 16 columns of 2 bytes
@@ -255,12 +323,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
               first = false;
             }
           } else {
-            const uint64_t wh = tc_smem_desc(sa + off), wl = tc_smem_desc(sa + TC_A_BYTES + off);
+            // Q8_0: Wh.Xh + Wh.Xl + Wl.Xh; K-quants: Wh.Xh + Wh.Xl + Wm.Xh + Wl.Xh.
+            const uint64_t wh = tc_smem_desc(sa + off);
             const uint64_t xh = tc_smem_desc(sb + off), xl = tc_smem_desc(sb + TC_B_BYTES + off);
             tc_mma(d, wh, xh, idesc, first ? 0u : 1u);
             first = false;
             tc_mma(d, wh, xl, idesc, 1u);
-            tc_mma(d, wl, xh, idesc, 1u);
+#pragma unroll
+            for (int p = 1; p < NP; p++) tc_mma(d, tc_smem_desc(sa + p * TC_A_BYTES + off), xh, idesc, 1u);
           }
         }
         tc_commit(&mma_done[b]);
@@ -275,46 +345,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     for (int i = 0; i < (WB ? 0 : iters); i++) {
       const int b = i & 1;
       if (i >= 2) mbar_wait(&mma_done[b], ((i >> 1) - 1) & 1, a.err);
-      uint8_t* ah = buf(b);
-      uint8_t* al = ah + TC_A_BYTES;
+      uint8_t* aw = buf(b);
       const int k0 = k_begin + i * TC_BK + kc;
       for (int rr = tid >> 2; rr < TC_BM; rr += TC_DQW * 8) {
-        const int r = r0 + rr;
-        uint4 h0 = make_uint4(0, 0, 0, 0), l0 = h0, h1 = h0, l1 = h0;
-        if (a.W.fmt != FMT_Q8_0) {
-          // K-quant rows of whole super-blocks (K % 256 == 0, k_end too).
-          if (r < R && k0 < k_end) {
-            float v[16];
-            kquant_decode8(a.W, r, k0, v);
-            kquant_decode8(a.W, r, k0 + 8, v + 8);
-            uint32_t hh[8], ll[8];
+        uint4 pc[NP][2];
+        tc_weight_pieces<WM>(a.W, r0 + rr, k0, k_end, wscale, pc);
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-              const float x0 = v[2 * i] * wscale, x1 = v[2 * i + 1] * wscale;
-              const __half2 h = __floats2half2_rn(x0, x1);
-              const float2 hf = __half22float2(h);
-              const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
-              hh[i] = *reinterpret_cast<const uint32_t*>(&h);
-              ll[i] = *reinterpret_cast<const uint32_t*>(&l);
-            }
-            h0 = make_uint4(hh[0], hh[1], hh[2], hh[3]);
-            h1 = make_uint4(hh[4], hh[5], hh[6], hh[7]);
-            l0 = make_uint4(ll[0], ll[1], ll[2], ll[3]);
-            l1 = make_uint4(ll[4], ll[5], ll[6], ll[7]);
-          }
-        } else if (r < R && k0 < k_end) {
-          const uint4 q = *reinterpret_cast<const uint4*>(a.W.w + (size_t)r * K + k0);
-          const float s = __half2float(a.W.s[(size_t)r * a.W.sstride + k0 / 32]) * wscale;
-          const __half2 s2 = __float2half2_rn(s);
-          tc_dequant8(make_uint2(q.x, q.y), s2, h0, l0);
-          tc_dequant8(make_uint2(q.z, q.w), s2, h1, l1);
-          if (k0 + 8 > k_end) h0 = l0 = make_uint4(0, 0, 0, 0);
-          if (k0 + 16 > k_end) h1 = l1 = make_uint4(0, 0, 0, 0);
+        for (int p = 0; p < NP; p++) {
+          *reinterpret_cast<uint4*>(aw + p * TC_A_BYTES + tc_sw128(rr, kc)) = pc[p][0];
+          *reinterpret_cast<uint4*>(aw + p * TC_A_BYTES + tc_sw128(rr, kc + 8)) = pc[p][1];
         }
-        *reinterpret_cast<uint4*>(ah + tc_sw128(rr, kc)) = h0;
-        *reinterpret_cast<uint4*>(ah + tc_sw128(rr, kc + 8)) = h1;
-        *reinterpret_cast<uint4*>(al + tc_sw128(rr, kc)) = l0;
-        *reinterpret_cast<uint4*>(al + tc_sw128(rr, kc + 8)) = l1;
       }
       // Generic writes must be visible to the tensor core (async proxy).
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

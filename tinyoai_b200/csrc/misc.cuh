@@ -164,3 +164,156 @@ __global__ void k_argmax_rows(const float* logits, int V, int stride, unsigned l
 }
 
 }  // namespace tcu
+
+namespace tcu {
+
+// Keeps the better of two (score, id) pairs: higher score, then lower id
+// (id < 0: empty).
+__device__ __forceinline__ void cand_better(double& bv, int& bi, double v, int i) {
+  if (i >= 0 && (bi < 0 || v > bv || (v == bv && i < bi))) {
+    bv = v;
+    bi = i;
+  }
+}
+
+// The block's best (score, id) pair; every thread returns it. red_v / red_i:
+// one slot per warp.
+__device__ __forceinline__ void cand_block_best(double& bv, int& bi, double* red_v, int* red_i) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double v = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int i = __shfl_xor_sync(0xffffffffu, bi, o);
+    cand_better(bv, bi, v, i);
+  }
+  __syncthreads();
+  if (lane == 0) {
+    red_v[warp] = bv;
+    red_i[warp] = bi;
+  }
+  __syncthreads();
+  bv = red_v[0];
+  bi = red_i[0];
+  for (int w = 1; w < nw; w++) cand_better(bv, bi, red_v[w], red_i[w]);
+}
+
+// summarizeLogits (logprobs.go:64-95) for row r = blockIdx.x of a logits
+// matrix: z = best + log(sum exp(v - best)) in float64 over the whole row,
+// then logits[targets[r]] - z and the `count` largest logits (descending,
+// ties by lower id) as (id, logit - z). One CTA per row, count <= 256.
+__global__ void __launch_bounds__(1024) k_logprob_rows(const float* logits, int V, int stride, const int* targets, int count,
+                                                       double* chosen, int* top_ids, double* top_vals) {
+  extern __shared__ uint32_t lp_taken[];  // V bits
+  __shared__ double red_v[32];
+  __shared__ int red_i[32];
+  __shared__ double z_s;
+  const int r = blockIdx.x;
+  const float* row = logits + (size_t)r * stride;
+  for (int i = threadIdx.x; i < (V + 31) / 32; i += blockDim.x) lp_taken[i] = 0;
+  double bv = 0.0;
+  int bi = -1;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) cand_better(bv, bi, (double)row[i], i);
+  cand_block_best(bv, bi, red_v, red_i);
+  const double best = bv;
+  double s = 0.0;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) s += exp((double)row[i] - best);
+  s = warp_sum_d(s);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red_v[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += red_v[w];
+    z_s = best + log(t);
+    chosen[r] = (double)row[targets[r]] - z_s;
+  }
+  __syncthreads();
+  const double z = z_s;
+  for (int j = 0; j < count; j++) {
+    double v = 0.0;
+    int id = -1;
+    for (int i = threadIdx.x; i < V; i += blockDim.x)
+      if (!((lp_taken[i >> 5] >> (i & 31)) & 1u)) cand_better(v, id, (double)row[i], i);
+    cand_block_best(v, id, red_v, red_i);
+    if (threadIdx.x == 0) {
+      top_ids[(size_t)r * count + j] = id;
+      top_vals[(size_t)r * count + j] = id >= 0 ? (double)row[id] - z : 0.0;
+      if (id >= 0) lp_taken[id >> 5] |= 1u << (id & 31);
+    }
+    __syncthreads();
+  }
+}
+
+// Penalised scores of several rows, grouped by id on the host: row r has
+// the distinct ids ids[row_off[r] .. row_off[r + 1]) in ascending order, and
+// id j's float64 score is (double)logit - terms[term_off[j]] - ... -
+// terms[term_off[j + 1] - 1], subtracted in that order (the order
+// penalizedLogits applies them, sampling.go:76-101).
+struct PenaltyRows {
+  const int* row_off;
+  const int* ids;
+  const int* term_off;
+  const double* terms;
+};
+
+// samplingCandidates(penalizedLogits(row), k) (sampling.go:76-143) for row
+// r = blockIdx.x: the k largest float64 scores, descending, ties by lower id.
+// Dynamic shared memory: two V-bit maps, then the row's penalised ids and
+// scores (max_ids each).
+__global__ void __launch_bounds__(1024) k_candidates_rows(const float* logits, int V, int stride, PenaltyRows pr, int max_ids, int k,
+                                                          int* out_ids, double* out_vals) {
+  extern __shared__ __align__(8) uint8_t cand_smem[];
+  const int nwords = (V + 31) / 32;
+  double* pv = reinterpret_cast<double*>(cand_smem);
+  int* pid = reinterpret_cast<int*>(pv + max_ids);
+  uint32_t* taken = reinterpret_cast<uint32_t*>(pid + max_ids);
+  uint32_t* pen = taken + nwords;
+  __shared__ double red_v[32];
+  __shared__ int red_i[32];
+  const int r = blockIdx.x;
+  const float* row = logits + (size_t)r * stride;
+  for (int i = threadIdx.x; i < nwords; i += blockDim.x) taken[i] = pen[i] = 0;
+  __syncthreads();
+  const int j0 = pr.row_off[r], nd = pr.row_off[r + 1] - j0;
+  for (int j = threadIdx.x; j < nd; j += blockDim.x) {
+    const int id = pr.ids[j0 + j];
+    double v = (double)row[id];
+    for (int t = pr.term_off[j0 + j]; t < pr.term_off[j0 + j + 1]; t++) v = __dsub_rn(v, pr.terms[t]);
+    pv[j] = v;
+    pid[j] = id;
+    atomicOr(&pen[id >> 5], 1u << (id & 31));
+  }
+  __syncthreads();
+  for (int j = 0; j < k; j++) {
+    double bv = 0.0;
+    int bi = -1;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const uint32_t bit = 1u << (i & 31);
+      if (taken[i >> 5] & bit) continue;
+      double v;
+      if (pen[i >> 5] & bit) {
+        int lo = 0, hi = nd - 1;  // ids ascending: binary search
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (pid[mid] < i)
+            lo = mid + 1;
+          else
+            hi = mid;
+        }
+        v = pv[lo];
+      } else {
+        v = (double)row[i];
+      }
+      cand_better(bv, bi, v, i);
+    }
+    cand_block_best(bv, bi, red_v, red_i);
+    if (threadIdx.x == 0) {
+      out_ids[(size_t)r * k + j] = bi;
+      out_vals[(size_t)r * k + j] = bv;
+      if (bi >= 0) taken[bi >> 5] |= 1u << (bi & 31);
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace tcu

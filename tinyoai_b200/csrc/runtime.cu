@@ -13,6 +13,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -29,11 +30,13 @@
 #include "gemm_tc.cuh"
 #include <cudaTypedefs.h>
 #include "misc.cuh"
+#include "read_values.cuh"
 
 using namespace tcu;
 
 static const int CHUNK = 512;      // prompt tokens per internal chunk (mlx.go:352-355)
 static const int SPLIT_PAGES = 2;  // KV pages per decode attention unit
+static const int LP_ROWS = 32;     // log-probability rows per head product (mlx_native.go's probabilityBatch)
 
 // ---------------------------------------------------------------------------
 // Errors: integer status + thread-local message (internal/mlx/bridge.c:13-33).
@@ -127,6 +130,7 @@ struct tcu_model {
   uint32_t mega_slot_bytes = 0, mega_off[5] = {0, 0, 0, 0, 0};
   int mega_slots = 0, mega_split = 0, mega_att_warp = 0;
   size_t mega_smem = 0;
+  bool mega_prefetch = false;  // L2 prefetch of the next layer's W1 (TCU_L2_PREFETCH=1 turns it on)
 };
 
 static int dalloc(tcu_model* m, void** p, size_t n) {
@@ -280,6 +284,23 @@ static int upload_floats(tcu_model* m, const std::vector<float>& v, float** out)
   return TCU_OK;
 }
 
+// Once per device (with it current): the largest dynamic shared memory of
+// the one-CTA-per-row sampling kernels, whose need varies with the
+// vocabulary. Set once, not per launch, so no other thread can lower it
+// between another call's set and its launch.
+static std::mutex g_attr_mu;
+static bool g_attr_done[64] = {};
+static int sampling_smem_attrs(int device) {
+  std::lock_guard<std::mutex> g(g_attr_mu);
+  if (device < 0 || device >= 64 || g_attr_done[device]) return TCU_OK;
+  const int lim = 227 * 1024;
+  CK(cudaFuncSetAttribute(k_shortlist, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+  CK(cudaFuncSetAttribute(k_logprob_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+  CK(cudaFuncSetAttribute(k_candidates_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+  g_attr_done[device] = true;
+  return TCU_OK;
+}
+
 static int check_device(int device) {
   int n = 0;
   if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return fail(TCU_ENODEV, "no CUDA device available");
@@ -288,7 +309,7 @@ static int check_device(int device) {
   CK(cudaGetDeviceProperties(&prop, device));
   if (prop.major != 10) return fail(TCU_ENODEV, "device %d is sm_%d%d; this library is built for sm_100a", device, prop.major, prop.minor);
   CK(cudaSetDevice(device));
-  return TCU_OK;
+  return sampling_smem_attrs(device);
 }
 
 static void init_common(tcu_model* m, const tcu_load_options* o) {
@@ -301,6 +322,8 @@ static void init_common(tcu_model* m, const tcu_load_options* o) {
   m->disable_stream = k && strcmp(k, "portable") == 0;
   const char* g = getenv("TCU_GEMM");
   m->use_tc = !(g && strcmp(g, "simt") == 0);
+  const char* pf = getenv("TCU_L2_PREFETCH");
+  m->mega_prefetch = pf && strcmp(pf, "1") == 0;
 }
 
 // StableLM rotary table (stablelm.go:309-326): per position and rotary pair,
@@ -724,6 +747,19 @@ struct Work {
   int asx_stride = 0;
   int* grab = nullptr;
   int* done = nullptr;
+  // Log-probability rows (k_logprob_rows), LP_ROWS rows at a time: targets,
+  // chosen log probabilities, top ids and log probabilities (count <= 256).
+  int* lp_targets = nullptr;
+  double* lp_chosen = nullptr;
+  int* lp_ids = nullptr;
+  double* lp_vals = nullptr;
+  // Sampling candidates (k_candidates_rows): [seqs][256] ids and scores, and
+  // the penalty rows of one call (row offsets, ids, term offsets, terms),
+  // grown when a call needs more.
+  int* cd_ids = nullptr;
+  double* cd_vals = nullptr;
+  uint8_t* pen_buf = nullptr;
+  size_t pen_cap = 0;
   // Tensor-core GEMM workspace (allocated on first use): binary16 split of
   // the activations [2][tc_npad][tc_kmax], their shifts, split-K partials.
   __half* tc_split = nullptr;
@@ -734,6 +770,7 @@ struct Work {
   std::vector<void*> allocs;
   ~Work() {
     for (void* p : allocs) cudaFree(p);
+    if (pen_buf) cudaFree(pen_buf);
     if (tc_split) cudaFree(tc_split);
     if (tc_sx) cudaFree(tc_sx);
     if (tc_part) cudaFree(tc_part);
@@ -779,6 +816,12 @@ static int work_init(tcu_model* m, Work* w, int rows, int seqs, int logits_rows,
   TRY(w->get(&w->err, 1));
   TRY(w->get(&w->keys, 2));
   TRY(w->get(&w->step, 1));
+  TRY(w->get(&w->lp_targets, LP_ROWS));
+  TRY(w->get(&w->lp_chosen, LP_ROWS));
+  TRY(w->get(&w->lp_ids, (size_t)LP_ROWS * 256));
+  TRY(w->get(&w->lp_vals, (size_t)LP_ROWS * 256));
+  TRY(w->get(&w->cd_ids, (size_t)seqs * 256));
+  TRY(w->get(&w->cd_vals, (size_t)seqs * 256));
   if (m->mega) {
     const size_t nb16 = (size_t)(m->d + m->ff) / 16;
     w->asx_stride = (int)((nb16 + 3) / 4 * 4);
@@ -1097,18 +1140,19 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // Power of two for the tensor-core split of a Q8_0 matrix: the largest
 // |s * q| (q <= 128) scaled below 2^13.
-static int set_tc_shift(tcu_model* m, DMat* W) {
+// Power of two of a matrix's tensor-core split (Q8_0, Q6_K, Q5_K; others 0),
+// from a bound on |value| reduced into *scratch (one device word).
+static int tc_shift_of(DMat* W, unsigned* scratch, int sm_count) {
   const bool kq = (W->fmt == FMT_Q6_K || W->fmt == FMT_Q5_K) && W->cols % 256 == 0;
   if (W->fmt != FMT_Q8_0 && !kq) return TCU_OK;
-  if (!m->scratch_u32) TRY(dalloc(m, (void**)&m->scratch_u32, sizeof(unsigned)));
-  CK(cudaMemset(m->scratch_u32, 0, sizeof(unsigned)));
+  CK(cudaMemset(scratch, 0, sizeof(unsigned)));
   if (kq)
-    k_kquant_absmax<<<m->sm_count * 4, 256>>>(W->w, (size_t)W->rows * (W->cols / 256), W->fmt, m->scratch_u32);
+    k_kquant_absmax<<<sm_count * 4, 256>>>(W->w, (size_t)W->rows * (W->cols / 256), W->fmt, scratch);
   else
-    k_scale_absmax<<<m->sm_count * 4, 256>>>(W->s, W->rows, W->sstride, W->cols / 32, m->scratch_u32);
+    k_scale_absmax<<<sm_count * 4, 256>>>(W->s, W->rows, W->sstride, W->cols / 32, scratch);
   CK(cudaGetLastError());
   unsigned bits = 0;
-  CK(cudaMemcpy(&bits, m->scratch_u32, sizeof(unsigned), cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(&bits, scratch, sizeof(unsigned), cudaMemcpyDeviceToHost));
   float mx;
   memcpy(&mx, &bits, sizeof(mx));
   if (kq) mx /= 128.f;  // the bound below is for |scale| * 128
@@ -1116,6 +1160,13 @@ static int set_tc_shift(tcu_model* m, DMat* W) {
   if (mx > 0.f) frexpf(mx * 128.f, &e);
   W->tc_sw = mx > 0.f ? std::max(-100, std::min(100, 13 - e)) : 0;
   return TCU_OK;
+}
+
+static int set_tc_shift(tcu_model* m, DMat* W) {
+  const bool kq = (W->fmt == FMT_Q6_K || W->fmt == FMT_Q5_K) && W->cols % 256 == 0;
+  if (W->fmt != FMT_Q8_0 && !kq) return TCU_OK;
+  if (!m->scratch_u32) TRY(dalloc(m, (void**)&m->scratch_u32, sizeof(unsigned)));
+  return tc_shift_of(W, m->scratch_u32, m->sm_count);
 }
 
 static int set_tc_shifts(tcu_model* m) {
@@ -1225,8 +1276,10 @@ static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaS
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return false;
   }
-  auto kern = wb ? k_gemm_tc<EPI, true> : k_gemm_tc<EPI, false>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) != cudaSuccess) {
+  const int wm = wb ? TCW_BF16 : kq ? TCW_KQ : TCW_Q8;
+  auto kern = wm == TCW_BF16 ? k_gemm_tc<EPI, TCW_BF16> : wm == TCW_KQ ? k_gemm_tc<EPI, TCW_KQ> : k_gemm_tc<EPI, TCW_Q8>;
+  const int tc_smem = tc_smem_bytes(wm);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem) != cudaSuccess) {
     cudaGetLastError();
     return false;
   }
@@ -1264,7 +1317,7 @@ static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaS
   // measured faster with row tiles first.
   a.tok_fast = (wb || kq) ? 1 : 0;
   const dim3 grid = a.tok_fast ? dim3(n_pad / n_tile, row_tiles, z) : dim3(row_tiles, n_pad / n_tile, z);
-  kern<<<grid, TC_THREADS, TC_SMEM, s>>>(map, wmap, a);
+  kern<<<grid, TC_THREADS, tc_smem, s>>>(map, wmap, a);
   NOTE("k_gemm_tc");
   if (z > 1) {
     if constexpr (EPI == EPI_RESID2) {
@@ -1751,6 +1804,7 @@ struct tcu_session {
   size_t graph_events = 0;
   int branches_open = 0;
   Prof prof;
+  int hold_layer = -1;  // failure-detection test hook of the persistent step (TCU_TEST_HOLD_ARRIVAL)
 };
 
 // Routes the launch helpers' stage events (when profiling) and bounded-wait
@@ -1843,9 +1897,63 @@ static int check_tokens(const tcu_model* m, const int32_t* tokens, int n) {
   return TCU_OK;
 }
 
+// Probability rows of a forward (ForwardWithLogprobs): per input position
+// the target's log probability and `count` top (id, log probability).
+struct LogprobReq {
+  const int32_t* targets;
+  int count;
+  double* chosen;
+  int32_t* top_ids;
+  double* top_vals;
+};
+
+// summarizeLogits of `rows` logits rows at blk (stride V) for input
+// positions i0 .. i0 + rows - 1: targets up, k_logprob_rows, results down
+// into the caller's arrays (stream order keeps the device buffers of one
+// block from being overwritten before their copies).
+static int enqueue_logprob_block(const tcu_model* m, Work* w, const float* blk, int rows, int i0, const LogprobReq& lp, cudaStream_t s) {
+  CK(cudaMemcpyAsync(w->lp_targets, lp.targets + i0, rows * sizeof(int), cudaMemcpyHostToDevice, s));
+  const size_t smem = ((size_t)m->V + 31) / 32 * 4;
+  k_logprob_rows<<<rows, 1024, smem, s>>>(blk, m->V, m->V, w->lp_targets, lp.count, w->lp_chosen, w->lp_ids, w->lp_vals);
+  NOTE("k_logprob_rows");
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(lp.chosen + i0, w->lp_chosen, rows * sizeof(double), cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(lp.top_ids + (size_t)i0 * lp.count, w->lp_ids, (size_t)rows * lp.count * sizeof(int), cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(lp.top_vals + (size_t)i0 * lp.count, w->lp_vals, (size_t)rows * lp.count * sizeof(double), cudaMemcpyDeviceToHost,
+                     s));
+  return TCU_OK;
+}
+
+// Probability rows of the c positions of a prefill chunk (hidden rows in
+// w->x): final norm, the head product over up to LP_ROWS rows at a time
+// into the chunk's attention/SwiGLU buffer (free once the chunk's layers
+// ran), then enqueue_logprob_block (mlx_native.go:436-478 in batches).
+static int enqueue_logprob_chunk(const tcu_model* m, Work* w, int c, int i0, const LogprobReq& lp, cudaStream_t s) {
+  const size_t cap_rows = (size_t)w->rows * (m->d + m->ff) / (size_t)m->V;
+  const int nb = (int)std::min<size_t>(LP_ROWS, cap_rows);
+  if (nb < 1) return fail(TCU_EUNSUP, "vocabulary of %d is too large for the probability rows of this workspace", m->V);
+  float* blk = w->ah;
+  for (int j0 = 0; j0 < c; j0 += nb) {
+    const int r = std::min(nb, c - j0);
+    launch_norm_rows(m, w->x + (size_t)j0 * m->d, w->xn, r, m->fnw, m->fnb, s);
+    GemmArgs g{};
+    g.W = m->head;
+    g.n = r;
+    g.A = w->xn;
+    g.lda = m->d;
+    g.out = blk;
+    g.out_stride = m->V;
+    g_stage = ST_HEAD;
+    launch_gemm<EPI_STORE>(m, w, g, s);
+    TRY(enqueue_logprob_block(m, w, blk, r, i0 + j0, lp, s));
+  }
+  return TCU_OK;
+}
+
 // Runs tokens[0..n) at positions prefix.. and leaves the last row's argmax in
-// w.argmax[0] and (if logits) its logits in w.logits.
-static int session_run(tcu_session* s, int prefix, const int32_t* tokens, int n, float* all_logits) {
+// w.argmax[0] and (if logits) its logits in w.logits; with lp, also every
+// position's probability row.
+static int session_run(tcu_session* s, int prefix, const int32_t* tokens, int n, float* all_logits, const LogprobReq* lp = nullptr) {
   tcu_model* m = s->m;
   TRY(prepare_pages(m, s->pool, s->pages, prefix, prefix + n, s->stream));
   TRY(upload_pt(s));
@@ -1856,6 +1964,7 @@ static int session_run(tcu_session* s, int prefix, const int32_t* tokens, int n,
     const int split = SPLIT_PAGES * m->P;
     enqueue_decode(m, s->pool, &s->w, 1, false, (prefix + 1 + split - 1) / split, true, s->stream);
     CK(cudaGetLastError());
+    if (lp) TRY(enqueue_logprob_block(m, &s->w, s->w.logits, 1, 0, *lp, s->stream));
     return TCU_OK;
   }
   for (int off = 0; off < n; off += CHUNK) {
@@ -1863,6 +1972,7 @@ static int session_run(tcu_session* s, int prefix, const int32_t* tokens, int n,
     CK(cudaMemcpyAsync(s->w.tokens, tokens + off, c * sizeof(int), cudaMemcpyHostToDevice, s->stream));
     enqueue_prefill(m, s->pool, &s->w, c, prefix + off, s->stream);
     CK(cudaGetLastError());
+    if (lp) TRY(enqueue_logprob_chunk(m, &s->w, c, off, *lp, s->stream));
     if (all_logits) {
       for (int j = 0; j < c; j++) {
         enqueue_head_row(m, &s->w, j, s->w.logits, s->stream);
@@ -1940,6 +2050,109 @@ static void branches_release(tcu_branches* b) {
   cudaStreamSynchronize(s->stream);
   for (auto& pl : b->pages) release_pages(s->m, s->pool, pl, 0);
   s->branches_open--;
+}
+
+// ---------------------------------------------------------------------------
+// Sampling penalties (sampling.go:45-101): the host turns each row's history
+// into ordered float64 terms per penalised id; k_candidates_rows subtracts
+// them on the device and ranks the row.
+
+// SamplingOptions.Validate (sampling.go:45-58) for the penalty fields.
+static int penalties_check(const tcu_penalties& p) {
+  for (double v : {p.repetition_penalty, p.presence_penalty, p.frequency_penalty, p.repetition_slope})
+    if (!std::isfinite(v)) return fail(TCU_EINVAL, "sampling values must be finite");
+  if (p.repetition_penalty < 1 || p.repetition_range < 0 || p.repetition_slope < 0) return fail(TCU_EINVAL, "sampling value out of range");
+  return TCU_OK;
+}
+
+// repetitionWeight (sampling.go:64-70).
+static double repetition_weight(int age, int window, double slope) {
+  if (slope == 0 || window <= 1) return 1;
+  const double x = 1 - 2 * (double)age / (double)(window - 1);
+  return 1 + slope * x / (1 + std::fabs(x) * (slope - 1));
+}
+
+// Rows of penalised ids, as k_candidates_rows reads them (PenaltyRows).
+struct PenaltyHost {
+  std::vector<int> row_off{0}, ids, term_off{0};
+  std::vector<double> terms;
+  int max_ids = 0;
+};
+
+// penalizedLogits (sampling.go:76-101) for one row as ordered terms: for the
+// last `window` ids (most recent first), frequency * weight on every
+// occurrence and (log(repetition) + presence) * weight on an id's most
+// recent one; ids outside the vocabulary are skipped. Terms are grouped by id
+// keeping their order, so each id's score is the same chain of float64
+// subtractions the reference performs.
+static void penalties_add_row(PenaltyHost& h, const int32_t* hist, int n_hist, const tcu_penalties& p, int V) {
+  const int window = p.repetition_range == 0 ? n_hist : p.repetition_range;
+  const int m = std::min(window, n_hist);
+  std::vector<std::pair<int, double>> ops;
+  ops.reserve((size_t)2 * m);
+  std::vector<uint8_t> seen(m > 0 ? V : 0, 0);
+  for (int age = 0; age < m; age++) {
+    const int id = hist[n_hist - 1 - age];
+    if (id < 0 || id >= V) continue;
+    const double weight = repetition_weight(age, window, p.repetition_slope);
+    ops.emplace_back(id, p.frequency_penalty * weight);
+    if (!seen[id]) {
+      ops.emplace_back(id, (std::log(p.repetition_penalty) + p.presence_penalty) * weight);
+      seen[id] = 1;
+    }
+  }
+  std::stable_sort(ops.begin(), ops.end(), [](const std::pair<int, double>& a, const std::pair<int, double>& b) { return a.first < b.first; });
+  int nd = 0;
+  for (size_t i = 0; i < ops.size(); i++) {
+    if (i == 0 || ops[i].first != ops[i - 1].first) {
+      if (i > 0) h.term_off.push_back((int)h.terms.size());
+      h.ids.push_back(ops[i].first);
+      nd++;
+    }
+    h.terms.push_back(ops[i].second);
+  }
+  if (nd > 0) h.term_off.push_back((int)h.terms.size());
+  h.row_off.push_back((int)h.ids.size());
+  h.max_ids = std::max(h.max_ids, nd);
+}
+
+static const int CAND_MAX_IDS = 16384;  // penalised ids per row (k_candidates_rows shared memory)
+
+// Uploads the penalty rows and enqueues k_candidates_rows over `rows` logits
+// rows; results in w->cd_ids / w->cd_vals ([rows][k]).
+static int enqueue_candidates(const tcu_model* m, Work* w, const float* logits, int rows, const PenaltyHost& h, int k, cudaStream_t s) {
+  if (h.max_ids > CAND_MAX_IDS) return fail(TCU_EINVAL, "%d distinct penalised ids in one row (at most %d)", h.max_ids, CAND_MAX_IDS);
+  auto r16 = [](size_t b) { return (b + 15) / 16 * 16; };
+  const size_t o_ids = r16(h.row_off.size() * 4), o_toff = o_ids + r16(std::max<size_t>(h.ids.size(), 1) * 4);
+  const size_t o_terms = o_toff + r16(h.term_off.size() * 4), bytes = o_terms + std::max<size_t>(h.terms.size(), 1) * 8;
+  if (bytes > w->pen_cap) {
+    // Grows (rarely): synchronise the stream so no queued kernel still reads it.
+    cudaStreamSynchronize(s);
+    if (w->pen_buf) cudaFree(w->pen_buf);
+    w->pen_buf = nullptr;
+    w->pen_cap = 0;
+    const size_t cap = std::max<size_t>(bytes * 2, 64 << 10);
+    if (cudaMalloc(&w->pen_buf, cap) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(TCU_ENOMEM, "penalty rows: cannot allocate %zu bytes", cap);
+    }
+    w->pen_cap = cap;
+  }
+  std::vector<uint8_t> stage(bytes, 0);
+  memcpy(stage.data(), h.row_off.data(), h.row_off.size() * 4);
+  if (!h.ids.empty()) memcpy(stage.data() + o_ids, h.ids.data(), h.ids.size() * 4);
+  memcpy(stage.data() + o_toff, h.term_off.data(), h.term_off.size() * 4);
+  if (!h.terms.empty()) memcpy(stage.data() + o_terms, h.terms.data(), h.terms.size() * 8);
+  CK(cudaMemcpyAsync(w->pen_buf, stage.data(), bytes, cudaMemcpyHostToDevice, s));
+  PenaltyRows pr{(const int*)w->pen_buf, (const int*)(w->pen_buf + o_ids), (const int*)(w->pen_buf + o_toff),
+                 (const double*)(w->pen_buf + o_terms)};
+  const int max_ids = std::max(1, h.max_ids);
+  const size_t smem = (size_t)max_ids * 12 + ((size_t)m->V + 31) / 32 * 8;
+  if (smem > 227 * 1024) return fail(TCU_EINVAL, "penalised ids and vocabulary exceed the candidates kernel's shared memory");
+  k_candidates_rows<<<rows, 1024, smem, s>>>(logits, m->V, m->V, pr, max_ids, k, w->cd_ids, w->cd_vals);
+  NOTE("k_candidates_rows");
+  CK(cudaGetLastError());
+  return TCU_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -2123,6 +2336,8 @@ static int launch_mega(tcu_session* s) {
   mega_dn_scales(m, &a.dn_sstride, &a.dn_soff);
   a.xdn = s->w.xdn;
   a.err = s->w.err;
+  a.hold_layer = s->hold_layer;
+  a.l2_prefetch = m->mega_prefetch ? 1 : 0;
   a.slot_bytes = m->mega_slot_bytes;
   a.nslots = m->mega_slots;
   a.off_x = m->mega_off[0];
@@ -2164,6 +2379,10 @@ int tcu_session_generate_greedy(tcu_session* s, int32_t prefix, const int32_t* t
   if (rc == TCU_OK) rc = upload_pt(s);
   if (rc == TCU_OK && m->mega && steps > 1) {
     // Persistent decode: one cooperative launch per generated token.
+    // TCU_TEST_HOLD_ARRIVAL=<layer> makes the first launch hold back one
+    // arrival in that layer (a failure-detection test: its waits run out).
+    const char* hold = getenv("TCU_TEST_HOLD_ARRIVAL");
+    s->hold_layer = (hold && *hold) ? std::max(-1, std::min(m->L - 1, atoi(hold))) : -1;
     const int first = prefix + n;
     CK(cudaMemcpyAsync(s->w.pos, &first, sizeof(int), cudaMemcpyHostToDevice, s->stream));
     CK(cudaMemcpyAsync(s->w.keys, s->w.argmax, sizeof(unsigned long long), cudaMemcpyDeviceToDevice, s->stream));
@@ -2229,15 +2448,53 @@ int tcu_session_shortlist(tcu_session* s, int32_t k, int32_t* ids, float* logits
   if (s->length == 0) return fail(TCU_EINVAL, "no logits: forward first");
   CK(cudaSetDevice(s->m->device));
   const int kk = std::min<int>(k, s->m->V);
-  const size_t smem = ((size_t)s->m->V + 31) / 32 * 4;
-  cudaFuncSetAttribute(k_shortlist, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  NOTE("cudaFuncSetAttribute(k_shortlist)");
+  const size_t smem = ((size_t)s->m->V + 31) / 32 * 4;  // attribute set at load (sampling_smem_attrs)
   k_shortlist<<<1, 1024, smem, s->stream>>>(s->w.logits, s->m->V, kk, s->w.sl_ids, s->w.sl_vals, s->w.sl_lse);
   NOTE("k_shortlist");
   CK(cudaGetLastError());
   CK(cudaMemcpyAsync(ids, s->w.sl_ids, kk * sizeof(int), cudaMemcpyDeviceToHost, s->stream));
   CK(cudaMemcpyAsync(logits, s->w.sl_vals, kk * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
   CK(cudaMemcpyAsync(logsumexp, s->w.sl_lse, sizeof(double), cudaMemcpyDeviceToHost, s->stream));
+  TRY(session_sync(s));
+  *n_out = kk;
+  return TCU_OK;
+}
+
+int tcu_session_forward_logprobs(tcu_session* s, int32_t prefix, const int32_t* tokens, const int32_t* targets, int32_t n,
+                                 int32_t count, double* chosen, int32_t* top_ids, double* top_logprobs, float* logits_out) {
+  TRY(validate_forward(s, prefix, tokens, n));
+  if (!targets || !chosen || !top_ids || !top_logprobs) return fail(TCU_EINVAL, "null argument");
+  // mlx_native.go:303-313
+  if (count < 1 || count > s->m->V || count > 256) return fail(TCU_EINVAL, "invalid probability request (count %d)", count);
+  for (int i = 0; i < n; i++)
+    if (targets[i] < 0 || targets[i] >= s->m->V) return fail(TCU_EINVAL, "invalid probability target %d", targets[i]);
+  CK(cudaSetDevice(s->m->device));
+  ProfScope ps(s);
+  const LogprobReq lp{targets, count, chosen, top_ids, top_logprobs};
+  int rc = session_run(s, prefix, tokens, n, nullptr, &lp);
+  if (rc == TCU_OK && logits_out) {
+    cudaError_t e = cudaMemcpyAsync(logits_out, s->w.logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToHost, s->stream);
+    if (e != cudaSuccess) rc = fail(TCU_ECUDA, "logits copy: %s", cudaGetErrorString(e));
+  }
+  return session_finish(s, rc, prefix + n);
+}
+
+int tcu_session_sample_candidates(tcu_session* s, const int32_t* history, int32_t n_history, const tcu_penalties* p, int32_t k,
+                                  int32_t* ids, double* scores, int32_t* n_out) {
+  if (!s || !ids || !scores || !n_out || (n_history > 0 && !history) || n_history < 0) return fail(TCU_EINVAL, "null argument");
+  if (s->closed) return fail(TCU_ECLOSED, "session is closed");
+  if (k < 1 || k > 256) return fail(TCU_EINVAL, "candidate count must be in [1, 256]");
+  if (s->length == 0) return fail(TCU_EINVAL, "no logits: forward first");
+  const tcu_penalties neutral{1.0, 0.0, 0.0, 0.0, 0};
+  const tcu_penalties& pp = p ? *p : neutral;
+  TRY(penalties_check(pp));
+  CK(cudaSetDevice(s->m->device));
+  const int kk = std::min<int>(k, s->m->V);
+  PenaltyHost h;
+  penalties_add_row(h, history, n_history, pp, s->m->V);
+  TRY(enqueue_candidates(s->m, &s->w, s->w.logits, 1, h, kk, s->stream));
+  CK(cudaMemcpyAsync(ids, s->w.cd_ids, kk * sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaMemcpyAsync(scores, s->w.cd_vals, kk * sizeof(double), cudaMemcpyDeviceToHost, s->stream));
   TRY(session_sync(s));
   *n_out = kk;
   return TCU_OK;
@@ -2447,6 +2704,7 @@ int tcu_branches_close(tcu_branches* b) {
 struct tcu_batch {
   tcu_model* m = nullptr;
   int max_rows = 0;
+  int last_rows = 0;  // rows of the last successful step (their logits stay in w.logits)
   Work w;
   cudaStream_t stream = nullptr;
 };
@@ -2528,7 +2786,28 @@ int tcu_batch_forward(tcu_batch* b, tcu_session* const* sessions, const int32_t*
   if (ids_out)
     for (int i = 0; i < n; i++) ids_out[i] = (int)(0xffffffffu - (uint32_t)(keys[i] & 0xffffffffu));
   for (int i = 0; i < n; i++) sessions[i]->length++;
+  b->last_rows = n;
   return TCU_OK;
+}
+
+int tcu_batch_sample_candidates(tcu_batch* b, int32_t n, const int32_t* history, const int32_t* history_len, const tcu_penalties* p,
+                                int32_t k, int32_t* ids, double* scores) {
+  if (!b || !history_len || !p || !ids || !scores) return fail(TCU_EINVAL, "null argument");
+  if (n < 1 || n > b->last_rows) return fail(TCU_EINVAL, "%d rows requested, the last step had %d", n, b->last_rows);
+  if (k < 1 || k > 256 || k > b->m->V) return fail(TCU_EINVAL, "candidate count must be in [1, min(256, vocab)]");
+  PenaltyHost h;
+  size_t off = 0;
+  for (int i = 0; i < n; i++) {
+    if (history_len[i] < 0 || (history_len[i] > 0 && !history)) return fail(TCU_EINVAL, "row %d: invalid history", i);
+    TRY(penalties_check(p[i]));
+    penalties_add_row(h, history + off, history_len[i], p[i], b->m->V);
+    off += (size_t)history_len[i];
+  }
+  CK(cudaSetDevice(b->m->device));
+  TRY(enqueue_candidates(b->m, &b->w, b->w.logits, n, h, k, b->stream));
+  CK(cudaMemcpyAsync(ids, b->w.cd_ids, (size_t)n * k * sizeof(int), cudaMemcpyDeviceToHost, b->stream));
+  CK(cudaMemcpyAsync(scores, b->w.cd_vals, (size_t)n * k * sizeof(double), cudaMemcpyDeviceToHost, b->stream));
+  return sync_stream(b->stream, b->w.err);
 }
 
 int tcu_batch_close(tcu_batch* b) {
@@ -2543,6 +2822,81 @@ int tcu_batch_close(tcu_batch* b) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// weightTensor.readValues (matmul.go:12-50) through the device decoders.
+
+namespace {
+// Device buffers of one tcu_read_values call, freed on every return path.
+struct ReadBufs {
+  std::vector<void*> p;
+  ~ReadBufs() {
+    for (void* q : p) cudaFree(q);
+  }
+  int get(void** out, size_t bytes) {
+    *out = nullptr;
+    cudaError_t e = cudaMalloc(out, std::max<size_t>(bytes, 16));
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(e == cudaErrorMemoryAllocation ? TCU_ENOMEM : TCU_ECUDA, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    }
+    p.push_back(*out);
+    return TCU_OK;
+  }
+};
+}  // namespace
+
+extern "C" int tcu_read_values(int32_t device, int32_t dtype, const void* data, uint64_t nbytes, int32_t rows, int32_t cols,
+                               int64_t offset, int64_t n, int32_t decoder, float* out) {
+  if (!data || (n > 0 && !out)) return fail(TCU_EINVAL, "null argument");
+  if (!fmt_known(dtype)) return fail(TCU_EUNSUP, "unsupported dtype %d", dtype);
+  if (rows <= 0 || cols <= 0) return fail(TCU_EINVAL, "invalid shape %d x %d", rows, cols);
+  if ((dtype == FMT_Q8_0 || dtype == FMT_Q5_1) && cols % 32) return fail(TCU_EINVAL, "rows of this format must be divisible by 32");
+  if ((dtype == FMT_Q5_K || dtype == FMT_Q6_K) && cols % 256) return fail(TCU_EINVAL, "K-quant rows must be divisible by 256");
+  if (nbytes != file_bytes(dtype, rows, cols))
+    return fail(TCU_EINVAL, "%llu bytes, want %zu", (unsigned long long)nbytes, file_bytes(dtype, rows, cols));
+  const int64_t total = (int64_t)rows * cols;
+  if (offset < 0 || n < 0 || offset > total || n > total - offset)
+    return fail(TCU_EINVAL, "read of %lld values at %lld exceeds %lld", (long long)n, (long long)offset, (long long)total);
+  const bool kq = dtype == FMT_Q5_K || dtype == FMT_Q6_K;
+  if (decoder == RD_GROUP8 && !kq) return fail(TCU_EUNSUP, "the 8-value group decoder serves Q6_K and Q5_K");
+  if (decoder == RD_TC && !kq && dtype != FMT_Q8_0) return fail(TCU_EUNSUP, "the tensor-core operand serves Q8_0, Q6_K and Q5_K");
+  if (decoder != RD_ELEMENT && decoder != RD_GROUP8 && decoder != RD_TC) return fail(TCU_EINVAL, "unknown decoder %d", decoder);
+  TRY(check_device(device));
+  if (n == 0) return TCU_OK;
+  ReadBufs bufs;
+  void *raw = nullptr, *dout = nullptr, *scratch = nullptr;
+  TRY(bufs.get(&raw, nbytes));
+  TRY(bufs.get(&dout, (size_t)n * 4));
+  TRY(bufs.get(&scratch, sizeof(unsigned)));
+  CK(cudaMemcpy(raw, data, nbytes, cudaMemcpyHostToDevice));
+  DMat W{};
+  W.fmt = dtype;
+  W.rows = rows;
+  W.cols = cols;
+  if (dtype == FMT_Q8_0) {
+    // The device layout of a loaded Q8_0 matrix, made by the load-time repack.
+    W.sstride = (cols / 32 + 7) / 8 * 8;
+    void *q = nullptr, *sc = nullptr;
+    TRY(bufs.get(&q, (size_t)rows * cols));
+    TRY(bufs.get(&sc, (size_t)rows * W.sstride * 2));
+    W.w = (const uint8_t*)q;
+    W.s = (const __half*)sc;
+    RepackArgs ra{(const uint8_t*)raw, dtype, rows, cols, W, 0, 1, 0};
+    k_repack<<<1184, 256>>>(ra);
+    CK(cudaGetLastError());
+  } else {
+    W.w = (const uint8_t*)raw;
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (decoder == RD_TC) TRY(tc_shift_of(&W, (unsigned*)scratch, sms));
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)sms * 8);
+  k_read_values<<<blocks, 256>>>(W, offset, n, decoder, (float*)dout);
+  CK(cudaGetLastError());
+  CK(cudaMemcpy(out, dout, (size_t)n * 4, cudaMemcpyDeviceToHost));
+  return TCU_OK;
+}
 
 // ---------------------------------------------------------------------------
 // Shortlist with no device allocation (tcu_shortlist_static). No counterpart
@@ -2588,6 +2942,9 @@ static int shortlist_static_setup(int device, unsigned char** out) {
     e = cudaGetSymbolAddress(&p, g_shortlist_scratch);
     if (e != cudaSuccess || !p)
       return fail(TCU_ECUDA, "shortlist set-up on device %d: cudaGetSymbolAddress: %s", device, cudaGetErrorString(e));
+    // The kernel's largest bitmap, once per device (not per call, where
+    // another thread could lower it between this call's set and launch).
+    TRY(sampling_smem_attrs(device));
     g_sl_static_ptr[device] = (unsigned char*)p;
   }
   *out = g_sl_static_ptr[device];
@@ -2622,8 +2979,7 @@ extern "C" int tcu_shortlist_static(int32_t device, const float* logits, int32_t
   double* d_lse = reinterpret_cast<double*>(scratch + TCU_SHORTLIST_STATIC_MAX_K * 8);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int kk = std::min<int>(k, vocab);
-  const size_t smem = ((size_t)vocab + 31) / 32 * 4;
-  CK(cudaFuncSetAttribute(k_shortlist, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const size_t smem = ((size_t)vocab + 31) / 32 * 4;  // within the attribute set up once per device
   k_shortlist<<<1, 1024, smem, st>>>(logits, vocab, kk, d_ids, d_vals, d_lse);
   CK(cudaGetLastError());
   CK(cudaMemcpyAsync(ids, d_ids, kk * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
