@@ -883,6 +883,58 @@ double oc_summarize_logits(const float* logits, int n, int chosen, int count, in
   return (double)logits[chosen] - z;
 }
 
+/* sampling.go:64-70 repetitionWeight */
+double oc_repetition_weight(int age, int window, double slope) {
+  if (slope == 0 || window <= 1) return 1;
+  double x = 1 - 2 * (double)age / (double)(window - 1);
+  return 1 + slope * x / (1 + fabs(x) * (slope - 1));
+}
+
+/* sampling.go:76-101 penalizedLogits: float64 copy of the logits, then for
+ * each of the last `window` history ids (most recent first) the frequency
+ * penalty times its recency weight, and on an id's most recent occurrence
+ * also (log(repetition) + presence) times that weight. */
+void oc_penalized_logits(const float* logits, int n, const int* history, int n_history, double repetition_penalty,
+                         int repetition_range, double repetition_slope, double presence_penalty, double frequency_penalty,
+                         double* out) {
+  for (int i = 0; i < n; i++) out[i] = (double)logits[i];
+  int window = repetition_range == 0 ? n_history : repetition_range;
+  int m = window < n_history ? window : n_history;
+  unsigned char* seen = (unsigned char*)calloc((size_t)n, 1);
+  for (int age = 0; age < m; age++) {
+    int id = history[n_history - 1 - age];
+    if (id < 0 || id >= n) continue;
+    double weight = oc_repetition_weight(age, window, repetition_slope);
+    out[id] -= frequency_penalty * weight;
+    if (!seen[id]) {
+      out[id] -= (log(repetition_penalty) + presence_penalty) * weight;
+      seen[id] = 1;
+    }
+  }
+  free(seen);
+}
+
+/* sampling.go:112-143 samplingCandidates over float64 scores (k > 0). */
+int oc_sampling_candidates_f64(const double* scores, int n, int k, int* ids, double* values) {
+  if (k <= 0 || k > n) k = n;
+  int len = 0;
+  for (int id = 0; id < n; id++) {
+    double p = scores[id];
+    if (len == k && p <= values[k - 1]) continue;
+    int at = 0;
+    while (at < len && !(p > values[at])) at++;
+    int end = len < k ? len : k - 1;
+    for (int j = end; j > at; j--) {
+      ids[j] = ids[j - 1];
+      values[j] = values[j - 1];
+    }
+    ids[at] = id;
+    values[at] = p;
+    if (len < k) len++;
+  }
+  return len;
+}
+
 /* sampling.go:112-143 samplingCandidates (k > 0): descending score, ties by
  * ascending id, at most k entries. */
 int oc_sampling_candidates(const float* logits, int n, int k, int* ids, double* values) {

@@ -81,6 +81,16 @@ double oc_summarize_logits(const float* logits, int n, int chosen, int count, in
 /* sampling.go:112-143 samplingCandidates over float32 logits promoted to float64. */
 int oc_sampling_candidates(const float* logits, int n, int k, int* ids, double* values);
 
+/* sampling.go:64-70 repetitionWeight and sampling.go:76-101 penalizedLogits
+ * (float64 scores with recency-weighted frequency, presence and logarithmic
+ * repetition penalties). */
+double oc_repetition_weight(int age, int window, double slope);
+void oc_penalized_logits(const float* logits, int n, const int* history, int n_history, double repetition_penalty,
+                         int repetition_range, double repetition_slope, double presence_penalty, double frequency_penalty,
+                         double* out);
+/* sampling.go:112-143 samplingCandidates over float64 scores. */
+int oc_sampling_candidates_f64(const double* scores, int n, int k, int* ids, double* values);
+
 void oc_set_threads(int n);
 int oc_get_threads(void);
 

@@ -64,6 +64,10 @@ def lib():
         "oc_llama_transformer": ([P, C.c_int, C.c_int, f32p], C.c_int),
         "oc_summarize_logits": ([f32p, C.c_int, C.c_int, C.c_int, i32p, f64p, i32p], C.c_double),
         "oc_sampling_candidates": ([f32p, C.c_int, C.c_int, i32p, f64p], C.c_int),
+        "oc_repetition_weight": ([C.c_int, C.c_int, C.c_double], C.c_double),
+        "oc_penalized_logits": ([f32p, C.c_int, i32p, C.c_int, C.c_double, C.c_int, C.c_double, C.c_double, C.c_double, f64p],
+                                None),
+        "oc_sampling_candidates_f64": ([f64p, C.c_int, C.c_int, i32p, f64p], C.c_int),
         "oc_set_threads": ([C.c_int], None),
         "oc_get_threads": ([], C.c_int),
     }
@@ -155,6 +159,31 @@ def sampling_candidates(logits, k):
     vals = np.empty(k, np.float64)
     n = lib().oc_sampling_candidates(lp, len(logits), k, ids.ctypes.data_as(C.POINTER(C.c_int)),
                                      vals.ctypes.data_as(C.POINTER(C.c_double)))
+    return ids[:n], vals[:n]
+
+
+def repetition_weight(age, window, slope):
+    return lib().oc_repetition_weight(int(age), int(window), float(slope))
+
+
+def penalized_logits(logits, history, repetition_penalty=1.0, repetition_range=0, repetition_slope=0.0,
+                     presence_penalty=0.0, frequency_penalty=0.0):
+    """sampling.go:76-101 penalizedLogits -> float64 scores."""
+    logits, lp = _f32(logits)
+    h = np.ascontiguousarray(history, dtype=np.int32)
+    out = np.empty(len(logits), np.float64)
+    lib().oc_penalized_logits(lp, len(logits), h.ctypes.data_as(C.POINTER(C.c_int)), len(h), float(repetition_penalty),
+                              int(repetition_range), float(repetition_slope), float(presence_penalty),
+                              float(frequency_penalty), out.ctypes.data_as(C.POINTER(C.c_double)))
+    return out
+
+
+def sampling_candidates_f64(scores, k):
+    scores = np.ascontiguousarray(scores, dtype=np.float64)
+    ids = np.empty(k, np.int32)
+    vals = np.empty(k, np.float64)
+    n = lib().oc_sampling_candidates_f64(scores.ctypes.data_as(C.POINTER(C.c_double)), len(scores), k,
+                                         ids.ctypes.data_as(C.POINTER(C.c_int)), vals.ctypes.data_as(C.POINTER(C.c_double)))
     return ids[:n], vals[:n]
 
 

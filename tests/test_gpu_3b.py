@@ -1,8 +1,16 @@
-"""Full-size parity: the Clio-shaped 3B StableLM with Q8_0 weights (config 2's
-model) against the CPU oracle on the same bytes. The oracle restates the Go
-scalar path in float64-accumulating C, so the prompt is kept short (the oracle
-needs ~2.9 G multiply-adds per token); the greedy stream, the logits of the
-prefill and the logits after decoding are compared."""
+"""Full-size parity at the benchmarked workload: the Clio-shaped 3B StableLM
+with Q8_0 weights (config 2's model) against the CPU oracle on the same
+bytes, with config 2's 512-token prompt.
+
+The device prefills the prompt (tcgen05 GEMM, prefill attention), then
+generates 64 greedy tokens with the persistent decode step (k_decode_mega at
+history T = 512 ... 575: 8-9 attention splits per KV head and the merge warp).
+The oracle restates the Go scalar path (prefill.go in 128-token chunks, then
+stablelm.go's one-token forward), so this costs about a minute of host time.
+logits within 2e-3 of the logit range (f32 KV), the
+64-token greedy stream identical."""
+import os
+
 import numpy as np
 import pytest
 
@@ -12,20 +20,33 @@ from tinyoai_b200.synth import CLIO_3B, prompt_ids, synth_stablelm
 
 pytestmark = [pytest.mark.gpu, pytest.mark.slow]
 
+PROMPT, STEPS = 512, 64
 
-def test_clio_3b_q8_greedy_parity():
-    import os
+
+def top2(v):
+    i = int(np.argmax(v))
+    rest = np.delete(v, i)
+    return i, float(v[i] - rest.max())
+
+
+def test_clio_3b_q8_prompt512_greedy64():
     cfg, tensors = synth_stablelm(CLIO_3B, "Q8_0", seed=0, device="cuda")
     oc.set_threads(os.cpu_count() or 1)
-    ids = prompt_ids(24, cfg["vocab_size"], seed=0)
-    steps = 24
-    ora = oc.StableLM(cfg, tensors, capacity=64)
+    ids = prompt_ids(PROMPT, cfg["vocab_size"], seed=0)
+    ora = oc.StableLM(cfg, tensors, capacity=PROMPT + STEPS + 8)
     want_pf = ora.prefill(ids)
+    logits, want, margins = want_pf, [], []
+    for i in range(STEPS):
+        t, mg = top2(logits)
+        want.append(t)
+        margins.append(mg)
+        if i + 1 < STEPS:
+            logits = ora.forward(t, PROMPT + i)
+    # The resident context after the device loop is prompt + 63 tokens; one
+    # more forward of the last generated token gives logits at the end.
+    want_last = ora.forward(want[-1], PROMPT + STEPS - 1)
     ora.close()
-    ora = oc.StableLM(cfg, tensors, capacity=64)
-    want, margins = ora.greedy(ids, steps)
-    last = ora.forward(int(want[-1]), len(ids) + steps - 1)
-    ora.close()
+    want = np.array(want, np.int32)
     model = Model.load_stablelm(cfg, tensors)
     del tensors
     try:
@@ -33,12 +54,17 @@ def test_clio_3b_q8_greedy_parity():
         try:
             got_pf = s.forward(0, ids)
             rng = float(want_pf.max() - want_pf.min())
-            assert np.max(np.abs(got_pf - want_pf)) <= 2e-3 * rng
-            got = s.generate_greedy(0, ids, steps)
+            err_pf = float(np.max(np.abs(got_pf - want_pf))) / rng
+            got = s.generate_greedy(0, ids, STEPS)
             bad = np.nonzero(got != want)[0]
-            assert bad.size == 0, f"divergence at {bad[0]} (oracle margin {margins[bad[0]]:.3g})"
-            got_last = s.forward(len(ids) + steps - 1, [int(got[-1])])
-            assert np.max(np.abs(got_last - last)) <= 2e-3 * float(last.max() - last.min())
+            print(f"3B Q8_0 512+64: prefill rel err {err_pf:.3g}; min top-2 margin {min(margins):.3g} "
+                  f"at step {int(np.argmin(margins))}")
+            assert err_pf <= 2e-3
+            assert bad.size == 0, f"divergence at step {bad[0]} (oracle margin {margins[bad[0]]:.3g})"
+            assert s.length == PROMPT + STEPS - 1
+            got_last = s.forward(PROMPT + STEPS - 1, [int(got[-1])])
+            err_last = float(np.max(np.abs(got_last - want_last))) / float(want_last.max() - want_last.min())
+            assert err_last <= 2e-3, err_last
         finally:
             s.close()
     finally:

@@ -1,0 +1,138 @@
+"""Parity at the long-context and branch shapes of configs 3 and 4, against
+the CPU oracle (small models, so the oracle finishes in seconds).
+
+- An 8,000-token prompt with f16 KV crosses 16 prefill chunks of 512
+  (prefill.go:33-115 semantics with the device's chunk size), then greedy
+  decoding runs at positions 8,000 ... 8,064: long-context split-half RoPE
+  (stablelm.go:309-326) and 125+ attention splits per KV head in both the
+  per-layer decode kernels and the persistent step.
+- 64 branches over a 1,100-token shared prefix with ragged suffixes of 1-64
+  tokens (config 4's shape, mlx_branches.go:98-184), Q6_K and Q5_K weights,
+  f16 KV: each branch's greedy tokens and final row against the oracle
+  evaluating prefix + that branch's own tokens.
+
+North-star tolerance for f16 KV: logits within 1e-2 of the logit range;
+greedy streams identical.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as oc
+from tinyoai_b200 import Model
+from tinyoai_b200.synth import prompt_ids, synth_stablelm
+
+pytestmark = pytest.mark.gpu
+
+BASE = dict(model_type="stablelm", vocab_size=2048, hidden_size=320, intermediate_size=864, num_hidden_layers=3,
+            num_attention_heads=4, num_key_value_heads=4, max_position_embeddings=8192, layer_norm_eps=1e-5,
+            rope_theta=10000.0, partial_rotary_factor=0.25, use_parallel_residual=True, use_qkv_bias=False,
+            qk_layernorm=False, tie_word_embeddings=False, hidden_act="silu", bos_token_id=0, eos_token_id=0)
+# K-quant super-blocks span 256 columns.
+KQ = dict(BASE, hidden_size=256, intermediate_size=768, max_position_embeddings=2048)
+
+
+def rel_err(got, want):
+    return float(np.max(np.abs(got - want)) / max(1e-30, float(np.max(want) - np.min(want))))
+
+
+def top2_margin(v):
+    i = int(np.argmax(v))
+    return float(v[i] - np.delete(v, i).max())
+
+
+def test_long_context_f16_multichunk_prefill_and_decode():
+    cfg, tensors = synth_stablelm(BASE, "Q8_0", seed=53)
+    oc.set_threads(os.cpu_count() or 1)
+    n_prompt, steps = 8000, 64
+    ids = prompt_ids(n_prompt + 1, cfg["vocab_size"], seed=59)
+    ora = oc.StableLM(cfg, tensors, half_kv=True, capacity=cfg["max_position_embeddings"])
+    want_pf = ora.prefill(ids[:n_prompt])
+    logits = ora.forward(int(ids[n_prompt]), n_prompt)
+    want_first = logits
+    want, margins = [], []
+    for i in range(steps):
+        t = int(np.argmax(logits))
+        want.append(t)
+        margins.append(top2_margin(logits))
+        if i + 1 < steps:
+            logits = ora.forward(t, n_prompt + 1 + i)
+    want_last = ora.forward(want[-1], n_prompt + steps)
+    ora.close()
+    m = Model.load_stablelm(cfg, tensors)
+    try:
+        s = m.session("f16")
+        try:
+            got_pf = s.forward(0, ids[:n_prompt])
+            assert rel_err(got_pf, want_pf) <= 1e-2
+            # One token through the per-layer decode kernels at position 8000.
+            got_first = s.forward(n_prompt, [int(ids[n_prompt])])
+            assert rel_err(got_first, want_first) <= 1e-2
+            # The same token again, then 63 persistent steps at 8001 ... 8063.
+            got = s.generate_greedy(n_prompt, [int(ids[n_prompt])], steps)
+            bad = np.nonzero(got != np.array(want, np.int32))[0]
+            assert bad.size == 0, f"divergence at step {bad[0]} (oracle margin {margins[bad[0]]:.3g})"
+            assert s.length == n_prompt + steps
+            got_last = s.forward(n_prompt + steps, [int(got[-1])])
+            assert rel_err(got_last, want_last) <= 1e-2
+        finally:
+            s.close()
+    finally:
+        m.close()
+
+
+@pytest.mark.parametrize("fmt", ["Q6_K", "Q5_K"])
+def test_64_ragged_branches_vs_oracle(fmt):
+    cfg, tensors = synth_stablelm(KQ, fmt, seed=61)
+    oc.set_threads(os.cpu_count() or 1)
+    V, prefix, count, gen = cfg["vocab_size"], 1100, 64, 8
+    ids = prompt_ids(prefix, V, seed=67)
+    rng = np.random.default_rng(71)
+    lens = rng.integers(1, 65, count)
+    lens[0], lens[1] = 1, 64  # both ends of U[1, 64]
+    suffix = [rng.integers(3, V, int(n)).astype(np.int32) for n in lens]
+    steps = int(lens.max()) + gen
+
+    m = Model.load_stablelm(cfg, tensors)
+    try:
+        s = m.session("f16")
+        try:
+            s.forward(0, ids, want_logits=False)
+            br = s.new_branches(prefix, count)
+            try:
+                fed = np.zeros((count, steps), np.int32)
+                nxt = np.zeros(count, np.int32)
+                for t in range(steps):
+                    for b in range(count):
+                        fed[b, t] = suffix[b][t] if t < lens[b] else nxt[b]
+                    rows = br.forward(fed[:, t])
+                    nxt = br.argmax()
+                    assert np.array_equal(nxt, np.argmax(rows, axis=1))
+                last_rows = rows
+            finally:
+                br.close()
+        finally:
+            s.close()
+    finally:
+        m.close()
+
+    ora = oc.StableLM(cfg, tensors, half_kv=True, capacity=prefix + steps + 1)
+    try:
+        ora.prefill(ids)
+        worst = 0.0
+        for b in range(count):
+            # The branch's suffix, evaluated after the shared prefix (the
+            # oracle's state keeps positions < prefix), then its own greedy
+            # continuation through the remaining steps.
+            logits = ora.prefill(suffix[b], start=prefix)
+            for t in range(int(lens[b]), steps):
+                want_tok = int(np.argmax(logits))
+                assert fed[b, t] == want_tok, f"branch {b} (suffix {lens[b]}): token {t} differs (margin {top2_margin(logits):.3g})"
+                logits = ora.forward(want_tok, prefix + t)
+            err = rel_err(last_rows[b], logits)
+            worst = max(worst, err)
+            assert err <= 1e-2, (b, err)
+        print(f"{fmt}: 64 ragged branches over a {prefix}-token prefix, worst row rel err {worst:.3g}")
+    finally:
+        ora.close()

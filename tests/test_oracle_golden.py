@@ -164,3 +164,42 @@ def test_summarize_logits():
     assert list(ids[:2]) == [10, 20]
     order = np.lexsort((np.arange(1000), -logits.astype(np.float64)))[:5]
     assert list(ids) == list(order)
+
+
+def test_penalties_known_answers():
+    """sampling_test.go:14-31 TestProbabilityPenalties: repetition 2, presence
+    0.1, frequency 0.2 over a 3-token window, and invariance to a constant
+    logit offset."""
+    kw = dict(repetition_penalty=2.0, presence_penalty=0.1, frequency_penalty=0.2, repetition_range=3)
+    got = oc.penalized_logits(np.zeros(4, np.float32), [3, 1, 2, 1], **kw)
+    want = [0.0, -math.log(2) - 0.1 - 0.4, -math.log(2) - 0.1 - 0.2, 0.0]
+    assert np.all(np.abs(got - want) <= 1e-12)
+    shifted = oc.penalized_logits(np.full(4, 20, np.float32), [3, 1, 2, 1], **kw)
+    assert np.all(np.abs(shifted - got - 20) <= 1e-12)
+
+
+def test_repetition_slope_and_range_known_answers():
+    """sampling_test.go:35-57 TestRepetitionSlopeAndRange."""
+    assert oc.repetition_weight(0, 5, 1) == 2 and oc.repetition_weight(2, 5, 1) == 1 and oc.repetition_weight(4, 5, 1) == 0
+    assert oc.repetition_weight(1, 5, 3.33) > oc.repetition_weight(1, 5, 1)
+    kw = dict(repetition_penalty=math.e, repetition_slope=1.0, repetition_range=5)
+    got = oc.penalized_logits(np.zeros(5, np.float32), [4, 3, 2, 1, 0], **kw)
+    assert np.all(np.abs(got - [-2, -1.5, -1, -0.5, 0]) <= 1e-12)
+    got = oc.penalized_logits(np.zeros(5, np.float32), [1, 0], **kw)
+    assert abs(got[1] + 1.5) <= 1e-12
+
+
+def test_float64_candidates_match_full_sort():
+    """sampling_test.go:105-149: the bounded shortlist equals the full sort
+    (descending, ties by ascending id) for random, tied and monotone scores."""
+    rng = np.random.default_rng(42)
+    for size in (1, 300, 4096):
+        for pattern in ("random", "ties", "ascending", "descending"):
+            i = np.arange(size)
+            v = {"random": rng.standard_normal(size), "ties": (i % 7).astype(np.float64),
+                 "ascending": i.astype(np.float64), "descending": -i.astype(np.float64)}[pattern]
+            order = sorted(range(size), key=lambda j: (-v[j], j))
+            for k in (1, 12, 25, 64, 256):
+                ids, vals = oc.sampling_candidates_f64(v, k)
+                assert list(ids) == order[:k]
+                assert np.array_equal(vals, v[order[:k]])
