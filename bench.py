@@ -127,32 +127,72 @@ class ClockSampler:
                 "samples": len(self.samples), "reasons": sorted(self.reasons)}
 
 
-def cpu_sample(cfg, tensors, prompt, budget_s=20.0, fmt="Q8_0", extrapolation=None):
-    """Times the CPU oracle (a C restatement of the reference's Go scalar path,
-    OpenMP over rows and heads on every host core) on a bounded sample of the
-    workload: a short prompt prefill and a few decode forwards of the same 3B
-    model. Returns (prefill tok/s, decode tok/s, cores, sample text)."""
-    from oracle import oracle as oc
-    cores = os.cpu_count() or 1
-    oc.set_threads(cores)
-    m = oc.StableLM(cfg, tensors, capacity=64)
-    try:
-        n_pf = 8
+class OracleJob:
+    """The config-2 job on the CPU oracle (a C restatement of the reference's
+    Go scalar path, OpenMP over rows and heads on every host core), advanced
+    one unit of work at a time: the 512-token prompt as prefill.go's
+    128-token chunks (prefill.go:33-115, matmul.go:8), then 256 greedy tokens
+    as blocks of 32 one-token forwards at their real positions
+    (stablelm.go:519-540; the last sampled token is not evaluated). A job is
+    4 + 8 units and 768 tokens; the next job starts over at position 0."""
+    CHUNK, BLOCK = 128, 32
+
+    def __init__(self, cfg, tensors, prompt):
+        from oracle import oracle as oc
+        self.oc = oc
+        oc.set_threads(os.cpu_count() or 1)
+        self.m = oc.StableLM(cfg, tensors, capacity=PROMPT + GEN + 1)
+        self.prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        self.units = PROMPT // self.CHUNK + GEN // self.BLOCK
+        self.i = 0  # unit index within the job
+        self.logits = None
+
+    def step(self):
+        """Runs the next unit; returns (kind, tokens counted, seconds)."""
+        u = self.i
         t0 = time.perf_counter()
-        m.prefill(prompt[:n_pf], chunk=128)
+        n_pf = PROMPT // self.CHUNK
+        if u < n_pf:
+            a = u * self.CHUNK
+            self.logits = self.m.prefill(self.prompt[a:a + self.CHUNK], start=a, chunk=self.CHUNK)
+            kind, n = "prefill", self.CHUNK
+        else:
+            j = u - n_pf
+            for k in range(self.BLOCK):
+                g = j * self.BLOCK + k  # generated token index
+                tok = int(np.argmax(self.logits))
+                if g + 1 < GEN:
+                    self.logits = self.m.forward(tok, PROMPT + g)
+            kind, n = "decode", self.BLOCK
+        dt = time.perf_counter() - t0
+        self.i = (u + 1) % self.units
+        return kind, n, dt, u
+
+    def close(self):
+        self.m.close()
+
+
+def cpu_sample(cfg, tensors, prompt, fmt="Q8_0", extrapolation=None):
+    """Bounded sample of the workload on the CPU oracle for the b200 arm's
+    cpu_baseline (about 10-30 s of host time): the prompt's first 128-token
+    prefill chunk (prefill.go's batch) and 32 greedy decode forwards at
+    positions 128-159. Returns (prefill tok/s, decode tok/s, cores, sample)."""
+    from oracle import oracle as oc
+    job = OracleJob(cfg, tensors, prompt)
+    try:
+        t0 = time.perf_counter()
+        logits = job.m.prefill(job.prompt[:job.CHUNK], start=0, chunk=job.CHUNK)
         t_pf = time.perf_counter() - t0
-        n_dec, t_dec = 0, 0.0
-        while n_dec < 2 or (t_dec < budget_s / 2 and n_dec < 16):
-            t0 = time.perf_counter()
-            m.forward(int(prompt[n_pf + n_dec]), n_pf + n_dec)
-            t_dec += time.perf_counter() - t0
-            n_dec += 1
+        t0 = time.perf_counter()
+        for k in range(job.BLOCK):
+            logits = job.m.forward(int(np.argmax(logits)), job.CHUNK + k)
+        t_dc = time.perf_counter() - t0
     finally:
-        m.close()
+        job.close()
     extrapolation = extrapolation or f"{PROMPT}/prefill_rate + {GEN}/decode_rate"
-    sample = (f"oracle (C port of the Go scalar path, {oc.threads()} OpenMP threads): prefill of {n_pf} prompt tokens "
-              f"and {n_dec} decode forwards of the full 3B {fmt} model; step time extrapolated as {extrapolation}")
-    return n_pf / t_pf, n_dec / t_dec, oc.threads(), sample
+    sample = (f"oracle (C port of the Go scalar path, {oc.threads()} OpenMP threads) on the full 3B {fmt} model: one "
+              f"128-token prefill chunk and 32 decode forwards at positions 128-159; job time extrapolated as {extrapolation}")
+    return job.CHUNK / t_pf, job.BLOCK / t_dc, oc.threads(), sample
 
 
 def synth(device, layers=None):
@@ -164,6 +204,13 @@ def synth(device, layers=None):
 
 
 def run_reference(args):
+    """The reference arm: the CPU restatement of the Go scalar path on this
+    box's host cores, on config 2's model, prompt and KV precision. Each
+    step is the next unit of a running config-2 job (OracleJob), so every
+    step is measured; the W warm-up steps run the first units. value is the
+    rate of the last complete job inside the timed steps (768 tokens / its
+    measured time), or, when the timed steps hold no complete job, 768 tokens
+    over prefill and decode times from the timed units' own rates."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -175,23 +222,56 @@ def run_reference(args):
     cfg, tensors = synth(dev)
     from tinyoai_b200.synth import prompt_ids
     prompt = prompt_ids(PROMPT, cfg["vocab_size"], seed=0)
-    rates = []
-    for i in range(args.warmup + args.steps):
-        pf, dc, cores, sample = cpu_sample(cfg, tensors, prompt, budget_s=4.0)
-        if i >= args.warmup:
-            rates.append((pf, dc))
-    pf = statistics.median(r[0] for r in rates)
-    dc = statistics.median(r[1] for r in rates)
-    step_s = PROMPT / pf + GEN / dc
-    value = (PROMPT + GEN) / step_s
+    job = OracleJob(cfg, tensors, prompt)
+    timed = []
+    try:
+        for i in range(args.warmup + args.steps):
+            rec = job.step()
+            if i >= args.warmup:
+                timed.append(rec)
+    finally:
+        job.close()
+    cores = job.oc.threads()
+    total_s = sum(r[2] for r in timed)
+    pf_t = sum(r[2] for r in timed if r[0] == "prefill")
+    pf_n = sum(r[1] for r in timed if r[0] == "prefill")
+    dc_t = sum(r[2] for r in timed if r[0] == "decode")
+    dc_n = sum(r[1] for r in timed if r[0] == "decode")
+    # Complete jobs inside the timed steps: unit 0 ... unit (units - 1) in a row.
+    jobs, start = [], None
+    for k, r in enumerate(timed):
+        if r[3] == 0:
+            start = k
+        if start is not None and r[3] == job.units - 1:
+            jobs.append(sum(x[2] for x in timed[start:k + 1]))
+            start = None
+    pf_rate = pf_n / pf_t if pf_t else None
+    dc_rate = dc_n / dc_t if dc_t else None
+    if jobs:
+        value, how = (PROMPT + GEN) / jobs[-1], f"measured: the last of {len(jobs)} complete job(s) in the timed steps"
+    elif pf_rate and dc_rate:
+        value, how = (PROMPT + GEN) / (PROMPT / pf_rate + GEN / dc_rate), "from the timed units' prefill and decode rates"
+    else:
+        value, how = (pf_n + dc_n) / total_s, "tokens of the timed units over their time (too few steps for both kinds)"
+    sample = (f"oracle (C port of the Go scalar path, {cores} OpenMP threads) running config 2 itself: each step is the "
+              f"next unit of a 512 + 256 job (a 128-token prefill chunk or 32 decode forwards at their positions); "
+              f"value {how}")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": total_s / len(timed) * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f64-accumulate/f32", "data": "synthetic (seeded N(0,0.02) weights, uniform ids)",
-            "config": {"workload": WORKLOAD, "prompt": PROMPT, "generate": GEN, "kv": "f32"},
-            "prefill_tok_s": pf, "decode_tok_s": dc,
+            "config": config2(args.gpus),
+            "job_s": jobs[-1] if jobs else None, "jobs_timed": len(jobs),
+            "prefill_tok_s": pf_rate, "decode_tok_s": dc_rate, "timed_tok_s": (pf_n + dc_n) / total_s,
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def config2(world, layers=None):
+    """The config dict both arms print for config 2."""
+    workload = WORKLOAD if not layers else WORKLOAD + f" [PROFILING CASE: {layers} layers, not a bench line]"
+    return {"workload": workload, "prompt": PROMPT, "generate": GEN, "kv": "f32", "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (2.9 GB of weights streamed per token)"}
 
 
 def run_b200(args):
@@ -290,26 +370,25 @@ def run_b200(args):
             dom_n, dom_ms = prof["decode_step"]
             dom_bytes, dom_kernel = step_bytes, "k_decode_mega (persistent decode step: all layers, lm_head, argmax)"
             dom_traffic = MEGA_TRAFFIC_RATIO * step_bytes
-            dom_traffic_src = "ncu 4-layer capture (profiles/k_decode_mega_3b_4layer.md), scaled by algorithmic bytes"
+            dom_traffic_src = ("scaled, not measured on this launch: DRAM read + write of one ncu capture of the same kernel "
+                               "on a 4-layer case, times this launch's algorithmic bytes over that case's")
         else:
             dom_n, dom_ms = prof["norm_qkv_gate_up"]
             dom_bytes, dom_kernel = w1_bytes, "k_gemv<Q8_0, LayerNorm prologue, q/k/v + SwiGLU epilogue>"
             dom_traffic, dom_traffic_src = None, None
         achieved = dom_bytes / (dom_ms / dom_n / 1e3) / 1e9 if dom_n else None
-        workload = WORKLOAD if not args.layers else WORKLOAD + f" [PROFILING CASE: {args.layers} layers, not a bench line]"
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "q8_0 weights, f32 activations/accumulate", "data": "synthetic (seeded N(0,0.02) weights quantised to Q8_0, uniform prompt ids)",
-            "config": {"workload": workload, "prompt": PROMPT, "generate": GEN, "kv": "f32", "parallelism": f"replicas x{world}",
-                       "l2": "inputs larger than L2 (2.9 GB of weights streamed per token)"},
+            "config": config2(world, args.layers),
             "prefill_tok_s": world * (PROMPT - 1) * args.steps / (pf_ms / 1e3),
             "decode_tok_s": world * GEN * args.steps / (dc_ms / 1e3),
             "decode_ms_per_token": dc_ms / args.steps / GEN,
             "roofline": {"bound": "hbm", "kernel": dom_kernel,
                          "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": (achieved / hbm) if achieved else None, "peak_kind": peak_kind,
-                         "traffic": dom_traffic, "traffic_source": dom_traffic_src, "bytes_per_launch": dom_bytes,
+                         "traffic": dom_traffic, "traffic_scaled_from_capture": dom_traffic is not None, "traffic_source": dom_traffic_src, "bytes_per_launch": dom_bytes,
                          "avg_launch_us": (dom_ms / dom_n * 1e3) if dom_n else None,
                          "decode_step_gbs": dec_gbs, "decode_step_frac": dec_gbs / hbm},
             "profile": {k: {"launches": v[0], "ms": round(v[1], 3)} for k, v in prof.items()},
@@ -491,7 +570,7 @@ def run_config(args):
                         "h2d_bytes_per_step": 4 * units, "d2h_bytes_per_step": 4 * (c["gen"] if args.config == 3 else rest_units * (hi - lo))}}
         if cpu_tensors is not None:
             prompt0 = prompt_ids(512, V, seed=0)
-            pf, dc, cores, sample = cpu_sample(cfg, cpu_tensors, prompt0, budget_s=12.0, fmt=c["fmt"],
+            pf, dc, cores, sample = cpu_sample(cfg, cpu_tensors, prompt0, fmt=c["fmt"],
                                                extrapolation=f"{n_pf}/prefill_rate + {units - n_pf}/decode_rate "
                                                              "(short-context rates: attention over long histories not included)")
             line["cpu_baseline"] = {"value": units / (n_pf / pf + (units - n_pf) / dc), "unit": "tok/s", "cores": cores,
