@@ -415,8 +415,8 @@ def run_b200(args):
 CONFIGS = {
     3: dict(fmt="BF16", kv="f16", prompt=8129, gen=64,
             metric="prefill & decode tok/s, 3B StableLM BF16, 8129-token prompt + 64 greedy, f16 KV",
-            workload="config 3: 3B StableLM BF16, prompt 8129 + greedy 64 (8192 context), f16 KV, 512-token prefill chunks, "
-                     "one sequence per GPU (head-parallel sharding not built: replicas)"),
+            workload="config 3: 3B StableLM BF16, prompt 8129 + greedy 64 (8192 context), f16 KV, 512-token prefill chunks; "
+                     "one GPU: one sequence; N GPUs: one sequence, head-parallel over N ranks"),
     4: dict(fmt="Q6_K", kv="f16", prefix=4043, branches=64, suffix_max=64, gen=32,
             metric="prefix prefill & branch tok/s, 3B StableLM K-quant, 4043-token prefix + 64 ragged branches x 32 greedy",
             workload="config 4: 3B StableLM {fmt}, f16 KV, shared prefix 4043, 64 branches with suffix lengths U[1,64] "
@@ -454,7 +454,16 @@ def run_config(args):
     if args.layers:
         cfg["num_hidden_layers"] = args.layers
     cfg, tensors = synth_stablelm(cfg, c["fmt"], seed=0, device=f"cuda:{local}")
-    model = Model.load_stablelm(cfg, tensors, device=local, kv_pool_bytes=args.kv_pool_mb << 20)
+    # Config 3 on N > 1 GPUs: head-parallel tensor parallelism, one sequence
+    # over all ranks, one NCCL all-reduce per layer (strong scaling).
+    tp = args.config == 3 and world > 1
+    tp_arg = None
+    if tp:
+        from tinyoai_b200 import tp_unique_id
+        box = [tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        tp_arg = (world, rank, box[0])
+    model = Model.load_stablelm(cfg, tensors, device=local, kv_pool_bytes=args.kv_pool_mb << 20, tp=tp_arg)
     torch.cuda.empty_cache()
     cpu_tensors = tensors if (rank == 0 and world == 1 and args.cpu_baseline) else None
     del tensors
@@ -462,20 +471,19 @@ def run_config(args):
     torch.cuda.set_stream(stream)
     V = cfg["vocab_size"]
     if args.config == 3:
-        prompt = prompt_ids(c["prompt"], V, seed=rank)
+        prompt = prompt_ids(c["prompt"], V, seed=0 if tp else rank)
         units = c["prompt"] + c["gen"]
+        # One session for every step (its workspace is reused; each step's
+        # prefill from position 0 replaces the previous step's tokens).
+        sess3 = model.session(c["kv"])
+        sess3.set_stream(stream.cuda_stream)
 
         def step(ev):
-            sess = model.session(c["kv"])
-            sess.set_stream(stream.cuda_stream)
-            try:
-                ev[0].record(stream)
-                sess.forward(0, prompt[:-1], want_logits=False)
-                ev[1].record(stream)
-                out = sess.generate_greedy(len(prompt) - 1, prompt[-1:], c["gen"])
-                ev[2].record(stream)
-            finally:
-                sess.close()
+            ev[0].record(stream)
+            sess3.forward(0, prompt[:-1], want_logits=False)
+            ev[1].record(stream)
+            out = sess3.generate_greedy(len(prompt) - 1, prompt[-1:], c["gen"])
+            ev[2].record(stream)
             return out
     else:
         rng = np.random.default_rng(1234)
@@ -525,6 +533,23 @@ def run_config(args):
     pf_ms = sum(e[0].elapsed_time(e[1]) for e in evs)
     rest_ms = sum(e[1].elapsed_time(e[2]) for e in evs)
     total_ms, pf_ms, rest_ms, host_ms = replicas.max_over_ranks([total_ms, pf_ms, rest_ms, sum(host)], device="cuda")
+    comm = None
+    if tp:
+        # One more step with stage timing (every rank, same calls): the
+        # all-reduce's share of the device time.
+        sess3.profile(True)
+        sess3.profile_read(reset=True)
+        step([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+        torch.cuda.synchronize()
+        prof = sess3.profile_read(reset=True)
+        sess3.profile(False)
+        all_ms = sum(v[1] for v in prof.values())
+        comm = {"allreduce_launches": prof["allreduce"][0], "allreduce_ms": prof["allreduce"][1],
+                "profiled_ms": all_ms, "allreduce_share": prof["allreduce"][1] / all_ms if all_ms else None,
+                "bytes_per_prefill_allreduce": 512 * cfg["hidden_size"] * 4,
+                "note": "stage timing synchronises after every decode step; shares, not a throughput"}
+    if args.config == 3:
+        sess3.close()
     if rank == 0:
         hbm, peak_kind = peaks()
         peaks_f = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
@@ -535,13 +560,15 @@ def run_config(args):
         n_pf = (c["prompt"] - 1) if args.config == 3 else c["prefix"]
         # Prefill work: projections 2 * weights * n plus causal attention 2 * 2 * L * d * n^2 / 2.
         pf_flop = 2.0 * per_tok * n_pf + 2.0 * L * d * float(n_pf) ** 2
-        pf_tfs = pf_flop / (pf_ms / args.steps / 1e3) / 1e12
+        # Per GPU: under tensor parallelism each rank does 1/world of the work.
+        share = world if tp else 1
+        pf_tfs = pf_flop / share / (pf_ms / args.steps / 1e3) / 1e12
         if args.config == 3:
             T = c["prompt"] + c["gen"] / 2
             step_bytes = kquant_bytes(c["fmt"], per_tok + cfg["vocab_size"] * d) + 2 * L * kvw * 2 * (T + 1)
             rest_units = c["gen"]
-            rest_gbs = step_bytes * rest_units / (rest_ms / args.steps / 1e3) / 1e9
-            rest_name = "decode (per token: all weights + f16 KV history)"
+            rest_gbs = step_bytes / share * rest_units / (rest_ms / args.steps / 1e3) / 1e9
+            rest_name = "decode (per token: all weights + f16 KV history" + (f", each rank 1/{world})" if tp else ")")
         else:
             n_steps = int(suffix_len.max()) + c["gen"]
             rows = hi - lo
@@ -556,17 +583,20 @@ def run_config(args):
                 if dominant == "prefill" else
                 {"bound": "hbm", "stage": rest_name, "achieved": rest_gbs, "peak": hbm, "unit": "GB/s", "frac": rest_gbs / hbm,
                  "peak_kind": peak_kind, "traffic": None})
-        value = replicas.aggregate_rate(units * args.steps, world, total_ms / 1e3)
+        # Tensor parallelism: one sequence over all ranks (units counted once).
+        value = units * args.steps / (total_ms / 1e3) if tp else replicas.aggregate_rate(units * args.steps, world, total_ms / 1e3)
         line = {"metric": c["metric"], "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
                 "dtype": f"{c['fmt']} weights, f32 activations, f16 KV",
                 "data": "synthetic (seeded N(0,0.02) weights quantised to the format, uniform ids)",
                 "config": {"workload": c["workload"].format(fmt=c["fmt"]) + (f" [PROFILING CASE: {args.layers} layers]" if args.layers else ""),
-                           "parallelism": f"replicas x{world}", "l2": "inputs larger than L2 (GBs of weights per step)"},
-                "prefill_tok_s": world * n_pf * args.steps / (pf_ms / 1e3), "prefill_tflops": pf_tfs,
+                           "parallelism": f"tp{world} (head-parallel, NCCL all-reduce per layer)" if tp else f"replicas x{world}",
+                           "l2": "inputs larger than L2 (GBs of weights per step)"},
+                "tp_comm": comm,
+                "prefill_tok_s": (1 if tp else world) * n_pf * args.steps / (pf_ms / 1e3), "prefill_tflops_per_gpu": pf_tfs,
                 "rest_ms_per_step": rest_ms / args.steps, "rest_gbs": rest_gbs,
                 "roofline": roof, "clocks": clocks.summary(),
-                "e2e": {"value": replicas.aggregate_rate(units * args.steps, world, host_ms / 1e3), "unit": "tok/s",
+                "e2e": {"value": (units * args.steps / (host_ms / 1e3)) if tp else replicas.aggregate_rate(units * args.steps, world, host_ms / 1e3), "unit": "tok/s",
                         "h2d_bytes_per_step": 4 * units, "d2h_bytes_per_step": 4 * (c["gen"] if args.config == 3 else rest_units * (hi - lo))}}
         if cpu_tensors is not None:
             prompt0 = prompt_ids(512, V, seed=0)

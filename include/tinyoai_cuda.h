@@ -91,6 +91,33 @@ int tcu_device_count(int32_t* count);
 int tcu_stablelm_load(const tcu_stablelm_config* config, const tcu_tensor* tensors, int32_t n_tensors,
                       const tcu_load_options* options, tcu_model** out);
 
+/* Head-parallel tensor parallelism for one long sequence (an 8K-token
+ * prefill, say): `world` processes, one GPU each, load the same checkpoint
+ * and each keeps a contiguous block of query heads (and their KV heads),
+ * the matching rows of q/k/v, a block of MLP rows (gate/up rows, down
+ * columns) and the matching columns of o_proj; embedding, norms and lm_head
+ * are replicated. Every layer sums the ranks' out + down partials with one
+ * NCCL all-reduce (the parallel residual, stablelm.go:365-377, lets both
+ * products share it) and adds the sum to the residual. Rank 0 makes the
+ * communicator id with tcu_tp_unique_id and shares its 128 bytes with the
+ * others (any host channel); every rank then calls tcu_stablelm_load_tp with
+ * the same id. world must divide the heads, KV heads and MLP width, and the
+ * o/down column slices must be whole quantisation blocks. A tensor-parallel
+ * model serves one session at a time (every rank runs the same calls, in the
+ * same order, with the same tokens). NCCL is loaded at run time
+ * (libnccl.so.2); without it these return TCU_EUNSUP. */
+typedef struct {
+  int32_t world;
+  int32_t rank;
+  uint8_t nccl_id[128];
+} tcu_tp_options;
+int tcu_tp_unique_id(uint8_t* id);
+int tcu_stablelm_load_tp(const tcu_stablelm_config* config, const tcu_tensor* tensors, int32_t n_tensors,
+                         const tcu_load_options* options, const tcu_tp_options* tp, tcu_model** out);
+/* The share of rank `rank`: out[0..6) = first query head, query heads, first
+ * KV head, KV heads, first MLP row, MLP rows. Needs no GPU. */
+int tcu_tp_plan(const tcu_stablelm_config* config, int32_t world, int32_t rank, int32_t* out);
+
 /* Replaces LoadModel/readWeights (model.go:90-166) for the legacy llama2.c
  * checkpoint (7 x int32 header then float32 tensors), and DefaultMLX /
  * LoadLlamaMLX (mlx_llama.go:37-53). */
@@ -220,8 +247,9 @@ int tcu_session_set_stream(tcu_session* session, void* stream);
  * the per-stage launch counts and milliseconds accumulate. Stages, in order:
  * embedding, norm+q/k/v/gate/up projection, decode attention, out/down
  * projection + residual, final norm+head, prefill projection, prefill
- * attention, other, whole persistent decode step. tcu_session_profile_read
- * returns the number of stages (9) and fills up to n_stages entries;
+ * attention, other, whole persistent decode step, tensor-parallel
+ * all-reduce. tcu_session_profile_read returns the number of stages (10) and
+ * fills up to n_stages entries;
  * reset != 0 clears the totals.
  * Profiling synchronises after every decode step, so it is for diagnosis,
  * not for throughput runs. */
@@ -243,7 +271,7 @@ int tcu_branches_argmax(tcu_branches* branches, int32_t* ids);
  * tcu_branches_forward already released the pages; close it all the same. */
 int tcu_branches_close(tcu_branches* branches);
 
-/* Continuous batching (BASELINE config 5's serving load). The reference's
+/* Continuous batching (a serving load of many sessions). The reference's
  * Go server runs one request at a time per model (the request gate,
  * mlx.go:291-296); a batching scheduler instead advances all active
  * sessions together. tcu_batch_open reserves a workspace and stream for up

@@ -24,7 +24,7 @@ from . import _lib
 from ._lib import BackendError, check, lib
 from .checkpoint import as_bytes, dtype_code
 
-__all__ = ["Model", "Session", "Branches", "BackendError", "device_count", "read_values"]
+__all__ = ["Model", "Session", "Branches", "BackendError", "device_count", "read_values", "tp_unique_id", "tp_plan"]
 
 
 def _i32(a):
@@ -59,6 +59,31 @@ def penalties_struct(repetition_penalty=1.0, presence_penalty=0.0, frequency_pen
     return _lib.Penalties(repetition_penalty, presence_penalty, frequency_penalty, repetition_slope, repetition_range)
 
 
+def _config_struct(config):
+    return _lib.StableLMConfig(
+        config["vocab_size"], config["hidden_size"], config["intermediate_size"], config["num_hidden_layers"],
+        config["num_attention_heads"], config["num_key_value_heads"], config["max_position_embeddings"],
+        int(config.get("bos_token_id", 0)), int(config.get("eos_token_id", 0)), float(config["layer_norm_eps"]),
+        float(config["rope_theta"]), float(config["partial_rotary_factor"]))
+
+
+def tp_unique_id():
+    """128 bytes naming a new NCCL communicator (rank 0 makes it; every rank
+    passes the same bytes to Model.load_stablelm(..., tp=...))."""
+    buf = (C.c_uint8 * 128)()
+    check(lib().tcu_tp_unique_id(buf))
+    return bytes(buf)
+
+
+def tp_plan(config, world, rank):
+    """Rank `rank`'s share of a head-parallel model (needs no GPU):
+    (first query head, query heads, first KV head, KV heads, first MLP row,
+    MLP rows)."""
+    out = (C.c_int32 * 6)()
+    check(lib().tcu_tp_plan(C.byref(_config_struct(config)), world, rank, out))
+    return tuple(out)
+
+
 def _options(device, kv_page_tokens, kv_pool_bytes):
     return _lib.LoadOptions(device, kv_page_tokens, kv_pool_bytes)
 
@@ -75,14 +100,12 @@ class Model:
         self.num_heads, self.num_kv_heads, self.max_positions = H.value, KVH.value, P.value
 
     @classmethod
-    def load_stablelm(cls, config, tensors, device=0, kv_page_tokens=0, kv_pool_bytes=0):
+    def load_stablelm(cls, config, tensors, device=0, kv_page_tokens=0, kv_pool_bytes=0, tp=None):
         """config: validated dict (checkpoint.stablelm_config); tensors: {name:
-        (dtype name, shape, payload)} in file encoding (LoadStableLM)."""
-        cfg = _lib.StableLMConfig(
-            config["vocab_size"], config["hidden_size"], config["intermediate_size"], config["num_hidden_layers"],
-            config["num_attention_heads"], config["num_key_value_heads"], config["max_position_embeddings"],
-            int(config.get("bos_token_id", 0)), int(config.get("eos_token_id", 0)), float(config["layer_norm_eps"]),
-            float(config["rope_theta"]), float(config["partial_rotary_factor"]))
+        (dtype name, shape, payload)} in file encoding (LoadStableLM). tp:
+        (world, rank, nccl_id bytes) loads this rank's share of a
+        head-parallel model (tcu_stablelm_load_tp)."""
+        cfg = _config_struct(config)
         arr = (_lib.Tensor * len(tensors))()
         keep = []
         for i, (name, (dt, shape, payload)) in enumerate(tensors.items()):
@@ -100,9 +123,16 @@ class Model:
             arr[i] = _lib.Tensor(nm, dtype_code(dt), len(shape), sh, ptr, n)
         out = C.c_void_p()
         opts = _options(device, kv_page_tokens, kv_pool_bytes)
-        check(lib().tcu_stablelm_load(C.byref(cfg), arr, len(tensors), C.byref(opts), C.byref(out)))
+        if tp is None:
+            check(lib().tcu_stablelm_load(C.byref(cfg), arr, len(tensors), C.byref(opts), C.byref(out)))
+        else:
+            world, rank, nccl_id = tp
+            t = _lib.TpOptions(world, rank)
+            C.memmove(t.nccl_id, bytes(nccl_id), 128)
+            check(lib().tcu_stablelm_load_tp(C.byref(cfg), arr, len(tensors), C.byref(opts), C.byref(t), C.byref(out)))
         m = cls(out.value, "stablelm")
         m.config = dict(config)
+        m.tp = tp
         return m
 
     @classmethod
@@ -245,7 +275,7 @@ class Session:
         check(lib().tcu_session_set_stream(self._h, C.c_void_p(stream) if stream else None))
 
     STAGES = ("embed", "norm_qkv_gate_up", "attention", "out_down_residual", "head", "prefill_projection",
-              "prefill_attention", "other", "decode_step")
+              "prefill_attention", "other", "decode_step", "allreduce")
 
     def profile(self, enable=True):
         check(lib().tcu_session_profile(self._h, int(bool(enable))))

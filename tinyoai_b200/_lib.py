@@ -20,6 +20,7 @@ EXPORTS = [
     "tcu_session_reset", "tcu_session_set_stream", "tcu_session_profile", "tcu_session_profile_read", "tcu_branches_open", "tcu_branches_forward", "tcu_branches_argmax", "tcu_branches_close",
     "tcu_batch_open", "tcu_batch_forward", "tcu_batch_close", "tcu_shortlist_static", "tcu_read_values",
     "tcu_session_forward_logprobs", "tcu_session_sample_candidates", "tcu_batch_sample_candidates",
+    "tcu_tp_unique_id", "tcu_stablelm_load_tp", "tcu_tp_plan",
 ]
 
 
@@ -40,6 +41,11 @@ class Penalties(C.Structure):
     """tcu_penalties: SamplingOptions' penalty fields (sampling.go:12-58)."""
     _fields_ = [("repetition_penalty", C.c_double), ("presence_penalty", C.c_double), ("frequency_penalty", C.c_double),
                 ("repetition_slope", C.c_double), ("repetition_range", C.c_int32)]
+
+
+class TpOptions(C.Structure):
+    """tcu_tp_options: this process's rank of `world` and the NCCL id bytes."""
+    _fields_ = [("world", C.c_int32), ("rank", C.c_int32), ("nccl_id", C.c_uint8 * 128)]
 
 
 class LoadOptions(C.Structure):
@@ -97,6 +103,10 @@ def lib():
         "tcu_session_forward_logprobs": ([P, C.c_int32, i32p, i32p, C.c_int32, C.c_int32, f64p, i32p, f64p, f32p], C.c_int),
         "tcu_session_sample_candidates": ([P, i32p, C.c_int32, C.POINTER(Penalties), C.c_int32, i32p, f64p, i32p], C.c_int),
         "tcu_batch_sample_candidates": ([P, C.c_int32, i32p, i32p, C.POINTER(Penalties), C.c_int32, i32p, f64p], C.c_int),
+        "tcu_tp_unique_id": ([C.POINTER(C.c_uint8)], C.c_int),
+        "tcu_stablelm_load_tp": ([C.POINTER(StableLMConfig), C.POINTER(Tensor), C.c_int32, C.POINTER(LoadOptions),
+                                  C.POINTER(TpOptions), C.POINTER(P)], C.c_int),
+        "tcu_tp_plan": ([C.POINTER(StableLMConfig), C.c_int32, C.c_int32, i32p], C.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

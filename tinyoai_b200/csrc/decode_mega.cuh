@@ -116,9 +116,6 @@ struct MegaArgs {
   // sets the error word, and the launch still ends. Set from the host only by
   // the TCU_TEST_HOLD_ARRIVAL environment variable.
   int hold_layer;
-  // L2 prefetch of the next layer's fused q/k/v/gate/up matrix by the merge
-  // warps of CTAs that merge no KV head (0: off).
-  int l2_prefetch;
   uint32_t slot_bytes;
   int nslots;  // ring depth (<= MG_MAX_SLOTS)
   uint32_t off_x, off_att, off_dig, off_sx, off_slots;
@@ -378,26 +375,6 @@ __device__ __forceinline__ void mg_await(const int* ctr, int target, int* err) {
     fence_proxy_async();  // later bulk copies read what the counter covers
   }
   named_bar_sync(1, MG_CT);
-}
-
-// Queues an L2 prefetch of bytes (a multiple of 16) at p (16-byte aligned)
-// of this GPU's memory; nothing is copied to shared memory.
-__device__ __forceinline__ void l2_prefetch_bulk(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-// Bounded poll (with back-off) until *ctr >= target; false after TCU_WAIT_NS
-// or once the error word is set. Does not set the error word: a prefetcher
-// that gives up only stops prefetching.
-__device__ bool mg_poll_quiet(const int* ctr, int target, const int* err) {
-  const unsigned long long t0 = global_ns();
-  for (;;) {
-    int v;
-    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
-    if (v >= target) return true;
-    if (*(volatile const int*)err || global_ns() - t0 > TCU_WAIT_NS) return false;
-    __nanosleep(256);
-  }
 }
 
 // Merges the nsplit partials (rows of hd outputs, max, sum) of each of the
@@ -853,32 +830,6 @@ __global__ void __launch_bounds__(MG_REG_THREADS, 1) k_decode_mega(MegaArgs a) {
           if (!(l == a.hold_layer && g == 0 && step == 0)) mg_red_add_release(dl + 3, 1);
         }
         __syncwarp();
-      }
-      // CTAs without a KV head to merge prefetch layer l + 1's W1 into L2
-      // once every W1 tile of layer l is taken: HBM would otherwise idle
-      // through this layer's attention -> merge -> out -> residual chain,
-      // and the next layer's W1 stream then starts from L2. The matrix
-      // (quants, then scales) is cut into 32 KB pieces dealt round robin to
-      // the prefetching CTAs, front to back, the order its tiles are taken.
-      if (a.l2_prefetch && c >= a.KVH && l + 1 < a.L) {
-        int ok = 1;
-        if (lane == 0) ok = mg_poll_quiet(grab + l * MG_CTL + 0, n_w1t, a.err);
-        if (!__shfl_sync(0xffffffffu, ok, 0)) continue;
-        const MegaLayer& nx = a.layers[l + 1];
-        const size_t rows1 = (size_t)(d + 2 * kvw + 2 * ff);
-        const size_t qbytes = rows1 * d, sbytes = rows1 * a.s1_stride * 2;
-        constexpr size_t PIECE = 32768;
-        const size_t nq = (qbytes + PIECE - 1) / PIECE, ns = (sbytes + PIECE - 1) / PIECE;
-        const int np = G - a.KVH, pi = c - a.KVH;
-        for (size_t k = (size_t)pi + (size_t)np * lane; k < nq + ns; k += (size_t)np * 32) {
-          if (k < nq) {
-            const size_t o = k * PIECE;
-            l2_prefetch_bulk(reinterpret_cast<const uint8_t*>(nx.w1) + o, (uint32_t)min(PIECE, qbytes - o));
-          } else {
-            const size_t o = (k - nq) * PIECE;
-            l2_prefetch_bulk(reinterpret_cast<const uint8_t*>(nx.s1) + o, (uint32_t)min(PIECE, sbytes - o));
-          }
-        }
       }
     }
     return;

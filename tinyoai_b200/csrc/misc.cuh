@@ -317,3 +317,14 @@ __global__ void __launch_bounds__(1024) k_candidates_rows(const float* logits, i
 }
 
 }  // namespace tcu
+
+namespace tcu {
+
+// x[i] += p[i] over n values: the residual update of a tensor-parallel layer
+// after the all-reduce of the ranks' out + down partial sums
+// (stablelm.go:365-377 with the two products summed across ranks).
+__global__ void k_add_rows(float* x, const float* p, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) x[i] = __fadd_rn(x[i], p[i]);
+}
+
+}  // namespace tcu

@@ -8,6 +8,8 @@
 // branches share full pages by reference count and copy only a page they
 // write while it is shared.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -102,11 +104,14 @@ struct KVPool {
   }
 };
 
+struct Work;
+
 struct tcu_model {
   Arch arch = ARCH_STABLELM;
   int device = 0;
   int V = 0, d = 0, ff = 0, L = 0, H = 0, KVH = 0, hd = 0, max_pos = 0;
   int kvw = 0;  // KVH * hd
+  int aw = 0;   // attention width H * hd: the hidden size, or this rank's heads under tensor parallelism
   double eps = 1e-5;
   Rope rope{};
   std::vector<Layer> layers;
@@ -130,7 +135,12 @@ struct tcu_model {
   uint32_t mega_slot_bytes = 0, mega_off[5] = {0, 0, 0, 0, 0};
   int mega_slots = 0, mega_split = 0, mega_att_warp = 0;
   size_t mega_smem = 0;
-  bool mega_prefetch = false;  // L2 prefetch of the next layer's W1 (TCU_L2_PREFETCH=1 turns it on)
+  std::vector<Work*> work_pool;  // workspaces of closed handles (work_take / work_give), guarded by mu
+  // Head-parallel tensor parallelism (tcu_stablelm_load_tp): this rank's
+  // share of the heads and of the MLP, and the communicator of the per-layer
+  // all-reduce of the out + down partial sums.
+  int tp_world = 1, tp_rank = 0;
+  ncclComm_t tp_comm = nullptr;
 };
 
 static int dalloc(tcu_model* m, void** p, size_t n) {
@@ -142,9 +152,42 @@ static int dalloc(tcu_model* m, void** p, size_t n) {
   return TCU_OK;
 }
 
+// NCCL, resolved at run time so that the library loads where NCCL is absent;
+// only tensor-parallel models use it. If the process already holds a
+// libnccl.so.2 (a framework's), dlopen returns that one.
+struct NcclApi {
+  bool ok = false;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+static NcclApi g_nccl;
+static std::once_flag g_nccl_once;
+
+static const NcclApi* nccl_api() {
+  std::call_once(g_nccl_once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+    g_nccl.get_unique_id = reinterpret_cast<decltype(g_nccl.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    g_nccl.comm_init_rank = reinterpret_cast<decltype(g_nccl.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    g_nccl.all_reduce = reinterpret_cast<decltype(g_nccl.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    g_nccl.comm_destroy = reinterpret_cast<decltype(g_nccl.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    g_nccl.error_string = reinterpret_cast<decltype(g_nccl.error_string)>(dlsym(h, "ncclGetErrorString"));
+    g_nccl.ok = g_nccl.get_unique_id && g_nccl.comm_init_rank && g_nccl.all_reduce && g_nccl.comm_destroy && g_nccl.error_string;
+  });
+  return g_nccl.ok ? &g_nccl : nullptr;
+}
+
+static void work_pool_free(tcu_model* m);
+
 static void model_release(tcu_model* m) {
   if (!m) return;
   cudaSetDevice(m->device);
+  work_pool_free(m);
+  if (m->tp_comm && nccl_api()) nccl_api()->comm_destroy(m->tp_comm);
   for (void* p : m->allocs) cudaFree(p);
   for (KVPool* p : m->pools)
     if (p) {
@@ -293,10 +336,18 @@ static bool g_attr_done[64] = {};
 static int sampling_smem_attrs(int device) {
   std::lock_guard<std::mutex> g(g_attr_mu);
   if (device < 0 || device >= 64 || g_attr_done[device]) return TCU_OK;
-  const int lim = 227 * 1024;
-  CK(cudaFuncSetAttribute(k_shortlist, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
-  CK(cudaFuncSetAttribute(k_logprob_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
-  CK(cudaFuncSetAttribute(k_candidates_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+  int optin = 0;
+  CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  // Dynamic shared memory may take what the kernel's static arrays leave.
+  auto set_max = [&](const void* f) -> int {
+    cudaFuncAttributes fa;
+    CK(cudaFuncGetAttributes(&fa, f));
+    CK(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes));
+    return TCU_OK;
+  };
+  TRY(set_max((const void*)k_shortlist));
+  TRY(set_max((const void*)k_logprob_rows));
+  TRY(set_max((const void*)k_candidates_rows));
   g_attr_done[device] = true;
   return TCU_OK;
 }
@@ -322,8 +373,6 @@ static void init_common(tcu_model* m, const tcu_load_options* o) {
   m->disable_stream = k && strcmp(k, "portable") == 0;
   const char* g = getenv("TCU_GEMM");
   m->use_tc = !(g && strcmp(g, "simt") == 0);
-  const char* pf = getenv("TCU_L2_PREFETCH");
-  m->mega_prefetch = pf && strcmp(pf, "1") == 0;
 }
 
 // StableLM rotary table (stablelm.go:309-326): per position and rotary pair,
@@ -389,7 +438,7 @@ static void mega_dn_scales(const tcu_model* m, int* sstride, int* soff) {
 
 static int build_mega(tcu_model* m) {
   m->mega = false;
-  if (m->disable_stream || m->arch != ARCH_STABLELM) return TCU_OK;
+  if (m->disable_stream || m->arch != ARCH_STABLELM || m->tp_world > 1 || m->aw != m->d) return TCU_OK;
   if (m->embed.fmt != FMT_Q8_0 || m->head.fmt != FMT_Q8_0) return TCU_OK;
   for (const Layer& ly : m->layers)
     if (ly.w1.fmt != FMT_Q8_0 || ly.w2.fmt != FMT_Q8_0) return TCU_OK;
@@ -454,7 +503,64 @@ static int build_mega(tcu_model* m) {
   return TCU_OK;
 }
 
-static int stablelm_load(const tcu_stablelm_config* c, const tcu_tensor* t, int n, const tcu_load_options* o, tcu_model** out) {
+// One rank's share of a StableLM under head-parallel tensor parallelism:
+// contiguous blocks of query heads, KV heads and MLP rows. Query head h uses
+// KV head h / (H / KVH), so rank r's query heads use exactly its KV heads.
+struct TpSlice {
+  int world = 1, rank = 0;
+  int h0 = 0, nh = 0;    // query heads
+  int kv0 = 0, nkv = 0;  // KV heads
+  int f0 = 0, nf = 0;    // MLP rows (gate/up) = down columns
+};
+
+static int tp_slice(const tcu_stablelm_config* c, int world, int rank, TpSlice* out) {
+  if (world < 1 || rank < 0 || rank >= world) return fail(TCU_EINVAL, "invalid rank %d of %d", rank, world);
+  if (c->num_attention_heads % world || c->num_key_value_heads % world || c->intermediate_size % world)
+    return fail(TCU_EINVAL, "%d ranks must divide the heads (%d), KV heads (%d) and MLP width (%d)", world, c->num_attention_heads,
+                c->num_key_value_heads, c->intermediate_size);
+  TpSlice t;
+  t.world = world;
+  t.rank = rank;
+  t.nh = c->num_attention_heads / world;
+  t.h0 = rank * t.nh;
+  t.nkv = c->num_key_value_heads / world;
+  t.kv0 = rank * t.nkv;
+  t.nf = c->intermediate_size / world;
+  t.f0 = rank * t.nf;
+  *out = t;
+  return TCU_OK;
+}
+
+// Bytes of `cols` values of one row in a format's file encoding.
+static size_t file_row_bytes(int fmt, int64_t cols) { return file_bytes(fmt, 1, cols); }
+
+// Columns [c0, c0 + nc) of every row of a file-encoded [rows x cols] tensor,
+// gathered into one buffer (whole blocks: c0 and nc divisible by the block
+// width of the format).
+static void gather_cols(const tcu_tensor* t, int rows, int cols, int c0, int nc, std::vector<uint8_t>& out) {
+  const size_t rb = file_row_bytes(t->dtype, cols), off = file_row_bytes(t->dtype, c0), nb = file_row_bytes(t->dtype, nc);
+  out.resize((size_t)rows * nb);
+  const uint8_t* src = (const uint8_t*)t->data;
+  for (int r = 0; r < rows; r++) memcpy(out.data() + (size_t)r * nb, src + (size_t)r * rb + off, nb);
+}
+
+static int fmt_block_width(int fmt) {
+  switch (fmt) {
+    case FMT_Q8_0:
+    case FMT_Q5_1:
+      return 32;
+    case FMT_Q5_K:
+    case FMT_Q6_K:
+      return 256;
+    default:
+      return 1;
+  }
+}
+
+// tp == nullptr: the whole model. Otherwise this rank's share (the tensors
+// are the whole checkpoint's; the load takes its rows and columns).
+static int stablelm_load(const tcu_stablelm_config* c, const tcu_tensor* t, int n, const tcu_load_options* o, const TpSlice* tp,
+                         tcu_model** out) {
   // stablelm.go:85-111 validate() (the structural flags are checked by the caller's config parser).
   if (!c || !out || (n > 0 && !t)) return fail(TCU_EINVAL, "null argument");
   if (c->hidden_size <= 0 || c->intermediate_size <= 0 || c->num_hidden_layers <= 0 || c->num_attention_heads <= 0 ||
@@ -468,6 +574,9 @@ static int stablelm_load(const tcu_stablelm_config* c, const tcu_tensor* t, int 
     return fail(TCU_EINVAL, "invalid LayerNorm or partial RoPE settings");
   if (c->bos_token_id < 0 || c->bos_token_id >= c->vocab_size || c->eos_token_id < 0 || c->eos_token_id >= c->vocab_size)
     return fail(TCU_EINVAL, "invalid BOS/EOS token IDs");
+  TpSlice whole;
+  if (!tp) TRY(tp_slice(c, 1, 0, &whole));
+  const TpSlice& sl = tp ? *tp : whole;
   const int device = o ? o->device : 0;
   TRY(check_device(device));
   tcu_model* m = new tcu_model();
@@ -475,15 +584,19 @@ static int stablelm_load(const tcu_stablelm_config* c, const tcu_tensor* t, int 
   m->arch = ARCH_STABLELM;
   m->V = c->vocab_size;
   m->d = c->hidden_size;
-  m->ff = c->intermediate_size;
   m->L = c->num_hidden_layers;
-  m->H = c->num_attention_heads;
-  m->KVH = c->num_key_value_heads;
-  m->hd = m->d / m->H;
+  m->hd = m->d / c->num_attention_heads;
+  m->H = sl.nh;
+  m->KVH = sl.nkv;
+  m->ff = sl.nf;
   m->kvw = m->hd * m->KVH;
+  m->aw = m->hd * m->H;
+  m->tp_world = sl.world;
+  m->tp_rank = sl.rank;
   m->max_pos = c->max_position_embeddings;
   m->eps = c->layer_norm_eps;
-  const int d = m->d, ff = m->ff, kvw = m->kvw;
+  const int d = m->d, ff = m->ff, kvw = m->kvw, aw = m->aw, hd = m->hd;
+  const int ffg = c->intermediate_size, kvg = hd * c->num_key_value_heads;  // whole-checkpoint widths
   auto bail = [&](int code) {
     model_release(m);
     return code;
@@ -491,7 +604,6 @@ static int stablelm_load(const tcu_stablelm_config* c, const tcu_tensor* t, int 
   // The prefill attention kernel holds up to 128 output dimensions per query.
   if (m->hd < 4 || m->hd > 128 || m->hd % 4) return bail(fail(TCU_EINVAL, "head size %d: a multiple of 4 in 4..128 is supported", m->hd));
   // Validate every tensor before allocating (loadStableWeights, stablelm.go:167-199).
-  std::vector<std::string> names;
   auto chk = [&](const std::string& name, int64_t r, int64_t cc) { return check_tensor(find_tensor(t, n, name), name, r, cc); };
   int rc;
   if ((rc = chk("model.embed_tokens.weight", m->V, d)) || (rc = chk("lm_head.weight", m->V, d)) || (rc = chk("model.norm.weight", d, 0)) ||
@@ -500,10 +612,10 @@ static int stablelm_load(const tcu_stablelm_config* c, const tcu_tensor* t, int 
   for (int l = 0; l < m->L; l++) {
     std::string p = "model.layers." + std::to_string(l) + ".";
     if ((rc = chk(p + "input_layernorm.weight", d, 0)) || (rc = chk(p + "input_layernorm.bias", d, 0)) ||
-        (rc = chk(p + "self_attn.q_proj.weight", d, d)) || (rc = chk(p + "self_attn.k_proj.weight", kvw, d)) ||
-        (rc = chk(p + "self_attn.v_proj.weight", kvw, d)) || (rc = chk(p + "self_attn.o_proj.weight", d, d)) ||
-        (rc = chk(p + "mlp.gate_proj.weight", ff, d)) || (rc = chk(p + "mlp.up_proj.weight", ff, d)) ||
-        (rc = chk(p + "mlp.down_proj.weight", d, ff)))
+        (rc = chk(p + "self_attn.q_proj.weight", d, d)) || (rc = chk(p + "self_attn.k_proj.weight", kvg, d)) ||
+        (rc = chk(p + "self_attn.v_proj.weight", kvg, d)) || (rc = chk(p + "self_attn.o_proj.weight", d, d)) ||
+        (rc = chk(p + "mlp.gate_proj.weight", ffg, d)) || (rc = chk(p + "mlp.up_proj.weight", ffg, d)) ||
+        (rc = chk(p + "mlp.down_proj.weight", d, ffg)))
       return bail(rc);
     const int f1 = find_tensor(t, n, p + "self_attn.q_proj.weight")->dtype;
     for (const char* nm : {"self_attn.k_proj.weight", "self_attn.v_proj.weight", "mlp.gate_proj.weight", "mlp.up_proj.weight"})
@@ -512,12 +624,17 @@ static int stablelm_load(const tcu_stablelm_config* c, const tcu_tensor* t, int 
     const int f2 = find_tensor(t, n, p + "self_attn.o_proj.weight")->dtype;
     if (find_tensor(t, n, p + "mlp.down_proj.weight")->dtype != f2)
       return bail(fail(TCU_EUNSUP, "layer %d: o_proj and down_proj must share one dtype (fused projection)", l));
-    if ((f2 == FMT_Q5_K || f2 == FMT_Q6_K) && d % 256) return bail(fail(TCU_EUNSUP, "layer %d: K-quant o|down fusion needs hidden %% 256 == 0", l));
+    if ((f2 == FMT_Q5_K || f2 == FMT_Q6_K) && aw % 256) return bail(fail(TCU_EUNSUP, "layer %d: K-quant o|down fusion needs an attention width divisible by 256", l));
+    const int bw = fmt_block_width(f2);
+    if (sl.world > 1 && ((sl.h0 * hd) % bw || aw % bw || sl.f0 % bw || ff % bw))
+      return bail(fail(TCU_EUNSUP, "layer %d: the o/down column slices of %d ranks split %s blocks", l, sl.world,
+                       f2 == FMT_Q8_0 ? "Q8_0" : "quantised"));
   }
   if ((rc = build_stablelm_rope(m, c->rope_theta, (int)rotary_f))) return bail(rc);
   Stager st;
   m->layers.resize(m->L);
-  const int n_plain = d + 2 * kvw;
+  const int n_plain = aw + 2 * kvw;
+  std::vector<uint8_t> cols;
   for (int l = 0; l < m->L; l++) {
     std::string p = "model.layers." + std::to_string(l) + ".";
     Layer& ly = m->layers[l];
@@ -525,16 +642,28 @@ static int stablelm_load(const tcu_stablelm_config* c, const tcu_tensor* t, int 
     const tcu_tensor *q = T("self_attn.q_proj.weight"), *k = T("self_attn.k_proj.weight"), *v = T("self_attn.v_proj.weight");
     const tcu_tensor *o_ = T("self_attn.o_proj.weight"), *g = T("mlp.gate_proj.weight"), *u = T("mlp.up_proj.weight"),
                      *dn = T("mlp.down_proj.weight");
+    // Row slices of q/k/v/gate/up start inside the file tensors; o and down
+    // columns are gathered.
+    auto rows_of = [&](const tcu_tensor* x, int r0) { return (const uint8_t*)x->data + (size_t)r0 * file_row_bytes(x->dtype, d); };
+    const size_t rq = file_row_bytes(q->dtype, d);
     // W1 rows: [q | k | v | (gate_i, up_i) interleaved]; W2 columns: [o | down].
-    if ((rc = alloc_dmat(m, &ly.w1, q->dtype, n_plain + 2 * ff, d)) || (rc = alloc_dmat(m, &ly.w2, o_->dtype, d, d + ff)) ||
-        (rc = place(st, q->data, q->nbytes, q->dtype, d, d, ly.w1, 0, 1, 0)) ||
-        (rc = place(st, k->data, k->nbytes, k->dtype, kvw, d, ly.w1, d, 1, 0)) ||
-        (rc = place(st, v->data, v->nbytes, v->dtype, kvw, d, ly.w1, d + kvw, 1, 0)) ||
-        (rc = place(st, g->data, g->nbytes, g->dtype, ff, d, ly.w1, n_plain, 2, 0)) ||
-        (rc = place(st, u->data, u->nbytes, u->dtype, ff, d, ly.w1, n_plain + 1, 2, 0)) ||
-        (rc = place(st, o_->data, o_->nbytes, o_->dtype, d, d, ly.w2, 0, 1, 0)) ||
-        (rc = place(st, dn->data, dn->nbytes, dn->dtype, d, ff, ly.w2, 0, 1, d)))
+    if ((rc = alloc_dmat(m, &ly.w1, q->dtype, n_plain + 2 * ff, d)) || (rc = alloc_dmat(m, &ly.w2, o_->dtype, d, aw + ff)) ||
+        (rc = place(st, rows_of(q, sl.h0 * hd), rq * aw, q->dtype, aw, d, ly.w1, 0, 1, 0)) ||
+        (rc = place(st, rows_of(k, sl.kv0 * hd), rq * kvw, k->dtype, kvw, d, ly.w1, aw, 1, 0)) ||
+        (rc = place(st, rows_of(v, sl.kv0 * hd), rq * kvw, v->dtype, kvw, d, ly.w1, aw + kvw, 1, 0)) ||
+        (rc = place(st, rows_of(g, sl.f0), rq * ff, g->dtype, ff, d, ly.w1, n_plain, 2, 0)) ||
+        (rc = place(st, rows_of(u, sl.f0), rq * ff, u->dtype, ff, d, ly.w1, n_plain + 1, 2, 0)))
       return bail(rc);
+    if (sl.world == 1) {
+      if ((rc = place(st, o_->data, o_->nbytes, o_->dtype, d, d, ly.w2, 0, 1, 0)) ||
+          (rc = place(st, dn->data, dn->nbytes, dn->dtype, d, ff, ly.w2, 0, 1, d)))
+        return bail(rc);
+    } else {
+      gather_cols(o_, d, d, sl.h0 * hd, aw, cols);
+      if ((rc = place(st, cols.data(), cols.size(), o_->dtype, d, aw, ly.w2, 0, 1, 0))) return bail(rc);
+      gather_cols(dn, d, ffg, sl.f0, ff, cols);
+      if ((rc = place(st, cols.data(), cols.size(), dn->dtype, d, ff, ly.w2, 0, 1, aw))) return bail(rc);
+    }
     std::vector<float> nw, nb;
     if ((rc = decode_vec(T("input_layernorm.weight"), d, nw)) || (rc = decode_vec(T("input_layernorm.bias"), d, nb)) ||
         (rc = upload_floats(m, nw, &ly.n1w)) || (rc = upload_floats(m, nb, &ly.n1b)))
@@ -584,6 +713,7 @@ static int llama_load(const void* ck, uint64_t nbytes, const tcu_load_options* o
   m->KVH = h[4];
   m->hd = (int)hs;
   m->kvw = (int)kvd;
+  m->aw = (int)dim;
   m->max_pos = (int)seq;
   auto bail = [&](int code) {
     model_release(m);
@@ -760,6 +890,9 @@ struct Work {
   double* cd_vals = nullptr;
   uint8_t* pen_buf = nullptr;
   size_t pen_cap = 0;
+  // Tensor parallelism: this rank's out + down partial sums [rows][d], then
+  // their sum over the ranks (in place).
+  float* tp_part = nullptr;
   // Tensor-core GEMM workspace (allocated on first use): binary16 split of
   // the activations [2][tc_npad][tc_kmax], their shifts, split-K partials.
   __half* tc_split = nullptr;
@@ -796,11 +929,11 @@ static int work_init(tcu_model* m, Work* w, int rows, int seqs, int logits_rows,
   // decode step may use; the other kernels use SPLIT_PAGES pages.
   w->max_splits = (m->max_pos + m->P - 1) / m->P;
   w->out_cap = out_cap;
-  const int qkvw = m->d + 2 * m->kvw;
+  const int qkvw = m->aw + 2 * m->kvw;
   TRY(w->get(&w->x, (size_t)rows * m->d));
   TRY(w->get(&w->xn, (size_t)rows * m->d));
   TRY(w->get(&w->qkv, (size_t)rows * qkvw));
-  TRY(w->get(&w->ah, (size_t)rows * (m->d + m->ff)));
+  TRY(w->get(&w->ah, (size_t)rows * (m->aw + m->ff)));
   TRY(w->get(&w->logits, (size_t)logits_rows * m->V));
   TRY(w->get(&w->tokens, (size_t)std::max(rows, seqs)));
   TRY(w->get(&w->pos, (size_t)seqs));
@@ -822,6 +955,7 @@ static int work_init(tcu_model* m, Work* w, int rows, int seqs, int logits_rows,
   TRY(w->get(&w->lp_vals, (size_t)LP_ROWS * 256));
   TRY(w->get(&w->cd_ids, (size_t)seqs * 256));
   TRY(w->get(&w->cd_vals, (size_t)seqs * 256));
+  if (m->tp_world > 1) TRY(w->get(&w->tp_part, (size_t)rows * m->d));
   if (m->mega) {
     const size_t nb16 = (size_t)(m->d + m->ff) / 16;
     w->asx_stride = (int)((nb16 + 3) / 4 * 4);
@@ -832,9 +966,56 @@ static int work_init(tcu_model* m, Work* w, int rows, int seqs, int logits_rows,
     TRY(w->get(&w->grab, (size_t)2 * (m->L + 1) * MG_CTL));
     TRY(w->get(&w->done, (size_t)2 * (m->L + 1) * MG_CTL));
   }
-  // The zeroing memsets ran on the legacy stream (see pool_get).
-  CK(cudaDeviceSynchronize());
+  // The zeroing memsets ran on the legacy stream; wait for that stream only
+  // (a device-wide synchronisation would stall the other sessions' streams).
+  CK(cudaStreamSynchronize(cudaStreamLegacy));
   return TCU_OK;
+}
+
+// Workspaces of closed sessions, branch batches and batch runners are kept
+// per model and handed to the next handle whose shape they cover, so opening
+// and closing handles on a serving path neither allocates device memory nor
+// frees it (cudaFree synchronises the whole device and would stall every
+// other session). A reused workspace is in the state its last call left,
+// the state a live session's next call also starts from.
+static int work_take(tcu_model* m, Work** out, int rows, int seqs, int logits_rows, int out_cap) {
+  *out = nullptr;
+  {
+    std::lock_guard<std::mutex> g(m->mu);
+    int best = -1;
+    for (int i = 0; i < (int)m->work_pool.size(); i++) {
+      const Work* w = m->work_pool[i];
+      if (w->rows < rows || w->seqs < seqs || w->logits_rows < logits_rows || w->out_cap < out_cap) continue;
+      if (best < 0 || (size_t)w->rows * w->seqs < (size_t)m->work_pool[best]->rows * m->work_pool[best]->seqs) best = i;
+    }
+    if (best >= 0) {
+      *out = m->work_pool[best];
+      m->work_pool.erase(m->work_pool.begin() + best);
+      return TCU_OK;
+    }
+  }
+  Work* w = new Work();
+  const int rc = work_init(m, w, rows, seqs, logits_rows, out_cap);
+  if (rc != TCU_OK) {
+    delete w;
+    return rc;
+  }
+  *out = w;
+  return TCU_OK;
+}
+
+// Returns a workspace to the model's pool; the caller has synchronised every
+// stream that used it.
+static void work_give(tcu_model* m, Work* w) {
+  if (!w) return;
+  w->shared_splits = 0;
+  std::lock_guard<std::mutex> g(m->mu);
+  m->work_pool.push_back(w);
+}
+
+static void work_pool_free(tcu_model* m) {
+  for (Work* w : m->work_pool) delete w;
+  m->work_pool.clear();
 }
 
 // ---------------------------------------------------------------------------
@@ -843,7 +1024,7 @@ static int work_init(tcu_model* m, Work* w, int rows, int seqs, int logits_rows,
 // are accumulated after the stream is synchronised. With profiling off no
 // event is recorded.
 
-enum Stage { ST_EMBED = 0, ST_W1, ST_ATTN, ST_W2, ST_HEAD, ST_PF_GEMM, ST_PF_ATTN, ST_OTHER, ST_MEGA, ST_COUNT };
+enum Stage { ST_EMBED = 0, ST_W1, ST_ATTN, ST_W2, ST_HEAD, ST_PF_GEMM, ST_PF_ATTN, ST_OTHER, ST_MEGA, ST_COMM, ST_COUNT };
 
 struct Prof {
   bool on = false;
@@ -1392,7 +1573,7 @@ static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M,
   a.hd = m->hd;
   a.rope = m->rope;
   a.qkv = w->qkv;
-  a.qkv_stride = m->d + 2 * m->kvw;
+  a.qkv_stride = m->aw + 2 * m->kvw;
   a.kv = pool->view();
   a.layer = layer;
   a.page_table = w->pt;
@@ -1403,7 +1584,7 @@ static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M,
   a.part = w->part;
   a.counters = w->counters;
   a.out = w->ah;
-  a.out_stride = m->d + m->ff;
+  a.out_stride = m->aw + m->ff;
   a.scale = (float)sqrt((double)m->hd);
   a.s_begin = 0;
   const int es = pool->half ? 2 : 4;
@@ -1448,12 +1629,39 @@ static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M,
   PROF_END(s);
 }
 
+// First failure of a collective on this thread (the enqueue paths report it
+// after they return).
+static thread_local std::string g_comm_err;
+
+// The per-layer exchange of a tensor-parallel model: the ranks' out + down
+// partial sums of n rows (w->tp_part) are summed in place by NCCL over
+// NVLink, then added to the residual rows x (fp32, k_add_rows).
+static void tp_reduce_add(const tcu_model* m, Work* w, int n, cudaStream_t s) {
+  const size_t count = (size_t)n * m->d;
+  PROF_BEGIN(ST_COMM, s);
+  const ncclResult_t r = nccl_api()->all_reduce(w->tp_part, w->tp_part, count, ncclFloat32, ncclSum, m->tp_comm, s);
+  PROF_END(s);
+  if (r != ncclSuccess && g_comm_err.empty()) g_comm_err = std::string("ncclAllReduce: ") + nccl_api()->error_string(r);
+  PROF_BEGIN(ST_OTHER, s);
+  k_add_rows<<<(int)std::min<size_t>((count + 255) / 256, (size_t)m->sm_count * 4), 256, 0, s>>>(w->x, w->tp_part, count);
+  NOTE("k_add_rows");
+  PROF_END(s);
+}
+
+// Reports (once) a collective that failed while work was being enqueued.
+static int comm_check() {
+  if (g_comm_err.empty()) return TCU_OK;
+  std::string e = g_comm_err;
+  g_comm_err.clear();
+  return fail(TCU_ECUDA, "%s", e.c_str());
+}
+
 // One decode step for M sequences whose tokens are in w->tokens (token mode)
 // or in w->argmax (step mode) and whose new positions are w->pos (token
 // mode) / w->pos + 1 (step mode). Ends with the head: logits rows and argmax.
 static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, bool step_mode, int grid_splits, bool write_logits,
                            cudaStream_t s) {
-  const int d = m->d, ff = m->ff, qkvw = d + 2 * m->kvw;
+  const int d = m->d, ff = m->ff, aw = m->aw, qkvw = aw + 2 * m->kvw;
   EmbedArgs ea{};
   ea.E = m->embed;
   ea.n = M;
@@ -1486,8 +1694,8 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
         a.out = w->qkv;
         a.out_stride = qkvw;
         a.n_plain = qkvw;
-        a.glu_out = w->ah + d;
-        a.glu_stride = d + ff;
+        a.glu_out = w->ah + aw;
+        a.glu_stride = aw + ff;
         a.glu_act = 0;
         launch_gemv<PRO_LN, EPI_GLU>(m, a, s);
       } else {
@@ -1500,32 +1708,54 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
         g.out = w->qkv;
         g.out_stride = qkvw;
         g.n_plain = qkvw;
-        g.glu_out = w->ah + d;
-        g.glu_stride = d + ff;
+        g.glu_out = w->ah + aw;
+        g.glu_stride = aw + ff;
         g.glu_act = 0;
         launch_gemm<EPI_GLU>(m, w, g, s);
       }
       launch_attn_decode(m, pool, w, M, l, grid_splits, s);
       g_stage = ST_W2;
-      if (gemv) {
+      if (m->tp_world > 1) {
+        // This rank's out + down partial of every row, summed over the ranks.
+        if (gemv) {
+          GemvArgs a{};
+          a.W = ly.w2;
+          a.M = M;
+          a.in = w->ah;
+          a.in_stride = aw + ff;
+          a.out = w->tp_part;
+          a.out_stride = d;
+          launch_gemv<PRO_COPY, EPI_STORE>(m, a, s);
+        } else {
+          GemmArgs g{};
+          g.W = ly.w2;
+          g.n = M;
+          g.A = w->ah;
+          g.lda = aw + ff;
+          g.out = w->tp_part;
+          g.out_stride = d;
+          launch_gemm<EPI_STORE>(m, w, g, s);
+        }
+        tp_reduce_add(m, w, M, s);
+      } else if (gemv) {
         GemvArgs a{};
         a.W = ly.w2;
         a.M = M;
         a.in = w->ah;
-        a.in_stride = d + ff;
+        a.in_stride = aw + ff;
         a.resid = w->x;
         a.resid_stride = d;
-        a.k_split = d;
+        a.k_split = aw;
         launch_gemv<PRO_COPY, EPI_RESID2>(m, a, s);
       } else {
         GemmArgs g{};
         g.W = ly.w2;
         g.n = M;
         g.A = w->ah;
-        g.lda = d + ff;
+        g.lda = aw + ff;
         g.resid = w->x;
         g.resid_stride = d;
-        g.k_split = d;
+        g.k_split = aw;
         launch_gemm<EPI_RESID2>(m, w, g, s);
       }
     } else {
@@ -1558,7 +1788,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
         a.W = ly.w2;
         a.M = M;
         a.in = w->ah;
-        a.in_stride = d + ff;
+        a.in_stride = aw + ff;
         a.resid = w->x;
         a.resid_stride = d;
         launch_gemv<PRO_COPY, EPI_RESID1>(m, a, s);
@@ -1569,15 +1799,15 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
         b.in_stride = d;
         b.nw = ly.n2w;
         b.n_plain = 0;
-        b.glu_out = w->ah + d;
-        b.glu_stride = d + ff;
+        b.glu_out = w->ah + aw;
+        b.glu_stride = aw + ff;
         b.glu_act = 1;
         launch_gemv<PRO_RMS, EPI_GLU>(m, b, s);
         GemvArgs c{};
         c.W = ly.w4;
         c.M = M;
-        c.in = w->ah + d;
-        c.in_stride = d + ff;
+        c.in = w->ah + aw;
+        c.in_stride = aw + ff;
         c.resid = w->x;
         c.resid_stride = d;
         launch_gemv<PRO_COPY, EPI_RESID1>(m, c, s);
@@ -1586,7 +1816,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
         g.W = ly.w2;
         g.n = M;
         g.A = w->ah;
-        g.lda = d + ff;
+        g.lda = aw + ff;
         g.resid = w->x;
         g.resid_stride = d;
         launch_gemm<EPI_RESID1>(m, w, g, s);
@@ -1597,15 +1827,15 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
         g3.A = w->xn;
         g3.lda = d;
         g3.n_plain = 0;
-        g3.glu_out = w->ah + d;
-        g3.glu_stride = d + ff;
+        g3.glu_out = w->ah + aw;
+        g3.glu_stride = aw + ff;
         g3.glu_act = 1;
         launch_gemm<EPI_GLU>(m, w, g3, s);
         GemmArgs g4{};
         g4.W = ly.w4;
         g4.n = M;
-        g4.A = w->ah + d;
-        g4.lda = d + ff;
+        g4.A = w->ah + aw;
+        g4.lda = aw + ff;
         g4.resid = w->x;
         g4.resid_stride = d;
         launch_gemm<EPI_RESID1>(m, w, g4, s);
@@ -1650,7 +1880,7 @@ static void enqueue_decode(const tcu_model* m, KVPool* pool, Work* w, int M, boo
 // Prompt chunk of n tokens for one sequence at positions start..start+n-1
 // (prefill.go:33-115 / mlx_native.go:324-495). Tokens are in w->tokens.
 static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, int start, cudaStream_t s) {
-  const int d = m->d, ff = m->ff, qkvw = d + 2 * m->kvw;
+  const int d = m->d, ff = m->ff, aw = m->aw, qkvw = aw + 2 * m->kvw;
   EmbedArgs ea{};
   ea.E = m->embed;
   ea.n = n;
@@ -1674,8 +1904,8 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
     g.out_stride = qkvw;
     if (m->arch == ARCH_STABLELM) {
       g.n_plain = qkvw;
-      g.glu_out = w->ah + d;
-      g.glu_stride = d + ff;
+      g.glu_out = w->ah + aw;
+      g.glu_stride = aw + ff;
       g.glu_act = 0;
       launch_gemm<EPI_GLU>(m, w, g, s);
     } else {
@@ -1709,7 +1939,7 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
     pa.layer = l;
     pa.page_table = w->pt;
     pa.out = w->ah;
-    pa.out_stride = d + ff;
+    pa.out_stride = aw + ff;
     pa.scale = (float)sqrt((double)m->hd);
     const size_t smem = pa_smem_bytes(m->hd);
     const int nc = (m->hd + 15) / 16;
@@ -1720,22 +1950,32 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
     kern<<<dim3((n + PA_QT - 1) / PA_QT, m->H), PA_THREADS, smem, s>>>(pa);
     NOTE("k_attn_prefill");
     PROF_END(s);
-    if (m->arch == ARCH_STABLELM) {
+    if (m->arch == ARCH_STABLELM && m->tp_world > 1) {
       GemmArgs g2{};
       g2.W = ly.w2;
       g2.n = n;
       g2.A = w->ah;
-      g2.lda = d + ff;
+      g2.lda = aw + ff;
+      g2.out = w->tp_part;
+      g2.out_stride = d;
+      launch_gemm<EPI_STORE>(m, w, g2, s);
+      tp_reduce_add(m, w, n, s);
+    } else if (m->arch == ARCH_STABLELM) {
+      GemmArgs g2{};
+      g2.W = ly.w2;
+      g2.n = n;
+      g2.A = w->ah;
+      g2.lda = aw + ff;
       g2.resid = w->x;
       g2.resid_stride = d;
-      g2.k_split = d;
+      g2.k_split = aw;
       launch_gemm<EPI_RESID2>(m, w, g2, s);
     } else {
       GemmArgs g2{};
       g2.W = ly.w2;
       g2.n = n;
       g2.A = w->ah;
-      g2.lda = d + ff;
+      g2.lda = aw + ff;
       g2.resid = w->x;
       g2.resid_stride = d;
       launch_gemm<EPI_RESID1>(m, w, g2, s);
@@ -1746,15 +1986,15 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
       g3.A = w->xn;
       g3.lda = d;
       g3.n_plain = 0;
-      g3.glu_out = w->ah + d;
-      g3.glu_stride = d + ff;
+      g3.glu_out = w->ah + aw;
+      g3.glu_stride = aw + ff;
       g3.glu_act = 1;
       launch_gemm<EPI_GLU>(m, w, g3, s);
       GemmArgs g4{};
       g4.W = ly.w4;
       g4.n = n;
-      g4.A = w->ah + d;
-      g4.lda = d + ff;
+      g4.A = w->ah + aw;
+      g4.lda = aw + ff;
       g4.resid = w->x;
       g4.resid_stride = d;
       launch_gemm<EPI_RESID1>(m, w, g4, s);
@@ -1794,7 +2034,7 @@ struct tcu_session {
   std::vector<int> pages;
   int length = 0;
   cudaStream_t stream = nullptr;
-  Work w;
+  Work* w = nullptr;  // from the model's workspace pool (work_take)
   bool closed = false;
   cudaStream_t own_stream = nullptr;  // created by the session; stream may be the caller's
   // cached decode-step graph (step mode, M = 1)
@@ -1812,7 +2052,7 @@ struct tcu_session {
 struct ProfScope {
   explicit ProfScope(tcu_session* s, int* err = nullptr) {
     g_prof = (s && s->prof.on) ? &s->prof : nullptr;
-    g_err_word = err ? err : (s ? s->w.err : nullptr);
+    g_err_word = err ? err : (s ? s->w->err : nullptr);
   }
   ~ProfScope() {
     g_prof = nullptr;
@@ -1831,7 +2071,7 @@ struct tcu_branches {
   tcu_session* s = nullptr;
   int prefix = 0, count = 0, step = 0;
   std::vector<std::vector<int>> pages;
-  Work w;
+  Work* w = nullptr;  // from the model's workspace pool (work_take)
   bool closed = false;
 };
 
@@ -1883,10 +2123,10 @@ static int sync_stream(cudaStream_t stream, int* err_word) {
   return TCU_OK;
 }
 
-static int session_sync(tcu_session* s) { return sync_stream(s->stream, s->w.err); }
+static int session_sync(tcu_session* s) { return sync_stream(s->stream, s->w->err); }
 
 static int upload_pt(tcu_session* s) {
-  CK(cudaMemcpyAsync(s->w.pt, s->pages.data(), s->pages.size() * sizeof(int), cudaMemcpyHostToDevice, s->stream));
+  CK(cudaMemcpyAsync(s->w->pt, s->pages.data(), s->pages.size() * sizeof(int), cudaMemcpyHostToDevice, s->stream));
   return TCU_OK;
 }
 
@@ -1929,7 +2169,7 @@ static int enqueue_logprob_block(const tcu_model* m, Work* w, const float* blk, 
 // into the chunk's attention/SwiGLU buffer (free once the chunk's layers
 // ran), then enqueue_logprob_block (mlx_native.go:436-478 in batches).
 static int enqueue_logprob_chunk(const tcu_model* m, Work* w, int c, int i0, const LogprobReq& lp, cudaStream_t s) {
-  const size_t cap_rows = (size_t)w->rows * (m->d + m->ff) / (size_t)m->V;
+  const size_t cap_rows = (size_t)w->rows * (m->aw + m->ff) / (size_t)m->V;
   const int nb = (int)std::min<size_t>(LP_ROWS, cap_rows);
   if (nb < 1) return fail(TCU_EUNSUP, "vocabulary of %d is too large for the probability rows of this workspace", m->V);
   float* blk = w->ah;
@@ -1958,28 +2198,30 @@ static int session_run(tcu_session* s, int prefix, const int32_t* tokens, int n,
   TRY(prepare_pages(m, s->pool, s->pages, prefix, prefix + n, s->stream));
   TRY(upload_pt(s));
   if (n == 1 && !all_logits) {
-    CK(cudaMemcpyAsync(s->w.tokens, tokens, sizeof(int), cudaMemcpyHostToDevice, s->stream));
-    CK(cudaMemcpyAsync(s->w.pos, &prefix, sizeof(int), cudaMemcpyHostToDevice, s->stream));
-    CK(cudaMemsetAsync(s->w.argmax, 0, sizeof(unsigned long long), s->stream));
+    CK(cudaMemcpyAsync(s->w->tokens, tokens, sizeof(int), cudaMemcpyHostToDevice, s->stream));
+    CK(cudaMemcpyAsync(s->w->pos, &prefix, sizeof(int), cudaMemcpyHostToDevice, s->stream));
+    CK(cudaMemsetAsync(s->w->argmax, 0, sizeof(unsigned long long), s->stream));
     const int split = SPLIT_PAGES * m->P;
-    enqueue_decode(m, s->pool, &s->w, 1, false, (prefix + 1 + split - 1) / split, true, s->stream);
+    enqueue_decode(m, s->pool, s->w, 1, false, (prefix + 1 + split - 1) / split, true, s->stream);
     CK(cudaGetLastError());
-    if (lp) TRY(enqueue_logprob_block(m, &s->w, s->w.logits, 1, 0, *lp, s->stream));
+    TRY(comm_check());
+    if (lp) TRY(enqueue_logprob_block(m, s->w, s->w->logits, 1, 0, *lp, s->stream));
     return TCU_OK;
   }
   for (int off = 0; off < n; off += CHUNK) {
     const int c = std::min(CHUNK, n - off);
-    CK(cudaMemcpyAsync(s->w.tokens, tokens + off, c * sizeof(int), cudaMemcpyHostToDevice, s->stream));
-    enqueue_prefill(m, s->pool, &s->w, c, prefix + off, s->stream);
+    CK(cudaMemcpyAsync(s->w->tokens, tokens + off, c * sizeof(int), cudaMemcpyHostToDevice, s->stream));
+    enqueue_prefill(m, s->pool, s->w, c, prefix + off, s->stream);
     CK(cudaGetLastError());
-    if (lp) TRY(enqueue_logprob_chunk(m, &s->w, c, off, *lp, s->stream));
+    TRY(comm_check());
+    if (lp) TRY(enqueue_logprob_chunk(m, s->w, c, off, *lp, s->stream));
     if (all_logits) {
       for (int j = 0; j < c; j++) {
-        enqueue_head_row(m, &s->w, j, s->w.logits, s->stream);
-        CK(cudaMemcpyAsync(all_logits + (size_t)(off + j) * m->V, s->w.logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, s->stream));
+        enqueue_head_row(m, s->w, j, s->w->logits, s->stream);
+        CK(cudaMemcpyAsync(all_logits + (size_t)(off + j) * m->V, s->w->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, s->stream));
       }
     } else if (off + c == n) {
-      enqueue_head_row(m, &s->w, c - 1, s->w.logits, s->stream);
+      enqueue_head_row(m, s->w, c - 1, s->w->logits, s->stream);
     }
     CK(cudaGetLastError());
   }
@@ -2028,7 +2270,7 @@ static int session_graph(tcu_session* s, int splits) {
   cudaGraph_t g;
   s->prof.used = 0;
   CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeRelaxed));
-  enqueue_decode(s->m, s->pool, &s->w, 1, true, splits, true, s->stream);
+  enqueue_decode(s->m, s->pool, s->w, 1, true, splits, true, s->stream);
   cudaError_t e = cudaStreamEndCapture(s->stream, &g);
   s->graph_events = s->prof.used;
   s->graph_prof = s->prof.on;
@@ -2148,7 +2390,7 @@ static int enqueue_candidates(const tcu_model* m, Work* w, const float* logits, 
                  (const double*)(w->pen_buf + o_terms)};
   const int max_ids = std::max(1, h.max_ids);
   const size_t smem = (size_t)max_ids * 12 + ((size_t)m->V + 31) / 32 * 8;
-  if (smem > 227 * 1024) return fail(TCU_EINVAL, "penalised ids and vocabulary exceed the candidates kernel's shared memory");
+  if (smem > 224 * 1024) return fail(TCU_EINVAL, "penalised ids and vocabulary exceed the candidates kernel's shared memory");
   k_candidates_rows<<<rows, 1024, smem, s>>>(logits, m->V, m->V, pr, max_ids, k, w->cd_ids, w->cd_vals);
   NOTE("k_candidates_rows");
   CK(cudaGetLastError());
@@ -2179,7 +2421,50 @@ int tcu_device_count(int32_t* count) {
 
 int tcu_stablelm_load(const tcu_stablelm_config* config, const tcu_tensor* tensors, int32_t n_tensors, const tcu_load_options* options,
                       tcu_model** out) {
-  return stablelm_load(config, tensors, n_tensors, options, out);
+  return stablelm_load(config, tensors, n_tensors, options, nullptr, out);
+}
+
+int tcu_tp_unique_id(uint8_t* id) {
+  if (!id) return fail(TCU_EINVAL, "null argument");
+  const NcclApi* api = nccl_api();
+  if (!api) return fail(TCU_EUNSUP, "tensor parallelism needs NCCL (libnccl.so.2 not found)");
+  ncclUniqueId u;
+  const ncclResult_t r = api->get_unique_id(&u);
+  if (r != ncclSuccess) return fail(TCU_ECUDA, "ncclGetUniqueId: %s", api->error_string(r));
+  memcpy(id, &u, sizeof u);
+  return TCU_OK;
+}
+
+int tcu_tp_plan(const tcu_stablelm_config* config, int32_t world, int32_t rank, int32_t* out) {
+  if (!config || !out) return fail(TCU_EINVAL, "null argument");
+  TpSlice sl;
+  TRY(tp_slice(config, world, rank, &sl));
+  const int32_t v[6] = {sl.h0, sl.nh, sl.kv0, sl.nkv, sl.f0, sl.nf};
+  memcpy(out, v, sizeof v);
+  return TCU_OK;
+}
+
+int tcu_stablelm_load_tp(const tcu_stablelm_config* config, const tcu_tensor* tensors, int32_t n_tensors, const tcu_load_options* options,
+                         const tcu_tp_options* tp, tcu_model** out) {
+  if (!config || !tp || !out) return fail(TCU_EINVAL, "null argument");
+  TpSlice sl;
+  TRY(tp_slice(config, tp->world, tp->rank, &sl));
+  const NcclApi* api = nullptr;
+  if (tp->world > 1 && !(api = nccl_api())) return fail(TCU_EUNSUP, "tensor parallelism needs NCCL (libnccl.so.2 not found)");
+  TRY(stablelm_load(config, tensors, n_tensors, options, &sl, out));
+  if (tp->world > 1) {
+    tcu_model* m = *out;
+    ncclUniqueId u;
+    memcpy(&u, tp->nccl_id, sizeof u);
+    const ncclResult_t r = api->comm_init_rank(&m->tp_comm, tp->world, u, tp->rank);
+    if (r != ncclSuccess) {
+      m->tp_comm = nullptr;
+      model_release(m);
+      *out = nullptr;
+      return fail(TCU_ECUDA, "ncclCommInitRank: %s", api->error_string(r));
+    }
+  }
+  return TCU_OK;
 }
 
 int tcu_llama_load(const void* checkpoint, uint64_t nbytes, const tcu_load_options* options, tcu_model** out) {
@@ -2228,10 +2513,12 @@ int tcu_session_new(tcu_model* m, int32_t kv_dtype, tcu_session** out) {
   s->m = m;
   s->half = kv_dtype == TCU_F16;
   int rc = pool_get(m, s->half, &s->pool);
-  if (rc == TCU_OK) rc = work_init(m, &s->w, CHUNK, 1, 1, m->max_pos + 1);
+  if (rc == TCU_OK) rc = work_take(m, &s->w, CHUNK, 1, 1, m->max_pos + 1);
   if (rc == TCU_OK && cudaStreamCreateWithFlags(&s->own_stream, cudaStreamNonBlocking) != cudaSuccess) rc = fail(TCU_ECUDA, "stream create");
   s->stream = s->own_stream;
   if (rc != TCU_OK) {
+    if (s->own_stream) cudaStreamDestroy(s->own_stream);
+    work_give(m, s->w);
     delete s;
     return rc;
   }
@@ -2251,6 +2538,7 @@ int tcu_session_free(tcu_session* s) {
   release_pages(s->m, s->pool, s->pages, 0);
   if (s->graph) cudaGraphExecDestroy(s->graph);
   if (s->own_stream) cudaStreamDestroy(s->own_stream);
+  work_give(s->m, s->w);
   {
     std::lock_guard<std::mutex> g(s->m->mu);
     s->m->sessions--;
@@ -2272,7 +2560,7 @@ int tcu_session_forward(tcu_session* s, int32_t prefix, const int32_t* tokens, i
   ProfScope ps(s);
   int rc = session_run(s, prefix, tokens, n, nullptr);
   if (rc == TCU_OK && want_logits) {
-    cudaError_t e = cudaMemcpyAsync(logits_out, s->w.logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToHost, s->stream);
+    cudaError_t e = cudaMemcpyAsync(logits_out, s->w->logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToHost, s->stream);
     if (e != cudaSuccess) rc = fail(TCU_ECUDA, "logits copy: %s", cudaGetErrorString(e));
   }
   return session_finish(s, rc, prefix + n);
@@ -2313,31 +2601,30 @@ static int launch_mega(tcu_session* s) {
   a.fnb = m->fnb;
   a.rope = m->rope;
   a.kv = s->pool->view();
-  a.page_table = s->w.pt;
+  a.page_table = s->w->pt;
   a.split = m->mega_split;
-  a.max_splits = s->w.max_splits;
+  a.max_splits = s->w->max_splits;
   a.scale = (float)sqrt((double)m->hd);
-  a.pos = s->w.pos;
-  a.keys = s->w.keys;
-  a.step = s->w.step;
-  a.out_tokens = s->w.out_tokens;
-  a.out_count = s->w.out_count;
-  a.logits = s->w.logits;
-  a.xl = s->w.xl;
-  a.qkv = s->w.qkv;
-  a.part = s->w.part;
-  a.counters = s->w.counters;
-  a.adig = s->w.adig;
-  a.asx = s->w.asx;
-  a.asx_stride = s->w.asx_stride;
+  a.pos = s->w->pos;
+  a.keys = s->w->keys;
+  a.step = s->w->step;
+  a.out_tokens = s->w->out_tokens;
+  a.out_count = s->w->out_count;
+  a.logits = s->w->logits;
+  a.xl = s->w->xl;
+  a.qkv = s->w->qkv;
+  a.part = s->w->part;
+  a.counters = s->w->counters;
+  a.adig = s->w->adig;
+  a.asx = s->w->asx;
+  a.asx_stride = s->w->asx_stride;
   a.att_warp = m->mega_att_warp;
-  a.grab = s->w.grab;
-  a.done = s->w.done;
+  a.grab = s->w->grab;
+  a.done = s->w->done;
   mega_dn_scales(m, &a.dn_sstride, &a.dn_soff);
-  a.xdn = s->w.xdn;
-  a.err = s->w.err;
+  a.xdn = s->w->xdn;
+  a.err = s->w->err;
   a.hold_layer = s->hold_layer;
-  a.l2_prefetch = m->mega_prefetch ? 1 : 0;
   a.slot_bytes = m->mega_slot_bytes;
   a.nslots = m->mega_slots;
   a.off_x = m->mega_off[0];
@@ -2384,17 +2671,17 @@ int tcu_session_generate_greedy(tcu_session* s, int32_t prefix, const int32_t* t
     const char* hold = getenv("TCU_TEST_HOLD_ARRIVAL");
     s->hold_layer = (hold && *hold) ? std::max(-1, std::min(m->L - 1, atoi(hold))) : -1;
     const int first = prefix + n;
-    CK(cudaMemcpyAsync(s->w.pos, &first, sizeof(int), cudaMemcpyHostToDevice, s->stream));
-    CK(cudaMemcpyAsync(s->w.keys, s->w.argmax, sizeof(unsigned long long), cudaMemcpyDeviceToDevice, s->stream));
-    CK(cudaMemsetAsync(s->w.keys + 1, 0, sizeof(unsigned long long), s->stream));
-    CK(cudaMemsetAsync(s->w.step, 0, sizeof(int), s->stream));
-    CK(cudaMemsetAsync(s->w.out_count, 0, sizeof(int), s->stream));
+    CK(cudaMemcpyAsync(s->w->pos, &first, sizeof(int), cudaMemcpyHostToDevice, s->stream));
+    CK(cudaMemcpyAsync(s->w->keys, s->w->argmax, sizeof(unsigned long long), cudaMemcpyDeviceToDevice, s->stream));
+    CK(cudaMemsetAsync(s->w->keys + 1, 0, sizeof(unsigned long long), s->stream));
+    CK(cudaMemsetAsync(s->w->step, 0, sizeof(int), s->stream));
+    CK(cudaMemsetAsync(s->w->out_count, 0, sizeof(int), s->stream));
     // Work and arrival counters start at zero (a run cut short by a timeout
     // may have left them set).
     const size_t nctl = (size_t)2 * (m->L + 1) * MG_CTL * sizeof(int);
-    CK(cudaMemsetAsync(s->w.grab, 0, nctl, s->stream));
-    CK(cudaMemsetAsync(s->w.done, 0, nctl, s->stream));
-    CK(cudaMemsetAsync(s->w.counters, 0, (size_t)m->KVH * sizeof(int), s->stream));
+    CK(cudaMemsetAsync(s->w->grab, 0, nctl, s->stream));
+    CK(cudaMemsetAsync(s->w->done, 0, nctl, s->stream));
+    CK(cudaMemsetAsync(s->w->counters, 0, (size_t)m->KVH * sizeof(int), s->stream));
     for (int i = 1; rc == TCU_OK && i < steps; i++) {
       rc = launch_mega(s);
       if (rc == TCU_OK && s->prof.on) {
@@ -2403,26 +2690,38 @@ int tcu_session_generate_greedy(tcu_session* s, int32_t prefix, const int32_t* t
       }
     }
     if (rc == TCU_OK) {
-      k_finish_mega<<<1, 32, 0, s->stream>>>(s->w.keys, s->w.step, s->w.out_tokens, s->w.out_count);
+      k_finish_mega<<<1, 32, 0, s->stream>>>(s->w->keys, s->w->step, s->w->out_tokens, s->w->out_count);
       NOTE("k_finish_mega");
-      cudaError_t e = cudaMemcpyAsync(out_tokens, s->w.out_tokens, (size_t)steps * sizeof(int), cudaMemcpyDeviceToHost, s->stream);
+      cudaError_t e = cudaMemcpyAsync(out_tokens, s->w->out_tokens, (size_t)steps * sizeof(int), cudaMemcpyDeviceToHost, s->stream);
       if (e != cudaSuccess) rc = fail(TCU_ECUDA, "token copy: %s", cudaGetErrorString(e));
     }
     return session_finish(s, rc, end);
   }
   if (rc == TCU_OK) {
     const int last = prefix + n - 1;
-    cudaMemcpyAsync(s->w.pos, &last, sizeof(int), cudaMemcpyHostToDevice, s->stream);
-    NOTE("cudaMemcpyAsync(s->w.pos, &last, sizeof(");
-    cudaMemsetAsync(s->w.out_count, 0, sizeof(int), s->stream);
-    NOTE("cudaMemsetAsync(s->w.out_count, 0, sizeo");
+    cudaMemcpyAsync(s->w->pos, &last, sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    NOTE("cudaMemcpyAsync(s->w->pos, &last, sizeof(");
+    cudaMemsetAsync(s->w->out_count, 0, sizeof(int), s->stream);
+    NOTE("cudaMemsetAsync(s->w->out_count, 0, sizeo");
     const int split = SPLIT_PAGES * m->P;
     int splits = (end + split - 1) / split;
     int bucket = 1;
     while (bucket < splits) bucket *= 2;
-    bucket = std::min(bucket, s->w.max_splits);
-    if (steps > 1) rc = session_graph(s, bucket);
+    bucket = std::min(bucket, s->w->max_splits);
+    // Tensor-parallel models enqueue each step (their all-reduce stays out of
+    // captured graphs); others replay one captured step.
+    const bool tp = m->tp_world > 1;
+    if (steps > 1 && !tp) rc = session_graph(s, bucket);
     for (int i = 1; rc == TCU_OK && i < steps; i++) {
+      if (tp) {
+        enqueue_decode(m, s->pool, s->w, 1, true, bucket, true, s->stream);
+        rc = comm_check();
+        if (rc == TCU_OK && s->prof.on) {
+          rc = session_sync(s);
+          prof_collect(s);
+        }
+        continue;
+      }
       cudaError_t e = cudaGraphLaunch(s->graph, s->stream);
       if (e != cudaSuccess) rc = fail(TCU_ECUDA, "graph launch: %s", cudaGetErrorString(e));
       if (rc == TCU_OK && s->prof.on) {
@@ -2432,9 +2731,9 @@ int tcu_session_generate_greedy(tcu_session* s, int32_t prefix, const int32_t* t
       }
     }
     if (rc == TCU_OK) {
-      k_finish_greedy<<<1, 32, 0, s->stream>>>(s->w.argmax, s->w.out_tokens, s->w.out_cap, s->w.out_count, 1);
+      k_finish_greedy<<<1, 32, 0, s->stream>>>(s->w->argmax, s->w->out_tokens, s->w->out_cap, s->w->out_count, 1);
       NOTE("k_finish_greedy");
-      cudaError_t e = cudaMemcpyAsync(out_tokens, s->w.out_tokens, (size_t)steps * sizeof(int), cudaMemcpyDeviceToHost, s->stream);
+      cudaError_t e = cudaMemcpyAsync(out_tokens, s->w->out_tokens, (size_t)steps * sizeof(int), cudaMemcpyDeviceToHost, s->stream);
       if (e != cudaSuccess) rc = fail(TCU_ECUDA, "token copy: %s", cudaGetErrorString(e));
     }
   }
@@ -2449,12 +2748,12 @@ int tcu_session_shortlist(tcu_session* s, int32_t k, int32_t* ids, float* logits
   CK(cudaSetDevice(s->m->device));
   const int kk = std::min<int>(k, s->m->V);
   const size_t smem = ((size_t)s->m->V + 31) / 32 * 4;  // attribute set at load (sampling_smem_attrs)
-  k_shortlist<<<1, 1024, smem, s->stream>>>(s->w.logits, s->m->V, kk, s->w.sl_ids, s->w.sl_vals, s->w.sl_lse);
+  k_shortlist<<<1, 1024, smem, s->stream>>>(s->w->logits, s->m->V, kk, s->w->sl_ids, s->w->sl_vals, s->w->sl_lse);
   NOTE("k_shortlist");
   CK(cudaGetLastError());
-  CK(cudaMemcpyAsync(ids, s->w.sl_ids, kk * sizeof(int), cudaMemcpyDeviceToHost, s->stream));
-  CK(cudaMemcpyAsync(logits, s->w.sl_vals, kk * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
-  CK(cudaMemcpyAsync(logsumexp, s->w.sl_lse, sizeof(double), cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaMemcpyAsync(ids, s->w->sl_ids, kk * sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaMemcpyAsync(logits, s->w->sl_vals, kk * sizeof(float), cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaMemcpyAsync(logsumexp, s->w->sl_lse, sizeof(double), cudaMemcpyDeviceToHost, s->stream));
   TRY(session_sync(s));
   *n_out = kk;
   return TCU_OK;
@@ -2473,7 +2772,7 @@ int tcu_session_forward_logprobs(tcu_session* s, int32_t prefix, const int32_t* 
   const LogprobReq lp{targets, count, chosen, top_ids, top_logprobs};
   int rc = session_run(s, prefix, tokens, n, nullptr, &lp);
   if (rc == TCU_OK && logits_out) {
-    cudaError_t e = cudaMemcpyAsync(logits_out, s->w.logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToHost, s->stream);
+    cudaError_t e = cudaMemcpyAsync(logits_out, s->w->logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToHost, s->stream);
     if (e != cudaSuccess) rc = fail(TCU_ECUDA, "logits copy: %s", cudaGetErrorString(e));
   }
   return session_finish(s, rc, prefix + n);
@@ -2492,9 +2791,9 @@ int tcu_session_sample_candidates(tcu_session* s, const int32_t* history, int32_
   const int kk = std::min<int>(k, s->m->V);
   PenaltyHost h;
   penalties_add_row(h, history, n_history, pp, s->m->V);
-  TRY(enqueue_candidates(s->m, &s->w, s->w.logits, 1, h, kk, s->stream));
-  CK(cudaMemcpyAsync(ids, s->w.cd_ids, kk * sizeof(int), cudaMemcpyDeviceToHost, s->stream));
-  CK(cudaMemcpyAsync(scores, s->w.cd_vals, kk * sizeof(double), cudaMemcpyDeviceToHost, s->stream));
+  TRY(enqueue_candidates(s->m, s->w, s->w->logits, 1, h, kk, s->stream));
+  CK(cudaMemcpyAsync(ids, s->w->cd_ids, kk * sizeof(int), cudaMemcpyDeviceToHost, s->stream));
+  CK(cudaMemcpyAsync(scores, s->w->cd_vals, kk * sizeof(double), cudaMemcpyDeviceToHost, s->stream));
   TRY(session_sync(s));
   *n_out = kk;
   return TCU_OK;
@@ -2511,7 +2810,7 @@ int tcu_session_fork(tcu_session* s, tcu_session** child) {
   c->length = s->length;
   // The child starts with the parent's last logits row (sessions.go:36-72
   // keeps probability rows; the next Forward recomputes them anyway).
-  CK(cudaMemcpyAsync(c->w.logits, s->w.logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToDevice, c->stream));
+  CK(cudaMemcpyAsync(c->w->logits, s->w->logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToDevice, c->stream));
   CK(cudaStreamSynchronize(c->stream));
   *child = c;
   return TCU_OK;
@@ -2608,7 +2907,7 @@ int tcu_branches_open(tcu_session* s, int32_t prefix, int32_t count, tcu_branche
   b->s = s;
   b->prefix = prefix;
   b->count = count;
-  int rc = work_init(s->m, &b->w, count, count, count, 2);
+  int rc = work_take(s->m, &b->w, count, count, count, 2);
   if (rc != TCU_OK) {
     delete b;
     return rc;
@@ -2633,36 +2932,37 @@ int tcu_branches_forward(tcu_branches* b, const int32_t* tokens, float* rows_out
   if (b->prefix + b->step >= m->max_pos) return fail(TCU_EINVAL, "invalid branch batch or context length");
   TRY(check_tokens(m, tokens, b->count));
   CK(cudaSetDevice(m->device));
-  ProfScope ps(s, b->w.err);
+  ProfScope ps(s, b->w->err);
   const int pos = b->prefix + b->step;
   int rc = TCU_OK;
-  std::vector<int> pt((size_t)b->count * b->w.pt_stride, 0);
+  std::vector<int> pt((size_t)b->count * b->w->pt_stride, 0);
   for (int i = 0; rc == TCU_OK && i < b->count; i++) {
     rc = prepare_pages(m, s->pool, b->pages[i], pos, pos + 1, s->stream);
-    std::copy(b->pages[i].begin(), b->pages[i].end(), pt.begin() + (size_t)i * b->w.pt_stride);
+    std::copy(b->pages[i].begin(), b->pages[i].end(), pt.begin() + (size_t)i * b->w->pt_stride);
   }
   if (rc == TCU_OK) {
     std::vector<int> posv(b->count, pos);
-    cudaMemcpyAsync(b->w.pt, pt.data(), pt.size() * sizeof(int), cudaMemcpyHostToDevice, s->stream);
-    NOTE("cudaMemcpyAsync(b->w.pt, pt.data(), pt.s");
-    cudaMemcpyAsync(b->w.pos, posv.data(), b->count * sizeof(int), cudaMemcpyHostToDevice, s->stream);
-    NOTE("cudaMemcpyAsync(b->w.pos, posv.data(), b");
-    cudaMemcpyAsync(b->w.tokens, tokens, b->count * sizeof(int), cudaMemcpyHostToDevice, s->stream);
-    NOTE("cudaMemcpyAsync(b->w.tokens, tokens, b->");
-    cudaMemsetAsync(b->w.argmax, 0, b->count * sizeof(unsigned long long), s->stream);
-    NOTE("cudaMemsetAsync(b->w.argmax, 0, b->count");
+    cudaMemcpyAsync(b->w->pt, pt.data(), pt.size() * sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    NOTE("cudaMemcpyAsync(b->w->pt, pt.data(), pt.s");
+    cudaMemcpyAsync(b->w->pos, posv.data(), b->count * sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    NOTE("cudaMemcpyAsync(b->w->pos, posv.data(), b");
+    cudaMemcpyAsync(b->w->tokens, tokens, b->count * sizeof(int), cudaMemcpyHostToDevice, s->stream);
+    NOTE("cudaMemcpyAsync(b->w->tokens, tokens, b->");
+    cudaMemsetAsync(b->w->argmax, 0, b->count * sizeof(unsigned long long), s->stream);
+    NOTE("cudaMemsetAsync(b->w->argmax, 0, b->count");
     const int split = SPLIT_PAGES * m->P;
     // Whole splits inside the prefix's full pages are shared by every branch.
-    b->w.shared_splits = (b->prefix / m->P) / SPLIT_PAGES;
-    enqueue_decode(m, s->pool, &b->w, b->count, false, (pos + 1 + split - 1) / split, true, s->stream);
+    b->w->shared_splits = (b->prefix / m->P) / SPLIT_PAGES;
+    enqueue_decode(m, s->pool, b->w, b->count, false, (pos + 1 + split - 1) / split, true, s->stream);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) rc = fail(TCU_ECUDA, "launch: %s", cudaGetErrorString(e));
+    if (rc == TCU_OK) rc = comm_check();
     if (rc == TCU_OK && rows_out) {
-      e = cudaMemcpyAsync(rows_out, b->w.logits, (size_t)b->count * m->V * 4, cudaMemcpyDeviceToHost, s->stream);
+      e = cudaMemcpyAsync(rows_out, b->w->logits, (size_t)b->count * m->V * 4, cudaMemcpyDeviceToHost, s->stream);
       if (e != cudaSuccess) rc = fail(TCU_ECUDA, "rows copy: %s", cudaGetErrorString(e));
     }
   }
-  if (rc == TCU_OK) rc = sync_stream(s->stream, b->w.err);
+  if (rc == TCU_OK) rc = sync_stream(s->stream, b->w->err);
   if (rc == TCU_OK) prof_collect(s);
   s->prof.used = 0;
   if (rc != TCU_OK) {
@@ -2682,14 +2982,15 @@ int tcu_branches_argmax(tcu_branches* b, int32_t* ids) {
   if (b->closed) return fail(TCU_ECLOSED, "token branches are closed");
   if (b->step == 0) return fail(TCU_EINVAL, "no rows: forward first");
   std::vector<unsigned long long> keys(b->count);
-  CK(cudaMemcpy(keys.data(), b->w.argmax, b->count * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(keys.data(), b->w->argmax, b->count * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
   for (int i = 0; i < b->count; i++) ids[i] = (int)(0xffffffffu - (uint32_t)(keys[i] & 0xffffffffu));
   return TCU_OK;
 }
 
 int tcu_branches_close(tcu_branches* b) {
   if (!b) return TCU_OK;
-  branches_release(b);
+  branches_release(b);  // synchronises the session's stream
+  work_give(b->s->m, b->w);
   delete b;
   return TCU_OK;
 }
@@ -2704,8 +3005,8 @@ int tcu_branches_close(tcu_branches* b) {
 struct tcu_batch {
   tcu_model* m = nullptr;
   int max_rows = 0;
-  int last_rows = 0;  // rows of the last successful step (their logits stay in w.logits)
-  Work w;
+  int last_rows = 0;  // rows of the last successful step (their logits stay in w->logits)
+  Work* w = nullptr;  // from the model's workspace pool (work_take)
   cudaStream_t stream = nullptr;
 };
 
@@ -2718,11 +3019,12 @@ int tcu_batch_open(tcu_model* m, int32_t max_rows, tcu_batch** out) {
   tcu_batch* b = new tcu_batch();
   b->m = m;
   b->max_rows = max_rows;
-  int rc = work_init(m, &b->w, max_rows, max_rows, max_rows, 2);
+  int rc = work_take(m, &b->w, max_rows, max_rows, max_rows, 2);
   if (rc == TCU_OK && cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking) != cudaSuccess)
     rc = fail(TCU_ECUDA, "stream creation failed");
   if (rc != TCU_OK) {
     if (b->stream) cudaStreamDestroy(b->stream);
+    work_give(m, b->w);
     delete b;
     return rc;
   }
@@ -2749,39 +3051,40 @@ int tcu_batch_forward(tcu_batch* b, tcu_session* const* sessions, const int32_t*
   }
   TRY(check_tokens(m, tokens, n));
   CK(cudaSetDevice(m->device));
-  ProfScope ps(nullptr, b->w.err);
+  ProfScope ps(nullptr, b->w->err);
   // Each session's earlier work precedes this step.
   for (int i = 0; i < n; i++) CK(cudaStreamSynchronize(sessions[i]->stream));
   int rc = TCU_OK, max_len = 0;
-  std::vector<int> pt((size_t)n * b->w.pt_stride, 0), posv(n);
+  std::vector<int> pt((size_t)n * b->w->pt_stride, 0), posv(n);
   for (int i = 0; rc == TCU_OK && i < n; i++) {
     tcu_session* s = sessions[i];
     rc = prepare_pages(m, pool, s->pages, s->length, s->length + 1, b->stream);
-    std::copy(s->pages.begin(), s->pages.end(), pt.begin() + (size_t)i * b->w.pt_stride);
+    std::copy(s->pages.begin(), s->pages.end(), pt.begin() + (size_t)i * b->w->pt_stride);
     posv[i] = s->length;
     max_len = std::max(max_len, s->length + 1);
   }
   if (rc == TCU_OK) {
-    cudaMemcpyAsync(b->w.pt, pt.data(), pt.size() * sizeof(int), cudaMemcpyHostToDevice, b->stream);
-    cudaMemcpyAsync(b->w.pos, posv.data(), n * sizeof(int), cudaMemcpyHostToDevice, b->stream);
-    cudaMemcpyAsync(b->w.tokens, tokens, n * sizeof(int), cudaMemcpyHostToDevice, b->stream);
-    cudaMemsetAsync(b->w.argmax, 0, n * sizeof(unsigned long long), b->stream);
+    cudaMemcpyAsync(b->w->pt, pt.data(), pt.size() * sizeof(int), cudaMemcpyHostToDevice, b->stream);
+    cudaMemcpyAsync(b->w->pos, posv.data(), n * sizeof(int), cudaMemcpyHostToDevice, b->stream);
+    cudaMemcpyAsync(b->w->tokens, tokens, n * sizeof(int), cudaMemcpyHostToDevice, b->stream);
+    cudaMemsetAsync(b->w->argmax, 0, n * sizeof(unsigned long long), b->stream);
     const int split = SPLIT_PAGES * m->P;
-    b->w.shared_splits = 0;
-    enqueue_decode(m, pool, &b->w, n, false, (max_len + split - 1) / split, true, b->stream);
+    b->w->shared_splits = 0;
+    enqueue_decode(m, pool, b->w, n, false, (max_len + split - 1) / split, true, b->stream);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) rc = fail(TCU_ECUDA, "launch: %s", cudaGetErrorString(e));
+    if (rc == TCU_OK) rc = comm_check();
     if (rc == TCU_OK && rows_out) {
-      e = cudaMemcpyAsync(rows_out, b->w.logits, (size_t)n * m->V * 4, cudaMemcpyDeviceToHost, b->stream);
+      e = cudaMemcpyAsync(rows_out, b->w->logits, (size_t)n * m->V * 4, cudaMemcpyDeviceToHost, b->stream);
       if (e != cudaSuccess) rc = fail(TCU_ECUDA, "rows copy: %s", cudaGetErrorString(e));
     }
   }
   std::vector<unsigned long long> keys(n);
   if (rc == TCU_OK && ids_out) {
-    cudaError_t e = cudaMemcpyAsync(keys.data(), b->w.argmax, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost, b->stream);
+    cudaError_t e = cudaMemcpyAsync(keys.data(), b->w->argmax, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost, b->stream);
     if (e != cudaSuccess) rc = fail(TCU_ECUDA, "argmax copy: %s", cudaGetErrorString(e));
   }
-  if (rc == TCU_OK) rc = sync_stream(b->stream, b->w.err);
+  if (rc == TCU_OK) rc = sync_stream(b->stream, b->w->err);
   if (rc != TCU_OK) return rc;  // lengths unchanged: the new positions are rewritten next time
   if (ids_out)
     for (int i = 0; i < n; i++) ids_out[i] = (int)(0xffffffffu - (uint32_t)(keys[i] & 0xffffffffu));
@@ -2804,19 +3107,20 @@ int tcu_batch_sample_candidates(tcu_batch* b, int32_t n, const int32_t* history,
     off += (size_t)history_len[i];
   }
   CK(cudaSetDevice(b->m->device));
-  TRY(enqueue_candidates(b->m, &b->w, b->w.logits, n, h, k, b->stream));
-  CK(cudaMemcpyAsync(ids, b->w.cd_ids, (size_t)n * k * sizeof(int), cudaMemcpyDeviceToHost, b->stream));
-  CK(cudaMemcpyAsync(scores, b->w.cd_vals, (size_t)n * k * sizeof(double), cudaMemcpyDeviceToHost, b->stream));
-  return sync_stream(b->stream, b->w.err);
+  TRY(enqueue_candidates(b->m, b->w, b->w->logits, n, h, k, b->stream));
+  CK(cudaMemcpyAsync(ids, b->w->cd_ids, (size_t)n * k * sizeof(int), cudaMemcpyDeviceToHost, b->stream));
+  CK(cudaMemcpyAsync(scores, b->w->cd_vals, (size_t)n * k * sizeof(double), cudaMemcpyDeviceToHost, b->stream));
+  return sync_stream(b->stream, b->w->err);
 }
 
 int tcu_batch_close(tcu_batch* b) {
   if (!b) return TCU_OK;
+  cudaSetDevice(b->m->device);
   if (b->stream) {
-    cudaSetDevice(b->m->device);
     cudaStreamSynchronize(b->stream);
     cudaStreamDestroy(b->stream);
   }
+  work_give(b->m, b->w);
   delete b;
   return TCU_OK;
 }

@@ -156,5 +156,5 @@ def synth_stablelm(config=None, dtype="Q8_0", seed=0, std=0.02, device="cpu"):
 
 
 def prompt_ids(n, vocab, seed=0, low=3):
-    """n token ids uniform in [low, vocab)."""
+    """n token ids uniform in [low, vocab), as the benchmark configurations draw them."""
     return np.random.default_rng(seed).integers(low, vocab, size=n, dtype=np.int64).astype(np.int32)
