@@ -463,7 +463,9 @@ def run_config(args):
         box = [tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         tp_arg = (world, rank, box[0])
-    model = Model.load_stablelm(cfg, tensors, device=local, kv_pool_bytes=args.kv_pool_mb << 20, tp=tp_arg)
+    # An 8K-token sequence or a 4K prefix with 64 branches needs a few GB of
+    # f16 KV pages.
+    model = Model.load_stablelm(cfg, tensors, device=local, kv_pool_bytes=max(args.kv_pool_mb, 8192) << 20, tp=tp_arg)
     torch.cuda.empty_cache()
     cpu_tensors = tensors if (rank == 0 and world == 1 and args.cpu_baseline) else None
     del tensors
@@ -619,10 +621,12 @@ def run_config5(args):
     of prompt tokens on the waiting prompts in chunks, shortest remaining
     first (time to first token = first token ready - arrival), then all
     sessions with finished prompts advance together, one tcu_batch_forward.
-    Tokens are the greedy argmax (the reference's seeded top-k / top-p draw
-    runs on the host over the device shortlist and does not change the device
-    work per token). Under torchrun every rank serves its own share of the
-    arrivals (round robin); value = all ranks' tokens / the longest makespan."""
+    Tokens are sampled as configured (temperature 0.8, top-k 40, top-p 0.9):
+    every step's rows get their top-40 candidates on the device in one call
+    (tcu_batch_sample_candidates) and the host draws from them with a seeded
+    generator, as sampleWithOptions does after samplingCandidates. Under
+    torchrun every rank serves its own share of the arrivals (round robin);
+    value = all ranks' tokens / the longest makespan."""
     import torch
     import torch.distributed as dist
 
@@ -657,6 +661,19 @@ def run_config5(args):
         plen = np.clip(np.round(rng.lognormal(np.log(1024.0), 0.8, n)), 16, np.minimum(8000, ctx - 1 - olen)).astype(int)
         fork = rng.random(n) < 0.25
         return [(float(arrive[i]), int(plen[i]), int(olen[i]), bool(fork[i]), i) for i in range(n)]
+
+    TEMP, TOP_K, TOP_P = 0.8, 40, 0.9
+
+    def draw(ids, scores, rng):
+        """sampleWithOptions (sampling.go:165-211) after samplingCandidates:
+        temperature, top-p, then one uniform draw over the kept weights."""
+        p = np.exp((scores - scores[0]) / TEMP)
+        total = p.sum()
+        cut = int(np.searchsorted(np.cumsum(p), total * TOP_P)) + 1
+        p = p[:min(cut, len(p))]
+        x = rng.random() * p.sum()
+        k = int(np.searchsorted(np.cumsum(p), x))
+        return int(ids[min(k, len(p) - 1)])
 
     def serve(reqs, max_rows=256, budget=1024):
         """Each tick: admit arrivals, spend up to `budget` prompt tokens on
@@ -701,15 +718,18 @@ def run_config5(args):
                     tokens += k
                     if last:
                         done_ttft.append(time.perf_counter() - t0 - r["arr"])
-                        active.append({"s": r["s"], "left": r["olen"] - 1, "tok": int(np.argmax(row))})
+                        cid, csc = r["s"].sample_candidates([], TOP_K)  # the device top-k of the prompt's last row
+                        active.append({"s": r["s"], "left": r["olen"] - 1, "tok": draw(cid, csc, rng)})
                         tokens += 1
                 waiting = [r for r in waiting if r["done"] < len(r["ids"])]
                 if active:
-                    _, out = batch.forward([r["s"] for r in active], np.array([r["tok"] for r in active], np.int32), want_rows=False)
+                    batch.forward([r["s"] for r in active], np.array([r["tok"] for r in active], np.int32), want_rows=False)
+                    # Every row's top-k on the device in one call; the host draws.
+                    cids, cscores = batch.sample_candidates([[]] * len(active), TOP_K)
                     tokens += len(active)
                     keep = []
-                    for r, t in zip(active, out):
-                        r["tok"], r["left"] = int(t), r["left"] - 1
+                    for i, r in enumerate(active):
+                        r["tok"], r["left"] = draw(cids[i], cscores[i], rng), r["left"] - 1
                         if r["left"] > 0:
                             keep.append(r)
                         else:
@@ -740,7 +760,8 @@ def run_config5(args):
                 "dtype": "q8_0 weights, f32 activations, f16 KV",
                 "data": "synthetic (seeded N(0,0.02) weights quantised to Q8_0; seeded arrival trace and ids)",
                 "config": {"workload": f"config 5: {n} sessions, Poisson 8 req/s, prompt lognormal(median 1024) in [16, 8000], "
-                                       "output U[32,512], 25% forks, greedy tokens" + (f" [PROFILING CASE: {args.layers} layers]" if args.layers else ""),
+                                       "output U[32,512], 25% forks, sampled: temperature 0.8, top-k 40, top-p 0.9"
+                                       + (f" [PROFILING CASE: {args.layers} layers]" if args.layers else ""),
                            "parallelism": f"replicas x{world} (arrivals round robin)"},
                 "p50_ttft_ms": ttft_p50 * 1e3, "makespan_s": span_max, "tokens": float(tok_all.item()),
                 "clocks": clocks.summary(),

@@ -118,6 +118,26 @@ int tcu_stablelm_load_tp(const tcu_stablelm_config* config, const tcu_tensor* te
  * KV head, KV heads, first MLP row, MLP rows. Needs no GPU. */
 int tcu_tp_plan(const tcu_stablelm_config* config, int32_t world, int32_t rank, int32_t* out);
 
+/* GGUF StableLM checkpoints (readGGUF and loadStableGGUF, gguf.go:139-357):
+ * tcu_gguf_open memory-maps a GGUF v3 file, validates its header as the
+ * reference does (magic and version, counts, metadata types, tensor ranks,
+ * dimensions and types, alignment, bounds, overlap, the StableLM metadata and
+ * tensor set) and derives the configuration. The vocabulary size is the
+ * length of tokenizer.ggml.tokens; comparing that vocabulary with the
+ * tokenizer.json beside the file stays with the caller's tokenizer.
+ * tcu_gguf_tensor returns tensor i under its Hugging Face name (the inverse of
+ * ggufNames, gguf.go:250-255) with data pointing into the mapping, valid until
+ * tcu_gguf_close. tcu_gguf_load_stablelm uploads the model straight from the
+ * mapping (no host copy of the weights); tp may be NULL (the whole model) or a
+ * rank's share as for tcu_stablelm_load_tp. Needs no GPU except the load. */
+typedef struct tcu_gguf tcu_gguf;
+int tcu_gguf_open(const char* path, tcu_gguf** out);
+int tcu_gguf_config(const tcu_gguf* gguf, tcu_stablelm_config* config);
+int tcu_gguf_tensor_count(const tcu_gguf* gguf, int32_t* n);
+int tcu_gguf_tensor(const tcu_gguf* gguf, int32_t index, tcu_tensor* out);
+int tcu_gguf_load_stablelm(const tcu_gguf* gguf, const tcu_load_options* options, const tcu_tp_options* tp, tcu_model** out);
+int tcu_gguf_close(tcu_gguf* gguf);
+
 /* Replaces LoadModel/readWeights (model.go:90-166) for the legacy llama2.c
  * checkpoint (7 x int32 header then float32 tensors), and DefaultMLX /
  * LoadLlamaMLX (mlx_llama.go:37-53). */
@@ -224,6 +244,25 @@ typedef struct {
  * 16384 distinct ids may carry a penalty. */
 int tcu_session_sample_candidates(tcu_session* session, const int32_t* history, int32_t n_history, const tcu_penalties* penalties,
                                   int32_t k, int32_t* ids, double* scores, int32_t* n_out);
+
+/* SaveCache / LoadCache (cache_file.go:55-176) for a session, in the
+ * reference's TNYKV001 format: "TNYKV001", the header length, the JSON header
+ * {"model_sha256", "float16", "tokens"} as encoding/json writes it, the
+ * resident positions' KV in layer -> KV head -> keys, values order (float32
+ * little-endian or binary16 bits, cachePayload cache_file.go:203-258), then
+ * the SHA-256 of all of that. model_sha256 is the caller's model identity
+ * (modelIdentity, cache_file.go:26-48: the config and tensor bytes), tokens
+ * the session's resident token ids (n_tokens == its length).
+ * Save writes a 0600 temporary file beside `path`, syncs it and renames it
+ * over `path`. Load checks, in LoadCache's order, the format, header size,
+ * context length, token ids, model identity, KV precision, file size and
+ * checksum; only then do the restored positions replace the session's
+ * context (on any error the session is unchanged) and the tokens go to
+ * tokens[0 .. *n_tokens) (capacity entries available). */
+int tcu_session_save_cache(tcu_session* session, const char* path, const uint8_t* model_sha256, const int32_t* tokens,
+                           int32_t n_tokens);
+int tcu_session_load_cache(tcu_session* session, const char* path, const uint8_t* model_sha256, int32_t* tokens, int32_t capacity,
+                           int32_t* n_tokens);
 
 /* mlxForker.Fork (sessions.go:26-30, mlx_sessions.go:10-71): the child shares
  * every full KV page copy-free (reference counted) and copies only the

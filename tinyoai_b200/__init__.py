@@ -24,7 +24,7 @@ from . import _lib
 from ._lib import BackendError, check, lib
 from .checkpoint import as_bytes, dtype_code
 
-__all__ = ["Model", "Session", "Branches", "BackendError", "device_count", "read_values", "tp_unique_id", "tp_plan"]
+__all__ = ["Model", "Session", "Branches", "BackendError", "GGUF", "device_count", "read_values", "tp_unique_id", "tp_plan"]
 
 
 def _i32(a):
@@ -65,6 +65,57 @@ def _config_struct(config):
         config["num_attention_heads"], config["num_key_value_heads"], config["max_position_embeddings"],
         int(config.get("bos_token_id", 0)), int(config.get("eos_token_id", 0)), float(config["layer_norm_eps"]),
         float(config["rope_theta"]), float(config["partial_rotary_factor"]))
+
+
+class GGUF:
+    """A memory-mapped GGUF StableLM checkpoint (tcu_gguf_open: readGGUF and
+    loadStableGGUF's checks, gguf.go:139-357). .config is the derived
+    configuration; .tensors() lists (name, dtype, shape, nbytes) under the
+    Hugging Face names; .load() uploads the model from the mapping."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        check(lib().tcu_gguf_open(str(path).encode(), C.byref(h)))
+        self._h = h
+        c = _lib.StableLMConfig()
+        check(lib().tcu_gguf_config(self._h, C.byref(c)))
+        self.config = dict(model_type="stablelm", vocab_size=c.vocab_size, hidden_size=c.hidden_size,
+                           intermediate_size=c.intermediate_size, num_hidden_layers=c.num_hidden_layers,
+                           num_attention_heads=c.num_attention_heads, num_key_value_heads=c.num_key_value_heads,
+                           max_position_embeddings=c.max_position_embeddings, bos_token_id=c.bos_token_id,
+                           eos_token_id=c.eos_token_id, layer_norm_eps=c.layer_norm_eps, rope_theta=c.rope_theta,
+                           partial_rotary_factor=c.partial_rotary_factor, use_parallel_residual=True)
+
+    def tensors(self):
+        n = C.c_int32()
+        check(lib().tcu_gguf_tensor_count(self._h, C.byref(n)))
+        out = []
+        for i in range(n.value):
+            t = _lib.Tensor()
+            check(lib().tcu_gguf_tensor(self._h, i, C.byref(t)))
+            shape = tuple(t.shape[j] for j in range(t.ndim))
+            out.append((t.name.decode(), t.dtype, shape, C.string_at(t.data, t.nbytes)))
+        return out
+
+    def load(self, device=0, kv_page_tokens=0, kv_pool_bytes=0):
+        out = C.c_void_p()
+        opts = _options(device, kv_page_tokens, kv_pool_bytes)
+        check(lib().tcu_gguf_load_stablelm(self._h, C.byref(opts), None, C.byref(out)))
+        m = Model(out.value, "stablelm")
+        m.config = dict(self.config)
+        m.tp = None
+        return m
+
+    def close(self):
+        if self._h:
+            check(lib().tcu_gguf_close(self._h))
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
 
 
 def tp_unique_id():
@@ -246,6 +297,24 @@ class Session:
         check(lib().tcu_session_shortlist(self._h, k, ids.ctypes.data_as(C.POINTER(C.c_int32)),
                                           vals.ctypes.data_as(C.POINTER(C.c_float)), C.byref(lse), C.byref(n)))
         return ids[:n.value], vals[:n.value], lse.value
+
+    def save_cache(self, path, model_sha256, tokens):
+        """SaveCache (cache_file.go:55-104): the resident positions' KV to a
+        TNYKV001 file; tokens are the session's resident token ids."""
+        t, tp = _i32(tokens)
+        ident = (C.c_uint8 * 32).from_buffer_copy(bytes(model_sha256))
+        check(lib().tcu_session_save_cache(self._h, str(path).encode(), ident, tp, len(t)))
+
+    def load_cache(self, path, model_sha256):
+        """LoadCache (cache_file.go:108-176): restores a TNYKV001 file's
+        positions as this session's context; returns their token ids."""
+        ident = (C.c_uint8 * 32).from_buffer_copy(bytes(model_sha256))
+        cap = self.model.max_positions
+        out = np.empty(max(cap, 1), np.int32)
+        n = C.c_int32()
+        check(lib().tcu_session_load_cache(self._h, str(path).encode(), ident, out.ctypes.data_as(C.POINTER(C.c_int32)), cap,
+                                           C.byref(n)))
+        return out[:n.value]
 
     def fork(self):
         h = C.c_void_p()

@@ -21,6 +21,8 @@ EXPORTS = [
     "tcu_batch_open", "tcu_batch_forward", "tcu_batch_close", "tcu_shortlist_static", "tcu_read_values",
     "tcu_session_forward_logprobs", "tcu_session_sample_candidates", "tcu_batch_sample_candidates",
     "tcu_tp_unique_id", "tcu_stablelm_load_tp", "tcu_tp_plan",
+    "tcu_gguf_open", "tcu_gguf_config", "tcu_gguf_tensor_count", "tcu_gguf_tensor", "tcu_gguf_load_stablelm", "tcu_gguf_close",
+    "tcu_session_save_cache", "tcu_session_load_cache",
 ]
 
 
@@ -107,6 +109,14 @@ def lib():
         "tcu_stablelm_load_tp": ([C.POINTER(StableLMConfig), C.POINTER(Tensor), C.c_int32, C.POINTER(LoadOptions),
                                   C.POINTER(TpOptions), C.POINTER(P)], C.c_int),
         "tcu_tp_plan": ([C.POINTER(StableLMConfig), C.c_int32, C.c_int32, i32p], C.c_int),
+        "tcu_gguf_open": ([C.c_char_p, C.POINTER(P)], C.c_int),
+        "tcu_gguf_config": ([P, C.POINTER(StableLMConfig)], C.c_int),
+        "tcu_gguf_tensor_count": ([P, i32p], C.c_int),
+        "tcu_gguf_tensor": ([P, C.c_int32, C.POINTER(Tensor)], C.c_int),
+        "tcu_gguf_load_stablelm": ([P, C.POINTER(LoadOptions), C.POINTER(TpOptions), C.POINTER(P)], C.c_int),
+        "tcu_gguf_close": ([P], C.c_int),
+        "tcu_session_save_cache": ([P, C.c_char_p, C.POINTER(C.c_uint8), i32p, C.c_int32], C.c_int),
+        "tcu_session_load_cache": ([P, C.c_char_p, C.POINTER(C.c_uint8), i32p, C.c_int32, i32p], C.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -33,6 +33,8 @@
 #include <cudaTypedefs.h>
 #include "misc.cuh"
 #include "read_values.cuh"
+#include "gguf.h"
+#include "kv_snapshot.h"
 
 using namespace tcu;
 
@@ -2467,6 +2469,180 @@ int tcu_stablelm_load_tp(const tcu_stablelm_config* config, const tcu_tensor* te
   return TCU_OK;
 }
 
+}  // extern "C"
+
+// A memory-mapped GGUF StableLM checkpoint: the parsed file, the derived
+// configuration and its tensors under their Hugging Face names (data
+// pointing into the mapping).
+struct tcu_gguf {
+  GgufFile f;
+  tcu_stablelm_config config{};
+  std::vector<std::string> names;
+  std::vector<tcu_tensor> tensors;
+};
+
+// loadStableGGUF's metadata rules (gguf.go:258-357), without the tokenizer
+// check (the caller compares its tokenizer.json with the GGUF vocabulary).
+static int gguf_stablelm(tcu_gguf* g) {
+  const auto& meta = g->f.meta;
+  auto get = [&](const char* k) -> const GgufValue* {
+    auto it = meta.find(k);
+    return it == meta.end() ? nullptr : &it->second;
+  };
+  const GgufValue* arch = get("general.architecture");
+  const GgufValue* type = get("general.type");
+  if (!arch || arch->kind != GgufValue::STR || arch->s != "stablelm" || (type && (type->kind != GgufValue::STR || type->s != "model")))
+    return fail(TCU_EINVAL, "GGUF must contain a StableLM model");
+  std::string bad;
+  auto integer = [&](const char* k) -> int32_t {
+    const GgufValue* v = get(k);
+    if (!v || v->kind != GgufValue::UINT || v->u > (uint64_t)INT32_MAX) {
+      if (bad.empty()) bad = k;
+      return 0;
+    }
+    return (int32_t)v->u;
+  };
+  tcu_stablelm_config& c = g->config;
+  c.hidden_size = integer("stablelm.embedding_length");
+  c.intermediate_size = integer("stablelm.feed_forward_length");
+  c.num_hidden_layers = integer("stablelm.block_count");
+  c.num_attention_heads = integer("stablelm.attention.head_count");
+  c.num_key_value_heads = integer("stablelm.attention.head_count_kv");
+  c.max_position_embeddings = integer("stablelm.context_length");
+  c.bos_token_id = integer("tokenizer.ggml.bos_token_id");
+  c.eos_token_id = integer("tokenizer.ggml.eos_token_id");
+  const GgufValue* par = get("stablelm.use_parallel_residual");
+  const bool parallel = par && par->kind == GgufValue::BOOL && par->b;
+  const GgufValue* eps = get("stablelm.attention.layer_norm_epsilon");
+  c.layer_norm_eps = (eps && eps->kind == GgufValue::FLOAT) ? eps->f : 0.0;
+  c.rope_theta = 10000.0;
+  if (const GgufValue* th = get("stablelm.rope.freq_base")) {
+    if (th->kind != GgufValue::FLOAT) return fail(TCU_EINVAL, "invalid GGUF RoPE frequency base");
+    c.rope_theta = th->f;
+  }
+  if (c.hidden_size > 0 && c.num_attention_heads > 0)
+    c.partial_rotary_factor = (double)integer("stablelm.rope.dimension_count") * (double)c.num_attention_heads / (double)c.hidden_size;
+  const GgufValue* vocab = get("tokenizer.ggml.tokens");
+  if (!vocab || vocab->kind != GgufValue::ARRAY) return fail(TCU_EINVAL, "GGUF missing vocabulary");
+  c.vocab_size = (int32_t)vocab->count;
+  if (!bad.empty()) return fail(TCU_EINVAL, "missing or invalid GGUF integer %s", bad.c_str());
+  // validate() (stablelm.go:85-111).
+  if (!parallel) return fail(TCU_EINVAL, "unsupported StableLM variant: require parallel residuals");
+  if (c.hidden_size <= 0 || c.intermediate_size <= 0 || c.num_hidden_layers <= 0 || c.num_attention_heads <= 0 ||
+      c.num_key_value_heads <= 0 || c.vocab_size <= 0 || c.max_position_embeddings <= 0 || c.hidden_size % c.num_attention_heads ||
+      c.num_attention_heads % c.num_key_value_heads)
+    return fail(TCU_EINVAL, "invalid StableLM dimensions");
+  const double rotary = (double)(c.hidden_size / c.num_attention_heads) * c.partial_rotary_factor;
+  if (!(c.layer_norm_eps > 0) || std::isinf(c.layer_norm_eps) || !(c.rope_theta > 0) || std::isinf(c.rope_theta) ||
+      !(c.partial_rotary_factor > 0) || c.partial_rotary_factor > 1 || rotary != std::trunc(rotary) || (int)rotary % 2 != 0 || rotary < 2)
+    return fail(TCU_EINVAL, "invalid LayerNorm or partial RoPE settings");
+  if (c.bos_token_id < 0 || c.bos_token_id >= c.vocab_size || c.eos_token_id < 0 || c.eos_token_id >= c.vocab_size)
+    return fail(TCU_EINVAL, "invalid BOS/EOS token IDs");
+  const size_t nt = g->f.tensors.size();
+  if (nt < 4 || (nt - 4) % 9 != 0 || (int)((nt - 4) / 9) != c.num_hidden_layers)
+    return fail(TCU_EINVAL, "unexpected GGUF tensor count for %d StableLM layers", c.num_hidden_layers);
+  if (const GgufValue* sc = get("stablelm.rope.scaling.type"))
+    if (!(sc->kind == GgufValue::STR && sc->s == "none")) return fail(TCU_EINVAL, "GGUF RoPE scaling is not supported");
+  for (const GgufTensor& t : g->f.tensors) {
+    const std::string& n = t.name;
+    const bool bias = n.size() >= 5 && n.compare(n.size() - 5, 5, ".bias") == 0;
+    if (n.find("attn_q_norm") != std::string::npos || n.find("attn_k_norm") != std::string::npos ||
+        n.find("ffn_norm") != std::string::npos || (bias && n.find("norm") == std::string::npos))
+      return fail(TCU_EUNSUP, "unsupported StableLM tensor %s", n.c_str());
+  }
+  // The tensors loadStableWeights reads (stablelm.go:167-199), by their GGUF
+  // names, with their row-major shapes checked.
+  const int d = c.hidden_size, ff = c.intermediate_size, kv = d / c.num_attention_heads * c.num_key_value_heads;
+  struct Want {
+    std::string hf;
+    std::vector<int64_t> shape;
+  };
+  std::vector<Want> want = {{"model.embed_tokens.weight", {c.vocab_size, d}}, {"lm_head.weight", {c.vocab_size, d}},
+                            {"model.norm.weight", {d}}, {"model.norm.bias", {d}}};
+  for (int l = 0; l < c.num_hidden_layers; l++) {
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    want.push_back({p + "input_layernorm.weight", {d}});
+    want.push_back({p + "input_layernorm.bias", {d}});
+    want.push_back({p + "self_attn.q_proj.weight", {d, d}});
+    want.push_back({p + "self_attn.k_proj.weight", {kv, d}});
+    want.push_back({p + "self_attn.v_proj.weight", {kv, d}});
+    want.push_back({p + "self_attn.o_proj.weight", {d, d}});
+    want.push_back({p + "mlp.gate_proj.weight", {ff, d}});
+    want.push_back({p + "mlp.up_proj.weight", {ff, d}});
+    want.push_back({p + "mlp.down_proj.weight", {d, ff}});
+  }
+  g->names.clear();
+  g->tensors.clear();
+  g->names.reserve(want.size());
+  for (const Want& w : want) {
+    const std::string gn = gguf_name(w.hf);
+    auto it = g->f.by_name.find(gn);
+    if (it == g->f.by_name.end()) return fail(TCU_EINVAL, "missing GGUF tensor %s", w.hf.c_str());
+    const GgufTensor& t = g->f.tensors[it->second];
+    if (t.shape != w.shape) return fail(TCU_EINVAL, "GGUF tensor %s: shape mismatch", w.hf.c_str());
+    g->names.push_back(w.hf);
+    tcu_tensor x{};
+    x.dtype = t.dtype;
+    x.ndim = (int32_t)t.shape.size();
+    for (size_t j = 0; j < t.shape.size(); j++) x.shape[j] = t.shape[j];
+    x.data = g->f.map + t.offset;
+    x.nbytes = t.size;
+    g->tensors.push_back(x);
+  }
+  for (size_t i = 0; i < g->tensors.size(); i++) g->tensors[i].name = g->names[i].c_str();
+  return TCU_OK;
+}
+
+extern "C" {
+
+int tcu_gguf_open(const char* path, tcu_gguf** out) {
+  if (!path || !out) return fail(TCU_EINVAL, "null argument");
+  *out = nullptr;
+  tcu_gguf* g = new tcu_gguf();
+  std::string err;
+  if (!gguf_read(path, &g->f, &err)) {
+    delete g;
+    return fail(TCU_EINVAL, "%s", err.c_str());
+  }
+  const int rc = gguf_stablelm(g);
+  if (rc != TCU_OK) {
+    delete g;
+    return rc;
+  }
+  *out = g;
+  return TCU_OK;
+}
+
+int tcu_gguf_config(const tcu_gguf* g, tcu_stablelm_config* config) {
+  if (!g || !config) return fail(TCU_EINVAL, "null argument");
+  *config = g->config;
+  return TCU_OK;
+}
+
+int tcu_gguf_tensor_count(const tcu_gguf* g, int32_t* n) {
+  if (!g || !n) return fail(TCU_EINVAL, "null argument");
+  *n = (int32_t)g->tensors.size();
+  return TCU_OK;
+}
+
+int tcu_gguf_tensor(const tcu_gguf* g, int32_t i, tcu_tensor* out) {
+  if (!g || !out) return fail(TCU_EINVAL, "null argument");
+  if (i < 0 || i >= (int32_t)g->tensors.size()) return fail(TCU_EINVAL, "tensor index %d out of range", i);
+  *out = g->tensors[i];
+  return TCU_OK;
+}
+
+int tcu_gguf_load_stablelm(const tcu_gguf* g, const tcu_load_options* options, const tcu_tp_options* tp, tcu_model** out) {
+  if (!g || !out) return fail(TCU_EINVAL, "null argument");
+  if (tp) return tcu_stablelm_load_tp(&g->config, g->tensors.data(), (int32_t)g->tensors.size(), options, tp, out);
+  return stablelm_load(&g->config, g->tensors.data(), (int32_t)g->tensors.size(), options, nullptr, out);
+}
+
+int tcu_gguf_close(tcu_gguf* g) {
+  delete g;
+  return TCU_OK;
+}
+
 int tcu_llama_load(const void* checkpoint, uint64_t nbytes, const tcu_load_options* options, tcu_model** out) {
   return llama_load(checkpoint, nbytes, options, out);
 }
@@ -2796,6 +2972,177 @@ int tcu_session_sample_candidates(tcu_session* s, const int32_t* history, int32_
   CK(cudaMemcpyAsync(scores, s->w->cd_vals, kk * sizeof(double), cudaMemcpyDeviceToHost, s->stream));
   TRY(session_sync(s));
   *n_out = kk;
+  return TCU_OK;
+}
+
+// KV snapshots (cache_file.go:16-258) of a session's resident positions.
+
+// Device staging for one layer of the payload, freed on every return path.
+struct DevBuf {
+  void* p = nullptr;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+};
+
+int tcu_session_save_cache(tcu_session* s, const char* path, const uint8_t* model_sha256, const int32_t* tokens, int32_t n_tokens) {
+  if (!s || !path || !model_sha256 || (n_tokens > 0 && !tokens)) return fail(TCU_EINVAL, "null argument");
+  if (s->closed) return fail(TCU_ECLOSED, "session is closed");
+  if (s->branches_open) return fail(TCU_EINVAL, "close the open branches first");
+  if (n_tokens != s->length) return fail(TCU_EINVAL, "%d tokens given for %d resident positions", n_tokens, s->length);
+  tcu_model* m = s->m;
+  CK(cudaSetDevice(m->device));
+  CK(cudaStreamSynchronize(s->stream));
+  const std::string js = kv_header_json(model_sha256, s->half != 0, tokens, n_tokens);
+  // A temporary file beside the target, renamed over it when complete
+  // (SaveCache writes the same way, with mode 0600: prompt-derived data).
+  std::string dir = path;
+  const size_t slash = dir.find_last_of('/');
+  dir = slash == std::string::npos ? std::string(".") : dir.substr(0, slash == 0 ? 1 : slash);
+  std::string tmpl = dir + "/.tinyoai-kv-XXXXXX";
+  std::vector<char> name(tmpl.begin(), tmpl.end());
+  name.push_back('\0');
+  const int fd = mkstemp(name.data());
+  if (fd < 0) return fail(TCU_EINVAL, "cannot create a file beside %s: %s", path, strerror(errno));
+  fchmod(fd, 0600);
+  FILE* f = fdopen(fd, "wb");
+  if (!f) {
+    close(fd);
+    unlink(name.data());
+    return fail(TCU_EINVAL, "fdopen: %s", strerror(errno));
+  }
+  auto abandon = [&](int code) {
+    fclose(f);
+    unlink(name.data());
+    return code;
+  };
+  Sha256 dg;
+  auto put = [&](const void* p, size_t n) {
+    dg.update(p, n);
+    return fwrite(p, 1, n, f) == n;
+  };
+  uint8_t prefix[12];
+  memcpy(prefix, "TNYKV001", 8);
+  const uint32_t hl = (uint32_t)js.size();
+  memcpy(prefix + 8, &hl, 4);
+  if (!put(prefix, 12) || !put(js.data(), js.size())) return abandon(fail(TCU_EINVAL, "write %s: %s", path, strerror(errno)));
+  if (n_tokens > 0) {
+    const int es = s->half ? 2 : 4;
+    const size_t layer_bytes = (size_t)m->KVH * 2 * n_tokens * m->hd * es;
+    DevBuf dbuf;
+    if (cudaMalloc(&dbuf.p, layer_bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return abandon(fail(TCU_ENOMEM, "snapshot staging: cannot allocate %zu bytes", layer_bytes));
+    }
+    std::vector<uint8_t> hbuf(layer_bytes);
+    int rc = upload_pt(s);
+    if (rc != TCU_OK) return abandon(rc);
+    for (int l = 0; l < m->L; l++) {
+      k_kv_gather<<<m->sm_count * 4, 256, 0, s->stream>>>(s->pool->view(), l, s->w->pt, n_tokens, (uint8_t*)dbuf.p);
+      if (cudaMemcpyAsync(hbuf.data(), dbuf.p, layer_bytes, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess ||
+          cudaStreamSynchronize(s->stream) != cudaSuccess)
+        return abandon(fail(TCU_ECUDA, "snapshot copy: %s", cudaGetErrorString(cudaGetLastError())));
+      if (!put(hbuf.data(), layer_bytes)) return abandon(fail(TCU_EINVAL, "write %s: %s", path, strerror(errno)));
+    }
+  }
+  uint8_t sum[32];
+  dg.final(sum);
+  if (fwrite(sum, 1, 32, f) != 32 || fflush(f) != 0 || fsync(fileno(f)) != 0)
+    return abandon(fail(TCU_EINVAL, "write %s: %s", path, strerror(errno)));
+  if (fclose(f) != 0) {
+    unlink(name.data());
+    return fail(TCU_EINVAL, "close %s: %s", path, strerror(errno));
+  }
+  if (rename(name.data(), path) != 0) {
+    unlink(name.data());
+    return fail(TCU_EINVAL, "rename to %s: %s", path, strerror(errno));
+  }
+  return TCU_OK;
+}
+
+int tcu_session_load_cache(tcu_session* s, const char* path, const uint8_t* model_sha256, int32_t* tokens, int32_t capacity,
+                           int32_t* n_tokens) {
+  if (!s || !path || !model_sha256 || !n_tokens || (capacity > 0 && !tokens)) return fail(TCU_EINVAL, "null argument");
+  if (s->closed) return fail(TCU_ECLOSED, "session is closed");
+  if (s->branches_open) return fail(TCU_EINVAL, "close the open branches first");
+  tcu_model* m = s->m;
+  FILE* f = fopen(path, "rb");
+  if (!f) return fail(TCU_EINVAL, "open %s: %s", path, strerror(errno));
+  struct FileCloser {
+    FILE* f;
+    ~FileCloser() { fclose(f); }
+  } closer{f};
+  Sha256 dg;
+  auto get = [&](void* p, size_t n) {
+    if (fread(p, 1, n, f) != n) return false;
+    dg.update(p, n);
+    return true;
+  };
+  uint8_t prefix[12];
+  if (!get(prefix, 12)) return fail(TCU_EINVAL, "KV cache: unexpected end of file");
+  if (memcmp(prefix, "TNYKV001", 8) != 0) return fail(TCU_EINVAL, "unsupported KV cache format");
+  uint32_t hl;
+  memcpy(&hl, prefix + 8, 4);
+  if (hl > (1u << 20)) return fail(TCU_EINVAL, "KV cache header too large");
+  std::string js(hl, '\0');
+  if (hl && !get(&js[0], hl)) return fail(TCU_EINVAL, "KV cache: unexpected end of file");
+  uint8_t model[32];
+  bool half = false;
+  std::vector<int32_t> toks;
+  if (!kv_header_parse(js, model, &half, &toks)) return fail(TCU_EINVAL, "KV cache header is not valid");
+  // LoadCache's checks, in its order (cache_file.go:128-153).
+  if ((int64_t)toks.size() > m->max_pos) return fail(TCU_EINVAL, "KV cache exceeds model context");
+  for (int32_t id : toks)
+    if (id < 0 || id >= m->V) return fail(TCU_EINVAL, "invalid KV cache token %d", id);
+  if (memcmp(model, model_sha256, 32) != 0) return fail(TCU_EINVAL, "KV cache model does not match checkpoint");
+  if (half != (s->half != 0)) return fail(TCU_EINVAL, "KV cache precision does not match model options");
+  const int T = (int)toks.size();
+  const int es = half ? 2 : 4;
+  const uint64_t values = (uint64_t)m->L * 2 * m->KVH * m->hd * T;
+  const uint64_t expected = 12 + (uint64_t)hl + values * es + 32;
+  struct stat st;
+  if (fstat(fileno(f), &st) != 0 || (uint64_t)st.st_size != expected)
+    return fail(TCU_EINVAL, "KV cache size %lld, expected %llu", (long long)st.st_size, (unsigned long long)expected);
+  if (T > capacity) return fail(TCU_EINVAL, "token buffer holds %d of %d snapshot tokens", capacity, T);
+  CK(cudaSetDevice(m->device));
+  CK(cudaStreamSynchronize(s->stream));
+  // Fresh pages for the restored positions; the session keeps its own until
+  // the whole file is verified.
+  std::vector<int> pages;
+  auto drop = [&](int code) {
+    release_pages(m, s->pool, pages, 0);
+    return code;
+  };
+  if (T > 0) {
+    int rc = prepare_pages(m, s->pool, pages, 0, T, s->stream);
+    if (rc != TCU_OK) return drop(rc);
+    const size_t layer_bytes = (size_t)m->KVH * 2 * T * m->hd * es;
+    DevBuf dbuf, dpt;
+    if (cudaMalloc(&dbuf.p, layer_bytes) != cudaSuccess || cudaMalloc(&dpt.p, pages.size() * sizeof(int)) != cudaSuccess) {
+      cudaGetLastError();
+      return drop(fail(TCU_ENOMEM, "snapshot staging: cannot allocate %zu bytes", layer_bytes));
+    }
+    std::vector<uint8_t> hbuf(layer_bytes);
+    if (cudaMemcpy(dpt.p, pages.data(), pages.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+      return drop(fail(TCU_ECUDA, "snapshot page table copy failed"));
+    for (int l = 0; l < m->L; l++) {
+      if (!get(hbuf.data(), layer_bytes)) return drop(fail(TCU_EINVAL, "KV cache: unexpected end of file"));
+      if (cudaMemcpyAsync(dbuf.p, hbuf.data(), layer_bytes, cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
+        return drop(fail(TCU_ECUDA, "snapshot copy failed"));
+      k_kv_scatter<<<m->sm_count * 4, 256, 0, s->stream>>>(s->pool->view(), l, (const int*)dpt.p, T, (const uint8_t*)dbuf.p);
+      if (cudaStreamSynchronize(s->stream) != cudaSuccess)
+        return drop(fail(TCU_ECUDA, "snapshot scatter: %s", cudaGetErrorString(cudaGetLastError())));
+    }
+  }
+  uint8_t want[32], got[32];
+  dg.final(want);
+  if (fread(got, 1, 32, f) != 32 || memcmp(got, want, 32) != 0) return drop(fail(TCU_EINVAL, "KV cache checksum mismatch"));
+  // Verified: the restored positions replace the session's context.
+  release_pages(m, s->pool, s->pages, 0);
+  s->pages.swap(pages);
+  s->length = T;
+  if (T > 0) memcpy(tokens, toks.data(), (size_t)T * sizeof(int32_t));
+  *n_tokens = T;
   return TCU_OK;
 }
 
