@@ -464,8 +464,9 @@ def run_config(args):
         dist.broadcast_object_list(box, src=0)
         tp_arg = (world, rank, box[0])
     # An 8K-token sequence or a 4K prefix with 64 branches needs a few GB of
-    # f16 KV pages.
-    model = Model.load_stablelm(cfg, tensors, device=local, kv_pool_bytes=max(args.kv_pool_mb, 8192) << 20, tp=tp_arg)
+    # f16 KV pages (32 layers; profiling cases with fewer layers need less).
+    pool_floor = max(1024, 8192 * cfg["num_hidden_layers"] // 32)
+    model = Model.load_stablelm(cfg, tensors, device=local, kv_pool_bytes=max(args.kv_pool_mb, pool_floor) << 20, tp=tp_arg)
     torch.cuda.empty_cache()
     cpu_tensors = tensors if (rank == 0 and world == 1 and args.cpu_baseline) else None
     del tensors

@@ -33,6 +33,7 @@
 #include <cudaTypedefs.h>
 #include "misc.cuh"
 #include "read_values.cuh"
+#include "attn_tc.cuh"
 #include "gguf.h"
 #include "kv_snapshot.h"
 
@@ -130,6 +131,7 @@ struct tcu_model {
   int gemv_smem_optin = 0;
   bool disable_stream = false;  // TCU_DECODE_KERNELS=portable selects the non-TMA kernels
   bool use_tc = true;           // tensor-core prefill GEMM (TCU_GEMM=simt selects the CUDA-core one)
+  bool use_tc_attn = true;      // tensor-core shared-prefix attention (TCU_ATTN=simt selects the CUDA-core one)
   unsigned* scratch_u32 = nullptr;
   // Persistent decode step (decode_mega.cuh): Q8_0 StableLM shapes that fit.
   bool mega = false;
@@ -375,6 +377,8 @@ static void init_common(tcu_model* m, const tcu_load_options* o) {
   m->disable_stream = k && strcmp(k, "portable") == 0;
   const char* g = getenv("TCU_GEMM");
   m->use_tc = !(g && strcmp(g, "simt") == 0);
+  const char* at = getenv("TCU_ATTN");
+  m->use_tc_attn = !(at && strcmp(at, "simt") == 0);
 }
 
 // StableLM rotary table (stablelm.go:309-326): per position and rotary pair,
@@ -1593,7 +1597,20 @@ static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M,
   const int G = m->H / m->KVH;
   // Splits every row shares (branches): keys and values read once for all
   // rows; the per-row kernels start after them.
-  if (w->shared_splits > 0 && a.split == PA_KT && w->shared_splits < grid_splits) {
+  if (w->shared_splits > 0 && a.split == AT_KEYS && w->shared_splits < grid_splits && pool->half && m->use_tc_attn &&
+      m->hd % 16 == 0 && m->hd <= 256 && at_smem_bytes(m->hd) <= (size_t)m->gemv_smem_optin) {
+    // Tensor cores: runs of splits per CTA, about two CTAs per SM.
+    const int qt = (M * G + AT_ROWS - 1) / AT_ROWS;
+    const int want = std::max(1, 2 * m->sm_count / (m->KVH * qt));
+    const int per = (w->shared_splits + want - 1) / want;
+    const int runs = (w->shared_splits + per - 1) / per;
+    const size_t smem = at_smem_bytes(m->hd);
+    cudaFuncSetAttribute(k_attn_shared_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    NOTE("cudaFuncSetAttribute(k_attn_shared_tc)");
+    k_attn_shared_tc<<<dim3(runs, m->KVH, qt), AT_THREADS, smem, s>>>(a, w->shared_splits, per, w->err);
+    NOTE("k_attn_shared_tc");
+    a.s_begin = w->shared_splits;
+  } else if (w->shared_splits > 0 && a.split == PA_KT && w->shared_splits < grid_splits) {
     const int nc = (m->hd + 15) / 16;
     auto kern = nc <= 2 ? k_attn_shared<2> : nc <= 4 ? k_attn_shared<4> : nc <= 5 ? k_attn_shared<5> : k_attn_shared<8>;
     const size_t smem = pa_shared_smem_bytes(m->hd);
@@ -1943,14 +1960,27 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
     pa.out = w->ah;
     pa.out_stride = aw + ff;
     pa.scale = (float)sqrt((double)m->hd);
-    const size_t smem = pa_smem_bytes(m->hd);
-    const int nc = (m->hd + 15) / 16;
-    auto kern = nc <= 2 ? k_attn_prefill<2> : nc <= 4 ? k_attn_prefill<4> : nc <= 5 ? k_attn_prefill<5> : k_attn_prefill<8>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    NOTE("cudaFuncSetAttribute(k_attn_prefill)");
-    PROF_BEGIN(ST_PF_ATTN, s);
-    kern<<<dim3((n + PA_QT - 1) / PA_QT, m->H), PA_THREADS, smem, s>>>(pa);
-    NOTE("k_attn_prefill");
+    const int hd16 = m->hd % 16 == 0 ? m->hd / 16 : 0;
+    if (pool->half && m->use_tc_attn && (hd16 == 4 || hd16 == 5 || hd16 == 6 || hd16 == 8) &&
+        at_smem_bytes(m->hd) <= (size_t)m->gemv_smem_optin) {
+      // Tensor cores (binary16 KV): one CTA per 128 queries and head.
+      auto kern = hd16 == 4 ? k_attn_prefill_tc<4> : hd16 == 5 ? k_attn_prefill_tc<5> : hd16 == 6 ? k_attn_prefill_tc<6> : k_attn_prefill_tc<8>;
+      const size_t smem = at_smem_bytes(m->hd);
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      NOTE("cudaFuncSetAttribute(k_attn_prefill_tc)");
+      PROF_BEGIN(ST_PF_ATTN, s);
+      kern<<<dim3((n + AT_ROWS - 1) / AT_ROWS, m->H), AT_THREADS, smem, s>>>(pa, w->err);
+      NOTE("k_attn_prefill_tc");
+    } else {
+      const size_t smem = pa_smem_bytes(m->hd);
+      const int nc = (m->hd + 15) / 16;
+      auto kern = nc <= 2 ? k_attn_prefill<2> : nc <= 4 ? k_attn_prefill<4> : nc <= 5 ? k_attn_prefill<5> : k_attn_prefill<8>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      NOTE("cudaFuncSetAttribute(k_attn_prefill)");
+      PROF_BEGIN(ST_PF_ATTN, s);
+      kern<<<dim3((n + PA_QT - 1) / PA_QT, m->H), PA_THREADS, smem, s>>>(pa);
+      NOTE("k_attn_prefill");
+    }
     PROF_END(s);
     if (m->arch == ARCH_STABLELM && m->tp_world > 1) {
       GemmArgs g2{};
