@@ -120,27 +120,41 @@ struct DecodeAttnArgs {
   int out_stride;
   float scale;  // float32(sqrt(hd))
   int s_begin;  // splits below this are computed for all rows by k_attn_shared
+  int s_runs;   // > 0: the shared splits left s_runs merged partials in slots [0, s_runs)
 };
 
-// Merges the nsplit partials (hd outputs, max, sum) of each of the G heads
-// of one (row, KV head) into out[G][hd], by the whole CTA: fp32 maximum over
+// Partial slots of a row's merge: the first `lo` slots, then the per-row
+// splits from slot lo + off on (off = 0: slots 0 .. n-1 in order).
+struct SplitSlots {
+  int n, lo, off;
+  __device__ __forceinline__ int operator()(int j) const { return j < lo ? j : j + off; }
+};
+
+__device__ __forceinline__ SplitSlots split_slots(const DecodeAttnArgs& a, int nsplit) {
+  if (a.s_runs > 0 && a.s_begin > 0) return SplitSlots{a.s_runs + nsplit - a.s_begin, a.s_runs, a.s_begin - a.s_runs};
+  return SplitSlots{nsplit, nsplit, 0};
+}
+
+// Merges the sl.n partials (hd outputs, max, sum; partial j in slot sl(j))
+// of each of the G heads of one (row, KV head) into out[G][hd], by the whole
+// CTA: fp32 maximum over
 // the splits, weights expf(max_j - max), the sum and the outputs accumulated
 // in split order. The splits' maxima and sums load in parallel into shared
 // memory (wsm: cap floats, at least 2 * nsplit); each output loads its
 // partials 16 splits at a time, so the merge costs a few L2 round trips
 // rather than one per split. Longer merges (2 * nsplit > cap) read the
 // partials one split at a time.
-__device__ void attn_merge_splits(const float* part, int max_splits, int hd, int G, int nsplit, float* wsm, int cap, float* out) {
-  const int rs = hd + 2;
+__device__ void attn_merge_splits(const float* part, int max_splits, int hd, int G, SplitSlots sl, float* wsm, int cap, float* out) {
+  const int rs = hd + 2, nsplit = sl.n;
   for (int hh = 0; hh < G; hh++) {
     const float* ph = part + (size_t)hh * max_splits * rs;
     if (2 * nsplit > cap) {
       for (int i = threadIdx.x; i < hd; i += blockDim.x) {
         float mx = -INFINITY;
-        for (int j = 0; j < nsplit; j++) mx = fmaxf(mx, __ldcg(ph + (size_t)j * rs + hd));
+        for (int j = 0; j < nsplit; j++) mx = fmaxf(mx, __ldcg(ph + (size_t)sl(j) * rs + hd));
         float l = 0.f, o = 0.f;
         for (int j = 0; j < nsplit; j++) {
-          const float* pj = ph + (size_t)j * rs;
+          const float* pj = ph + (size_t)sl(j) * rs;
           const float w = expf(__ldcg(pj + hd) - mx);
           l = fmaf(__ldcg(pj + hd + 1), w, l);
           o = fmaf(__ldcg(pj + i), w, o);
@@ -151,8 +165,8 @@ __device__ void attn_merge_splits(const float* part, int max_splits, int hd, int
     }
     __syncthreads();  // wsm is free (previous head or the attention tiles)
     for (int j = threadIdx.x; j < nsplit; j += blockDim.x) {
-      wsm[j] = __ldcg(ph + (size_t)j * rs + hd);
-      wsm[nsplit + j] = __ldcg(ph + (size_t)j * rs + hd + 1);
+      wsm[j] = __ldcg(ph + (size_t)sl(j) * rs + hd);
+      wsm[nsplit + j] = __ldcg(ph + (size_t)sl(j) * rs + hd + 1);
     }
     __syncthreads();
     float mx = -INFINITY;
@@ -167,7 +181,7 @@ __device__ void attn_merge_splits(const float* part, int max_splits, int hd, int
       for (int j0 = 0; j0 < nsplit; j0 += 16) {
         float pv[16];
 #pragma unroll
-        for (int jj = 0; jj < 16; jj++) pv[jj] = j0 + jj < nsplit ? __ldcg(ph + (size_t)(j0 + jj) * rs + i) : 0.f;
+        for (int jj = 0; jj < 16; jj++) pv[jj] = j0 + jj < nsplit ? __ldcg(ph + (size_t)sl(j0 + jj) * rs + i) : 0.f;
 #pragma unroll
         for (int jj = 0; jj < 16; jj++)
           if (j0 + jj < nsplit) o = fmaf(pv[jj], wsm[j0 + jj], o);
@@ -308,7 +322,7 @@ __global__ void __launch_bounds__(128) k_attn_decode(DecodeAttnArgs a) {
   if (!is_last) return;
   __threadfence();
   // Merge the nsplit partial states of each head in the group.
-  attn_merge_splits(part, a.max_splits, hd, G, nsplit, ks, split * (hd + 1), a.out + (size_t)m * a.out_stride + g * G * hd);
+  attn_merge_splits(part, a.max_splits, hd, G, split_slots(a, nsplit), ks, split * (hd + 1), a.out + (size_t)m * a.out_stride + g * G * hd);
   if (threadIdx.x == 0) a.counters[m * a.KVH + g] = 0;
 }
 
@@ -876,7 +890,7 @@ __global__ void __launch_bounds__(128) k_attn_decode_bulk(DecodeAttnArgs a, Deco
   __threadfence();
   // Merge the nsplit partial states of each head in the group (the key
   // tile's shared memory is free by now).
-  attn_merge_splits(part, a.max_splits, hd, G, nsplit, reinterpret_cast<float*>(ktile), split * hd * es / 4,
+  attn_merge_splits(part, a.max_splits, hd, G, split_slots(a, nsplit), reinterpret_cast<float*>(ktile), split * hd * es / 4,
                     a.out + (size_t)m * a.out_stride + g * G * hd);
   if (threadIdx.x == 0) a.counters[m * a.KVH + g] = 0;
 }

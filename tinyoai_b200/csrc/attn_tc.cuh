@@ -1,28 +1,38 @@
-// Shared-prefix attention on the 5th-generation tensor cores (binary16 KV).
+// Attention on the 5th-generation tensor cores (binary16 KV).
 //
-// Branches of one prefix (mlx_branches.go:98-114) all read the prefix's KV
-// pages. k_attn_shared_tc computes, for every query row of the branch batch,
-// each whole 64-position split of that prefix: the per-split partial
-// (sum_t exp(s_t - m) v_t, m, sum_t exp(s_t - m)) that k_attn_shared writes
-// on CUDA cores, in the same place, for the per-row kernels to merge.
+// k_attn_shared_tc: branches of one prefix (mlx_branches.go:98-114) all read
+// the prefix's KV pages. For every query row of the branch batch it attends
+// to a run of whole 64-position splits of that prefix and writes the run's
+// partial (sum_t exp(s_t - m) v_t, m, sum_t exp(s_t - m)) for the per-row
+// kernels to merge with the rest of the row's history.
 //
-// One CTA per (run of splits, KV head, tile of 128 query rows). Query row qi
-// is head g * G + qi % G of batch row qi / G, rotated at that row's position
-// (the reference's RoPE operations, stablelm.go:309-326). Per split:
-//   S = Q K^T      tcgen05.mma M = 128 rows, N = 64 positions, K = hd.
-//                  The binary16 keys are exact operands; each float32 query
-//                  row is scaled by 2^sx (sx = 13 - exponent of its max) and
-//                  split into an exact binary16 pair Qh + Ql (22 of its 24
-//                  bits), so S = Qh.K + Ql.K is accumulated in float32.
-//   s = S 2^-sx / sqrt(hd) (correctly rounded division), per row the
-//       split's max m, p_t = expf(s_t - m), l = sum_t p_t in position order
-//       (one thread per row, scores read from TMEM).
-//   O = P V        M = 128 rows, N = hd, K = 64 positions; P in [0, 1]
-//                  split into a binary16 pair Ph + Pl (absolute error below
-//                  2^-24 per weight), V exact.
-// The dropped terms are ~2^-22 of each product, the accumulation order is
-// the tensor core's: results agree with the float32 CUDA-core kernel to
-// ~1e-6 relative, not bit for bit.
+// k_attn_prefill_tc: causal attention of a prefill chunk (attention.go:6-45).
+//
+// Both take 128 query rows per CTA as the MMA's M. Per 64-position block:
+//   S = Q K^T      tcgen05.mma M = 128, N = 64, K = hd. The binary16 keys
+//                  are exact operands; each float32 query row is scaled by
+//                  2^sx (sx = 13 - exponent of its max) and split into an
+//                  exact binary16 pair Qh + Ql (22 of its 24 bits), so
+//                  S = Qh.K + Ql.K is accumulated in float32.
+//   s = S * (2^-sx / sqrt(hd)), m' = max(m, block max),
+//   p = 2^((s - m') log2 e) (ex2.approx), alpha = 2^((m - m') log2 e),
+//   l = l alpha + sum p in position order (one thread per query row, scores
+//   read from TMEM).
+//   O = P V        M = 128, N = hd, K = 64 positions; P split into a
+//                  binary16 pair Ph + Pl, V exact; o = o alpha + O in
+//                  registers.
+// Scaling by the reciprocal, ex2.approx and the dropped 2^-22 terms put the
+// results ~1e-6 (relative) from the float32 CUDA-core kernels, not bit for
+// bit.
+//
+// Work is done by groups of four warps (128 threads, one per query row and
+// TMEM lane). A group owns a P tile, two K/V stages, an mbarrier, a named
+// barrier and 256 TMEM columns (scores at 0, block outputs at 128); one
+// thread of the group issues its MMAs. cp.async brings the group's next K/V
+// block while the current one is computed. The prefill kernel runs two
+// groups on alternate key blocks (when shared memory allows) and merges
+// their states at the end; the shared kernel runs one group, two CTAs per
+// SM.
 //
 // Shared-memory operands use the no-swizzle K-major / MN-major layouts of
 // 8-row x 16-byte core matrices. A K or V tile is stored [hd/8 chunks][64
@@ -31,26 +41,29 @@
 // positions and 1024 over hd; as the B operand of O (MN-major: N = hd
 // contiguous) they step 1024 bytes over hd and 128 over positions. Q and P
 // tiles are [chunks][128 rows][8 values] (K-major A, 2048 bytes per chunk).
-// cp.async brings the K/V tile of the next split while the current one is
-// computed. All copies read this GPU's own memory into this CTA's shared
-// memory; every mbarrier wait is bounded.
+// The regions are ordered P, Q, K/V, so that every operand read stays inside
+// the CTA's allocation under either reading of the two descriptor strides.
+// All copies read this GPU's own memory into this CTA's shared memory;
+// every mbarrier wait is bounded.
 #pragma once
+#include <climits>
+
 #include "attention.cuh"
 #include "gemm_tc.cuh"
 
 namespace tcu {
 
-constexpr int AT_ROWS = 128;    // query rows per CTA (MMA M)
-constexpr int AT_KEYS = 64;     // positions per split
-constexpr int AT_THREADS = 128;  // one thread per query row / TMEM lane
-constexpr uint32_t AT_TMEM_COLS = 256;  // scores at column 0, outputs at 128
+constexpr int AT_ROWS = 128;   // query rows per CTA (MMA M)
+constexpr int AT_KEYS = 64;    // positions per block (one split)
+constexpr int AT_GROUP = 128;  // threads per group: one per query row / TMEM lane
+constexpr float AT_LOG2E = 1.4426950408889634f;
 
-// Dynamic shared memory for head size hd (multiple of 16, at most 256):
-// Q pieces 2 x 128 x hd, K/V 2 stages x 2 x 64 x hd, P pieces 2 x 128 x 64
-// (binary16), barrier and TMEM slot. At least 80 KB, so that at most two
-// CTAs (2 x 256 TMEM columns) share an SM.
-__host__ __device__ inline size_t at_smem_bytes(int hd) {
-  const size_t b = (size_t)4 * AT_ROWS * hd + (size_t)8 * AT_KEYS * hd + (size_t)4 * AT_ROWS * AT_KEYS + 64;
+// Dynamic shared memory for head size hd (multiple of 16) and ng groups:
+// P tiles ng x 2 x 128 x 64, Q pieces 2 x 128 x hd, K/V ng x 2 stages x 2 x
+// 64 x hd (binary16), the mbarriers and the TMEM slot. At least 80 KB, so
+// that at most two CTAs (2 x 256 TMEM columns) share an SM.
+__host__ __device__ inline size_t at_smem_bytes(int hd, int ng) {
+  const size_t b = (size_t)ng * 4 * AT_ROWS * AT_KEYS + (size_t)4 * AT_ROWS * hd + (size_t)ng * 8 * AT_KEYS * hd + 64;
   return b < 80 * 1024 ? 80 * 1024 : b;
 }
 
@@ -72,6 +85,13 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// 2^x (PTX ex2.approx; 2^-inf = +0).
+__device__ __forceinline__ float at_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // Sixteen TMEM columns of this thread's lane, without waiting.
@@ -110,89 +130,117 @@ __device__ __forceinline__ void at_split2(float v0, float v1, uint32_t& h, uint3
   l = *reinterpret_cast<const uint32_t*>(&ll);
 }
 
-// Shared memory of the attention kernels: P pieces first, then Q pieces,
-// then the two K/V stages (the order keeps every operand read inside the
-// allocation), then the barrier and the TMEM slot.
+// The CTA's shared regions: the Q tiles (one copy for all groups), the
+// mbarriers and the TMEM slot.
 struct AtSmem {
-  uint8_t* ps;   // [2 pieces][8 chunks][128 rows][16 B]
-  uint8_t* qs;   // [2 pieces][hd/8 chunks][128 rows][16 B]
-  uint8_t* kvs;  // [2 stages][K, V][hd/8 chunks][64 positions][16 B]
-  uint64_t* bar;
+  uint8_t* qs;  // [2 pieces][hd/8 chunks][128 rows][16 B]
+  uint32_t q_piece;
+  uint64_t* bars;  // one per group
   uint32_t* tslot;
-  uint32_t q_piece, kv_tile, p_piece;  // bytes of one Q piece, one K (or V) tile, one P piece
+  int hd;
 };
 
-__device__ __forceinline__ AtSmem at_carve(uint8_t* base, int hd) {
+// One group's resources.
+struct AtGroup {
+  uint8_t* ps;   // [2 pieces][8 chunks][128 rows][16 B]
+  uint8_t* kvs;  // [2 stages][K, V][hd/8 chunks][64 positions][16 B]
+  uint64_t* bar;
+  uint32_t tmem;  // this group's 256 columns
+  int id;         // named barrier of the group: 1 + group index
+  int tid;        // thread within the group (query row / TMEM lane)
+};
+
+__device__ __forceinline__ AtSmem at_carve(uint8_t* base, int hd, int ng) {
   AtSmem m;
-  m.ps = base;
-  m.qs = m.ps + 4 * AT_ROWS * AT_KEYS;
-  m.kvs = m.qs + 4 * AT_ROWS * hd;
-  m.bar = reinterpret_cast<uint64_t*>(m.kvs + 8 * AT_KEYS * hd);
-  m.tslot = reinterpret_cast<uint32_t*>(m.bar + 1);
+  m.qs = base + (size_t)ng * 4 * AT_ROWS * AT_KEYS;
   m.q_piece = 2 * AT_ROWS * hd;
-  m.kv_tile = 2 * AT_KEYS * hd;
-  m.p_piece = 2 * AT_ROWS * AT_KEYS;
+  m.bars = reinterpret_cast<uint64_t*>(m.qs + 4 * AT_ROWS * hd + (size_t)ng * 8 * AT_KEYS * hd);
+  m.tslot = reinterpret_cast<uint32_t*>(m.bars + ng);
+  m.hd = hd;
   return m;
 }
 
-// Barrier init (thread 0) and the TMEM allocation (warp 0).
-__device__ __forceinline__ void at_begin(const AtSmem& sm) {
+__device__ __forceinline__ AtGroup at_group(uint8_t* base, const AtSmem& sm, int g) {
+  AtGroup G;
+  G.ps = base + (size_t)g * 4 * AT_ROWS * AT_KEYS;
+  G.kvs = sm.qs + 4 * AT_ROWS * sm.hd + (size_t)g * 8 * AT_KEYS * sm.hd;
+  G.bar = sm.bars + g;
+  G.tmem = 0;
+  G.id = 1 + g;
+  G.tid = threadIdx.x - g * AT_GROUP;
+  return G;
+}
+
+// Barrier init (thread 0) and the TMEM allocation, 256 columns per group
+// (warp 0).
+__device__ __forceinline__ void at_begin(const AtSmem& sm, int ng) {
   if (threadIdx.x == 0) {
-    mbar_init(sm.bar, 1);
+    for (int g = 0; g < ng; g++) mbar_init(sm.bars + g, 1);
     fence_barrier_init();
   }
   if (threadIdx.x < 32) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(sm.tslot)), "r"(AT_TMEM_COLS));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(sm.tslot)), "r"(256u * ng));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
 }
 
-__device__ __forceinline__ void at_end(const AtSmem& sm, uint32_t tmem) {
+__device__ __forceinline__ void at_end(uint32_t tmem, int ng) {
   cp_async_wait<0>();
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x < 32) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(AT_TMEM_COLS));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256u * ng));
   }
 }
 
-// This thread's query row x (float32, hd values; rotated at pos first when
-// ROPE) as the binary16 pair of x * 2^sx into the Q tiles; returns sx.
+// The power of two sx of query row x (float32, hd values; rotated at pos
+// first when ROPE): 13 - exponent of its largest magnitude.
 template <bool ROPE>
-__device__ __forceinline__ int at_q_pieces(const AtSmem& sm, const float* x, bool valid, int hd, const Rope& rope, int pos) {
-  auto val = [&](int k) { return !valid ? 0.f : ROPE ? rope_elem(x, k, rope, pos) : x[k]; };
+__device__ __forceinline__ int at_q_sx(const float* x, bool valid, int hd, const Rope& rope, int pos) {
   float mx = 0.f;
-  for (int k = 0; k < hd; k++) mx = fmaxf(mx, fabsf(val(k)));
+  if (valid)
+    for (int k = 0; k < hd; k++) mx = fmaxf(mx, fabsf(ROPE ? rope_elem(x, k, rope, pos) : x[k]));
   int ex = 0;
   if (mx > 0.f) frexpf(mx, &ex);
-  const int sx = mx > 0.f ? 13 - ex : 0;
-  const float qscale = tc_pow2(sx);
-  for (int c = 0; c < hd / 8; c++) {
-    uint32_t h[4], l[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) at_split2(val(8 * c + 2 * j) * qscale, val(8 * c + 2 * j + 1) * qscale, h[j], l[j]);
-    *reinterpret_cast<uint4*>(sm.qs + c * (AT_ROWS * 16) + threadIdx.x * 16) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4*>(sm.qs + sm.q_piece + c * (AT_ROWS * 16) + threadIdx.x * 16) = make_uint4(l[0], l[1], l[2], l[3]);
-  }
-  return sx;
+  return mx > 0.f ? 13 - ex : 0;
 }
 
-// Keys and values of positions [t0, t0 + 64) of KV head g into stage st
-// (chunk c of position t at c * 1024 + t * 16); positions past last are
-// zero (their weights are zero, and 0 * 0 keeps the products finite).
-__device__ __forceinline__ void at_load_kv(const AtSmem& sm, int st, const KVView& kv, int layer, const int* page_table, int g, int t0,
-                                           int last, int hd) {
-  uint8_t* kb = sm.kvs + (size_t)st * 2 * sm.kv_tile;
-  uint8_t* vb = kb + sm.kv_tile;
-  const int cpr = hd / 8;
-  for (int e = threadIdx.x; e < AT_KEYS * cpr; e += AT_THREADS) {
-    const int t = e % AT_KEYS, c = e / AT_KEYS, ta = t0 + t;
+// That row as the binary16 pair of x * 2^sx into row `row` of the Q tiles.
+template <bool ROPE>
+__device__ __forceinline__ void at_q_write(const AtSmem& sm, int row, const float* x, bool valid, const Rope& rope, int pos, int sx) {
+  const float qscale = tc_pow2(sx);
+  for (int c = 0; c < sm.hd / 8; c++) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int k = 8 * c + 2 * j;
+      const float v0 = !valid ? 0.f : ROPE ? rope_elem(x, k, rope, pos) : x[k];
+      const float v1 = !valid ? 0.f : ROPE ? rope_elem(x, k + 1, rope, pos) : x[k + 1];
+      at_split2(v0 * qscale, v1 * qscale, h[j], l[j]);
+    }
+    *reinterpret_cast<uint4*>(sm.qs + c * (AT_ROWS * 16) + row * 16) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(sm.qs + sm.q_piece + c * (AT_ROWS * 16) + row * 16) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// Keys and values of positions [t0, t0 + 64) of KV head g into the group's
+// stage st (chunk c of position t at c * 1024 + t * 16); positions past
+// `last` are zero (their weights are zero, and zero values keep the
+// products finite). Each thread looks up one position's page.
+__device__ __forceinline__ void at_load_kv(const AtGroup& G, int hd, int st, const KVView& kv, int layer, const int* page_table, int g,
+                                           int t0, int last) {
+  uint8_t* kb = G.kvs + (size_t)st * 4 * AT_KEYS * hd;
+  uint8_t* vb = kb + 2 * AT_KEYS * hd;
+  const int t = G.tid % AT_KEYS, ta = t0 + t;
+  const bool ok = ta <= last;
+  size_t base = 0;
+  if (ok) base = kv.off(layer, page_table[ta / kv.P], g, ta % kv.P);
+  for (int c = G.tid / AT_KEYS; c < hd / 8; c += AT_GROUP / AT_KEYS) {
     const int so = c * (AT_KEYS * 16) + t * 16;
-    if (ta <= last) {
-      const size_t off = kv.off(layer, page_table[ta / kv.P], g, ta % kv.P) + 8 * c;
-      cp_async16(kb + so, reinterpret_cast<const __half*>(kv.k) + off);
-      cp_async16(vb + so, reinterpret_cast<const __half*>(kv.v) + off);
+    if (ok) {
+      cp_async16(kb + so, reinterpret_cast<const __half*>(kv.k) + base + 8 * c);
+      cp_async16(vb + so, reinterpret_cast<const __half*>(kv.v) + base + 8 * c);
     } else {
       *reinterpret_cast<uint4*>(kb + so) = make_uint4(0, 0, 0, 0);
       *reinterpret_cast<uint4*>(vb + so) = make_uint4(0, 0, 0, 0);
@@ -201,240 +249,274 @@ __device__ __forceinline__ void at_load_kv(const AtSmem& sm, int st, const KVVie
   cp_async_commit();
 }
 
-// Waits for the tensor core's last commit; true on every thread if any
-// thread's wait ran out (all threads then leave together).
-__device__ __forceinline__ bool at_wait_mma(const AtSmem& sm, uint32_t& phase, int* err) {
-  const bool failed = __syncthreads_or(!mbar_wait(sm.bar, phase, err));
-  phase ^= 1;
-  tc_fence_after();
-  return failed;
-}
-
 // Makes this thread's shared-memory writes (copies, P tiles) visible to the
-// tensor core, then synchronises the CTA.
-__device__ __forceinline__ void at_publish() {
+// tensor core, then synchronises the group.
+__device__ __forceinline__ void at_publish(const AtGroup& G) {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   tc_fence_before();
-  __syncthreads();
+  named_bar_sync(G.id, AT_GROUP);
   tc_fence_after();
 }
 
-// S = Qh.K + Ql.K into TMEM columns [0, 64) (thread 0 issues, then commits).
-__device__ __forceinline__ void at_issue_scores(const AtSmem& sm, uint32_t tmem, int st, int hd) {
+// Waits for the group's last MMA commit; true on every thread of the group
+// if any thread's wait ran out (the group then leaves its loop together).
+__device__ __forceinline__ bool at_wait_mma(const AtGroup& G, uint32_t& phase, int* err) {
+  const int ok = mbar_wait(G.bar, phase, err) ? 1 : 0;
+  int all;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.b32 p, %1, 0;\n barrier.red.and.pred q, %2, %3, p;\n selp.b32 %0, 1, 0, q;\n}\n"
+      : "=r"(all)
+      : "r"(ok), "r"(G.id), "r"(AT_GROUP)
+      : "memory");
+  phase ^= 1;
+  tc_fence_after();
+  return all == 0;
+}
+
+// S = Qh.K + Ql.K into the group's TMEM columns [0, 64).
+__device__ __forceinline__ void at_issue_scores(const AtSmem& sm, const AtGroup& G, int st) {
+  const int hd = sm.hd;
   const uint32_t idesc = (1u << 4) | ((uint32_t)(AT_KEYS >> 3) << 17) | ((uint32_t)(AT_ROWS >> 4) << 24);
-  const uint32_t qb = smem_u32(sm.qs), kb = smem_u32(sm.kvs + (size_t)st * 2 * sm.kv_tile);
+  const uint32_t qb = smem_u32(sm.qs), kb = smem_u32(G.kvs + (size_t)st * 4 * AT_KEYS * hd);
   for (int kk = 0; kk < hd / 16; kk++) {
     const uint64_t kd = at_desc(kb + kk * 2 * (AT_KEYS * 16), AT_KEYS * 16, 128);
-    tc_mma(tmem, at_desc(qb + kk * 2 * (AT_ROWS * 16), AT_ROWS * 16, 128), kd, idesc, kk > 0 ? 1u : 0u);
-    tc_mma(tmem, at_desc(qb + sm.q_piece + kk * 2 * (AT_ROWS * 16), AT_ROWS * 16, 128), kd, idesc, 1u);
+    tc_mma(G.tmem, at_desc(qb + kk * 2 * (AT_ROWS * 16), AT_ROWS * 16, 128), kd, idesc, kk > 0 ? 1u : 0u);
+    tc_mma(G.tmem, at_desc(qb + sm.q_piece + kk * 2 * (AT_ROWS * 16), AT_ROWS * 16, 128), kd, idesc, 1u);
   }
-  tc_commit(sm.bar);
+  tc_commit(G.bar);
 }
 
-// O = Ph.V + Pl.V into TMEM columns [128, 128 + hd) (V as the MN-major B).
-__device__ __forceinline__ void at_issue_values(const AtSmem& sm, uint32_t tmem, int st, int hd) {
+// O = Ph.V + Pl.V into the group's TMEM columns [128, 128 + hd) (V as the
+// MN-major B operand).
+__device__ __forceinline__ void at_issue_values(const AtSmem& sm, const AtGroup& G, int st) {
+  const int hd = sm.hd;
   const uint32_t idesc = (1u << 4) | (1u << 16) | ((uint32_t)(hd >> 3) << 17) | ((uint32_t)(AT_ROWS >> 4) << 24);
-  const uint32_t pb = smem_u32(sm.ps), vb = smem_u32(sm.kvs + (size_t)st * 2 * sm.kv_tile) + sm.kv_tile;
+  const uint32_t pb = smem_u32(G.ps), vb = smem_u32(G.kvs + (size_t)st * 4 * AT_KEYS * hd) + 2 * AT_KEYS * hd;
+  const uint32_t p_piece = 2 * AT_ROWS * AT_KEYS;
   for (int kk = 0; kk < AT_KEYS / 16; kk++) {
     const uint64_t vd = at_desc(vb + kk * 2 * 128, 128, AT_KEYS * 16);
-    tc_mma(tmem + 128, at_desc(pb + kk * 2 * (AT_ROWS * 16), AT_ROWS * 16, 128), vd, idesc, kk > 0 ? 1u : 0u);
-    tc_mma(tmem + 128, at_desc(pb + sm.p_piece + kk * 2 * (AT_ROWS * 16), AT_ROWS * 16, 128), vd, idesc, 1u);
+    tc_mma(G.tmem + 128, at_desc(pb + kk * 2 * (AT_ROWS * 16), AT_ROWS * 16, 128), vd, idesc, kk > 0 ? 1u : 0u);
+    tc_mma(G.tmem + 128, at_desc(pb + p_piece + kk * 2 * (AT_ROWS * 16), AT_ROWS * 16, 128), vd, idesc, 1u);
   }
-  tc_commit(sm.bar);
+  tc_commit(G.bar);
 }
 
-// This thread's 64 scores from TMEM (its warp's lanes).
-__device__ __forceinline__ void at_ld_scores(uint32_t tmem, float (&sc)[AT_KEYS]) {
-  const uint32_t lane_base = (uint32_t)((threadIdx.x >> 5) * 32) << 16;
+// This thread's 64 scores from TMEM, times k.
+__device__ __forceinline__ void at_ld_scores(const AtGroup& G, float k, float (&sc)[AT_KEYS]) {
+  const uint32_t lane_base = (uint32_t)((G.tid >> 5) * 32) << 16;
+  uint32_t r[AT_KEYS / 16][16];
 #pragma unroll
-  for (int j = 0; j < AT_KEYS / 16; j++) {
-    uint32_t r[16];
-    at_ld16(tmem + lane_base + j * 16, r);
-    at_wait_ld();
+  for (int j = 0; j < AT_KEYS / 16; j++) at_ld16(G.tmem + lane_base + j * 16, r[j]);
+  at_wait_ld();
 #pragma unroll
-    for (int i = 0; i < 16; i++) sc[j * 16 + i] = __uint_as_float(r[i]);
-  }
+  for (int j = 0; j < AT_KEYS / 16; j++)
+#pragma unroll
+    for (int i = 0; i < 16; i++) sc[j * 16 + i] = __uint_as_float(r[j][i]) * k;
 }
 
 // This thread's softmax weights as the binary16 pair of its P row.
-__device__ __forceinline__ void at_write_p(const AtSmem& sm, const float (&p)[AT_KEYS]) {
+__device__ __forceinline__ void at_write_p(const AtGroup& G, const float (&p)[AT_KEYS]) {
+  const uint32_t p_piece = 2 * AT_ROWS * AT_KEYS;
 #pragma unroll
   for (int c = 0; c < AT_KEYS / 8; c++) {
     uint32_t h[4], lo[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) at_split2(p[8 * c + 2 * j], p[8 * c + 2 * j + 1], h[j], lo[j]);
-    *reinterpret_cast<uint4*>(sm.ps + c * (AT_ROWS * 16) + threadIdx.x * 16) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4*>(sm.ps + sm.p_piece + c * (AT_ROWS * 16) + threadIdx.x * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(G.ps + c * (AT_ROWS * 16) + G.tid * 16) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(G.ps + p_piece + c * (AT_ROWS * 16) + G.tid * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
   }
 }
 
-// grid: (ceil(nshared / per), KVH, ceil(M * G / 128)); AT_THREADS threads.
-// Splits [blockIdx.x * per, min(nshared, +per)) of KV head blockIdx.y.
-// Requires a.kv.half, a.hd % 16 == 0, a.hd <= 256, a.split == AT_KEYS.
-__global__ void __launch_bounds__(AT_THREADS) k_attn_shared_tc(DecodeAttnArgs a, int nshared, int per, int* err) {
+// The online softmax of one block (scores in natural units, -inf where
+// masked): updates the running (m, l), turns sc into the block's weights
+// and returns alpha, the factor for the running outputs. A row that has seen
+// no visible position yet (a group's first blocks past its causal limit)
+// keeps m = -inf, l = 0 and gets zero weights.
+__device__ __forceinline__ float at_softmax(float (&sc)[AT_KEYS], float& m, float& l) {
+  float mb = m;
+#pragma unroll
+  for (int t = 0; t < AT_KEYS; t++) mb = fmaxf(mb, sc[t]);
+  const float alpha = m == -INFINITY ? 0.f : at_ex2((m - mb) * AT_LOG2E);
+  const float mref = mb == -INFINITY ? 0.f : mb;  // -inf - -inf would be NaN
+  float ls = 0.f;
+#pragma unroll
+  for (int t = 0; t < AT_KEYS; t++) {
+    sc[t] = at_ex2((sc[t] - mref) * AT_LOG2E);
+    ls += sc[t];
+  }
+  l = l * alpha + ls;
+  m = mb;
+  return alpha;
+}
+
+// o = o alpha + (the block's P V from TMEM).
+template <int HD>
+__device__ __forceinline__ void at_acc_values(const AtGroup& G, float alpha, float (&o)[HD]) {
+  const uint32_t lane_base = (uint32_t)((G.tid >> 5) * 32) << 16;
+#pragma unroll
+  for (int c0 = 0; c0 < HD; c0 += 16) {
+    uint32_t r[16];
+    at_ld16(G.tmem + lane_base + 128 + c0, r);
+    at_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 16; i++) o[c0 + i] = fmaf(o[c0 + i], alpha, __uint_as_float(r[i]));
+  }
+}
+
+// One group's pass over key blocks j = j0, j0 + step, ... < nblk of KV head
+// kvh: the online softmax state (o, m, l) of the group's query rows. qpos:
+// this row's last visible position (causal mask), or INT_MAX.
+template <int HD>
+__device__ __forceinline__ void at_blocks(const AtSmem& sm, const AtGroup& G, const KVView& kv, int layer, const int* page_table, int kvh,
+                                          int j0, int step, int nblk, int last, int qpos, float k, int* err, float (&o)[HD], float& m,
+                                          float& l) {
+#pragma unroll
+  for (int c = 0; c < HD; c++) o[c] = 0.f;
+  m = -INFINITY;
+  l = 0.f;
+  if (j0 >= nblk) return;
+  uint32_t phase = 0;
+  at_load_kv(G, HD, 0, kv, layer, page_table, kvh, j0 * AT_KEYS, last);
+  for (int j = j0, it = 0; j < nblk; j += step, it++) {
+    const int st = it & 1, t0 = j * AT_KEYS;
+    if (j + step < nblk) {
+      at_load_kv(G, HD, st ^ 1, kv, layer, page_table, kvh, t0 + step * AT_KEYS, last);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    at_publish(G);
+    if (G.tid == 0) at_issue_scores(sm, G, st);
+    if (at_wait_mma(G, phase, err)) break;
+    float sc[AT_KEYS];
+    at_ld_scores(G, k, sc);
+    if (qpos < t0 + AT_KEYS - 1) {
+#pragma unroll
+      for (int t = 0; t < AT_KEYS; t++)
+        if (t0 + t > qpos) sc[t] = -INFINITY;
+    }
+    const float alpha = at_softmax(sc, m, l);
+    at_write_p(G, sc);
+    at_publish(G);
+    if (G.tid == 0) at_issue_values(sm, G, st);
+    if (at_wait_mma(G, phase, err)) break;
+    at_acc_values<HD>(G, alpha, o);
+  }
+}
+
+// grid: (runs, KVH, ceil(M * G / 128)); 128 threads (one group); HD = hd.
+// Run r covers splits [r * per, min(nshared, (r + 1) * per)) of KV head
+// blockIdx.y and writes its partial into slot r of each row's partials.
+// Requires a.kv.half and a.split == AT_KEYS.
+template <int HD>
+__global__ void __launch_bounds__(AT_GROUP) k_attn_shared_tc(DecodeAttnArgs a, int nshared, int per, int* err) {
   extern __shared__ __align__(128) uint8_t at_smem[];
-  const int hd = a.hd, g = blockIdx.y, G = a.H / a.KVH, nrow = a.M * G;
+  const int kvh = blockIdx.y, Gq = a.H / a.KVH, nrow = a.M * Gq;
   const int q0 = blockIdx.z * AT_ROWS;
   const int s_lo = blockIdx.x * per, s_hi = min(nshared, s_lo + per);
   const int tid = threadIdx.x;
   if (s_lo >= s_hi) return;
-  const AtSmem sm = at_carve(at_smem, hd);
-  at_begin(sm);
+  const AtSmem sm = at_carve(at_smem, HD, 1);
+  AtGroup G = at_group(at_smem, sm, 0);
+  at_begin(sm, 1);
 
   // Query rows: float32 staging in the K/V buffers (128 x hd floats fill
   // them exactly), then RoPE at the row's position and the binary16 pair.
-  float* qf = reinterpret_cast<float*>(sm.kvs);
-  for (int e = tid; e < AT_ROWS * hd; e += AT_THREADS) {
-    const int qi = e / hd, i = e % hd, row = q0 + qi;
-    qf[e] = row < nrow ? a.qkv[(size_t)(row / G) * a.qkv_stride + (g * G + row % G) * hd + i] : 0.f;
+  float* qf = reinterpret_cast<float*>(G.kvs);
+  for (int e = tid; e < AT_ROWS * HD; e += AT_GROUP) {
+    const int qi = e / HD, i = e % HD, row = q0 + qi;
+    qf[e] = row < nrow ? a.qkv[(size_t)(row / Gq) * a.qkv_stride + (kvh * Gq + row % Gq) * HD + i] : 0.f;
   }
   __syncthreads();
   const int row = q0 + tid;
   const bool valid = row < nrow;
-  const int sx = at_q_pieces<true>(sm, qf + tid * hd, valid, hd, a.rope, valid ? a.pos[row / G] : 0);
-  const float unscale = tc_pow2(-sx);
+  const int pos = valid ? a.pos[row / Gq] : 0;
+  const int sx = at_q_sx<true>(qf + tid * HD, valid, HD, a.rope, pos);
+  at_q_write<true>(sm, tid, qf + tid * HD, valid, a.rope, pos, sx);
+  const float k = tc_pow2(-sx) * (1.f / a.scale);
   tc_fence_before();
   __syncthreads();  // staging read; the K/V buffers are free
   tc_fence_after();
-  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm.tslot);
-  const int last = nshared * AT_KEYS - 1;
-  at_load_kv(sm, 0, a.kv, a.layer, a.page_table, g, s_lo * AT_KEYS, last, hd);
+  G.tmem = *reinterpret_cast<volatile uint32_t*>(sm.tslot);
 
-  uint32_t phase = 0;
-  for (int s = s_lo; s < s_hi; s++) {
-    const int st = (s - s_lo) & 1;
-    if (s + 1 < s_hi) {
-      at_load_kv(sm, st ^ 1, a.kv, a.layer, a.page_table, g, (s + 1) * AT_KEYS, last, hd);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    at_publish();
-    if (tid == 0) at_issue_scores(sm, tmem, st, hd);
-    if (at_wait_mma(sm, phase, err)) break;
-    float sc[AT_KEYS];
-    at_ld_scores(tmem, sc);
-    float m = -INFINITY;
+  float o[HD], m, l;
+  at_blocks<HD>(sm, G, a.kv, a.layer, a.page_table, kvh, s_lo, 1, s_hi, nshared * AT_KEYS - 1, INT_MAX, k, err, o, m, l);
+  if (valid) {
+    float* part = a.part + (((size_t)(row / Gq) * a.H + kvh * Gq + row % Gq) * a.max_splits + blockIdx.x) * (HD + 2);
 #pragma unroll
-    for (int t = 0; t < AT_KEYS; t++) {
-      sc[t] = __fdiv_rn(sc[t] * unscale, a.scale);
-      m = fmaxf(m, sc[t]);
-    }
-    float l = 0.f;
-#pragma unroll
-    for (int t = 0; t < AT_KEYS; t++) {
-      sc[t] = expf(sc[t] - m);
-      l += sc[t];
-    }
-    at_write_p(sm, sc);
-    at_publish();
-    if (tid == 0) at_issue_values(sm, tmem, st, hd);
-    if (at_wait_mma(sm, phase, err)) break;
-    float* part = valid ? a.part + (((size_t)(row / G) * a.H + g * G + row % G) * a.max_splits + s) * (hd + 2) : nullptr;
-    const uint32_t lane_base = (uint32_t)((tid >> 5) * 32) << 16;
-    for (int c0 = 0; c0 < hd; c0 += 16) {
-      uint32_t r[16];
-      at_ld16(tmem + lane_base + 128 + c0, r);
-      at_wait_ld();
-      if (valid) {
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) *reinterpret_cast<float2*>(part + c0 + i) = make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-      }
-    }
-    if (valid) *reinterpret_cast<float2*>(part + hd) = make_float2(m, l);
+    for (int c = 0; c < HD; c += 2) *reinterpret_cast<float2*>(part + c) = make_float2(o[c], o[c + 1]);
+    *reinterpret_cast<float2*>(part + HD) = make_float2(m, l);
   }
-  at_end(sm, tmem);
+  at_end(G.tmem, 1);
 }
 
 // Causal attention of a prefill chunk (attention.go:6-45: query i at
 // position start + i attends to positions [0, start + i]; q already
-// rotated) on the tensor cores, binary16 KV. One CTA per (tile of 128
-// queries, query head); 64-position key blocks in order with the online
-// softmax of k_attn_prefill: per block s = S 2^-sx / sqrt(hd), masked past
-// the query's position, m' = max(m, block max), alpha = expf(m - m'),
-// p = expf(s - m'), l = l alpha + sum p, o = o alpha + P V (the block's
-// P V from TMEM), out = o / l. NC = hd / 16.
-template <int NC>
-__global__ void __launch_bounds__(AT_THREADS) k_attn_prefill_tc(PrefillAttnArgs a, int* err) {
+// rotated). grid: (ceil(n / 128), H); NG groups of 128 threads take
+// alternate 64-position key blocks; group 0 merges their states and writes
+// out = o / l. HD = hd.
+template <int HD, int NG>
+__global__ void __launch_bounds__(AT_GROUP * NG) k_attn_prefill_tc(PrefillAttnArgs a, int* err) {
   extern __shared__ __align__(128) uint8_t at_smem[];
-  constexpr int HD = 16 * NC;
-  const int h = blockIdx.y, g = h / (a.H / a.KVH);
+  const int h = blockIdx.y, kvh = h / (a.H / a.KVH);
   const int q0 = blockIdx.x * AT_ROWS, nq = min(AT_ROWS, a.n - q0);
   const int tid = threadIdx.x;
-  const AtSmem sm = at_carve(at_smem, HD);
-  at_begin(sm);
-  float* qf = reinterpret_cast<float*>(sm.kvs);
-  for (int e = tid; e < AT_ROWS * HD; e += AT_THREADS) {
+  const AtSmem sm = at_carve(at_smem, HD, NG);
+  AtGroup G = at_group(at_smem, sm, tid / AT_GROUP);
+  at_begin(sm, NG);
+  float* qf = reinterpret_cast<float*>(sm.qs + 4 * AT_ROWS * HD);  // group 0's K/V stages
+  for (int e = tid; e < AT_ROWS * HD; e += AT_GROUP * NG) {
     const int qi = e / HD, i = e % HD;
     qf[e] = qi < nq ? a.qkv[(size_t)(q0 + qi) * a.qkv_stride + h * HD + i] : 0.f;
   }
   __syncthreads();
-  const bool valid = tid < nq;
-  const int sx = at_q_pieces<false>(sm, qf + tid * HD, valid, HD, Rope{}, 0);
-  const float unscale = tc_pow2(-sx);
+  const int r = G.tid;
+  const bool valid = r < nq;
+  const int sx = at_q_sx<false>(qf + r * HD, valid, HD, Rope{}, 0);
+  if (G.id == 1) at_q_write<false>(sm, r, qf + r * HD, valid, Rope{}, 0, sx);
+  const float k = tc_pow2(-sx) * (1.f / a.scale);
   tc_fence_before();
-  __syncthreads();
+  __syncthreads();  // staging read; the K/V buffers are free
   tc_fence_after();
-  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm.tslot);
+  const uint32_t tmem0 = *reinterpret_cast<volatile uint32_t*>(sm.tslot);
+  G.tmem = tmem0 + 256u * (G.id - 1);
   const int last = a.start + q0 + nq - 1;
-  const int qpos = valid ? a.start + q0 + tid : last;  // rows past the chunk copy the last row's mask
+  const int qpos = valid ? a.start + q0 + r : last;  // rows past the chunk copy the last row's mask
   const int nblk = last / AT_KEYS + 1;
-  at_load_kv(sm, 0, a.kv, a.layer, a.page_table, g, 0, last, HD);
 
-  float o[HD];
+  float o[HD], m, l;
+  at_blocks<HD>(sm, G, a.kv, a.layer, a.page_table, kvh, G.id - 1, NG, nblk, last, qpos, k, err, o, m, l);
+  if (NG > 1) {
+    // Group 1 hands (o, m, l) to group 0 through the Q and K/V buffers
+    // ([HD + 2][128] floats), after every group's copies and MMAs are done.
+    cp_async_wait<0>();
+    tc_fence_before();
+    __syncthreads();
+    float* xs = reinterpret_cast<float*>(sm.qs);
+    if (G.id == 2) {
 #pragma unroll
-  for (int c = 0; c < HD; c++) o[c] = 0.f;
-  float m = -INFINITY, l = 0.f;
-  uint32_t phase = 0;
-  const uint32_t lane_base = (uint32_t)((tid >> 5) * 32) << 16;
-  for (int j = 0; j < nblk; j++) {
-    const int st = j & 1, t0 = j * AT_KEYS;
-    if (j + 1 < nblk) {
-      at_load_kv(sm, st ^ 1, a.kv, a.layer, a.page_table, g, t0 + AT_KEYS, last, HD);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+      for (int c = 0; c < HD; c++) xs[c * AT_ROWS + r] = o[c];
+      xs[HD * AT_ROWS + r] = m;
+      xs[(HD + 1) * AT_ROWS + r] = l;
     }
-    at_publish();
-    if (tid == 0) at_issue_scores(sm, tmem, st, HD);
-    if (at_wait_mma(sm, phase, err)) break;
-    float sc[AT_KEYS];
-    at_ld_scores(tmem, sc);
-    float mb = -INFINITY;
+    __syncthreads();
+    if (G.id == 1) {
+      const float m1 = xs[HD * AT_ROWS + r], l1 = xs[(HD + 1) * AT_ROWS + r];
+      const float mm = fmaxf(m, m1);
+      const float a0 = m == -INFINITY ? 0.f : at_ex2((m - mm) * AT_LOG2E);
+      const float a1 = m1 == -INFINITY ? 0.f : at_ex2((m1 - mm) * AT_LOG2E);
+      l = l * a0 + l1 * a1;
 #pragma unroll
-    for (int t = 0; t < AT_KEYS; t++) {
-      sc[t] = t0 + t <= qpos ? __fdiv_rn(sc[t] * unscale, a.scale) : -INFINITY;
-      mb = fmaxf(mb, sc[t]);
-    }
-    const float mnew = fmaxf(m, mb);
-    const float alpha = m == -INFINITY ? 0.f : expf(m - mnew);
-    float ls = 0.f;
-#pragma unroll
-    for (int t = 0; t < AT_KEYS; t++) {
-      sc[t] = sc[t] == -INFINITY ? 0.f : expf(sc[t] - mnew);
-      ls += sc[t];
-    }
-    l = l * alpha + ls;
-    m = mnew;
-    at_write_p(sm, sc);
-    at_publish();
-    if (tid == 0) at_issue_values(sm, tmem, st, HD);
-    if (at_wait_mma(sm, phase, err)) break;
-#pragma unroll
-    for (int c0 = 0; c0 < HD; c0 += 16) {
-      uint32_t r[16];
-      at_ld16(tmem + lane_base + 128 + c0, r);
-      at_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 16; i++) o[c0 + i] = __fadd_rn(__fmul_rn(o[c0 + i], alpha), __uint_as_float(r[i]));
+      for (int c = 0; c < HD; c++) o[c] = o[c] * a0 + xs[c * AT_ROWS + r] * a1;
     }
   }
-  if (valid) {
-    float* out = a.out + (size_t)(q0 + tid) * a.out_stride + h * HD;
+  if (G.id == 1 && valid) {
+    float* out = a.out + (size_t)(q0 + r) * a.out_stride + h * HD;
+    const float inv = 1.f / l;
 #pragma unroll
-    for (int c = 0; c < HD; c++) out[c] = __fdiv_rn(o[c], l);
+    for (int c = 0; c < HD; c++) out[c] = o[c] * inv;
   }
-  at_end(sm, tmem);
+  at_end(tmem0, NG);
 }
 
 }  // namespace tcu

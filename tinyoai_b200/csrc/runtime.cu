@@ -1593,23 +1593,28 @@ static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M,
   a.out_stride = m->aw + m->ff;
   a.scale = (float)sqrt((double)m->hd);
   a.s_begin = 0;
+  a.s_runs = 0;
   const int es = pool->half ? 2 : 4;
   const int G = m->H / m->KVH;
   // Splits every row shares (branches): keys and values read once for all
   // rows; the per-row kernels start after them.
-  if (w->shared_splits > 0 && a.split == AT_KEYS && w->shared_splits < grid_splits && pool->half && m->use_tc_attn &&
-      m->hd % 16 == 0 && m->hd <= 256 && at_smem_bytes(m->hd) <= (size_t)m->gemv_smem_optin) {
-    // Tensor cores: runs of splits per CTA, about two CTAs per SM.
+  const int hd16 = m->hd % 16 == 0 ? m->hd / 16 : 0;
+  const bool tc_hd = hd16 == 4 || hd16 == 5 || hd16 == 6 || hd16 == 8;
+  if (w->shared_splits > 0 && a.split == AT_KEYS && w->shared_splits < grid_splits && pool->half && m->use_tc_attn && tc_hd &&
+      at_smem_bytes(m->hd, 1) <= (size_t)m->gemv_smem_optin) {
+    // Tensor cores: one merged partial per run of splits, about two CTAs per SM.
     const int qt = (M * G + AT_ROWS - 1) / AT_ROWS;
     const int want = std::max(1, 2 * m->sm_count / (m->KVH * qt));
     const int per = (w->shared_splits + want - 1) / want;
     const int runs = (w->shared_splits + per - 1) / per;
-    const size_t smem = at_smem_bytes(m->hd);
-    cudaFuncSetAttribute(k_attn_shared_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const size_t smem = at_smem_bytes(m->hd, 1);
+    auto kern = hd16 == 4 ? k_attn_shared_tc<64> : hd16 == 5 ? k_attn_shared_tc<80> : hd16 == 6 ? k_attn_shared_tc<96> : k_attn_shared_tc<128>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     NOTE("cudaFuncSetAttribute(k_attn_shared_tc)");
-    k_attn_shared_tc<<<dim3(runs, m->KVH, qt), AT_THREADS, smem, s>>>(a, w->shared_splits, per, w->err);
+    kern<<<dim3(runs, m->KVH, qt), AT_GROUP, smem, s>>>(a, w->shared_splits, per, w->err);
     NOTE("k_attn_shared_tc");
     a.s_begin = w->shared_splits;
+    a.s_runs = runs;
   } else if (w->shared_splits > 0 && a.split == PA_KT && w->shared_splits < grid_splits) {
     const int nc = (m->hd + 15) / 16;
     auto kern = nc <= 2 ? k_attn_shared<2> : nc <= 4 ? k_attn_shared<4> : nc <= 5 ? k_attn_shared<5> : k_attn_shared<8>;
@@ -1962,14 +1967,21 @@ static void enqueue_prefill(const tcu_model* m, KVPool* pool, Work* w, int n, in
     pa.scale = (float)sqrt((double)m->hd);
     const int hd16 = m->hd % 16 == 0 ? m->hd / 16 : 0;
     if (pool->half && m->use_tc_attn && (hd16 == 4 || hd16 == 5 || hd16 == 6 || hd16 == 8) &&
-        at_smem_bytes(m->hd) <= (size_t)m->gemv_smem_optin) {
-      // Tensor cores (binary16 KV): one CTA per 128 queries and head.
-      auto kern = hd16 == 4 ? k_attn_prefill_tc<4> : hd16 == 5 ? k_attn_prefill_tc<5> : hd16 == 6 ? k_attn_prefill_tc<6> : k_attn_prefill_tc<8>;
-      const size_t smem = at_smem_bytes(m->hd);
+        at_smem_bytes(m->hd, 1) <= (size_t)m->gemv_smem_optin) {
+      // Tensor cores (binary16 KV): one CTA per 128 queries and head; two
+      // groups of four warps on alternate key blocks where shared memory
+      // allows.
+      auto pick = [&](int ng) -> void (*)(PrefillAttnArgs, int*) {
+        if (ng == 2) return hd16 == 4 ? k_attn_prefill_tc<64, 2> : hd16 == 5 ? k_attn_prefill_tc<80, 2> : hd16 == 6 ? k_attn_prefill_tc<96, 2> : nullptr;
+        return hd16 == 4 ? k_attn_prefill_tc<64, 1> : hd16 == 5 ? k_attn_prefill_tc<80, 1> : hd16 == 6 ? k_attn_prefill_tc<96, 1> : k_attn_prefill_tc<128, 1>;
+      };
+      const int ng = pick(2) && at_smem_bytes(m->hd, 2) <= (size_t)m->gemv_smem_optin ? 2 : 1;
+      void (*kern)(PrefillAttnArgs, int*) = pick(ng);
+      const size_t smem = at_smem_bytes(m->hd, ng);
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       NOTE("cudaFuncSetAttribute(k_attn_prefill_tc)");
       PROF_BEGIN(ST_PF_ATTN, s);
-      kern<<<dim3((n + AT_ROWS - 1) / AT_ROWS, m->H), AT_THREADS, smem, s>>>(pa, w->err);
+      kern<<<dim3((n + AT_ROWS - 1) / AT_ROWS, m->H), AT_GROUP * ng, smem, s>>>(pa, w->err);
       NOTE("k_attn_prefill_tc");
     } else {
       const size_t smem = pa_smem_bytes(m->hd);
