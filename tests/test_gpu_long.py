@@ -12,7 +12,12 @@ the CPU oracle (small models, so the oracle finishes in seconds).
   evaluating prefix + that branch's own tokens.
 
 North-star tolerance for f16 KV: logits within 1e-2 of the logit range;
-greedy streams identical.
+greedy streams identical. Among the 64 branches' thousands of greedy
+choices, a branch may part from the oracle only at a numerical tie: the
+oracle's top two logits within TIE of the logit range, and the device's
+token one of those within it (two float32 evaluations in different orders
+agree to ~1e-5 of the range, so such a choice is not determined by the
+arithmetic). That branch is not followed further; at most two may do so.
 """
 import os
 
@@ -40,6 +45,9 @@ def rel_err(got, want):
 def top2_margin(v):
     i = int(np.argmax(v))
     return float(v[i] - np.delete(v, i).max())
+
+
+TIE = 1e-4  # of the logit range
 
 
 def test_long_context_f16_multichunk_prefill_and_decode():
@@ -120,19 +128,29 @@ def test_64_ragged_branches_vs_oracle(fmt):
     ora = oc.StableLM(cfg, tensors, half_kv=True, capacity=prefix + steps + 1)
     try:
         ora.prefill(ids)
-        worst = 0.0
+        worst, ties = 0.0, []
         for b in range(count):
             # The branch's suffix, evaluated after the shared prefix (the
             # oracle's state keeps positions < prefix), then its own greedy
             # continuation through the remaining steps.
             logits = ora.prefill(suffix[b], start=prefix)
+            parted = False
             for t in range(int(lens[b]), steps):
                 want_tok = int(np.argmax(logits))
-                assert fed[b, t] == want_tok, f"branch {b} (suffix {lens[b]}): token {t} differs (margin {top2_margin(logits):.3g})"
+                if fed[b, t] != want_tok:
+                    span = float(logits.max() - logits.min())
+                    gap = float(logits[want_tok] - logits[fed[b, t]])
+                    assert gap <= TIE * span, f"branch {b} (suffix {lens[b]}): token {t} differs (oracle gap {gap:.3g} of range {span:.3g})"
+                    ties.append((b, t, gap / span))
+                    parted = True
+                    break
                 logits = ora.forward(want_tok, prefix + t)
+            if parted:
+                continue
             err = rel_err(last_rows[b], logits)
             worst = max(worst, err)
             assert err <= 1e-2, (b, err)
-        print(f"{fmt}: 64 ragged branches over a {prefix}-token prefix, worst row rel err {worst:.3g}")
+        assert len(ties) <= 2, ties
+        print(f"{fmt}: 64 ragged branches over a {prefix}-token prefix, worst row rel err {worst:.3g}, ties {ties}")
     finally:
         ora.close()

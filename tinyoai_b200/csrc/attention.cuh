@@ -121,18 +121,25 @@ struct DecodeAttnArgs {
   float scale;  // float32(sqrt(hd))
   int s_begin;  // splits below this are computed for all rows by k_attn_shared
   int s_runs;   // > 0: the shared splits left s_runs merged partials in slots [0, s_runs)
+  int per;      // k_attn_decode_bulk: splits per CTA (1 elsewhere)
 };
 
-// Partial slots of a row's merge: the first `lo` slots, then the per-row
-// splits from slot lo + off on (off = 0: slots 0 .. n-1 in order).
+// Partial slots of a row's merge: the first `lo` slots (the shared splits'
+// partials), then the row's own partials from slot lo + off on.
 struct SplitSlots {
   int n, lo, off;
   __device__ __forceinline__ int operator()(int j) const { return j < lo ? j : j + off; }
 };
 
+// The row's own splits [s_begin, nsplit) leave one partial per run of `per`
+// splits, in slots s_begin, s_begin + 1, ...; the shared splits below s_begin
+// leave s_runs partials in slots [0, s_runs) (tensor cores) or one per split
+// (s_runs = 0).
 __device__ __forceinline__ SplitSlots split_slots(const DecodeAttnArgs& a, int nsplit) {
-  if (a.s_runs > 0 && a.s_begin > 0) return SplitSlots{a.s_runs + nsplit - a.s_begin, a.s_runs, a.s_begin - a.s_runs};
-  return SplitSlots{nsplit, nsplit, 0};
+  const int per = a.per > 0 ? a.per : 1;
+  const int nruns = (nsplit - a.s_begin + per - 1) / per;
+  const int lo = a.s_runs > 0 && a.s_begin > 0 ? a.s_runs : a.s_begin;
+  return SplitSlots{lo + nruns, lo, a.s_begin - lo};
 }
 
 // Merges the sl.n partials (hd outputs, max, sum; partial j in slot sl(j))
@@ -741,10 +748,17 @@ __global__ void k_finish_greedy(const unsigned long long* argmax, int* out_token
 
 
 // ---------------------------------------------------------------------------
-// Decode attention with the history staged by bulk copies: each CTA copies its
-// chunk's K and V page tiles ([P][hd], contiguous per page and kv head) into
-// shared memory with cp.async.bulk while it rotates q and the new k. Same
-// arithmetic and merge as k_attn_decode.
+// Decode attention with the history staged by bulk copies: CTA r of (row m,
+// KV head g) takes the run of splits [s_begin + r per, s_begin + (r + 1) per)
+// and copies each split's K and V page tiles ([P][hd], contiguous per page and
+// kv head) into shared memory with cp.async.bulk, the next split's while the
+// current one is computed (two stages). Per split the arithmetic of
+// k_attn_decode (scores as float32 dot products in dimension order divided
+// by sqrt(hd), the split's max, expf weights, position-order sums); the run
+// keeps the online merge of its splits (o = o expf(m - m') + o_split expf(m_s
+// - m')) and writes one partial into slot s_begin + r. The run holding the
+// last split rotates and stores the new token's k and v. The last CTA of the
+// row and KV head merges every partial (attn_merge_splits).
 
 __device__ __forceinline__ float kv_ld(const void* base, int half, size_t i) {
   return half ? __half2float(reinterpret_cast<const __half*>(base)[i]) : reinterpret_cast<const float*>(base)[i];
@@ -754,49 +768,67 @@ struct DecodeAttn2Extra {
   int* err;
 };
 
+// Dynamic shared memory of k_attn_decode_bulk: barriers, two stages of K and V
+// tiles, q, scores, the new k/v and the run's outputs.
+__host__ __device__ inline size_t attn_bulk_smem(int G, int split, int hd, int es) {
+  return 128 + 4 * (size_t)split * hd * es + sizeof(float) * (2 * (size_t)G * hd + (size_t)G * split + 2 * (size_t)hd);
+}
+
 __global__ void __launch_bounds__(128) k_attn_decode_bulk(DecodeAttnArgs a, DecodeAttn2Extra x) {
   extern __shared__ __align__(128) uint8_t ab_smem[];
-  const int s = blockIdx.x + a.s_begin, g = blockIdx.y, m = blockIdx.z;
-  const int hd = a.hd, G = a.H / a.KVH, split = a.split, P = a.kv.P;
+  const int r = blockIdx.x, g = blockIdx.y, m = blockIdx.z;
+  const int hd = a.hd, G = a.H / a.KVH, split = a.split, P = a.kv.P, per = a.per;
   const int es = a.kv.half ? 2 : 4;
   pdl_launch_dependents();
   pdl_wait();
   const int pos = a.pos[m];
   const int T = pos + 1;
   const int nsplit = (T + split - 1) / split;
-  if (s >= nsplit) return;
-  const int t0 = s * split;
-  const int nt = min(T, t0 + split) - t0;
-  const bool has_cur = (s == nsplit - 1);
-  const int n_hist = has_cur ? nt - 1 : nt;
+  const int s_first = a.s_begin + r * per;
+  if (s_first >= nsplit) return;
+  const int s_last = min(nsplit, s_first + per) - 1;
+  const bool has_cur = s_last == nsplit - 1;
+  const size_t tile = (size_t)split * hd * es;
 
-  uint64_t* bar = reinterpret_cast<uint64_t*>(ab_smem);
-  uint8_t* ktile = ab_smem + 128;
-  uint8_t* vtile = ktile + (size_t)split * hd * es;
-  float* qs = reinterpret_cast<float*>(vtile + (size_t)split * hd * es);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(ab_smem);  // [2]
+  uint8_t* stages = ab_smem + 128;                        // [2][K tile, V tile]
+  float* qs = reinterpret_cast<float*>(stages + 4 * tile);
   float* sc = qs + G * hd;
   float* cur = sc + G * split;
+  float* orun = cur + 2 * hd;
   __shared__ int is_last;
-  __shared__ float mloc[32], lloc[32];
+  __shared__ float mloc[32], lloc[32], mrun[32], lrun[32];
 
   const int* pt = a.page_table + (size_t)m * a.pt_stride;
-  if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
-  const int npages = (n_hist + P - 1) / P;
-  if (threadIdx.x == 0 && npages > 0) {
+  // Thread 0: the bulk copies of split s's history pages into stage st.
+  auto issue = [&](int s, int st) {
+    const int t0 = s * split;
+    const int nt = min(T, t0 + split) - t0;
+    const int n_hist = s == nsplit - 1 ? nt - 1 : nt;
+    const int npages = (n_hist + P - 1) / P;
     const uint32_t pbytes = (uint32_t)(P * hd * es);
-    mbar_expect_tx(bar, 2u * npages * pbytes);
+    uint8_t* kt = stages + (size_t)st * 2 * tile;
+    mbar_expect_tx(bar + st, 2u * npages * pbytes);  // no pages: the phase completes at once
     for (int j = 0; j < npages; j++) {
       const int page = pt[t0 / P + j];
       const size_t o = a.kv.off(a.layer, page, g, 0) * es;
-      bulk_g2s(ktile + (size_t)j * pbytes, reinterpret_cast<const uint8_t*>(a.kv.k) + o, pbytes, bar);
-      bulk_g2s(vtile + (size_t)j * pbytes, reinterpret_cast<const uint8_t*>(a.kv.v) + o, pbytes, bar);
+      bulk_g2s(kt + (size_t)j * pbytes, reinterpret_cast<const uint8_t*>(a.kv.k) + o, pbytes, bar + st);
+      bulk_g2s(kt + tile + (size_t)j * pbytes, reinterpret_cast<const uint8_t*>(a.kv.v) + o, pbytes, bar + st);
     }
+  };
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    mbar_init(bar + 1, 1);
+    fence_barrier_init();
   }
-  // While the copies fly: q of the group and, in the last chunk, the new k/v.
+  if (threadIdx.x < G) {
+    mrun[threadIdx.x] = -INFINITY;
+    lrun[threadIdx.x] = 0.f;
+  }
+  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) orun[e] = 0.f;
+  __syncthreads();
+  if (threadIdx.x == 0) issue(s_first, 0);
+  // While the copies fly: q of the group and, for the last split, the new k/v.
   const float* q_in = a.qkv + (size_t)m * a.qkv_stride;
   for (int e = threadIdx.x; e < G * hd; e += blockDim.x) qs[e] = q_in[(g * G) * hd + e];
   if (has_cur) {
@@ -820,77 +852,102 @@ __global__ void __launch_bounds__(128) k_attn_decode_bulk(DecodeAttnArgs a, Deco
       kv_store(a.kv, a.kv.v, o + e, cur[hd + e]);
     }
   }
-  if (npages > 0) mbar_wait(bar, 0, x.err);
-  __syncthreads();
-  // Scores. Each thread walks the head dimension starting at its own offset,
-  // so the threads of a warp read distinct banks of their key rows.
-  for (int e = threadIdx.x; e < G * split; e += blockDim.x) {
-    const int hh = e / split, t = e % split;
-    if (t < nt) {
-      const float* q = qs + hh * hd;
-      float d = 0.f;
-      int i0 = t % hd;
-      if (has_cur && t == nt - 1) {
-        for (int i = 0; i < hd; i++) {
-          int ii = i0 + i;
-          ii -= ii >= hd ? hd : 0;
-          d = fmaf(q[ii], cur[ii], d);
-        }
-      } else {
-        const size_t rowo = (size_t)t * hd;
-        for (int i = 0; i < hd; i++) {
-          int ii = i0 + i;
-          ii -= ii >= hd ? hd : 0;
-          d = fmaf(q[ii], kv_ld(ktile, a.kv.half, rowo + ii), d);
-        }
-      }
-      sc[hh * split + t] = __fdiv_rn(d, a.scale);
-    }
-  }
-  __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  for (int hh = warp; hh < G; hh += nwarps) {
-    float mx = -INFINITY;
-    for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, sc[hh * split + t]);
+  for (int s = s_first, i = 0; s <= s_last; s++, i++) {
+    const int st = i & 1;
+    if (threadIdx.x == 0 && s < s_last) {
+      fence_proxy_async();  // the stage's earlier reads come before the copies into it
+      issue(s + 1, st ^ 1);
+    }
+    const int t0 = s * split;
+    const int nt = min(T, t0 + split) - t0;
+    const bool cur_here = s == nsplit - 1;
+    const int n_hist = cur_here ? nt - 1 : nt;
+    mbar_wait(bar + st, (i >> 1) & 1, x.err);
+    const uint8_t* ktile = stages + (size_t)st * 2 * tile;
+    const uint8_t* vtile = ktile + tile;
+    // Scores. Each thread walks the head dimension starting at its own offset,
+    // so the threads of a warp read distinct banks of their key rows.
+    for (int e = threadIdx.x; e < G * split; e += blockDim.x) {
+      const int hh = e / split, t = e % split;
+      if (t < nt) {
+        const float* q = qs + hh * hd;
+        float d = 0.f;
+        int i0 = t % hd;
+        if (cur_here && t == nt - 1) {
+          for (int k = 0; k < hd; k++) {
+            int ii = i0 + k;
+            ii -= ii >= hd ? hd : 0;
+            d = fmaf(q[ii], cur[ii], d);
+          }
+        } else {
+          const size_t rowo = (size_t)t * hd;
+          for (int k = 0; k < hd; k++) {
+            int ii = i0 + k;
+            ii -= ii >= hd ? hd : 0;
+            d = fmaf(q[ii], kv_ld(ktile, a.kv.half, rowo + ii), d);
+          }
+        }
+        sc[hh * split + t] = __fdiv_rn(d, a.scale);
+      }
+    }
+    __syncthreads();
+    for (int hh = warp; hh < G; hh += nwarps) {
+      float mx = -INFINITY;
+      for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, sc[hh * split + t]);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float l = 0.f;
-    for (int t = lane; t < nt; t += 32) {
-      float p = expf(sc[hh * split + t] - mx);
-      sc[hh * split + t] = p;
-      l += p;
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float l = 0.f;
+      for (int t = lane; t < nt; t += 32) {
+        float p = expf(sc[hh * split + t] - mx);
+        sc[hh * split + t] = p;
+        l += p;
+      }
+      l = warp_sum(l);
+      if (lane == 0) {
+        mloc[hh] = mx;
+        lloc[hh] = l;
+      }
     }
-    l = warp_sum(l);
-    if (lane == 0) {
-      mloc[hh] = mx;
-      lloc[hh] = l;
+    __syncthreads();
+    for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
+      const int hh = e / hd, k = e % hd;
+      float o = 0.f;
+      for (int t = 0; t < n_hist; t++) o = fmaf(sc[hh * split + t], kv_ld(vtile, a.kv.half, (size_t)t * hd + k), o);
+      if (cur_here) o = fmaf(sc[hh * split + nt - 1], cur[hd + k], o);
+      const float mo = mrun[hh], mn = fmaxf(mo, mloc[hh]);
+      const float alpha = mo == -INFINITY ? 0.f : expf(mo - mn), beta = expf(mloc[hh] - mn);
+      orun[e] = orun[e] * alpha + o * beta;
     }
+    __syncthreads();
+    if (threadIdx.x < G) {
+      const float mo = mrun[threadIdx.x], mn = fmaxf(mo, mloc[threadIdx.x]);
+      const float alpha = mo == -INFINITY ? 0.f : expf(mo - mn), beta = expf(mloc[threadIdx.x] - mn);
+      lrun[threadIdx.x] = lrun[threadIdx.x] * alpha + lloc[threadIdx.x] * beta;
+      mrun[threadIdx.x] = mn;
+    }
+    __syncthreads();
   }
-  __syncthreads();
   float* part = a.part + ((size_t)m * a.H + g * G) * a.max_splits * (hd + 2);
-  for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
-    const int hh = e / hd, i = e % hd;
-    float o = 0.f;
-    for (int t = 0; t < n_hist; t++) o = fmaf(sc[hh * split + t], kv_ld(vtile, a.kv.half, (size_t)t * hd + i), o);
-    if (has_cur) o = fmaf(sc[hh * split + nt - 1], cur[hd + i], o);
-    part[((size_t)hh * a.max_splits + s) * (hd + 2) + i] = o;
-  }
+  const int slot = a.s_begin + r;
+  for (int e = threadIdx.x; e < G * hd; e += blockDim.x)
+    part[((size_t)(e / hd) * a.max_splits + slot) * (hd + 2) + e % hd] = orun[e];
   if (threadIdx.x < G) {
-    part[((size_t)threadIdx.x * a.max_splits + s) * (hd + 2) + hd] = mloc[threadIdx.x];
-    part[((size_t)threadIdx.x * a.max_splits + s) * (hd + 2) + hd + 1] = lloc[threadIdx.x];
+    part[((size_t)threadIdx.x * a.max_splits + slot) * (hd + 2) + hd] = mrun[threadIdx.x];
+    part[((size_t)threadIdx.x * a.max_splits + slot) * (hd + 2) + hd + 1] = lrun[threadIdx.x];
   }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
+    const int nruns = (nsplit - a.s_begin + per - 1) / per;
     int prev = atomicAdd(a.counters + m * a.KVH + g, 1);
-    is_last = (prev == nsplit - a.s_begin - 1);
+    is_last = (prev == nruns - 1);
   }
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  // Merge the nsplit partial states of each head in the group (the key
-  // tile's shared memory is free by now).
-  attn_merge_splits(part, a.max_splits, hd, G, split_slots(a, nsplit), reinterpret_cast<float*>(ktile), split * hd * es / 4,
+  // Merge every partial of each head in the group (the stages are free).
+  attn_merge_splits(part, a.max_splits, hd, G, split_slots(a, nsplit), reinterpret_cast<float*>(stages), (int)(4 * tile / 4),
                     a.out + (size_t)m * a.out_stride + g * G * hd);
   if (threadIdx.x == 0) a.counters[m * a.KVH + g] = 0;
 }

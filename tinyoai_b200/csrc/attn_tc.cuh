@@ -349,18 +349,18 @@ __device__ __forceinline__ float at_softmax(float (&sc)[AT_KEYS], float& m, floa
   return alpha;
 }
 
-// o = o alpha + (the block's P V from TMEM).
+// o = o alpha + (the block's P V from TMEM; all columns loaded, then one wait).
 template <int HD>
 __device__ __forceinline__ void at_acc_values(const AtGroup& G, float alpha, float (&o)[HD]) {
   const uint32_t lane_base = (uint32_t)((G.tid >> 5) * 32) << 16;
+  uint32_t r[HD / 16][16];
 #pragma unroll
-  for (int c0 = 0; c0 < HD; c0 += 16) {
-    uint32_t r[16];
-    at_ld16(G.tmem + lane_base + 128 + c0, r);
-    at_wait_ld();
+  for (int c = 0; c < HD / 16; c++) at_ld16(G.tmem + lane_base + 128 + 16 * c, r[c]);
+  at_wait_ld();
 #pragma unroll
-    for (int i = 0; i < 16; i++) o[c0 + i] = fmaf(o[c0 + i], alpha, __uint_as_float(r[i]));
-  }
+  for (int c = 0; c < HD / 16; c++)
+#pragma unroll
+    for (int i = 0; i < 16; i++) o[16 * c + i] = fmaf(o[16 * c + i], alpha, __uint_as_float(r[c][i]));
 }
 
 // One group's pass over key blocks j = j0, j0 + step, ... < nblk of KV head

@@ -127,6 +127,10 @@ __device__ __forceinline__ float kquant_at(const uint8_t* block, int i, int fmt)
 }
 
 __host__ __device__ inline int kquant_block_bytes(int fmt) { return fmt == FMT_Q5_1 ? 24 : fmt == FMT_Q6_K ? 210 : 176; }
+// Bytes between super-blocks in device memory: a Q6_K block (210 bytes in
+// the file) is padded to 224, so that its ql, qh and scale sections start on
+// 16-byte boundaries; Q5_K (176) and Q5_1 keep the file's size.
+__host__ __device__ inline int kquant_dev_bytes(int fmt) { return fmt == FMT_Q6_K ? 224 : kquant_block_bytes(fmt); }
 __host__ __device__ inline int kquant_block_width(int fmt) { return fmt == FMT_Q5_1 ? 32 : 256; }
 
 // Eight values W[r][k0 .. k0 + 8) of a Q6_K or Q5_K matrix whose rows are
@@ -136,7 +140,7 @@ __host__ __device__ inline int kquant_block_width(int fmt) { return fmt == FMT_Q
 __device__ __forceinline__ void kquant_decode8(const DMat& W, int r, int k0, float* dst) {
   const int K = W.cols;
   const int i0 = k0 & 255;
-  const uint8_t* blk = W.w + ((size_t)r * (K >> 8) + (k0 >> 8)) * (W.fmt == FMT_Q6_K ? 210 : 176);
+  const uint8_t* blk = W.w + ((size_t)r * (K >> 8) + (k0 >> 8)) * (W.fmt == FMT_Q6_K ? 224 : 176);
   if (W.fmt == FMT_Q6_K) {
     const float d = __half2float(__ushort_as_half((unsigned short)(blk[208] | (blk[209] << 8))));
     const float scale = __fmul_rn(d, (float)(int8_t)blk[192 + i0 / 16]);
@@ -185,7 +189,7 @@ __device__ __forceinline__ float dmat_at(const DMat& m, int r, int c) {
     case FMT_BF16:
       return bf16_bits_to_float(((const uint16_t*)m.w)[(size_t)r * m.cols + c]);
     default: {
-      int width = kquant_block_width(m.fmt), bytes = kquant_block_bytes(m.fmt);
+      int width = kquant_block_width(m.fmt), bytes = kquant_dev_bytes(m.fmt);
       size_t index = (size_t)r * m.cols + c;
       return kquant_at(m.w + index / width * bytes, (int)(index % width), m.fmt);
     }

@@ -12,16 +12,16 @@
 // float32 product. Tiles of up to 128 tokens keep the three pieces within
 // one stage buffer.
 //
-// Q6_K / Q5_K weights: warps 0-15 decode each value as the reference does
-// (float32, quant_k.go:47-85), scale it by 2^sw and split it into three
-// binary16 pieces W' = Wh + Wm + Wl, each the rounding of what the previous
-// pieces leave (both differences are exact in float32). Eleven significant
-// bits per piece cover the decoded value's 24, so the operand is the
-// reference's float32 weight exactly whenever its lowest bit lands at or
-// above 2^-24 after scaling: every value within 2^14 of the matrix bound
-// 2^13 (tcu_read_values with TCU_DECODE_TC checks this bit for bit). Four
-// products Wh.Xh + Wh.Xl + Wm.Xh + Wl.Xh are accumulated; the dropped
-// Wm.Xl and Wl.Xl are ~2^-22 of the result, as for Q8_0 below.
+// Q6_K / Q5_K weights: warps 0-15 build three binary16 pieces whose sum is
+// the reference's float32 weight (quant_k.go:47-85) times 2^sw, exactly
+// whenever its lowest bit lands at or above 2^-24 after scaling: every value
+// within 2^14 of the matrix bound 2^13 (tcu_read_values with TCU_DECODE_TC
+// checks this bit for bit). Q6_K: the group scale d * sc split into three
+// six-bit pieces, each times the integer q - 32 (tc_q6k_pieces; exact
+// binary16 products, no float32 decode). Q5_K: the value decoded in float32
+// as the reference does, then W' = Wh + Wm + Wl, each piece the rounding of
+// what the previous ones leave. Five products W1.Xh + W1.Xl + W2.Xh + W2.Xl +
+// W3.Xh are accumulated; the dropped W3.Xl is ~2^-22 of the result.
 //
 // Q8_0 exactness: a Q8_0 weight
 // s*q has at most 19 significant bits and an activation 24, more than one
@@ -68,6 +68,7 @@ __host__ __device__ constexpr int tc_buf_bytes(int wm) { return tc_pieces(wm) * 
 // or 225.25 KB (K-quants) of the 227 KB a CTA may hold.
 __host__ __device__ constexpr int tc_smem_bytes(int wm) { return 2 * tc_buf_bytes(wm) + 1024 + 256; }
 static_assert(tc_smem_bytes(TCW_KQ) <= 227 * 1024, "tensor-core GEMM stage buffers exceed shared memory");
+static_assert(TC_DQW * 8 == TC_BM, "one weight row per decoding thread group and stage (the Q6_K prefetch relies on it)");
 
 struct TcArgs {
   DMat W;             // Q8_0 weights [rows][cols]
@@ -178,14 +179,86 @@ __device__ __forceinline__ void tc_dequant8(uint2 q, __half2 s2, uint4& hi, uint
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+// Top six significant bits of a float32 (sign, exponent and five stored
+// mantissa bits); x - tc_top6(x) is exact.
+__device__ __forceinline__ float tc_top6(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFC0000u); }
+
+// The Q6_K operand of sixteen weights W[r][k0 .. k0 + 16) (k0 % 16 == 0: one
+// scale group). The reference's value (quant_k.go:47-85) is
+// v = (d * sc) * (q - 32) with d binary16, sc int8 and q six bits: d * sc has
+// at most 18 significant bits and |q - 32| <= 32 at most 5, so both float32
+// products are exact and v = s * (q - 32) with s = d * sc. The scaled
+// s' = s * 2^sw is split into three pieces of at most six significant bits,
+// s' = s1 + s2 + s3 (each a masked remainder, exact), and each piece times
+// the integer q - 32 has at most 11 bits: an exact binary16 product
+// (HMUL2). So p1 + p2 + p3 = v * 2^sw exactly. The raw bytes come with one
+// 16-byte load each for the 16 low nibbles and the 16 high-bit pairs
+// (tc_q6k_load; the GEMM loads the next stage's while it builds this one).
+struct Q6Raw {
+  uint4 ql, qh;
+  float s;  // d * sc (exact), 0 for rows or columns past the matrix
+};
+
+__device__ __forceinline__ Q6Raw tc_q6k_load(const DMat& W, int r, int k0, bool valid) {
+  Q6Raw q;
+  if (!valid) {
+    q.ql = q.qh = make_uint4(0, 0, 0, 0);
+    q.s = 0.f;
+    return q;
+  }
+  const uint8_t* blk = W.w + ((size_t)r * (W.cols >> 8) + (k0 >> 8)) * 224;
+  const int i0 = k0 & 255;
+  q.ql = __ldg(reinterpret_cast<const uint4*>(blk + (i0 >> 7) * 64 + (i0 & 63)));
+  q.qh = __ldg(reinterpret_cast<const uint4*>(blk + 128 + (i0 >> 7) * 32 + (i0 & 31)));
+  const float d = __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(blk + 208))));
+  q.s = __fmul_rn(d, (float)(int8_t)__ldg(blk + 192 + (i0 >> 4)));
+  return q;
+}
+
+__device__ __forceinline__ void tc_q6k_build(const Q6Raw& q, int k0, float wscale, uint4 (&p)[3][2]) {
+  const int i0 = k0 & 255;
+  const float sc = __fmul_rn(q.s, wscale);
+  const float s1 = tc_top6(sc), r1 = __fsub_rn(sc, s1), s2 = tc_top6(r1), s3 = __fsub_rn(r1, s2);
+  const __half2 h1 = __float2half2_rn(s1), h2 = __float2half2_rn(s2), h3 = __float2half2_rn(s3);
+  const int ls = ((i0 & 127) >> 6) * 4, hs = ((i0 & 127) >> 5) * 2;
+  const uint32_t lw[4] = {q.ql.x, q.ql.y, q.ql.z, q.ql.w}, hw[4] = {q.qh.x, q.qh.y, q.qh.z, q.qh.w};
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6420), __ushort_as_half(0x6420));  // 1056 = 1024 + 32
+  uint32_t o1[8], o2[8], o3[8];
+#pragma unroll
+  for (int w = 0; w < 4; w++) {
+    const uint32_t q4 = ((lw[w] >> ls) & 0x0F0F0F0Fu) | (((hw[w] >> hs) & 0x03030303u) << 4);
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const uint32_t b = __byte_perm(q4, 0x64646464u, j == 0 ? 0x7170 : 0x7372);  // (1024 + q) pairs
+      const __half2 qq = __hsub2(*reinterpret_cast<const __half2*>(&b), bias);      // q - 32, exact
+      const __half2 a = __hmul2(h1, qq), m = __hmul2(h2, qq), l = __hmul2(h3, qq);
+      o1[2 * w + j] = *reinterpret_cast<const uint32_t*>(&a);
+      o2[2 * w + j] = *reinterpret_cast<const uint32_t*>(&m);
+      o3[2 * w + j] = *reinterpret_cast<const uint32_t*>(&l);
+    }
+  }
+  p[0][0] = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+  p[0][1] = make_uint4(o1[4], o1[5], o1[6], o1[7]);
+  p[1][0] = make_uint4(o2[0], o2[1], o2[2], o2[3]);
+  p[1][1] = make_uint4(o2[4], o2[5], o2[6], o2[7]);
+  p[2][0] = make_uint4(o3[0], o3[1], o3[2], o3[3]);
+  p[2][1] = make_uint4(o3[4], o3[5], o3[6], o3[7]);
+}
+
+__device__ __forceinline__ void tc_q6k_pieces(const DMat& W, int r, int k0, float wscale, uint4 (&p)[3][2]) {
+  tc_q6k_build(tc_q6k_load(W, r, k0, true), k0, wscale, p);
+}
+
 // The tensor-core operand of sixteen weights W[r][k0 .. k0 + 16), scaled by
 // wscale = 2^sw, as binary16 pieces p[piece][half] (eight values per uint4):
 //   Q8_0 (WM = TCW_Q8): the exact pair of tc_dequant8; values at or past
 //     k_end are zero;
-//   Q6_K / Q5_K (WM = TCW_KQ): each value decoded as kquant_decode8 does
-//     (the reference's float32 arithmetic), then split into three pieces,
-//     h = fp16(v), m = fp16(v - h), l = fp16(v - h - m). Rows are whole
-//     super-blocks (K % 256 == 0, k_end too), so k0 < k_end covers all 16.
+//   Q6_K (WM = TCW_KQ): tc_q6k_pieces;
+//   Q5_K (WM = TCW_KQ): each value decoded as kquant_decode8 does (the
+//     reference's float32 arithmetic), then split into three pieces,
+//     h = fp16(v), m = fp16(v - h), l = fp16(v - h - m).
+//   K-quant rows are whole super-blocks (K % 256 == 0, k_end too), so
+//   k0 < k_end covers all 16.
 // Rows r >= R give zeros. The GEMM's decoding warps and tcu_read_values
 // (TCU_DECODE_TC) both call this.
 template <int WM>
@@ -195,6 +268,10 @@ __device__ __forceinline__ void tc_weight_pieces(const DMat& W, int r, int k0, i
   for (int j = 0; j < tc_pieces(WM); j++) p[j][0] = p[j][1] = make_uint4(0, 0, 0, 0);
   if (r >= W.rows || k0 >= k_end) return;
   if constexpr (WM == TCW_KQ) {
+    if (W.fmt == FMT_Q6_K) {
+      tc_q6k_pieces(W, r, k0, wscale, p);
+      return;
+    }
     float v[16];
     kquant_decode8(W, r, k0, v);
     kquant_decode8(W, r, k0 + 8, v + 8);
@@ -323,7 +400,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
               first = false;
             }
           } else {
-            // Q8_0: Wh.Xh + Wh.Xl + Wl.Xh; K-quants: Wh.Xh + Wh.Xl + Wm.Xh + Wl.Xh.
+            // Q8_0: Wh.Xh + Wh.Xl + Wl.Xh; K-quants: W1.Xh + W1.Xl + W2.Xh + W2.Xl + W3.Xh.
             const uint64_t wh = tc_smem_desc(sa + off);
             const uint64_t xh = tc_smem_desc(sb + off), xl = tc_smem_desc(sb + TC_B_BYTES + off);
             tc_mma(d, wh, xh, idesc, first ? 0u : 1u);
@@ -331,6 +408,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             tc_mma(d, wh, xl, idesc, 1u);
 #pragma unroll
             for (int p = 1; p < NP; p++) tc_mma(d, tc_smem_desc(sa + p * TC_A_BYTES + off), xh, idesc, 1u);
+            if (WM == TCW_KQ) tc_mma(d, tc_smem_desc(sa + TC_A_BYTES + off), xl, idesc, 1u);
           }
         }
         tc_commit(&mma_done[b]);
@@ -342,14 +420,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     const int tid = threadIdx.x;  // 0..511
     const int kc = (tid & 3) * 16;
     const float wscale = tc_pow2(a.sw);
+    // Q6_K: each thread builds one row's 16 values per stage and loads the
+    // next stage's raw bytes first.
+    const bool q6 = WM == TCW_KQ && a.W.fmt == FMT_Q6_K;
+    Q6Raw nxt{};
+    if (q6 && iters > 0) nxt = tc_q6k_load(a.W, r0 + (tid >> 2), k_begin + kc, r0 + (tid >> 2) < R && k_begin + kc < k_end);
     for (int i = 0; i < (WB ? 0 : iters); i++) {
       const int b = i & 1;
+      const int k0 = k_begin + i * TC_BK + kc;
+      Q6Raw cur{};
+      if (q6) {
+        cur = nxt;
+        const int kn = k0 + TC_BK;
+        if (i + 1 < iters) nxt = tc_q6k_load(a.W, r0 + (tid >> 2), kn, r0 + (tid >> 2) < R && kn < k_end);
+      }
       if (i >= 2) mbar_wait(&mma_done[b], ((i >> 1) - 1) & 1, a.err);
       uint8_t* aw = buf(b);
-      const int k0 = k_begin + i * TC_BK + kc;
       for (int rr = tid >> 2; rr < TC_BM; rr += TC_DQW * 8) {
         uint4 pc[NP][2];
-        tc_weight_pieces<WM>(a.W, r0 + rr, k0, k_end, wscale, pc);
+        if constexpr (WM == TCW_KQ) {
+          if (q6)
+            tc_q6k_build(cur, k0, wscale, pc);
+          else
+            tc_weight_pieces<WM>(a.W, r0 + rr, k0, k_end, wscale, pc);
+        } else {
+          tc_weight_pieces<WM>(a.W, r0 + rr, k0, k_end, wscale, pc);
+        }
 #pragma unroll
         for (int p = 0; p < NP; p++) {
           *reinterpret_cast<uint4*>(aw + p * TC_A_BYTES + tc_sw128(rr, kc)) = pc[p][0];
@@ -517,7 +613,7 @@ __global__ void k_kquant_absmax(const uint8_t* w, size_t nblocks, int fmt, unsig
   for (size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x; b < nblocks; b += (size_t)gridDim.x * blockDim.x) {
     float v;
     if (fmt == FMT_Q6_K) {
-      const uint8_t* blk = w + b * 210;
+      const uint8_t* blk = w + b * 224;
       int ms = 0;
       for (int g = 0; g < 16; g++) ms = max(ms, abs((int)(int8_t)blk[192 + g]));
       v = fabsf(__half2float(__ushort_as_half((unsigned short)(blk[208] | (blk[209] << 8))))) * (float)ms * 32.f;

@@ -6,7 +6,8 @@ namespace tcu {
 
 // Copies a checkpoint tensor (file encoding) into a device matrix at
 // (row0 + i*row_step, col0), splitting Q8_0 blocks (gguf.go:186-189: 2-byte
-// binary16 scale + 32 int8) into the quant and scale planes.
+// binary16 scale + 32 int8) into the quant and scale planes and padding Q6_K
+// super-blocks to their device size (kquant_dev_bytes).
 struct RepackArgs {
   const uint8_t* raw;
   int fmt;
@@ -42,15 +43,16 @@ __global__ void k_repack(RepackArgs a) {
       for (int i = 0; i < es; i++) d[i] = s[i];
     }
   } else {
-    const int width = kquant_block_width(a.fmt), bytes = kquant_block_bytes(a.fmt);
+    const int width = kquant_block_width(a.fmt), bytes = kquant_block_bytes(a.fmt), dbytes = kquant_dev_bytes(a.fmt);
     const int nb = a.cols / width;
     const size_t total = (size_t)a.rows * nb;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
       const int r = (int)(idx / nb), b = (int)(idx % nb);
       const int dr = a.row0 + r * a.row_step;
-      uint8_t* d = dw + ((size_t)dr * (K2 / width) + a.col0 / width + b) * bytes;
+      uint8_t* d = dw + ((size_t)dr * (K2 / width) + a.col0 / width + b) * dbytes;
       const uint8_t* s = a.raw + idx * bytes;
       for (int i = 0; i < bytes; i++) d[i] = s[i];
+      for (int i = bytes; i < dbytes; i++) d[i] = 0;
     }
   }
 }

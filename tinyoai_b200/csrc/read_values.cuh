@@ -12,9 +12,9 @@ namespace tcu {
 enum ReadDecoder : int { RD_ELEMENT = 0, RD_GROUP8 = 1, RD_TC = 2 };
 
 // Value j (0..15) of a group of sixteen tensor-core operand pieces, summed
-// back in float32: Wh, + Wm (exact: at most 22 significant bits), + Wl.
-// Zero pieces are skipped, so a -0 weight (whose later pieces are +0) reads
-// back as -0.
+// back in float32 in piece order (each partial sum is exact: the pieces hold
+// disjoint bits of a value of at most 24 significant bits). Zero pieces
+// after the first are skipped, so a -0 weight reads back as -0.
 template <int NP>
 __device__ __forceinline__ float tc_pieces_value(const uint4 (&p)[NP][2], int j) {
   float s = 0.f;

@@ -212,7 +212,7 @@ static size_t fmt_row_bytes(int fmt, int cols) {
     case FMT_BF16:
       return (size_t)cols * 2;
     default:
-      return (size_t)cols / kquant_block_width(fmt) * kquant_block_bytes(fmt);
+      return (size_t)cols / kquant_block_width(fmt) * kquant_dev_bytes(fmt);
   }
 }
 
@@ -1594,6 +1594,7 @@ static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M,
   a.scale = (float)sqrt((double)m->hd);
   a.s_begin = 0;
   a.s_runs = 0;
+  a.per = 1;
   const int es = pool->half ? 2 : 4;
   const int G = m->H / m->KVH;
   // Splits every row shares (branches): keys and values read once for all
@@ -1625,14 +1626,18 @@ static void launch_attn_decode(const tcu_model* m, KVPool* pool, Work* w, int M,
     NOTE("k_attn_shared");
     a.s_begin = w->shared_splits;
   }
-  const size_t bulk_smem =
-      128 + 2 * (size_t)a.split * m->hd * es + sizeof(float) * ((size_t)G * m->hd + (size_t)G * a.split + 2 * m->hd);
+  const size_t bulk_smem = attn_bulk_smem(G, a.split, m->hd, es);
   if (!m->disable_stream && ((size_t)m->P * m->hd * es) % 16 == 0 && bulk_smem <= GS_SMEM_LIMIT && G <= 32) {
+    // Long histories (16+ splits past the shared ones): runs of splits per
+    // CTA, about five CTAs per SM, so the merge reads a partial per run.
+    const int rest = grid_splits - a.s_begin;
+    const int want = std::max(1, 5 * m->sm_count / (M * m->KVH));
+    a.per = rest >= 16 && rest > want ? std::min(8, (rest + want - 1) / want) : 1;
     DecodeAttn2Extra x{w->err};
     cudaFuncSetAttribute(k_attn_decode_bulk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bulk_smem);
     NOTE("cudaFuncSetAttribute(k_attn_decode_bulk)");
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid_splits - a.s_begin, m->KVH, M);
+    cfg.gridDim = dim3((rest + a.per - 1) / a.per, m->KVH, M);
     cfg.blockDim = dim3(128);
     cfg.dynamicSmemBytes = bulk_smem;
     cfg.stream = s;
@@ -3579,7 +3584,13 @@ extern "C" int tcu_read_values(int32_t device, int32_t dtype, const void* data, 
     k_repack<<<1184, 256>>>(ra);
     CK(cudaGetLastError());
   } else {
-    W.w = (const uint8_t*)raw;
+    // K-quants: the device super-block size of a loaded matrix.
+    void* q = nullptr;
+    TRY(bufs.get(&q, (size_t)rows * fmt_row_bytes(dtype, cols)));
+    W.w = (const uint8_t*)q;
+    RepackArgs ra{(const uint8_t*)raw, dtype, rows, cols, W, 0, 1, 0};
+    k_repack<<<1184, 256>>>(ra);
+    CK(cudaGetLastError());
   }
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
