@@ -467,6 +467,12 @@ def run_config(args):
     # f16 KV pages (32 layers; profiling cases with fewer layers need less).
     pool_floor = max(1024, 8192 * cfg["num_hidden_layers"] // 32)
     model = Model.load_stablelm(cfg, tensors, device=local, kv_pool_bytes=max(args.kv_pool_mb, pool_floor) << 20, tp=tp_arg)
+    if tp and args.tp_exchange == "peer":
+        # The per-layer exchange over NVLink peer memory (the library's kernel)
+        # rather than NCCL: the ranks share their CUDA IPC handles.
+        handles = [None] * world
+        dist.all_gather_object(handles, model.tp_exchange_handle())
+        model.tp_exchange_open(handles)
     torch.cuda.empty_cache()
     cpu_tensors = tensors if (rank == 0 and world == 1 and args.cpu_baseline) else None
     del tensors
@@ -593,7 +599,9 @@ def run_config(args):
                 "dtype": f"{c['fmt']} weights, f32 activations, f16 KV",
                 "data": "synthetic (seeded N(0,0.02) weights quantised to the format, uniform ids)",
                 "config": {"workload": c["workload"].format(fmt=c["fmt"]) + (f" [PROFILING CASE: {args.layers} layers]" if args.layers else ""),
-                           "parallelism": f"tp{world} (head-parallel, NCCL all-reduce per layer)" if tp else f"replicas x{world}",
+                           "parallelism": (f"tp{world} (head-parallel, one exchange per layer: "
+                                           + ("the library's kernel over NVLink peer memory)" if args.tp_exchange == "peer" else "NCCL all-reduce)"))
+                           if tp else f"replicas x{world}",
                            "l2": "inputs larger than L2 (GBs of weights per step)"},
                 "tp_comm": comm,
                 "prefill_tok_s": (1 if tp else world) * n_pf * args.steps / (pf_ms / 1e3), "prefill_tflops_per_gpu": pf_tfs,
@@ -787,6 +795,8 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
                     help="2: the bench line (default); 3, 4: BASELINE.json's long-context and branch workloads")
     ap.add_argument("--fmt", default=None, help="config 4 weight format: Q6_K (default) or Q5_K")
+    ap.add_argument("--tp-exchange", default="peer", choices=["peer", "nccl"],
+                    help="config 3 on N > 1 GPUs: per-layer exchange over NVLink peer memory (default) or NCCL")
     args = ap.parse_args()
     if args.config == 5 and args.impl == "b200":
         run_config5(args)

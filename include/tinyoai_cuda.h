@@ -118,6 +118,20 @@ int tcu_stablelm_load_tp(const tcu_stablelm_config* config, const tcu_tensor* te
  * KV head, KV heads, first MLP row, MLP rows. Needs no GPU. */
 int tcu_tp_plan(const tcu_stablelm_config* config, int32_t world, int32_t rank, int32_t* out);
 
+/* The per-layer exchange over NVLink peer memory instead of NCCL (no
+ * counterpart in the reference): every rank calls tcu_tp_exchange_handle
+ * (allocates its exchange buffer, returns its CUDA IPC handle), the ranks
+ * share the handles (any host channel), and every rank calls
+ * tcu_tp_exchange_open with all of them in rank order. From then on the
+ * exchange of up to 64 rows (decode steps) is one kernel per layer that stores
+ * this rank's partial into every rank's buffer, waits (bounded) for the
+ * others' and adds the rank-ordered sum to the residual, and tensor-parallel
+ * decode steps replay a captured CUDA graph; prefill chunks keep NCCL. Ranks
+ * on one node, at most 8. A wait that runs out returns TCU_ETIMEOUT. */
+#define TCU_TP_HANDLE_BYTES 64
+int tcu_tp_exchange_handle(tcu_model* model, uint8_t* handle);
+int tcu_tp_exchange_open(tcu_model* model, const uint8_t* handles);
+
 /* GGUF StableLM checkpoints (readGGUF and loadStableGGUF, gguf.go:139-357):
  * tcu_gguf_open memory-maps a GGUF v3 file, validates its header as the
  * reference does (magic and version, counts, metadata types, tensor ranks,

@@ -3,10 +3,14 @@
 Two processes, one GPU each, load their shares of a BF16 StableLM (the
 format of the long-context workload) with f16 KV and run the same calls: a
 1,200-token prompt in three prefill chunks, then 16 greedy tokens through the
-per-layer decode kernels, every layer ending in one NCCL all-reduce of the
-out + down partials. Both ranks must return the oracle's logits within the
-f16-KV tolerance (1e-2 of the logit range) and its greedy tokens. Skipped
-with fewer than two GPUs.
+per-layer decode kernels, every layer ending in one exchange of the out +
+down partials: NCCL's all-reduce, or (mode "peer", tcu_tp_exchange_open; the
+ranks share CUDA IPC handles) the library's own kernel over NVLink peer
+memory for the decode steps, replayed from a captured graph. Both ranks must
+return the oracle's logits within the f16-KV tolerance (1e-2 of the logit
+range) and its greedy tokens; every exchange gives every rank the same sums,
+so the two ranks' logits are bit-identical. Skipped with fewer than two
+GPUs.
 """
 import numpy as np
 import pytest
@@ -24,7 +28,7 @@ SMALL = dict(model_type="stablelm", vocab_size=2048, hidden_size=320, intermedia
 PROMPT, STEPS = 1200, 16
 
 
-def _rank(rank, world, nccl_id, out):
+def _rank(rank, world, nccl_id, out, mode, handles, barrier):
     import torch
     torch.cuda.set_device(rank)
     from tinyoai_b200 import Model
@@ -32,6 +36,10 @@ def _rank(rank, world, nccl_id, out):
     ids = prompt_ids(PROMPT, cfg["vocab_size"], seed=79)
     m = Model.load_stablelm(cfg, tensors, device=rank, tp=(world, rank, nccl_id))
     try:
+        if mode == "peer":
+            handles[rank] = m.tp_exchange_handle()
+            barrier.wait(60)
+            m.tp_exchange_open([handles[r] for r in range(world)])
         s = m.session("f16")
         try:
             s.profile(True)
@@ -45,7 +53,8 @@ def _rank(rank, world, nccl_id, out):
         m.close()
 
 
-def test_two_rank_head_parallel_matches_oracle():
+@pytest.mark.parametrize("mode", ["nccl", "peer"])
+def test_two_rank_head_parallel_matches_oracle(mode):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -54,7 +63,9 @@ def test_two_rank_head_parallel_matches_oracle():
     nccl_id = tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, nccl_id, q)) for r in range(world)]
+    manager = ctx.Manager()
+    handles, barrier = manager.dict(), ctx.Barrier(world)
+    procs = [ctx.Process(target=_rank, args=(r, world, nccl_id, q, mode, handles, barrier)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=600) for _ in range(world))
@@ -78,3 +89,5 @@ def test_two_rank_head_parallel_matches_oracle():
         assert bad.size == 0, f"rank {rank}: divergence at {bad[0]} (oracle margin {margins[bad[0]]:.3g})"
         # One exchange per layer: 3 prefill chunks x 2 calls + 15 decode steps.
         assert n_allreduce == L * (2 * 3 + STEPS - 1), (rank, n_allreduce)
+    assert np.array_equal(res[0][1], res[1][1]) and np.array_equal(res[0][2], res[1][2])
+    manager.shutdown()

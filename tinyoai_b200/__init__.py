@@ -186,6 +186,21 @@ class Model:
         m.tp = tp
         return m
 
+    def tp_exchange_handle(self):
+        """This rank's CUDA IPC handle of its exchange buffer (64 bytes;
+        tcu_tp_exchange_handle). Share it with the other ranks, then call
+        tp_exchange_open with every rank's handle in rank order."""
+        buf = (C.c_uint8 * 64)()
+        check(lib().tcu_tp_exchange_handle(self._h, buf))
+        return bytes(buf)
+
+    def tp_exchange_open(self, handles):
+        """Opens the other ranks' exchange buffers; from then on the per-layer
+        exchange runs over NVLink peer memory (tcu_tp_exchange_open)."""
+        raw = b"".join(bytes(h) for h in handles)
+        buf = (C.c_uint8 * len(raw)).from_buffer_copy(raw)
+        check(lib().tcu_tp_exchange_open(self._h, buf))
+
     @classmethod
     def load_llama(cls, checkpoint, device=0, kv_page_tokens=0, kv_pool_bytes=0):
         """llama2.c checkpoint bytes (LoadModel, model.go:90-122)."""

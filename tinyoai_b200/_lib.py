@@ -20,7 +20,7 @@ EXPORTS = [
     "tcu_session_reset", "tcu_session_set_stream", "tcu_session_profile", "tcu_session_profile_read", "tcu_branches_open", "tcu_branches_forward", "tcu_branches_argmax", "tcu_branches_close",
     "tcu_batch_open", "tcu_batch_forward", "tcu_batch_close", "tcu_shortlist_static", "tcu_read_values",
     "tcu_session_forward_logprobs", "tcu_session_sample_candidates", "tcu_batch_sample_candidates",
-    "tcu_tp_unique_id", "tcu_stablelm_load_tp", "tcu_tp_plan",
+    "tcu_tp_unique_id", "tcu_stablelm_load_tp", "tcu_tp_plan", "tcu_tp_exchange_handle", "tcu_tp_exchange_open",
     "tcu_gguf_open", "tcu_gguf_config", "tcu_gguf_tensor_count", "tcu_gguf_tensor", "tcu_gguf_load_stablelm", "tcu_gguf_close",
     "tcu_session_save_cache", "tcu_session_load_cache",
 ]
@@ -109,6 +109,8 @@ def lib():
         "tcu_stablelm_load_tp": ([C.POINTER(StableLMConfig), C.POINTER(Tensor), C.c_int32, C.POINTER(LoadOptions),
                                   C.POINTER(TpOptions), C.POINTER(P)], C.c_int),
         "tcu_tp_plan": ([C.POINTER(StableLMConfig), C.c_int32, C.c_int32, i32p], C.c_int),
+        "tcu_tp_exchange_handle": ([C.c_void_p, C.POINTER(C.c_uint8)], C.c_int),
+        "tcu_tp_exchange_open": ([C.c_void_p, C.POINTER(C.c_uint8)], C.c_int),
         "tcu_gguf_open": ([C.c_char_p, C.POINTER(P)], C.c_int),
         "tcu_gguf_config": ([P, C.POINTER(StableLMConfig)], C.c_int),
         "tcu_gguf_tensor_count": ([P, i32p], C.c_int),

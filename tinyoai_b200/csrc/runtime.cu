@@ -34,6 +34,7 @@
 #include "misc.cuh"
 #include "read_values.cuh"
 #include "attn_tc.cuh"
+#include "tp_exchange.cuh"
 #include "gguf.h"
 #include "kv_snapshot.h"
 
@@ -145,6 +146,13 @@ struct tcu_model {
   // all-reduce of the out + down partial sums.
   int tp_world = 1, tp_rank = 0;
   ncclComm_t tp_comm = nullptr;
+  // The exchange over NVLink peer memory (tp_exchange.cuh), once every rank
+  // has opened the others' buffers (tcu_tp_exchange_open); NCCL otherwise.
+  uint8_t* tp_ex = nullptr;
+  uint8_t* tp_peer[TPX_MAX_RANKS] = {};
+  long long tp_ex_count = 0;
+  uint32_t* tp_seq = nullptr;  // device: exchanges completed, CTAs finished in the current one
+  bool tp_ex_on = false;
 };
 
 static int dalloc(tcu_model* m, void** p, size_t n) {
@@ -192,6 +200,9 @@ static void model_release(tcu_model* m) {
   cudaSetDevice(m->device);
   work_pool_free(m);
   if (m->tp_comm && nccl_api()) nccl_api()->comm_destroy(m->tp_comm);
+  for (int p = 0; p < TPX_MAX_RANKS; p++)
+    if (m->tp_peer[p] && m->tp_peer[p] != m->tp_ex) cudaIpcCloseMemHandle(m->tp_peer[p]);
+  if (m->tp_ex) cudaFree(m->tp_ex);
   for (void* p : m->allocs) cudaFree(p);
   for (KVPool* p : m->pools)
     if (p) {
@@ -1667,6 +1678,29 @@ static thread_local std::string g_comm_err;
 // NVLink, then added to the residual rows x (fp32, k_add_rows).
 static void tp_reduce_add(const tcu_model* m, Work* w, int n, cudaStream_t s) {
   const size_t count = (size_t)n * m->d;
+  if (m->tp_ex_on && (long long)count <= std::min<long long>(m->tp_ex_count, (long long)TPX_PEER_ROWS * m->d)) {
+    // Decode-sized exchanges over peer memory: one kernel exchanges, sums
+    // and adds to the residual (prefill chunks keep NCCL, faster at MBs).
+    TpxArgs a{};
+    a.x = w->x;
+    a.part = w->tp_part;
+    a.count = (long long)count;
+    a.max_count = m->tp_ex_count;
+    // The chunking depends on the count only, so every rank pairs CTA c with
+    // the other ranks' CTA c; at most 128 CTAs, all resident at once.
+    const int ctas = (int)std::min<long long>(128, (count + 1023) / 1024);
+    a.chunk = (int)(((count + ctas - 1) / ctas + 3) / 4 * 4);
+    a.world = m->tp_world;
+    a.rank = m->tp_rank;
+    a.seq = m->tp_seq;
+    for (int p = 0; p < m->tp_world; p++) a.ex[p] = m->tp_peer[p];
+    a.err = w->err;
+    PROF_BEGIN(ST_COMM, s);
+    k_tp_exchange_add<<<(int)((count + a.chunk - 1) / a.chunk), TPX_THREADS, 0, s>>>(a);
+    NOTE("k_tp_exchange_add");
+    PROF_END(s);
+    return;
+  }
   PROF_BEGIN(ST_COMM, s);
   const ncclResult_t r = nccl_api()->all_reduce(w->tp_part, w->tp_part, count, ncclFloat32, ncclSum, m->tp_comm, s);
   PROF_END(s);
@@ -2516,6 +2550,57 @@ int tcu_stablelm_load_tp(const tcu_stablelm_config* config, const tcu_tensor* te
   return TCU_OK;
 }
 
+int tcu_tp_exchange_handle(tcu_model* m, uint8_t* handle) {
+  if (!m || !handle) return fail(TCU_EINVAL, "null argument");
+  if (m->tp_world < 2) return fail(TCU_EINVAL, "not a tensor-parallel model");
+  if (m->tp_world > TPX_MAX_RANKS) return fail(TCU_EUNSUP, "the peer exchange serves at most %d ranks", TPX_MAX_RANKS);
+  CK(cudaSetDevice(m->device));
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!m->tp_ex) {
+    const long long count = ((long long)CHUNK * m->d + 3) / 4 * 4;
+    void* p = nullptr;
+    CK(cudaMalloc(&p, tpx_bytes((size_t)count)));
+    CK(cudaMemset(p, 0, TPX_FLAG_BYTES));
+    m->tp_ex = (uint8_t*)p;
+    m->tp_ex_count = count;
+    TRY(dalloc(m, (void**)&m->tp_seq, 2 * sizeof(uint32_t)));
+    CK(cudaMemset(m->tp_seq, 0, 2 * sizeof(uint32_t)));
+  }
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, m->tp_ex));
+  static_assert(sizeof(cudaIpcMemHandle_t) == TCU_TP_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof h);
+  return TCU_OK;
+}
+
+int tcu_tp_exchange_open(tcu_model* m, const uint8_t* handles) {
+  if (!m || !handles) return fail(TCU_EINVAL, "null argument");
+  if (!m->tp_ex) return fail(TCU_EINVAL, "tcu_tp_exchange_handle first");
+  if (m->tp_ex_on) return fail(TCU_EINVAL, "the peer exchange is already open");
+  CK(cudaSetDevice(m->device));
+  std::lock_guard<std::mutex> lk(m->mu);
+  uint8_t* peer[TPX_MAX_RANKS] = {};
+  for (int p = 0; p < m->tp_world; p++) {
+    if (p == m->tp_rank) {
+      peer[p] = m->tp_ex;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handles + (size_t)p * TCU_TP_HANDLE_BYTES, sizeof h);
+    void* ptr = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < p; q++)
+        if (peer[q] && q != m->tp_rank) cudaIpcCloseMemHandle(peer[q]);
+      return fail(TCU_ECUDA, "cudaIpcOpenMemHandle(rank %d): %s", p, cudaGetErrorString(e));
+    }
+    peer[p] = (uint8_t*)ptr;
+  }
+  memcpy(m->tp_peer, peer, sizeof peer);
+  m->tp_ex_on = true;
+  return TCU_OK;
+}
+
 }  // extern "C"
 
 // A memory-mapped GGUF StableLM checkpoint: the parsed file, the derived
@@ -2931,9 +3016,10 @@ int tcu_session_generate_greedy(tcu_session* s, int32_t prefix, const int32_t* t
     int bucket = 1;
     while (bucket < splits) bucket *= 2;
     bucket = std::min(bucket, s->w->max_splits);
-    // Tensor-parallel models enqueue each step (their all-reduce stays out of
-    // captured graphs); others replay one captured step.
-    const bool tp = m->tp_world > 1;
+    // Tensor-parallel models on NCCL enqueue each step (the all-reduce stays
+    // out of captured graphs); others, the peer exchange included, replay one
+    // captured step.
+    const bool tp = m->tp_world > 1 && !m->tp_ex_on;
     if (steps > 1 && !tp) rc = session_graph(s, bucket);
     for (int i = 1; rc == TCU_OK && i < steps; i++) {
       if (tp) {
