@@ -768,6 +768,94 @@ struct DecodeAttn2Extra {
   int* err;
 };
 
+// Key / value elements of a staged tile as float32 (binary16 or float32 KV).
+template <bool HALF>
+__device__ __forceinline__ float kv_ld1(const uint8_t* tile, size_t i) {
+  if constexpr (HALF)
+    return __half2float(reinterpret_cast<const __half*>(tile)[i]);
+  else
+    return reinterpret_cast<const float*>(tile)[i];
+}
+template <bool HALF>
+__device__ __forceinline__ float2 kv_ld2(const uint8_t* tile, size_t i) {
+  if constexpr (HALF)
+    return __half22float2(*reinterpret_cast<const __half2*>(tile + 2 * i));
+  else
+    return *reinterpret_cast<const float2*>(tile + 4 * i);
+}
+template <bool HALF>
+__device__ __forceinline__ float4 kv_ld4(const uint8_t* tile, size_t i) {
+  if constexpr (HALF) {
+    const uint2 b = *reinterpret_cast<const uint2*>(tile + 2 * i);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&b.x)), c = __half22float2(*reinterpret_cast<const __half2*>(&b.y));
+    return make_float4(a.x, a.y, c.x, c.y);
+  } else {
+    return *reinterpret_cast<const float4*>(tile + 4 * i);
+  }
+}
+
+// Scores of one split for the G heads: two threads per (head, position), each
+// a float32 dot product over half the head dimension in dimension order, the
+// halves added by a shuffle, then divided by sqrt(hd).
+template <bool HALF>
+__device__ __forceinline__ void bulk_scores(const uint8_t* ktile, const float* qs, float* sc, int G, int split, int nt, int hd,
+                                            float scale) {
+  const int h2 = hd / 2;
+  const bool vec = (hd & 7) == 0;
+  for (int e = threadIdx.x; e < G * split * 2; e += blockDim.x) {
+    const int half = e & 1, r = e >> 1, hh = r / split, t = r % split;
+    float d = 0.f;
+    if (t < nt) {
+      const float* q = qs + hh * hd + half * h2;
+      const size_t row = (size_t)t * hd + half * h2;
+      int k = 0;
+      if (vec)
+        for (; k + 4 <= h2; k += 4) {
+          const float4 kv = kv_ld4<HALF>(ktile, row + k);
+          d = fmaf(q[k], kv.x, d);
+          d = fmaf(q[k + 1], kv.y, d);
+          d = fmaf(q[k + 2], kv.z, d);
+          d = fmaf(q[k + 3], kv.w, d);
+        }
+      for (; k < h2; k++) d = fmaf(q[k], kv_ld1<HALF>(ktile, row + k), d);
+    }
+    d += __shfl_xor_sync(0xffffffffu, d, 1);
+    if (half == 0 && t < nt) sc[hh * split + t] = __fdiv_rn(d, scale);
+  }
+}
+
+// The weighted values of one split merged into the run's outputs: two
+// threads per (head, pair of dimensions), each over half the positions in
+// position order, the halves added by a shuffle; then
+// orun = orun * alpha + o * beta with the run's and the split's maxima.
+template <bool HALF>
+__device__ __forceinline__ void bulk_values(const uint8_t* vtile, const float* sc, int G, int split, int nt, int hd, const float* mrun,
+                                            const float* mloc, float* orun) {
+  const int hp = hd / 2, tasks = G * hp * 2, th = (nt + 1) / 2;
+  for (int e = threadIdx.x; e < (tasks + 31) / 32 * 32; e += blockDim.x) {  // whole warps: every lane reaches the shuffles
+    const bool ok = e < tasks;
+    const int ph = e & 1, pr = e >> 1, hh = pr / hp, dp = pr % hp;
+    float o0 = 0.f, o1 = 0.f;
+    if (ok) {
+      const float* p = sc + hh * split;
+      for (int t = ph * th, t1 = min(nt, ph * th + th); t < t1; t++) {
+        const float2 v = kv_ld2<HALF>(vtile, (size_t)t * hd + 2 * dp);
+        o0 = fmaf(p[t], v.x, o0);
+        o1 = fmaf(p[t], v.y, o1);
+      }
+    }
+    o0 += __shfl_xor_sync(0xffffffffu, o0, 1);
+    o1 += __shfl_xor_sync(0xffffffffu, o1, 1);
+    if (ok && ph == 0) {
+      const float mo = mrun[hh], mn = fmaxf(mo, mloc[hh]);
+      const float alpha = mo == -INFINITY ? 0.f : expf(mo - mn), beta = expf(mloc[hh] - mn);
+      float* o = orun + hh * hd + 2 * dp;
+      o[0] = o[0] * alpha + o0 * beta;
+      o[1] = o[1] * alpha + o1 * beta;
+    }
+  }
+}
+
 // Dynamic shared memory of k_attn_decode_bulk: barriers, two stages of K and V
 // tiles, q, scores, the new k/v and the run's outputs.
 __host__ __device__ inline size_t attn_bulk_smem(int G, int split, int hd, int es) {
@@ -862,35 +950,29 @@ __global__ void __launch_bounds__(128) k_attn_decode_bulk(DecodeAttnArgs a, Deco
     const int t0 = s * split;
     const int nt = min(T, t0 + split) - t0;
     const bool cur_here = s == nsplit - 1;
-    const int n_hist = cur_here ? nt - 1 : nt;
     mbar_wait(bar + st, (i >> 1) & 1, x.err);
     const uint8_t* ktile = stages + (size_t)st * 2 * tile;
     const uint8_t* vtile = ktile + tile;
-    // Scores. Each thread walks the head dimension starting at its own offset,
-    // so the threads of a warp read distinct banks of their key rows.
-    for (int e = threadIdx.x; e < G * split; e += blockDim.x) {
-      const int hh = e / split, t = e % split;
-      if (t < nt) {
-        const float* q = qs + hh * hd;
-        float d = 0.f;
-        int i0 = t % hd;
-        if (cur_here && t == nt - 1) {
-          for (int k = 0; k < hd; k++) {
-            int ii = i0 + k;
-            ii -= ii >= hd ? hd : 0;
-            d = fmaf(q[ii], cur[ii], d);
-          }
+    // The new token's key and value (already rounded to the KV precision)
+    // take their row of the staged tiles, so every position reads alike.
+    if (cur_here) {
+      uint8_t* kt = stages + (size_t)st * 2 * tile;
+      for (int e = threadIdx.x; e < hd; e += blockDim.x) {
+        const size_t o = (size_t)(nt - 1) * hd + e;
+        if (a.kv.half) {
+          reinterpret_cast<__half*>(kt)[o] = __float2half_rn(cur[e]);
+          reinterpret_cast<__half*>(kt + tile)[o] = __float2half_rn(cur[hd + e]);
         } else {
-          const size_t rowo = (size_t)t * hd;
-          for (int k = 0; k < hd; k++) {
-            int ii = i0 + k;
-            ii -= ii >= hd ? hd : 0;
-            d = fmaf(q[ii], kv_ld(ktile, a.kv.half, rowo + ii), d);
-          }
+          reinterpret_cast<float*>(kt)[o] = cur[e];
+          reinterpret_cast<float*>(kt + tile)[o] = cur[hd + e];
         }
-        sc[hh * split + t] = __fdiv_rn(d, a.scale);
       }
+      __syncthreads();
     }
+    if (a.kv.half)
+      bulk_scores<true>(ktile, qs, sc, G, split, nt, hd, a.scale);
+    else
+      bulk_scores<false>(ktile, qs, sc, G, split, nt, hd, a.scale);
     __syncthreads();
     for (int hh = warp; hh < G; hh += nwarps) {
       float mx = -INFINITY;
@@ -910,15 +992,10 @@ __global__ void __launch_bounds__(128) k_attn_decode_bulk(DecodeAttnArgs a, Deco
       }
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < G * hd; e += blockDim.x) {
-      const int hh = e / hd, k = e % hd;
-      float o = 0.f;
-      for (int t = 0; t < n_hist; t++) o = fmaf(sc[hh * split + t], kv_ld(vtile, a.kv.half, (size_t)t * hd + k), o);
-      if (cur_here) o = fmaf(sc[hh * split + nt - 1], cur[hd + k], o);
-      const float mo = mrun[hh], mn = fmaxf(mo, mloc[hh]);
-      const float alpha = mo == -INFINITY ? 0.f : expf(mo - mn), beta = expf(mloc[hh] - mn);
-      orun[e] = orun[e] * alpha + o * beta;
-    }
+    if (a.kv.half)
+      bulk_values<true>(vtile, sc, G, split, nt, hd, mrun, mloc, orun);
+    else
+      bulk_values<false>(vtile, sc, G, split, nt, hd, mrun, mloc, orun);
     __syncthreads();
     if (threadIdx.x < G) {
       const float mo = mrun[threadIdx.x], mn = fmaxf(mo, mloc[threadIdx.x]);
