@@ -57,13 +57,17 @@ constexpr int AT_ROWS = 128;   // query rows per CTA (MMA M)
 constexpr int AT_KEYS = 64;    // positions per block (one split)
 constexpr int AT_GROUP = 128;  // threads per group: one per query row / TMEM lane
 constexpr float AT_LOG2E = 1.4426950408889634f;
+// Page ids a CTA copies into shared memory up front (192: two shared-prefix
+// CTAs at hd = 80 still fit one SM's 228 KB with their 1 KB reserves).
+constexpr int AT_PAGE_CACHE = 192;
 
 // Dynamic shared memory for head size hd (multiple of 16) and ng groups:
 // P tiles ng x 2 x 128 x 64, Q pieces 2 x 128 x hd, K/V ng x 2 stages x 2 x
-// 64 x hd (binary16), the mbarriers and the TMEM slot. At least 80 KB, so
-// that at most two CTAs (2 x 256 TMEM columns) share an SM.
+// 64 x hd (binary16), the mbarriers, the TMEM slot and a copy of the page
+// ids the CTA reads. At least 80 KB, so that at most two CTAs (2 x 256 TMEM
+// columns) share an SM.
 __host__ __device__ inline size_t at_smem_bytes(int hd, int ng) {
-  const size_t b = (size_t)ng * 4 * AT_ROWS * AT_KEYS + (size_t)4 * AT_ROWS * hd + (size_t)ng * 8 * AT_KEYS * hd + 64;
+  const size_t b = (size_t)ng * 4 * AT_ROWS * AT_KEYS + (size_t)4 * AT_ROWS * hd + (size_t)ng * 8 * AT_KEYS * hd + 64 + 4 * AT_PAGE_CACHE;
   return b < 80 * 1024 ? 80 * 1024 : b;
 }
 
@@ -104,23 +108,6 @@ __device__ __forceinline__ void at_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void at_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Element k of head vector x after RoPE at pos: the value rope_pair leaves
-// there (same operations, same rounding).
-__device__ __forceinline__ float rope_elem(const float* x, int k, const Rope& r, int pos) {
-  if (r.mode == 0) {
-    if (k >= 2 * r.pairs) return x[k];
-    const int i = k < r.pairs ? k : k - r.pairs;
-    const float2 cs = r.table[(size_t)pos * r.pairs + i];
-    const float a = x[i], b = x[i + r.pairs];
-    return k < r.pairs ? __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y)) : __fadd_rn(__fmul_rn(b, cs.x), __fmul_rn(a, cs.y));
-  }
-  const int i = k >> 1;
-  if (i >= r.pairs) return x[k];
-  const float2 cs = r.table[(size_t)pos * r.pairs + i];
-  const float v0 = x[2 * i], v1 = x[2 * i + 1];
-  return (k & 1) ? __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x)) : __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
-}
-
 // Binary16 pair (h, l) of two floats: h = fp16(v), l = fp16(v - h).
 __device__ __forceinline__ void at_split2(float v0, float v1, uint32_t& h, uint32_t& l) {
   const __half2 hh = __floats2half2_rn(v0, v1);
@@ -137,6 +124,7 @@ struct AtSmem {
   uint32_t q_piece;
   uint64_t* bars;  // one per group
   uint32_t* tslot;
+  int* pages;      // [AT_PAGE_CACHE]
   int hd;
 };
 
@@ -156,6 +144,7 @@ __device__ __forceinline__ AtSmem at_carve(uint8_t* base, int hd, int ng) {
   m.q_piece = 2 * AT_ROWS * hd;
   m.bars = reinterpret_cast<uint64_t*>(m.qs + 4 * AT_ROWS * hd + (size_t)ng * 8 * AT_KEYS * hd);
   m.tslot = reinterpret_cast<uint32_t*>(m.bars + ng);
+  m.pages = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(m.bars) + 64);
   m.hd = hd;
   return m;
 }
@@ -194,29 +183,27 @@ __device__ __forceinline__ void at_end(uint32_t tmem, int ng) {
   }
 }
 
-// The power of two sx of query row x (float32, hd values; rotated at pos
-// first when ROPE): 13 - exponent of its largest magnitude.
-template <bool ROPE>
-__device__ __forceinline__ int at_q_sx(const float* x, bool valid, int hd, const Rope& rope, int pos) {
+// The power of two sx of query row x (float32, hd values, already rotated):
+// 13 - exponent of its largest magnitude.
+__device__ __forceinline__ int at_q_sx(const float* x, bool valid, int hd) {
   float mx = 0.f;
   if (valid)
-    for (int k = 0; k < hd; k++) mx = fmaxf(mx, fabsf(ROPE ? rope_elem(x, k, rope, pos) : x[k]));
+    for (int k = 0; k < hd; k++) mx = fmaxf(mx, fabsf(x[k]));
   int ex = 0;
   if (mx > 0.f) frexpf(mx, &ex);
   return mx > 0.f ? 13 - ex : 0;
 }
 
 // That row as the binary16 pair of x * 2^sx into row `row` of the Q tiles.
-template <bool ROPE>
-__device__ __forceinline__ void at_q_write(const AtSmem& sm, int row, const float* x, bool valid, const Rope& rope, int pos, int sx) {
+__device__ __forceinline__ void at_q_write(const AtSmem& sm, int row, const float* x, bool valid, int sx) {
   const float qscale = tc_pow2(sx);
   for (int c = 0; c < sm.hd / 8; c++) {
     uint32_t h[4], l[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       const int k = 8 * c + 2 * j;
-      const float v0 = !valid ? 0.f : ROPE ? rope_elem(x, k, rope, pos) : x[k];
-      const float v1 = !valid ? 0.f : ROPE ? rope_elem(x, k + 1, rope, pos) : x[k + 1];
+      const float v0 = valid ? x[k] : 0.f;
+      const float v1 = valid ? x[k + 1] : 0.f;
       at_split2(v0 * qscale, v1 * qscale, h[j], l[j]);
     }
     *reinterpret_cast<uint4*>(sm.qs + c * (AT_ROWS * 16) + row * 16) = make_uint4(h[0], h[1], h[2], h[3]);
@@ -224,18 +211,33 @@ __device__ __forceinline__ void at_q_write(const AtSmem& sm, int row, const floa
   }
 }
 
+// Where a CTA reads page ids: page index i is pt[i - base] (a copy of the
+// CTA's range in shared memory, or the page table itself).
+struct AtPages {
+  const int* pt;
+  int base;
+};
+
+// Copies page ids [first, first + count) into shared memory when they fit
+// (every thread of the CTA calls this; a CTA barrier must follow).
+__device__ __forceinline__ AtPages at_cache_pages(const AtSmem& sm, const int* page_table, int first, int count) {
+  if (count > AT_PAGE_CACHE) return AtPages{page_table, 0};
+  for (int i = threadIdx.x; i < count; i += blockDim.x) sm.pages[i] = page_table[first + i];
+  return AtPages{sm.pages, first};
+}
+
 // Keys and values of positions [t0, t0 + 64) of KV head g into the group's
 // stage st (chunk c of position t at c * 1024 + t * 16); positions past
 // `last` are zero (their weights are zero, and zero values keep the
 // products finite). Each thread looks up one position's page.
-__device__ __forceinline__ void at_load_kv(const AtGroup& G, int hd, int st, const KVView& kv, int layer, const int* page_table, int g,
+__device__ __forceinline__ void at_load_kv(const AtGroup& G, int hd, int st, const KVView& kv, int layer, AtPages pages, int g,
                                            int t0, int last) {
   uint8_t* kb = G.kvs + (size_t)st * 4 * AT_KEYS * hd;
   uint8_t* vb = kb + 2 * AT_KEYS * hd;
   const int t = G.tid % AT_KEYS, ta = t0 + t;
   const bool ok = ta <= last;
   size_t base = 0;
-  if (ok) base = kv.off(layer, page_table[ta / kv.P], g, ta % kv.P);
+  if (ok) base = kv.off(layer, pages.pt[ta / kv.P - pages.base], g, ta % kv.P);
   for (int c = G.tid / AT_KEYS; c < hd / 8; c += AT_GROUP / AT_KEYS) {
     const int so = c * (AT_KEYS * 16) + t * 16;
     if (ok) {
@@ -367,7 +369,7 @@ __device__ __forceinline__ void at_acc_values(const AtGroup& G, float alpha, flo
 // kvh: the online softmax state (o, m, l) of the group's query rows. qpos:
 // this row's last visible position (causal mask), or INT_MAX.
 template <int HD>
-__device__ __forceinline__ void at_blocks(const AtSmem& sm, const AtGroup& G, const KVView& kv, int layer, const int* page_table, int kvh,
+__device__ __forceinline__ void at_blocks(const AtSmem& sm, const AtGroup& G, const KVView& kv, int layer, AtPages pages, int kvh,
                                           int j0, int step, int nblk, int last, int qpos, float k, int* err, float (&o)[HD], float& m,
                                           float& l) {
 #pragma unroll
@@ -376,11 +378,11 @@ __device__ __forceinline__ void at_blocks(const AtSmem& sm, const AtGroup& G, co
   l = 0.f;
   if (j0 >= nblk) return;
   uint32_t phase = 0;
-  at_load_kv(G, HD, 0, kv, layer, page_table, kvh, j0 * AT_KEYS, last);
+  at_load_kv(G, HD, 0, kv, layer, pages, kvh, j0 * AT_KEYS, last);
   for (int j = j0, it = 0; j < nblk; j += step, it++) {
     const int st = it & 1, t0 = j * AT_KEYS;
     if (j + step < nblk) {
-      at_load_kv(G, HD, st ^ 1, kv, layer, page_table, kvh, t0 + step * AT_KEYS, last);
+      at_load_kv(G, HD, st ^ 1, kv, layer, pages, kvh, t0 + step * AT_KEYS, last);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
@@ -421,18 +423,30 @@ __global__ void __launch_bounds__(AT_GROUP) k_attn_shared_tc(DecodeAttnArgs a, i
   at_begin(sm, 1);
 
   // Query rows: float32 staging in the K/V buffers (128 x hd floats fill
-  // them exactly), then RoPE at the row's position and the binary16 pair.
+  // them exactly), rotated in place at each row's position (one rotary pair
+  // per thread and step, as rope_pair does it), then the binary16 pair.
   float* qf = reinterpret_cast<float*>(G.kvs);
-  for (int e = tid; e < AT_ROWS * HD; e += AT_GROUP) {
-    const int qi = e / HD, i = e % HD, row = q0 + qi;
-    qf[e] = row < nrow ? a.qkv[(size_t)(row / Gq) * a.qkv_stride + (kvh * Gq + row % Gq) * HD + i] : 0.f;
+  constexpr int C4 = HD / 4;
+#pragma unroll 4
+  for (int e = tid; e < AT_ROWS * C4; e += AT_GROUP) {
+    const int qi = e / C4, c = e % C4, row = q0 + qi;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < nrow) v = *reinterpret_cast<const float4*>(a.qkv + (size_t)(row / Gq) * a.qkv_stride + (kvh * Gq + row % Gq) * HD + 4 * c);
+    reinterpret_cast<float4*>(qf)[e] = v;
+  }
+  const int first_page = s_lo * AT_KEYS / a.kv.P;
+  const AtPages pages = at_cache_pages(sm, a.page_table, first_page, (s_hi * AT_KEYS - 1) / a.kv.P - first_page + 1);
+  __syncthreads();
+  const int nq = min(AT_ROWS, nrow - q0);
+  for (int e = tid; e < nq * a.rope.pairs; e += AT_GROUP) {
+    const int qi = e / a.rope.pairs;
+    rope_pair(qf + qi * HD, e % a.rope.pairs, a.rope, a.pos[(q0 + qi) / Gq]);
   }
   __syncthreads();
   const int row = q0 + tid;
   const bool valid = row < nrow;
-  const int pos = valid ? a.pos[row / Gq] : 0;
-  const int sx = at_q_sx<true>(qf + tid * HD, valid, HD, a.rope, pos);
-  at_q_write<true>(sm, tid, qf + tid * HD, valid, a.rope, pos, sx);
+  const int sx = at_q_sx(qf + tid * HD, valid, HD);
+  at_q_write(sm, tid, qf + tid * HD, valid, sx);
   const float k = tc_pow2(-sx) * (1.f / a.scale);
   tc_fence_before();
   __syncthreads();  // staging read; the K/V buffers are free
@@ -440,7 +454,7 @@ __global__ void __launch_bounds__(AT_GROUP) k_attn_shared_tc(DecodeAttnArgs a, i
   G.tmem = *reinterpret_cast<volatile uint32_t*>(sm.tslot);
 
   float o[HD], m, l;
-  at_blocks<HD>(sm, G, a.kv, a.layer, a.page_table, kvh, s_lo, 1, s_hi, nshared * AT_KEYS - 1, INT_MAX, k, err, o, m, l);
+  at_blocks<HD>(sm, G, a.kv, a.layer, pages, kvh, s_lo, 1, s_hi, nshared * AT_KEYS - 1, INT_MAX, k, err, o, m, l);
   if (valid) {
     float* part = a.part + (((size_t)(row / Gq) * a.H + kvh * Gq + row % Gq) * a.max_splits + blockIdx.x) * (HD + 2);
 #pragma unroll
@@ -465,15 +479,20 @@ __global__ void __launch_bounds__(AT_GROUP * NG) k_attn_prefill_tc(PrefillAttnAr
   AtGroup G = at_group(at_smem, sm, tid / AT_GROUP);
   at_begin(sm, NG);
   float* qf = reinterpret_cast<float*>(sm.qs + 4 * AT_ROWS * HD);  // group 0's K/V stages
-  for (int e = tid; e < AT_ROWS * HD; e += AT_GROUP * NG) {
-    const int qi = e / HD, i = e % HD;
-    qf[e] = qi < nq ? a.qkv[(size_t)(q0 + qi) * a.qkv_stride + h * HD + i] : 0.f;
+  constexpr int C4 = HD / 4;
+#pragma unroll 4
+  for (int e = tid; e < AT_ROWS * C4; e += AT_GROUP * NG) {
+    const int qi = e / C4, c = e % C4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (qi < nq) v = *reinterpret_cast<const float4*>(a.qkv + (size_t)(q0 + qi) * a.qkv_stride + h * HD + 4 * c);
+    reinterpret_cast<float4*>(qf)[e] = v;
   }
+  const AtPages pages = at_cache_pages(sm, a.page_table, 0, (a.start + q0 + nq - 1) / a.kv.P + 1);
   __syncthreads();
   const int r = G.tid;
   const bool valid = r < nq;
-  const int sx = at_q_sx<false>(qf + r * HD, valid, HD, Rope{}, 0);
-  if (G.id == 1) at_q_write<false>(sm, r, qf + r * HD, valid, Rope{}, 0, sx);
+  const int sx = at_q_sx(qf + r * HD, valid, HD);
+  if (G.id == 1) at_q_write(sm, r, qf + r * HD, valid, sx);
   const float k = tc_pow2(-sx) * (1.f / a.scale);
   tc_fence_before();
   __syncthreads();  // staging read; the K/V buffers are free
@@ -485,7 +504,7 @@ __global__ void __launch_bounds__(AT_GROUP * NG) k_attn_prefill_tc(PrefillAttnAr
   const int nblk = last / AT_KEYS + 1;
 
   float o[HD], m, l;
-  at_blocks<HD>(sm, G, a.kv, a.layer, a.page_table, kvh, G.id - 1, NG, nblk, last, qpos, k, err, o, m, l);
+  at_blocks<HD>(sm, G, a.kv, a.layer, pages, kvh, G.id - 1, NG, nblk, last, qpos, k, err, o, m, l);
   if (NG > 1) {
     // Group 1 hands (o, m, l) to group 0 through the Q and K/V buffers
     // ([HD + 2][128] floats), after every group's copies and MMAs are done.
