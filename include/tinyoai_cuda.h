@@ -368,7 +368,9 @@ int tcu_batch_close(tcu_batch* batch);
  * TCU_SHORTLIST_STATIC_MAX_K. vocab is limited to
  * TCU_SHORTLIST_STATIC_MAX_VOCAB (the kernel marks taken ids in shared memory).
  * Larger values fail with TCU_EINVAL. The first call on a device does the set-up
- * (it looks up that array's device address); make it before any stream capture.
+ * (it looks up that array's device address). The call synchronises the stream
+ * and copies into host memory, so it cannot be captured into a CUDA graph: a
+ * stream under capture fails with TCU_EINVAL before any work is queued.
  * Calls on one device share the array: two calls in flight at the same time on
  * one device, from different host threads, overwrite each other's results. */
 #define TCU_SHORTLIST_STATIC_MAX_K 256

@@ -73,6 +73,25 @@ def test_static_shortlist_matches_session_shortlist():
                                              (C.c_int32 * 4)(), (C.c_float * 4)(), C.byref(C.c_double()),
                                              C.byref(C.c_int32()))
         assert rc == _lib.TCU_EINVAL
+
+        # A stream under capture is refused before any work is queued (the
+        # call synchronises and copies to host memory); the capture itself
+        # stays valid and the next plain call works.
+        side = torch.cuda.Stream()
+        graph = torch.cuda.CUDAGraph()
+        mark = torch.zeros(1, device="cuda:0")
+        with torch.cuda.graph(graph, stream=side, capture_error_mode="relaxed"):
+            rc = _lib.lib().tcu_shortlist_static(0, C.c_void_p(dev_a.data_ptr()), V, 4, C.c_void_p(side.cuda_stream),
+                                                 (C.c_int32 * 4)(), (C.c_float * 4)(), C.byref(C.c_double()),
+                                                 C.byref(C.c_int32()))
+            mark.add_(1)
+        assert rc == _lib.TCU_EINVAL
+        graph.replay()
+        torch.cuda.synchronize()
+        assert float(mark[0]) == 1.0
+        del graph
+        got_ids, got_vals, _ = shortlist_static(dev_a, V, 40)
+        assert list(got_ids) == list(want_a[0])
     finally:
         s.close()
         m.close()

@@ -3758,6 +3758,12 @@ extern "C" int tcu_shortlist_static(int32_t device, const float* logits, int32_t
   if (device < 0 || device >= n || device >= SL_STATIC_MAX_DEVICES)
     return fail(TCU_ENODEV, "device %d out of range (%d devices)", device, n);
   CK(cudaSetDevice(device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The call synchronises the stream and copies into host memory, neither of
+  // which a graph can hold.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  CK(cudaStreamIsCapturing(st, &cap));
+  if (cap != cudaStreamCaptureStatusNone) return fail(TCU_EINVAL, "the stream is being captured; this call cannot be");
   cudaPointerAttributes pa;
   CK(cudaPointerGetAttributes(&pa, logits));
   if ((pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged) || pa.device != device)
@@ -3767,7 +3773,6 @@ extern "C" int tcu_shortlist_static(int32_t device, const float* logits, int32_t
   int32_t* d_ids = reinterpret_cast<int32_t*>(scratch);
   float* d_vals = reinterpret_cast<float*>(scratch + TCU_SHORTLIST_STATIC_MAX_K * 4);
   double* d_lse = reinterpret_cast<double*>(scratch + TCU_SHORTLIST_STATIC_MAX_K * 8);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int kk = std::min<int>(k, vocab);
   const size_t smem = ((size_t)vocab + 31) / 32 * 4;  // within the attribute set up once per device
   k_shortlist<<<1, 1024, smem, st>>>(logits, vocab, kk, d_ids, d_vals, d_lse);
