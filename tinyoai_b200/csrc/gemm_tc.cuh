@@ -38,9 +38,18 @@
 // MMAs (one thread), warp 17 issues the TMA loads of the activation tiles.
 // Decoding sets the pace for quantised weights; four decoding warps per SM
 // sub-partition hide its load latency (4 -> 8 -> 16 warps: config-4 step
-// 2797 -> 2297 -> 2192 ms). Two shared-memory buffers; every wait is
-// bounded. All copies read this GPU's own memory into this CTA's shared
-// memory.
+// 2797 -> 2297 -> 2192 ms).
+//
+// Shared memory holds two rings: decoded weight stages (warps 0-15 fill
+// them) and activation stages (TMA fills them; for BF16 each also carries
+// the weight tile). The MMA thread frees a stage of each ring with a
+// tcgen05.commit once its MMAs have read it. DEEP = false: two stages each,
+// freed by one commit. DEEP = true (BF16 and Q8_0 tiles of up to 128
+// tokens): as many stages as 227 KB holds, up to four per ring, so the
+// activation copies of later stages are in flight while earlier ones are
+// multiplied -- one stage's turnaround is the copy's latency plus the MMAs'
+// completion, which two stages leave exposed. Every wait is bounded. All
+// copies read this GPU's own memory into this CTA's shared memory.
 #pragma once
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -57,17 +66,27 @@ constexpr int TC_DQW = 16;     // weight-decoding warps (a multiple of 4)
 constexpr int TC_MMA_WARP = TC_DQW, TC_TMA_WARP = TC_DQW + 1;
 constexpr int TC_THREADS = TC_DQW * 32 + 64;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;      // 16 KB per binary16 weight tile
-constexpr int TC_B_BYTES = TC_MAXN * TC_BK * 2;    // 32 KB per binary16 activation tile
+constexpr int TC_MAX_STAGES = 4;                   // per ring
+constexpr int TC_SMEM_LIMIT = 227 * 1024;          // a CTA's shared memory
 // Weight operand of a GEMM: Q8_0 decoded into a binary16 pair, Q6_K / Q5_K
 // into three binary16 pieces, BF16 brought by TMA as stored.
 enum TcWeights : int { TCW_Q8 = 0, TCW_KQ = 1, TCW_BF16 = 2 };
-// Binary16 weight pieces a stage buffer holds (BF16 uses the first).
+// Binary16 weight pieces of a decoded weight stage.
 __host__ __device__ constexpr int tc_pieces(int wm) { return wm == TCW_KQ ? 3 : 2; }
-__host__ __device__ constexpr int tc_buf_bytes(int wm) { return tc_pieces(wm) * TC_A_BYTES + 2 * TC_B_BYTES; }
-// Two stage buffers, 1 KB alignment slack, barriers: 193.25 KB (Q8_0, BF16)
-// or 225.25 KB (K-quants) of the 227 KB a CTA may hold.
-__host__ __device__ constexpr int tc_smem_bytes(int wm) { return 2 * tc_buf_bytes(wm) + 1024 + 256; }
-static_assert(tc_smem_bytes(TCW_KQ) <= 227 * 1024, "tensor-core GEMM stage buffers exceed shared memory");
+// Bytes of one weight stage (none for BF16, whose tile comes by TMA with the
+// activations) and of one activation stage (Xh and Xl, or the BF16 weight
+// tile and X0, X1, X2) for a tile of n_tile tokens.
+__host__ __device__ constexpr int tc_w_stage_bytes(int wm) { return wm == TCW_BF16 ? 0 : tc_pieces(wm) * TC_A_BYTES; }
+__host__ __device__ constexpr int tc_x_stage_bytes(int wm, int n_tile) {
+  return wm == TCW_BF16 ? TC_A_BYTES + 3 * n_tile * TC_BK * 2 : 2 * n_tile * TC_BK * 2;
+}
+// Both rings, 1 KB alignment slack, barriers: with two stages each and full
+// tiles 193.25 KB (Q8_0, BF16) or 225.25 KB (K-quants).
+__host__ __device__ constexpr int tc_smem_bytes(int wm, int n_tile, int ws, int xs) {
+  return ws * tc_w_stage_bytes(wm) + xs * tc_x_stage_bytes(wm, n_tile) + 1024 + 256;
+}
+static_assert(tc_smem_bytes(TCW_KQ, TC_MAXN, 2, 2) <= TC_SMEM_LIMIT, "tensor-core GEMM stages exceed shared memory");
+static_assert(tc_smem_bytes(TCW_BF16, 128, 0, 2) <= TC_SMEM_LIMIT, "tensor-core GEMM stages exceed shared memory");
 static_assert(TC_DQW * 8 == TC_BM, "one weight row per decoding thread group and stage (the Q6_K prefetch relies on it)");
 
 struct TcArgs {
@@ -90,6 +109,7 @@ struct TcArgs {
   float* part;        // split K: partial sums [gridDim.z][n][rows] (nullptr: apply the epilogue)
   int k_per_z;        // split K: columns per z slice (multiple of TC_BK)
   int tok_fast;       // grid x = token tiles (else x = weight-row tiles)
+  int ws, xs;         // DEEP: stages of the weight ring (0 for BF16) and of the activation ring, <= TC_MAX_STAGES
   int* err;
 };
 
@@ -308,20 +328,29 @@ __device__ __forceinline__ void tc_weight_pieces(const DMat& W, int r, int k0, i
 
 // WM: TCW_BF16 takes bfloat16 weight tiles through wmap; TCW_Q8 and TCW_KQ
 // weights are decoded by warps 0-15 (wmap unused).
-template <int EPI, int WM>
+template <int EPI, int WM, bool DEEP>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap xmap,
                                                            const __grid_constant__ CUtensorMap wmap, TcArgs a) {
   constexpr bool WB = WM == TCW_BF16;
   constexpr int NP = tc_pieces(WM);
-  constexpr int TC_BUF_BYTES = tc_buf_bytes(WM);
   extern __shared__ uint8_t tc_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * TC_BUF_BYTES);
-  uint64_t* x_full = bars;         // [2] activation tiles landed
-  uint64_t* w_full = bars + 2;     // [2] weight tiles written
-  uint64_t* mma_done = bars + 4;   // [2] MMAs reading the buffer finished
-  uint64_t* acc_full = bars + 6;   // accumulators final
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  const int NT = a.n_tile;
+  // Ring depths (BF16 has no weight ring: its weight stage is 0 bytes).
+  const int WS = DEEP && !WB ? a.ws : 2, XS = DEEP ? a.xs : 2;
+  const uint32_t w_stage = (uint32_t)tc_w_stage_bytes(WM), x_stage = (uint32_t)tc_x_stage_bytes(WM, NT);
+  const uint32_t x_piece = (uint32_t)NT * TC_BK * 2;  // one activation piece of the tile
+  uint8_t* wring = smem;                                        // [WS] decoded weight stages
+  uint8_t* xring = smem + (size_t)(WB ? 0 : WS) * w_stage;      // [XS] activation stages
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + (size_t)XS * x_stage);
+  uint64_t* x_full = bars;                       // [XS] activation tiles landed
+  uint64_t* x_empty = bars + TC_MAX_STAGES;      // [XS] MMAs reading the activation stage finished
+  uint64_t* w_full = bars + 2 * TC_MAX_STAGES;   // [WS] weight tiles written
+  // [WS] MMAs reading the weight stage finished; with two stages each, the
+  // activation barriers serve both rings.
+  uint64_t* w_empty = DEEP ? bars + 3 * TC_MAX_STAGES : x_empty;
+  uint64_t* acc_full = bars + 4 * TC_MAX_STAGES;  // accumulators final
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * TC_MAX_STAGES + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int R = a.W.rows, K = a.W.cols;
   // tok_fast: token tiles are the fastest grid index, so the CTAs that share
@@ -330,15 +359,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
   const int k_begin = a.part ? blockIdx.z * a.k_per_z : 0;
   const int k_end = a.part ? min(K, k_begin + a.k_per_z) : K;
   const int iters = (k_end - k_begin + TC_BK - 1) / TC_BK;
-  const int NT = a.n_tile;
   const bool two_acc = (EPI == EPI_RESID2) && !a.part;
   const uint32_t tmem_cols = two_acc ? 2 * TC_MAXN : TC_MAXN;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < XS; i++) {
       mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 1);
+    }
+    for (int i = 0; i < WS; i++) {
       mbar_init(&w_full[i], TC_DQW * 32);
-      mbar_init(&mma_done[i], 1);
+      if (DEEP) mbar_init(&w_empty[i], 1);
     }
     mbar_init(acc_full, 1);
     fence_barrier_init();
@@ -352,25 +383,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
 
-  auto buf = [&](int b) { return smem + (size_t)b * TC_BUF_BYTES; };
-
   if (warp == TC_TMA_WARP) {
-    // ---- activation tiles: Xh rows [t0, t0 + NT), Xl rows n_pad + the same.
+    // ---- activation stages: Xh rows [t0, t0 + NT), Xl rows n_pad + the same.
     // BF16: the weight tile, then pieces X0, X1, X2 (rows p * n_pad + t0).
     if (lane == 0) {
-      const uint32_t bytes = WB ? (uint32_t)(TC_A_BYTES + 3 * NT * TC_BK * 2) : (uint32_t)(2 * NT * TC_BK * 2);
+      const uint32_t bytes = WB ? (uint32_t)TC_A_BYTES + 3 * x_piece : 2 * x_piece;
       for (int i = 0; i < iters; i++) {
-        const int b = i & 1;
-        if (i >= 2) mbar_wait(&mma_done[b], ((i >> 1) - 1) & 1, a.err);
+        const int b = i % XS;
+        if (i >= XS) mbar_wait(&x_empty[b], ((i / XS) - 1) & 1, a.err);
+        uint8_t* xb = xring + (size_t)b * x_stage;
         mbar_expect_tx(&x_full[b], bytes);
         const int k = k_begin + i * TC_BK;
         if (WB) {
-          tc_tma_load(buf(b), &wmap, k, r0, &x_full[b]);
+          tc_tma_load(xb, &wmap, k, r0, &x_full[b]);
 #pragma unroll
-          for (int p = 0; p < 3; p++) tc_tma_load(buf(b) + NP * TC_A_BYTES + p * NT * TC_BK * 2, &xmap, k, p * a.n_pad + t0, &x_full[b]);
+          for (int p = 0; p < 3; p++) tc_tma_load(xb + TC_A_BYTES + p * x_piece, &xmap, k, p * a.n_pad + t0, &x_full[b]);
         } else {
-          tc_tma_load(buf(b) + NP * TC_A_BYTES, &xmap, k, t0, &x_full[b]);
-          tc_tma_load(buf(b) + NP * TC_A_BYTES + TC_B_BYTES, &xmap, k, a.n_pad + t0, &x_full[b]);
+          tc_tma_load(xb, &xmap, k, t0, &x_full[b]);
+          tc_tma_load(xb + x_piece, &xmap, k, a.n_pad + t0, &x_full[b]);
         }
       }
     }
@@ -380,15 +410,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
       const uint32_t idesc = tc_idesc(NT, WB);
       bool first0 = true, first1 = true;
       for (int i = 0; i < iters; i++) {
-        const int b = i & 1;
-        mbar_wait(&x_full[b], (i >> 1) & 1, a.err);
-        if (!WB) mbar_wait(&w_full[b], (i >> 1) & 1, a.err);
+        const int xb = i % XS, wb = i % WS;
+        mbar_wait(&x_full[xb], (i / XS) & 1, a.err);
+        if (!WB) mbar_wait(&w_full[wb], (i / WS) & 1, a.err);
         tc_fence_after();
         const int k = k_begin + i * TC_BK;
         const bool second = two_acc && k >= a.k_split;
         const uint32_t d = tmem + (second ? TC_MAXN : 0);
         bool& first = second ? first1 : first0;
-        const uint32_t sa = smem_u32(buf(b)), sb = sa + NP * TC_A_BYTES;
+        const uint32_t sx = smem_u32(xring + (size_t)xb * x_stage);
+        const uint32_t sa = WB ? sx : smem_u32(wring + (size_t)wb * w_stage);
 #pragma unroll
         for (int kk = 0; kk < TC_BK / 16; kk++) {
           const uint32_t off = kk * 32;  // 16 columns of 2 bytes
@@ -396,13 +427,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             const uint64_t w = tc_smem_desc(sa + off);
 #pragma unroll
             for (int p = 0; p < 3; p++) {
-              tc_mma(d, w, tc_smem_desc(sb + p * NT * TC_BK * 2 + off), idesc, first ? 0u : 1u);
+              tc_mma(d, w, tc_smem_desc(sx + TC_A_BYTES + p * x_piece + off), idesc, first ? 0u : 1u);
               first = false;
             }
           } else {
             // Q8_0: Wh.Xh + Wh.Xl + Wl.Xh; K-quants: W1.Xh + W1.Xl + W2.Xh + W2.Xl + W3.Xh.
             const uint64_t wh = tc_smem_desc(sa + off);
-            const uint64_t xh = tc_smem_desc(sb + off), xl = tc_smem_desc(sb + TC_B_BYTES + off);
+            const uint64_t xh = tc_smem_desc(sx + off), xl = tc_smem_desc(sx + x_piece + off);
             tc_mma(d, wh, xh, idesc, first ? 0u : 1u);
             first = false;
             tc_mma(d, wh, xl, idesc, 1u);
@@ -411,7 +442,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             if (WM == TCW_KQ) tc_mma(d, tc_smem_desc(sa + TC_A_BYTES + off), xl, idesc, 1u);
           }
         }
-        tc_commit(&mma_done[b]);
+        tc_commit(&x_empty[xb]);
+        if (DEEP && !WB) tc_commit(&w_empty[wb]);
       }
       tc_commit(acc_full);
     }
@@ -426,7 +458,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     Q6Raw nxt{};
     if (q6 && iters > 0) nxt = tc_q6k_load(a.W, r0 + (tid >> 2), k_begin + kc, r0 + (tid >> 2) < R && k_begin + kc < k_end);
     for (int i = 0; i < (WB ? 0 : iters); i++) {
-      const int b = i & 1;
+      const int b = i % WS;
       const int k0 = k_begin + i * TC_BK + kc;
       Q6Raw cur{};
       if (q6) {
@@ -434,8 +466,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         const int kn = k0 + TC_BK;
         if (i + 1 < iters) nxt = tc_q6k_load(a.W, r0 + (tid >> 2), kn, r0 + (tid >> 2) < R && kn < k_end);
       }
-      if (i >= 2) mbar_wait(&mma_done[b], ((i >> 1) - 1) & 1, a.err);
-      uint8_t* aw = buf(b);
+      if (i >= WS) mbar_wait(&w_empty[b], ((i / WS) - 1) & 1, a.err);
+      uint8_t* aw = wring + (size_t)b * w_stage;
       for (int rr = tid >> 2; rr < TC_BM; rr += TC_DQW * 8) {
         uint4 pc[NP][2];
         if constexpr (WM == TCW_KQ) {

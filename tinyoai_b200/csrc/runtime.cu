@@ -1475,8 +1475,28 @@ static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaS
       return false;
   }
   const int wm = wb ? TCW_BF16 : kq ? TCW_KQ : TCW_Q8;
-  auto kern = wm == TCW_BF16 ? k_gemm_tc<EPI, TCW_BF16> : wm == TCW_KQ ? k_gemm_tc<EPI, TCW_KQ> : k_gemm_tc<EPI, TCW_Q8>;
-  const int tc_smem = tc_smem_bytes(wm);
+  // Deep rings for BF16 and Q8_0 tiles of up to 128 tokens: activation and
+  // weight stages are added in turn (up to TC_MAX_STAGES each) while they
+  // fit. K-quant tiles and 256-token tiles keep two stages per ring.
+  const bool deep = n_tile <= 128 && !kq;
+  int ws = wb ? 0 : 2, xs = 2;
+  if (deep)
+    for (bool grew = true; grew;) {
+      grew = false;
+      if (xs < TC_MAX_STAGES && tc_smem_bytes(wm, n_tile, ws, xs + 1) <= TC_SMEM_LIMIT) {
+        xs++;
+        grew = true;
+      }
+      if (!wb && ws < TC_MAX_STAGES && tc_smem_bytes(wm, n_tile, ws + 1, xs) <= TC_SMEM_LIMIT) {
+        ws++;
+        grew = true;
+      }
+    }
+  auto kern = wm == TCW_BF16 ? k_gemm_tc<EPI, TCW_BF16, true>
+              : wm == TCW_KQ ? k_gemm_tc<EPI, TCW_KQ, false>
+              : deep         ? k_gemm_tc<EPI, TCW_Q8, true>
+                             : k_gemm_tc<EPI, TCW_Q8, false>;
+  const int tc_smem = tc_smem_bytes(wm, n_tile, ws, xs);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem) != cudaSuccess) {
     cudaGetLastError();
     return false;
@@ -1514,6 +1534,8 @@ static bool launch_gemm_tc(const tcu_model* m, Work* w, const GemmArgs& g, cudaS
   // (their weight reads hit L2). Q8_0 is bound by its dequantising warps and
   // measured faster with row tiles first.
   a.tok_fast = (wb || kq) ? 1 : 0;
+  a.ws = ws;
+  a.xs = xs;
   const dim3 grid = a.tok_fast ? dim3(n_pad / n_tile, row_tiles, z) : dim3(row_tiles, n_pad / n_tile, z);
   kern<<<grid, TC_THREADS, tc_smem, s>>>(map, wmap, a);
   NOTE("k_gemm_tc");
