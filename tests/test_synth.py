@@ -30,7 +30,7 @@ def test_prompt_ids():
     assert np.array_equal(a, prompt_ids(512, 65536, seed=0))
 
 
-def test_decode_bytes_match_the_survey():
+def test_decode_bytes_of_the_3b_shape():
     """Q8_0 weight bytes per decoded token: 2.874 GB for the 3B shape."""
     import bench
     total, w1 = bench.decode_bytes(CLIO_3B, -1)
